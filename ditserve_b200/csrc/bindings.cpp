@@ -1,0 +1,242 @@
+// torch bindings of the sm_100a kernels (module ditserve_b200._C).
+// Thin: validate tensors, fill the launch structs from kernels.h, launch on
+// the current CUDA stream.  All shape/stride rules are enforced here so a bad
+// call raises a Python exception instead of reaching the GPU.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "kernels.h"
+
+namespace {
+
+void check_cuda_bf16_2d(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must have unit column stride");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+}
+
+const void* opt_ptr(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr() : nullptr; }
+
+int* status_ptr(const at::Tensor& status) {
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt && status.numel() >= 2,
+              "status must be a CUDA int32 tensor with >= 2 elements");
+  return status.data_ptr<int>();
+}
+
+void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c10::optional<at::Tensor>& bias,
+          int64_t epilogue, const c10::optional<at::Tensor>& R, const c10::optional<at::Tensor>& gate,
+          int64_t gate_stride, int64_t rows_per_batch, const at::Tensor& status, int64_t bn_override) {
+  check_cuda_bf16_2d(A, "A");
+  check_cuda_bf16_2d(B, "B");
+  check_cuda_bf16_2d(C, "C");
+  TORCH_CHECK(A.size(1) == B.size(1), "gemm: K mismatch");
+  TORCH_CHECK(C.size(0) == A.size(0) && C.size(1) == B.size(0), "gemm: C shape mismatch");
+  if (bias.has_value()) {
+    TORCH_CHECK(bias->is_contiguous() && bias->scalar_type() == at::kBFloat16 && bias->numel() == B.size(0),
+                "gemm: bias must be contiguous bf16 [N]");
+  }
+  if (R.has_value()) {
+    check_cuda_bf16_2d(*R, "R");
+    TORCH_CHECK(R->size(0) == C.size(0) && R->size(1) == C.size(1), "gemm: residual shape mismatch");
+  }
+  if (gate.has_value()) {
+    TORCH_CHECK(gate->is_cuda() && gate->scalar_type() == at::kFloat, "gemm: gate must be fp32 CUDA");
+  }
+  const c10::cuda::CUDAGuard guard(A.device());
+  ds::GemmArgs a;
+  a.A = A.data_ptr();
+  a.lda = A.stride(0);
+  a.B = B.data_ptr();
+  a.ldb = B.stride(0);
+  a.C = C.data_ptr();
+  a.ldc = C.stride(0);
+  a.M = static_cast<int>(A.size(0));
+  a.N = static_cast<int>(B.size(0));
+  a.K = static_cast<int>(A.size(1));
+  a.bias = opt_ptr(bias);
+  a.epilogue = static_cast<int>(epilogue);
+  a.R = opt_ptr(R);
+  a.ldr = R.has_value() ? R->stride(0) : 0;
+  a.gate = gate.has_value() ? gate->data_ptr<float>() : nullptr;
+  a.gate_stride = gate_stride;
+  a.rows_per_batch = static_cast<int>(rows_per_batch);
+  a.status = status_ptr(status);
+  a.bn_override = static_cast<int>(bn_override);
+  ds::launch_gemm(a, at::cuda::getCurrentCUDAStream());
+}
+
+void attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
+               const c10::optional<at::Tensor>& lse, int64_t batch, int64_t seq_q, int64_t seq_k,
+               const c10::optional<at::Tensor>& cu_q, const c10::optional<at::Tensor>& cu_k, int64_t max_seq_q,
+               int64_t heads, int64_t heads_kv, int64_t head_dim, double scale, const at::Tensor& status) {
+  check_cuda_bf16_2d(q, "q");
+  check_cuda_bf16_2d(k, "k");
+  check_cuda_bf16_2d(v, "v");
+  check_cuda_bf16_2d(o, "o");
+  TORCH_CHECK(q.size(1) == heads * head_dim, "attention: q width != heads*head_dim");
+  TORCH_CHECK(k.size(1) == heads_kv * head_dim && v.size(1) == heads_kv * head_dim, "attention: kv width");
+  TORCH_CHECK(o.size(0) == q.size(0) && o.size(1) == q.size(1), "attention: o shape");
+  TORCH_CHECK(k.size(0) == v.size(0), "attention: k/v rows");
+  if (!cu_q.has_value()) {
+    TORCH_CHECK(batch * seq_q == q.size(0) && batch * seq_k == k.size(0), "attention: uniform segment sizes");
+  } else {
+    TORCH_CHECK(cu_q->scalar_type() == at::kInt && cu_k.has_value() && cu_k->scalar_type() == at::kInt,
+                "attention: cu_seqlens must be int32");
+    TORCH_CHECK(cu_q->numel() == batch + 1 && cu_k->numel() == batch + 1, "attention: cu_seqlens size");
+  }
+  if (lse.has_value()) {
+    TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->dim() == 2 && lse->size(0) == heads &&
+                    lse->size(1) >= q.size(0) && lse->stride(1) == 1,
+                "attention: lse must be fp32 [heads, >= tokens]");
+  }
+  const c10::cuda::CUDAGuard guard(q.device());
+  ds::AttnArgs a;
+  a.q = q.data_ptr();
+  a.q_row_stride = q.stride(0);
+  a.k = k.data_ptr();
+  a.k_row_stride = k.stride(0);
+  a.v = v.data_ptr();
+  a.v_row_stride = v.stride(0);
+  a.o = o.data_ptr();
+  a.o_row_stride = o.stride(0);
+  a.lse = lse.has_value() ? lse->data_ptr<float>() : nullptr;
+  a.lse_stride = lse.has_value() ? lse->stride(0) : 0;
+  a.total_q = static_cast<int>(q.size(0));
+  a.total_k = static_cast<int>(k.size(0));
+  a.batch = static_cast<int>(batch);
+  a.seq_q = static_cast<int>(seq_q);
+  a.seq_k = static_cast<int>(seq_k);
+  a.cu_seqlens_q = cu_q.has_value() ? cu_q->data_ptr<int>() : nullptr;
+  a.cu_seqlens_k = cu_k.has_value() ? cu_k->data_ptr<int>() : nullptr;
+  a.max_seq_q = static_cast<int>(max_seq_q);
+  a.heads = static_cast<int>(heads);
+  a.heads_kv = static_cast<int>(heads_kv);
+  a.head_dim = static_cast<int>(head_dim);
+  a.softmax_scale = static_cast<float>(scale);
+  a.status = status_ptr(status);
+  ds::launch_attention(a, at::cuda::getCurrentCUDAStream());
+}
+
+void layernorm_modulate(const at::Tensor& x, at::Tensor& y, const c10::optional<at::Tensor>& scale,
+                        const c10::optional<at::Tensor>& shift, int64_t mod_stride, int64_t rows_per_batch,
+                        const c10::optional<at::Tensor>& weight, const c10::optional<at::Tensor>& bias,
+                        double eps) {
+  check_cuda_bf16_2d(x, "x");
+  check_cuda_bf16_2d(y, "y");
+  TORCH_CHECK(x.sizes() == y.sizes(), "layernorm_modulate: shape mismatch");
+  if (scale.has_value()) TORCH_CHECK(scale->scalar_type() == at::kFloat, "scale must be fp32");
+  if (shift.has_value()) TORCH_CHECK(shift->scalar_type() == at::kFloat, "shift must be fp32");
+  if (scale.has_value()) TORCH_CHECK(reinterpret_cast<uintptr_t>(scale->data_ptr()) % 16 == 0, "scale alignment");
+  if (shift.has_value()) TORCH_CHECK(reinterpret_cast<uintptr_t>(shift->data_ptr()) % 16 == 0, "shift alignment");
+  const c10::cuda::CUDAGuard guard(x.device());
+  ds::LayerNormArgs a;
+  a.x = x.data_ptr();
+  a.x_stride = x.stride(0);
+  a.y = y.data_ptr();
+  a.y_stride = y.stride(0);
+  a.rows = static_cast<int>(x.size(0));
+  a.dim = static_cast<int>(x.size(1));
+  a.eps = static_cast<float>(eps);
+  a.scale = scale.has_value() ? scale->data_ptr<float>() : nullptr;
+  a.shift = shift.has_value() ? shift->data_ptr<float>() : nullptr;
+  a.mod_stride = mod_stride;
+  a.rows_per_batch = static_cast<int>(rows_per_batch);
+  a.weight = opt_ptr(weight);
+  a.bias = opt_ptr(bias);
+  ds::launch_layernorm_modulate(a, at::cuda::getCurrentCUDAStream());
+}
+
+void rmsnorm_rope(at::Tensor& x, const c10::optional<at::Tensor>& weight, int64_t width, int64_t groups, double eps,
+                  const c10::optional<at::Tensor>& cos, const c10::optional<at::Tensor>& sin,
+                  int64_t rows_per_batch, int64_t head_dim) {
+  check_cuda_bf16_2d(x, "x");
+  TORCH_CHECK(x.size(1) == width * groups, "rmsnorm_rope: width*groups must equal the view width");
+  if (cos.has_value()) {
+    TORCH_CHECK(sin.has_value() && cos->scalar_type() == at::kFloat && sin->scalar_type() == at::kFloat &&
+                    cos->is_contiguous() && sin->is_contiguous(),
+                "rmsnorm_rope: cos/sin must be contiguous fp32");
+    TORCH_CHECK(cos->size(-1) == head_dim / 2, "rmsnorm_rope: rope table width must be head_dim/2");
+    TORCH_CHECK(head_dim % 8 == 0, "rmsnorm_rope: head_dim must be a multiple of 8");
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  ds::RmsRopeArgs a;
+  a.x = x.data_ptr();
+  a.x_stride = x.stride(0);
+  a.rows = static_cast<int>(x.size(0));
+  a.width = static_cast<int>(width);
+  a.groups = static_cast<int>(groups);
+  a.weight = opt_ptr(weight);
+  a.eps = static_cast<float>(eps);
+  a.rope_cos = cos.has_value() ? cos->data_ptr<float>() : nullptr;
+  a.rope_sin = sin.has_value() ? sin->data_ptr<float>() : nullptr;
+  a.rows_per_batch = static_cast<int>(rows_per_batch);
+  a.head_dim = static_cast<int>(head_dim);
+  ds::launch_rmsnorm_rope(a, at::cuda::getCurrentCUDAStream());
+}
+
+const float* opt_f32(const c10::optional<at::Tensor>& t) {
+  if (!t.has_value()) return nullptr;
+  TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous(), "sched_step: buffers must be contiguous fp32");
+  return t->data_ptr<float>();
+}
+
+void sched_step(const at::Tensor& cond, const c10::optional<at::Tensor>& uncond, double guidance, at::Tensor& sample,
+                double sigma, bool do_corrector, const c10::optional<at::Tensor>& last, double c_last, double c_x0,
+                std::vector<c10::optional<at::Tensor>> c_hist, std::vector<double> c_coef, double p_x, double p_x0,
+                double p_v, std::vector<c10::optional<at::Tensor>> p_hist, std::vector<double> p_coef,
+                const c10::optional<at::Tensor>& x0_out, const c10::optional<at::Tensor>& last_out) {
+  TORCH_CHECK(sample.is_cuda() && sample.scalar_type() == at::kFloat && sample.is_contiguous(),
+              "sched_step: sample must be contiguous fp32 CUDA");
+  TORCH_CHECK(cond.is_contiguous() && cond.numel() == sample.numel(), "sched_step: cond size");
+  TORCH_CHECK(cond.scalar_type() == at::kBFloat16 || cond.scalar_type() == at::kFloat, "sched_step: cond dtype");
+  if (uncond.has_value())
+    TORCH_CHECK(uncond->is_contiguous() && uncond->scalar_type() == cond.scalar_type() &&
+                    uncond->numel() == cond.numel(),
+                "sched_step: uncond must match cond");
+  TORCH_CHECK(c_hist.size() <= 3 && p_hist.size() <= 3 && c_coef.size() == c_hist.size() &&
+                  p_coef.size() == p_hist.size(),
+              "sched_step: at most 3 history terms with matching coefficients");
+  const c10::cuda::CUDAGuard guard(sample.device());
+  ds::SchedStepArgs a;
+  a.cond = cond.data_ptr();
+  a.uncond = opt_ptr(uncond);
+  a.pred_is_bf16 = cond.scalar_type() == at::kBFloat16;
+  a.guidance = static_cast<float>(guidance);
+  a.n = sample.numel();
+  a.sample = sample.data_ptr<float>();
+  a.sigma = static_cast<float>(sigma);
+  a.do_corrector = do_corrector ? 1 : 0;
+  a.last = opt_f32(last);
+  TORCH_CHECK(!do_corrector || a.last != nullptr, "sched_step: corrector needs the last sample");
+  a.c_last = static_cast<float>(c_last);
+  a.c_x0 = static_cast<float>(c_x0);
+  for (size_t i = 0; i < c_hist.size(); ++i) {
+    a.c_hist_ptr[i] = opt_f32(c_hist[i]);
+    a.c_hist[i] = static_cast<float>(c_coef[i]);
+  }
+  a.p_x = static_cast<float>(p_x);
+  a.p_x0 = static_cast<float>(p_x0);
+  a.p_v = static_cast<float>(p_v);
+  for (size_t i = 0; i < p_hist.size(); ++i) {
+    a.p_hist_ptr[i] = opt_f32(p_hist[i]);
+    a.p_hist[i] = static_cast<float>(p_coef[i]);
+  }
+  a.x0_out = x0_out.has_value() ? const_cast<float*>(opt_f32(x0_out)) : nullptr;
+  a.last_out = last_out.has_value() ? const_cast<float*>(opt_f32(last_out)) : nullptr;
+  ds::launch_sched_step(a, at::cuda::getCurrentCUDAStream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of ditserve_b200 (tcgen05 GEMM/attention, fused norms, solver step)";
+  m.def("gemm", &gemm, "C = epilogue(A @ B^T)");
+  m.def("gemm_pick_bn", &ds::gemm_pick_bn);
+  m.def("attention", &attention, "non-causal flash attention (tcgen05/TMEM)");
+  m.def("layernorm_modulate", &layernorm_modulate, "LayerNorm + adaLN modulation");
+  m.def("rmsnorm_rope", &rmsnorm_rope, "RMS norm + interleaved RoPE, in place");
+  m.def("sched_step", &sched_step, "CFG combine + UniPC/Euler latent update");
+}

@@ -1,0 +1,81 @@
+"""Loader for the sm_100a extension and the per-device kernel status word.
+
+CUDA tensors always go through the hand-written kernels in ``ditserve_b200._C``;
+if the extension is missing on a GPU machine every op raises instead of
+silently falling back to PyTorch.  CPU tensors use the reference math in each
+op module (that path exists for the CPU/Gloo contract tests).
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+_lock = threading.Lock()
+_ext = None
+_ext_error: Exception | None = None
+_status: dict[int, torch.Tensor] = {}
+
+
+def ext():
+    """Return the compiled extension module, raising if it was not built."""
+    global _ext, _ext_error
+    if _ext is not None:
+        return _ext
+    with _lock:
+        if _ext is None and _ext_error is None:
+            try:
+                from .. import _C  # type: ignore[attr-defined]
+                _ext = _C
+            except Exception as exc:  # pragma: no cover - depends on the build
+                _ext_error = exc
+    if _ext is None:
+        raise RuntimeError(
+            "ditserve_b200._C is not built (run `python setup.py build_ext --inplace`); "
+            f"CUDA ops have no fallback: {_ext_error!r}")
+    return _ext
+
+
+def available() -> bool:
+    try:
+        ext()
+        return True
+    except RuntimeError:
+        return False
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Device int32[2] (code, site) that kernels write when a bounded wait expires."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _status.get(idx)
+    if buf is None:
+        with _lock:
+            buf = _status.get(idx)
+            if buf is None:
+                buf = torch.zeros(2, dtype=torch.int32, device=torch.device("cuda", idx))
+                _status[idx] = buf
+    return buf
+
+
+class KernelTimeout(RuntimeError):
+    """A device-side wait gave up; the kernel returned early with an error status."""
+
+
+STATUS_NAMES = {1: "mbarrier wait timed out", 2: "peer flag wait timed out", 3: "device argument check failed"}
+
+
+def check_status(device: torch.device | None = None, reset: bool = True) -> None:
+    """Synchronise and raise if any kernel on ``device`` reported an error status."""
+    devices = [device] if device is not None else [torch.device("cuda", i) for i in list(_status)]
+    for dev in devices:
+        buf = status_word(dev)
+        code, site = (int(v) for v in buf.cpu().tolist())
+        if code != 0:
+            if reset:
+                buf.zero_()
+            raise KernelTimeout(f"{STATUS_NAMES.get(code, 'error')} (code {code}, site {site}) on {dev}")
+
+
+def use_kernels(*tensors: torch.Tensor) -> bool:
+    """True when the tensors live on a CUDA device (the kernel path is mandatory there)."""
+    return any(t is not None and t.is_cuda for t in tensors)

@@ -1,0 +1,180 @@
+"""Numerics of every sm_100a kernel against the fp32 PyTorch statement of the op."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from ditserve_b200 import ops
+
+
+def _dev():
+    return torch.device("cuda", 0)
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / b.norm().clamp_min(1e-6)).item()
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 256, 192), (1000, 1536, 1536), (129, 128, 64), (77, 64, 4096),
+                                   (4096, 8960, 1536)])
+@pytest.mark.parametrize("epi", ["none", "gelu", "gated", "res"])
+def test_gemm_epilogues(M, N, K, epi):
+    torch.manual_seed(0)
+    d = _dev()
+    x = torch.randn(M, K, device=d).bfloat16()
+    w = (torch.randn(N, K, device=d) / math.sqrt(K)).bfloat16()
+    b = torch.randn(N, device=d).bfloat16()
+    kw = {}
+    if epi == "gelu":
+        kw["act"] = "gelu"
+    if epi in ("gated", "res"):
+        kw["residual"] = torch.randn(M, N, device=d).bfloat16()
+    if epi == "gated":
+        rpb = (M + 1) // 2
+        kw["gate"] = torch.randn(2, N, device=d)
+        kw["rows_per_batch"] = rpb
+    y = ops.linear(x, w, b, **kw)
+    ref = ops.linear_reference(x.cpu(), w.cpu(), b.cpu(), **{k: (v.cpu() if torch.is_tensor(v) else v)
+                                                              for k, v in kw.items()})
+    ops.check_status(d)
+    assert _rel(y.cpu(), ref) < 1e-2
+    torch.testing.assert_close(y.cpu().float(), ref.float(), rtol=3e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_gemm_tile_widths(bn):
+    torch.manual_seed(1)
+    d = _dev()
+    x = torch.randn(513, 512, device=d).bfloat16()
+    w = (torch.randn(512, 512, device=d) / 20).bfloat16()
+    y = ops.linear(x, w, None, bn=bn)
+    ref = ops.linear_reference(x.cpu(), w.cpu())
+    assert _rel(y.cpu(), ref) < 1e-2
+
+
+def test_gemm_inplace_gated_residual():
+    torch.manual_seed(2)
+    d = _dev()
+    x = torch.randn(640, 1536, device=d).bfloat16()
+    w = (torch.randn(1536, 1536, device=d) / 40).bfloat16()
+    r = torch.randn(640, 1536, device=d).bfloat16()
+    g = torch.randn(1, 1536, device=d)
+    ref = ops.linear_reference(x.cpu(), w.cpu(), None, residual=r.cpu(), gate=g.cpu())
+    ops.linear(x, w, None, residual=r, gate=g, out=r)
+    assert _rel(r.cpu(), ref) < 1e-2
+
+
+@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("B,Sq,Sk,H", [(2, 300, 300, 2), (1, 128, 512, 3), (1, 1000, 77, 2), (1, 64, 1030, 1)])
+def test_attention_dense(D, B, Sq, Sk, H):
+    torch.manual_seed(3)
+    d = _dev()
+    q = torch.randn(B, Sq, H * D, device=d).bfloat16()
+    k = torch.randn(B, Sk, H * D, device=d).bfloat16()
+    v = torch.randn(B, Sk, H * D, device=d).bfloat16()
+    o, lse = ops.attention(q, k, v, H, return_lse=True)
+    ro, rlse = ops.attention_reference(q.cpu(), k.cpu(), v.cpu(), H, return_lse=True)
+    ops.check_status(d)
+    assert _rel(o.cpu(), ro) < 2e-2
+    torch.testing.assert_close(o.cpu().float(), ro.float(), rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(lse.cpu().reshape(H, B, Sq).transpose(0, 1), rlse, rtol=1e-3, atol=2e-2)
+
+
+def test_attention_fused_qkv_view_and_large_logits():
+    torch.manual_seed(4)
+    d = _dev()
+    H, D, S = 4, 128, 777
+    qkv = torch.randn(S, 3 * H * D, device=d).bfloat16()
+    qkv[:, : H * D] *= 6  # large logits exercise the TMEM O rescale path
+    q, k, v = qkv[:, : H * D], qkv[:, H * D: 2 * H * D], qkv[:, 2 * H * D:]
+    o = ops.attention(q, k, v, H)
+    ro = ops.attention_reference(q.cpu(), k.cpu(), v.cpu(), H)
+    assert _rel(o.cpu(), ro) < 2e-2
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_attention_varlen(D):
+    torch.manual_seed(5)
+    d = _dev()
+    H = 3
+    lens_q = [100, 257, 1024, 5]
+    lens_k = [100, 257, 1024, 5]
+    cu = torch.tensor([0] + list(torch.tensor(lens_q).cumsum(0)), dtype=torch.int32)
+    cuk = torch.tensor([0] + list(torch.tensor(lens_k).cumsum(0)), dtype=torch.int32)
+    T, Tk = int(cu[-1]), int(cuk[-1])
+    q = torch.randn(T, H * D, device=d).bfloat16()
+    k = torch.randn(Tk, H * D, device=d).bfloat16()
+    v = torch.randn(Tk, H * D, device=d).bfloat16()
+    o = ops.attention(q, k, v, H, cu_seqlens_q=cu.to(d), cu_seqlens_k=cuk.to(d), max_seqlen_q=max(lens_q))
+    ro = ops.attention_reference(q.cpu(), k.cpu(), v.cpu(), H, cu_seqlens_q=cu, cu_seqlens_k=cuk)
+    assert _rel(o.cpu(), ro) < 2e-2
+
+
+@pytest.mark.parametrize("D", [1536, 3072])
+def test_layernorm_modulate(D):
+    torch.manual_seed(6)
+    d = _dev()
+    x = (torch.randn(2 * 333, D, device=d) * 3 + 1).bfloat16()
+    mod = torch.randn(2, 6, D, device=d)
+    y = ops.layernorm_modulate(x, scale=mod[:, 1], shift=mod[:, 0], rows_per_batch=333)
+    ref = ops.layernorm_modulate_reference(x.cpu(), mod[:, 1].cpu(), mod[:, 0].cpu(), rows_per_batch=333)
+    torch.testing.assert_close(y.cpu().float(), ref.float(), rtol=2e-2, atol=2e-2)
+    w = torch.randn(D, device=d).bfloat16()
+    bb = torch.randn(D, device=d).bfloat16()
+    y2 = ops.layernorm_modulate(x, weight=w, bias=bb)
+    ref2 = ops.layernorm_modulate_reference(x.cpu(), weight=w.cpu(), bias=bb.cpu())
+    torch.testing.assert_close(y2.cpu().float(), ref2.float(), rtol=2e-2, atol=2e-2)
+
+
+def test_rmsnorm_rope_across_heads():
+    torch.manual_seed(7)
+    d = _dev()
+    S, H, D = 300, 12, 128
+    qkv = torch.randn(S, 3 * H * D, device=d).bfloat16()
+    w = torch.randn(H * D, device=d).bfloat16()
+    ang = torch.rand(S, D // 2, device=d) * 6
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    q = qkv[:, : H * D]
+    ref = ops.rope_reference(ops.rms_norm_reference(q.cpu(), w.cpu(), 1e-6), cos.cpu(), sin.cpu(), D)
+    ops.rmsnorm_rope_(q, w, cos=cos, sin=sin, head_dim=D)
+    torch.testing.assert_close(q.cpu().float(), ref.float(), rtol=2e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_rmsnorm_per_head(D):
+    torch.manual_seed(8)
+    d = _dev()
+    H = 24 if D == 64 else 12
+    x = torch.randn(257, H * D, device=d).bfloat16()
+    w = torch.randn(D, device=d).bfloat16()
+    ref = ops.rms_norm_reference(x.cpu(), w.cpu(), 1e-6, groups=H)
+    ops.rmsnorm_rope_(x, w, groups=H, head_dim=D)
+    torch.testing.assert_close(x.cpu().float(), ref.float(), rtol=2e-2, atol=3e-2)
+
+
+def test_sched_step_matches_reference():
+    torch.manual_seed(9)
+    d = _dev()
+    n = 16 * 21 * 8 * 8
+    cond = torch.randn(n, device=d).bfloat16()
+    unc = torch.randn(n, device=d).bfloat16()
+    x = torch.randn(n, device=d)
+    last = torch.randn(n, device=d)
+    h1 = torch.randn(n, device=d)
+    corr = {"last": last, "last_coef": 0.9, "x0_coef": 0.3, "hist": [h1], "hist_coef": [-0.2]}
+    pred = {"x": 0.95, "x0": 0.1, "hist": [h1], "hist_coef": [0.05]}
+    x0o = torch.empty(n, device=d)
+    lo = torch.empty(n, device=d)
+    xr = x.cpu().clone()
+    x0r = torch.empty(n)
+    lr = torch.empty(n)
+    ops.sched_step_reference(cond.cpu(), unc.cpu(), 5.0, xr, 0.7,
+                             {**corr, "last": last.cpu(), "hist": [h1.cpu()]},
+                             {**pred, "hist": [h1.cpu()]}, x0r, lr)
+    ops.sched_step(cond, unc, 5.0, x, 0.7, corr, pred, x0o, lo)
+    torch.testing.assert_close(x.cpu(), xr, rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(x0o.cpu(), x0r, rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(lo.cpu(), lr, rtol=1e-5, atol=1e-4)

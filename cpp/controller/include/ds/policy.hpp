@@ -1,0 +1,52 @@
+// Scheduling-policy registry.  One PolicyTraits record per policy id holds
+// every behaviour the name implies, so the planner, the executor and the
+// simulator consult facts instead of comparing names.  The ids, families and
+// trait values are the reference registry's (src/ditserve/control/policy.cpp:36-265)
+// so study configurations and result records stay interchangeable; the
+// descriptions are ours.  Parameterised names: static-<form>, block-<form>,
+// xdit-<form>, fold-<form>, approx-<form>.
+#pragma once
+#include <string>
+
+#include "ds/form.hpp"
+#include "ds/json.hpp"
+
+namespace ds {
+
+struct PolicyTraits {
+  std::string id, display, family, source;
+  Form fixed_form;
+  int fixed_degree = 0;           // 0: planner chooses the form
+  bool elastic = false;           // regroup at step boundaries
+  bool blocks = false;            // block quanta + sub-step (doorbell) preemption
+  bool rounds = false;            // regroup only every round_steps steps
+  bool knapsack = false;          // v1 utility knapsack
+  bool deadline_dp = false;       // 0/1 deadline group knapsack (requests kept on track)
+  bool best_fit = false;          // EDF best fit + surplus redistribution
+  bool approx = false, v3 = false, v5 = false, fission = false;
+  double widen = 0.0;             // widen a video when per-GPU efficiency stays >= widen
+  std::string image_placement = "first";  // first | pair_fit
+  bool hold_diffuse = false;      // a started video keeps its GPUs (no decode shrink)
+  bool demote_late = true;        // late requests ranked behind feasible ones
+  std::string order = "edf";      // edf | srtf | fcfs
+  bool prune_dominated = false;   // drop forms that a no-wider form beats
+  int min_video_degree = 1;
+  int partition_divisor = 0;      // >0: gpus / divisor GPUs reserved for images
+  int round_steps = 5;
+  bool tiered_memory = false;
+  bool image_batching = false;
+  bool pin_started = false;
+  bool allow_cfg_forms = false;
+  bool feasible_img_priority = true;
+  bool continuous_batch = false;
+  bool sequence_packing = false;
+  bool bubble_free = false;
+};
+
+const PolicyTraits& policy_traits(const std::string& name);  // throws std::invalid_argument
+std::string canonical_policy(const std::string& name);
+std::string legacy_policy_alias(const std::string& name);     // "" when not an alias
+Json policy_catalog();
+Json describe_policy(const PolicyTraits& t);
+
+}  // namespace ds

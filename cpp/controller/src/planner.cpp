@@ -1,0 +1,878 @@
+#include "ds/planner.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <limits>
+#include <map>
+#include <set>
+#include <stdexcept>
+#include <tuple>
+
+namespace ds {
+
+std::vector<std::vector<int>> cluster_groups(int gpus, int size) {
+  std::vector<std::vector<int>> out;
+  if (size <= 0) return out;
+  for (int s = 0; s + size <= gpus; s += size) {
+    std::vector<int> g;
+    for (int i = 0; i < size; ++i) g.push_back(s + i);
+    out.push_back(g);
+  }
+  return out;
+}
+
+void PlanTrace::add(const Json& row) {
+  if (rows.size() < max_rows) rows.push_back(row);
+  else ++dropped;
+}
+
+namespace {
+
+constexpr double kInf = std::numeric_limits<double>::infinity();
+
+struct Settings {
+  PolicyTraits t;
+  std::vector<int> degrees{1, 2, 4, 8};
+  std::vector<Form> forms;  // explicit options.forms
+  int quantum_blocks = 0;   // 0: whole step
+  int continuous_batch = 0; // max members of a continuous image batch (0/1: off)
+  int image_batch = 1;
+  bool pairing = false;
+  bool preempt = true;
+  bool ring_forms = false;
+  int partition_image_gpus = -1;
+  int check_blocks = 1;
+};
+
+Settings resolve(const PolicyTraits& t, const Json& o) {
+  Settings s;
+  s.t = t;
+  if (o.contains("degrees")) {
+    s.degrees.clear();
+    for (const auto& d : o.at("degrees").as_array()) s.degrees.push_back(static_cast<int>(d.as_int()));
+  }
+  if (o.contains("forms"))
+    for (const auto& f : o.at("forms").as_array()) s.forms.push_back(parse_form(f.as_string()));
+  s.t.order = o.str("order", t.order);
+  if (s.t.order != "edf" && s.t.order != "srtf" && s.t.order != "fcfs") throw std::invalid_argument("order must be edf, srtf or fcfs");
+  s.t.widen = o.num("widen_efficiency", t.widen);
+  s.t.image_placement = o.str("image_placement", t.image_placement);
+  if (s.t.image_placement != "first" && s.t.image_placement != "pair_fit")
+    throw std::invalid_argument("image_placement must be first or pair_fit");
+  s.t.min_video_degree = static_cast<int>(o.integer("min_video_degree", t.min_video_degree));
+  s.t.prune_dominated = o.flag("prune_dominated", t.prune_dominated);
+  s.t.demote_late = o.flag("demote_late", t.demote_late);
+  s.t.hold_diffuse = o.flag("hold_diffuse", t.hold_diffuse);
+  s.t.round_steps = static_cast<int>(o.integer("round_steps", t.round_steps));
+  s.t.allow_cfg_forms = o.flag("allow_cfg_forms", t.allow_cfg_forms);
+  s.t.feasible_img_priority = o.flag("feasible_img_priority", t.feasible_img_priority);
+  s.t.blocks = o.flag("block_preemption", t.blocks);
+  s.t.sequence_packing = o.flag("sequence_packing", t.sequence_packing);
+  s.quantum_blocks = static_cast<int>(o.integer("quantum_blocks", 0));
+  const int cb_default = t.continuous_batch ? 8 : 0;
+  s.continuous_batch = static_cast<int>(o.integer("continuous_batch", cb_default));
+  if (!t.continuous_batch && !o.contains("continuous_batch")) s.continuous_batch = 0;
+  if (s.continuous_batch < 0 || s.continuous_batch > 8) throw std::invalid_argument("continuous_batch must be 0..8");
+  s.image_batch = static_cast<int>(o.integer("image_batch", t.image_batching ? 4 : 1));
+  s.pairing = o.flag("pairing", false);
+  s.preempt = o.flag("doorbell", true);
+  s.ring_forms = o.flag("ring_forms", t.id == "diag-2d-usp");
+  s.partition_image_gpus = static_cast<int>(o.integer("partition_image_gpus", -1));
+  s.check_blocks = static_cast<int>(o.integer("check_blocks", 1));
+  return s;
+}
+
+std::vector<Form> forms_for(const Settings& s, const ClusterCost& cost, const std::string& klass, int gpus) {
+  const PolicyTraits& t = s.t;
+  std::vector<Form> forms;
+  if (t.fixed_degree > 0) {
+    if (t.fixed_form.degree() <= gpus) forms.push_back(t.fixed_form);
+    return forms;
+  }
+  const bool cfg_forms = t.allow_cfg_forms || t.prune_dominated || t.min_video_degree >= 2;
+  if (!s.forms.empty()) {
+    for (const auto& f : s.forms)
+      if (f.degree() <= gpus && (cfg_forms || f.cfg == 1)) forms.push_back(f);
+  } else {
+    forms = enumerate_forms(s.degrees, cfg_forms, s.ring_forms, gpus);
+  }
+  const int heads = cost.heads(klass);
+  if (heads > 0)
+    forms.erase(std::remove_if(forms.begin(), forms.end(), [&](const Form& f) { return heads % f.ulysses() != 0; }),
+                forms.end());
+  if (t.prune_dominated && forms.size() > 1) {
+    std::vector<Form> kept;
+    for (const auto& f : forms) {
+      const double sf = cost.step_ms(klass, f);
+      bool dominated = false;
+      for (const auto& g : forms) {
+        if (g == f || g.degree() > f.degree()) continue;
+        const double sg = cost.step_ms(klass, g);
+        if (sg < sf || (sg == sf && g.degree() < f.degree())) {
+          dominated = true;
+          break;
+        }
+      }
+      if (!dominated) kept.push_back(f);
+    }
+    if (!kept.empty()) forms = kept;
+  }
+  if (t.min_video_degree > 1) {
+    std::vector<Form> wide;
+    for (const auto& f : forms)
+      if (f.degree() >= t.min_video_degree) wide.push_back(f);
+    if (!wide.empty()) forms = wide;
+  }
+  std::sort(forms.begin(), forms.end(), [&](const Form& a, const Form& b) {
+    if (a.degree() != b.degree()) return a.degree() < b.degree();
+    return cost.step_ms(klass, a) < cost.step_ms(klass, b);
+  });
+  // one form per degree: the fastest of that size
+  std::vector<Form> best;
+  for (const auto& f : forms)
+    if (best.empty() || best.back().degree() != f.degree()) best.push_back(f);
+  return best;
+}
+
+struct Req {
+  const Json* j = nullptr;
+  std::string id, kind, klass, status;
+  double arrival = 0, deadline = 0;
+  std::vector<int> group;
+  std::string form;
+  int steps_done = 0, steps_total = 0, blocks_done = 0, decode_done = 0;
+  int affinity = -1;
+  bool feasible = true;
+  double best_remaining = 0;
+  bool video() const { return kind == "video"; }
+  bool finished_denoise() const { return steps_done >= steps_total; }
+};
+
+struct Gpus {
+  std::vector<bool> free;
+  std::vector<bool> image_only;
+  int count() const {
+    int n = 0;
+    for (bool f : free) n += f;
+    return n;
+  }
+};
+
+// first fully free aligned group of `size`, preferring `prefer` (no resize), then the most overlap
+std::vector<int> pick_group(const Gpus& g, int size, const std::vector<int>& prefer, bool for_video) {
+  const int n = static_cast<int>(g.free.size());
+  auto usable = [&](int i) { return g.free[i] && !(for_video && g.image_only[i]); };
+  if (static_cast<int>(prefer.size()) == size) {
+    bool ok = true;
+    for (int i : prefer) ok = ok && i >= 0 && i < n && usable(i);
+    if (ok) return prefer;
+  }
+  std::vector<int> best;
+  int best_overlap = -1;
+  for (const auto& grp : cluster_groups(n, size)) {
+    bool ok = true;
+    for (int i : grp) ok = ok && usable(i);
+    if (!ok) continue;
+    int overlap = 0;
+    for (int i : grp) overlap += std::count(prefer.begin(), prefer.end(), i) > 0;
+    if (overlap > best_overlap) {
+      best = grp;
+      best_overlap = overlap;
+    }
+  }
+  return best;
+}
+
+int pick_image_gpu(const Gpus& g, const std::string& placement, int affinity) {
+  const int n = static_cast<int>(g.free.size());
+  if (affinity >= 0) return affinity < n && g.free[affinity] ? affinity : -1;
+  int first = -1;
+  // images prefer their reserved share when the cluster is partitioned
+  for (int pass = 0; pass < 2 && first < 0; ++pass)
+    for (int i = 0; i < n; ++i)
+      if (g.free[i] && (pass == 1 || g.image_only[i])) {
+        first = i;
+        break;
+      }
+  if (placement != "pair_fit" || first < 0) return first;
+  // pair_fit: take a GPU whose CFG-pair partner is already busy, so whole free pairs stay
+  // available for videos; then one whose quad is partly busy
+  for (int span : {2, 4}) {
+    for (int i = 0; i < n; ++i) {
+      if (!g.free[i]) continue;
+      const int base = i - i % span;
+      bool partner_busy = false;
+      for (int k = base; k < std::min(n, base + span); ++k)
+        if (k != i && !g.free[k]) partner_busy = true;
+      if (partner_busy) return i;
+    }
+  }
+  return first;
+}
+
+Json ints(const std::vector<int>& v) {
+  Json a = Json::array();
+  for (int i : v) a.push_back(i);
+  return a;
+}
+
+}  // namespace
+
+std::vector<Form> candidate_forms(const PolicyTraits& t, const ClusterCost& cost, const std::string& klass, int gpus,
+                                  const Json& options) {
+  return forms_for(resolve(t, options), cost, klass, gpus);
+}
+
+Json cluster_plan(const Json& state, const std::string& policy, const ClusterCost& cost, const Json& options,
+                  PlanTrace* trace) {
+  const PolicyTraits& traits = policy_traits(policy);
+  const Settings s = resolve(traits, options);
+  const PolicyTraits& t = s.t;
+  const double now = state.at("now_ms").as_double();
+  const int n = static_cast<int>(state.at("gpus").as_int());
+  if (n <= 0) throw std::invalid_argument("gpus must be positive");
+  Gpus g;
+  g.free.assign(n, true);
+  g.image_only.assign(n, false);
+  if (state.contains("busy")) {
+    const auto& busy = state.at("busy").as_array();
+    if (static_cast<int>(busy.size()) != n) throw std::invalid_argument("busy must list every GPU");
+    for (int i = 0; i < n; ++i) g.free[i] = !busy[i].as_bool();
+  }
+  // static image share
+  int image_share = 0;
+  if (t.partition_divisor > 0 || s.partition_image_gpus >= 0) {
+    image_share = s.partition_image_gpus >= 0 ? s.partition_image_gpus : std::max(1, n / t.partition_divisor);
+    const int video_min = std::max(1, t.fixed_degree > 0 ? t.fixed_degree : t.min_video_degree);
+    image_share = std::max(0, std::min(image_share, n - video_min));
+    for (int i = n - image_share; i < n; ++i) g.image_only[i] = true;
+  }
+  const int video_capacity = n - image_share;
+
+  std::vector<Req> reqs;
+  std::vector<Req> running;
+  std::set<std::string> seen;
+  for (const auto& rj : state.at("requests").as_array()) {
+    Req r;
+    r.j = &rj;
+    r.id = rj.at("request_id").as_string();
+    if (!seen.insert(r.id).second) throw std::invalid_argument("duplicate request_id " + r.id);
+    r.kind = rj.at("kind").as_string();
+    r.klass = rj.at("class").as_string();
+    if (r.kind != "video" && r.kind != "image") throw std::invalid_argument("kind must be video or image");
+    r.status = rj.str("status", "waiting");
+    r.arrival = rj.num("arrival_ms", 0.0);
+    r.deadline = rj.num("deadline_ms", kInf);
+    if (rj.contains("group"))
+      for (const auto& i : rj.at("group").as_array()) r.group.push_back(static_cast<int>(i.as_int()));
+    r.form = rj.str("form", r.group.empty() ? "" : "sp" + std::to_string(r.group.size()));
+    r.steps_total = static_cast<int>(rj.integer("steps_total", cost.steps(r.klass)));
+    r.steps_done = static_cast<int>(rj.integer("steps_done", 0));
+    r.blocks_done = static_cast<int>(rj.integer("blocks_done", 0));
+    r.decode_done = static_cast<int>(rj.integer("decode_done", 0));
+    r.affinity = static_cast<int>(rj.integer("affinity", -1));
+    if (r.status == "running") {
+      running.push_back(r);
+      continue;
+    }
+    if (r.status != "waiting" && r.status != "suspended") continue;
+    // best-case finish on the whole cluster decides feasibility
+    if (r.video()) {
+      double best = kInf;
+      for (const auto& f : forms_for(s, cost, r.klass, video_capacity)) best = std::min(best, cost.remaining_ms(rj, f));
+      if (!std::isfinite(best)) best = cost.remaining_ms(rj, Form{});
+      r.best_remaining = best;
+    } else {
+      r.best_remaining = r.finished_denoise() ? cost.decode_ms(r.klass) : cost.remaining_ms(rj, Form{}) + cost.decode_ms(r.klass);
+      if (!rj.contains("steps_done") && !(s.continuous_batch > 1)) r.best_remaining = cost.service_ms(r.klass);
+    }
+    r.feasible = now + r.best_remaining <= r.deadline;
+    reqs.push_back(r);
+  }
+
+  const bool image_boost = t.feasible_img_priority && t.elastic && !t.deadline_dp && !t.best_fit && !t.knapsack;
+  auto key = [&](const Req& r) {
+    const int late = (t.demote_late && !r.feasible) ? 1 : 0;
+    const int boost = (image_boost && !r.video() && r.feasible) ? 0 : 1;
+    double primary = r.deadline;
+    if (t.order == "srtf") primary = r.best_remaining;
+    if (t.order == "fcfs") primary = r.arrival;
+    // a suspended video that holds its group (no preemption) keeps its place first
+    const int held = (t.hold_diffuse && r.status == "suspended" && r.video()) ? 0 : 1;
+    return std::make_tuple(held, late, boost, primary, r.arrival, r.id);
+  };
+  std::stable_sort(reqs.begin(), reqs.end(), [&](const Req& a, const Req& b) { return key(a) < key(b); });
+  if (trace) {
+    for (const auto& r : reqs) {
+      Json row = Json::object();
+      row["request_id"] = r.id;
+      row["feasible"] = r.feasible;
+      row["laxity_ms"] = std::isfinite(r.deadline) ? r.deadline - now - r.best_remaining : 1e18;
+      row["best_remaining_ms"] = r.best_remaining;
+      trace->add(row);
+    }
+  }
+
+  Json assignments = Json::array();
+  std::set<std::string> placed;
+  struct Placed {
+    std::string id;
+    std::vector<int> group;
+    Form form;
+    size_t index;  // into assignments
+    std::string klass;
+    double deadline;
+    const Json* j;
+  };
+  std::vector<Placed> placed_videos;
+
+  auto take = [&](const std::vector<int>& grp) {
+    for (int i : grp) g.free[i] = false;
+  };
+  auto give = [&](const std::vector<int>& grp) {
+    for (int i : grp) g.free[i] = true;
+  };
+
+  auto video_quantum = [&](const Req& r, Json& a) {
+    if (r.finished_denoise()) {
+      a["quantum"] = "finish";
+      const int chunks = cost.decode_chunks(r.klass);
+      if (chunks > 1) a["decode_frames"] = t.blocks ? 1 : chunks - r.decode_done;
+      return;
+    }
+    if (t.blocks && s.quantum_blocks > 0) {
+      a["quantum"] = s.quantum_blocks;
+    } else {
+      a["quantum"] = "step";
+      if (t.rounds) a["steps"] = std::min(t.round_steps, r.steps_total - r.steps_done);
+    }
+  };
+
+  auto emit_video = [&](const Req& r, const Form& f, const std::vector<int>& grp, const std::string& reason) {
+    Json a = Json::object();
+    a["request_id"] = r.id;
+    a["group"] = ints(grp);
+    a["degree"] = static_cast<int>(grp.size());
+    a["form"] = form_name(f);
+    a["resize"] = !r.group.empty() && r.group != grp;
+    a["reason"] = reason;
+    video_quantum(r, a);
+    take(grp);
+    placed.insert(r.id);
+    placed_videos.push_back({r.id, grp, f, assignments.size(), r.klass, r.deadline, r.j});
+    assignments.push_back(a);
+  };
+
+  // ---- decode-only videos: a finished denoise decodes on one GPU (decode shrink) ----
+  auto place_finish = [&](const Req& r) -> bool {
+    std::vector<int> grp;
+    Form f{1, 1, 1};
+    if (t.hold_diffuse && !r.group.empty()) {
+      grp = pick_group(g, static_cast<int>(r.group.size()), r.group, true);
+      if (!r.form.empty()) f = parse_form(r.form);
+    } else {
+      std::vector<int> prefer;
+      if (!r.group.empty()) prefer.push_back(r.group.front());
+      grp = pick_group(g, 1, prefer, false);
+    }
+    if (grp.empty()) return false;
+    emit_video(r, f, grp, t.hold_diffuse ? "finish-held" : "decode-shrink");
+    return true;
+  };
+
+  std::vector<const Req*> videos, images;
+  for (const auto& r : reqs) (r.video() ? videos : images).push_back(&r);
+
+  // ---- deadline knapsack (TetriServe / SBP-ESP / v1) over movable videos --------------
+  std::map<std::string, Form> dp_choice;
+  if (t.deadline_dp || t.knapsack) {
+    int cap = 0;
+    for (int i = 0; i < n; ++i) cap += g.free[i] && !g.image_only[i];
+    struct Item {
+      const Req* r;
+      Form f;
+      int w;
+      double value;
+    };
+    std::vector<Item> items;
+    for (const Req* r : videos) {
+      if (r->finished_denoise()) continue;
+      for (const auto& f : forms_for(s, cost, r->klass, video_capacity)) {
+        if (now + cost.remaining_ms(*r->j, f) <= r->deadline) {
+          // unit value per request kept on track; v1 weighs urgency (small laxity first)
+          double value = 1.0;
+          if (t.knapsack) value += 1.0 / (1.0 + std::max(0.0, r->deadline - now) / 1000.0);
+          items.push_back({r, f, f.degree(), value});
+          break;  // minimal feasible degree
+        }
+      }
+    }
+    // 0/1 knapsack, max value then min weight
+    const int W = cap;
+    std::vector<double> best(W + 1, 0.0);
+    std::vector<std::vector<int>> pick(W + 1);
+    for (size_t k = 0; k < items.size(); ++k) {
+      for (int w = W; w >= items[k].w; --w) {
+        const double v = best[w - items[k].w] + items[k].value;
+        if (v > best[w] + 1e-12) {
+          best[w] = v;
+          pick[w] = pick[w - items[k].w];
+          pick[w].push_back(static_cast<int>(k));
+        }
+      }
+    }
+    int bw = 0;
+    for (int w = 0; w <= W; ++w)
+      if (best[w] > best[bw] + 1e-12) bw = w;
+    for (int k : pick[bw]) dp_choice[items[k].r->id] = items[k].f;
+  }
+
+  auto fastest_fit = [&](const Req& r, std::vector<int>& grp_out) -> Form {
+    auto forms = forms_for(s, cost, r.klass, video_capacity);
+    Form best{0, 0, 0};
+    double best_ms = kInf;
+    for (const auto& f : forms) {
+      auto grp = pick_group(g, f.degree(), r.group, true);
+      if (grp.empty()) continue;
+      const double ms = cost.remaining_ms(*r.j, f);
+      if (ms < best_ms) {
+        best_ms = ms;
+        best = f;
+        grp_out = grp;
+      }
+    }
+    return best;
+  };
+
+  auto any_waiting_image_unplaced = [&]() {
+    for (const Req* im : images)
+      if (!placed.count(im->id)) return true;
+    return false;
+  };
+
+  // ---- images ----------------------------------------------------------------------
+  auto place_image = [&](const Req& r) -> bool {
+    if (placed.count(r.id)) return true;
+    const int gpu = pick_image_gpu(g, t.image_placement, r.affinity);
+    if (gpu < 0) return false;
+    Json a = Json::object();
+    a["request_id"] = r.id;
+    a["group"] = ints({gpu});
+    a["degree"] = 1;
+    a["form"] = "sp1";
+    a["resize"] = false;
+    // continuous batching: same-class waiting images join while every member keeps its deadline
+    const bool cb = s.continuous_batch > 1 && cost.klass(r.klass).contains("batch_step_ms");
+    const bool ab = !cb && s.image_batch > 1 && cost.klass(r.klass).contains("batch_ms") && g.count() <= 1;
+    if (cb || ab) {
+      std::vector<const Req*> members{&r};
+      const int cap = cb ? s.continuous_batch : s.image_batch;
+      for (const Req* other : images) {
+        if (static_cast<int>(members.size()) >= cap) break;
+        if (other == &r || placed.count(other->id)) continue;
+        if (!s.t.sequence_packing && other->klass != r.klass) continue;
+        if (other->affinity >= 0 && other->affinity != gpu) continue;
+        std::vector<const Json*> js;
+        for (auto* m : members) js.push_back(m->j);
+        js.push_back(other->j);
+        bool ok = true;
+        for (auto* m : members) {
+          const double eff = cost.effective_batch(r.klass, js, s.t.sequence_packing);
+          const int left = m->steps_total - m->steps_done;
+          const double ms = cb ? left * cost.continuous_step_ms(r.klass, eff) + cost.decode_ms(m->klass)
+                               : cost.batch_ms(r.klass, static_cast<int>(js.size()));
+          if (m->feasible && now + ms > m->deadline) ok = false;
+        }
+        if (ok) members.push_back(other);
+      }
+      if (members.size() > 1 || cb) {
+        Json b = Json::array();
+        for (auto* m : members) {
+          b.push_back(m->id);
+          placed.insert(m->id);
+        }
+        a["batch"] = b;
+      }
+      a["quantum"] = cb ? "continuous_batch" : "atomic";
+      a["reason"] = cb ? "continuous-batch" : (members.size() > 1 ? "image-batch" : t.image_placement);
+    } else {
+      a["quantum"] = r.finished_denoise() && r.j->contains("steps_done") ? "finish" : "atomic";
+      a["reason"] = t.image_placement;
+    }
+    g.free[gpu] = false;
+    placed.insert(r.id);
+    assignments.push_back(a);
+    return true;
+  };
+
+  // ---- main pass in rank order -------------------------------------------------------
+  for (const auto& r : reqs) {
+    if (placed.count(r.id)) continue;
+    if (!r.video()) {
+      place_image(r);
+      continue;
+    }
+    if (r.finished_denoise()) {
+      place_finish(r);
+      continue;
+    }
+    const auto forms = forms_for(s, cost, r.klass, video_capacity);
+    if (forms.empty()) continue;
+    if (t.hold_diffuse && r.status == "suspended" && !r.group.empty()) {
+      // run-to-completion baselines resume on exactly their GPUs
+      auto grp = pick_group(g, static_cast<int>(r.group.size()), r.group, true);
+      if (grp == r.group) emit_video(r, r.form.empty() ? forms.front() : parse_form(r.form), grp, "held");
+      continue;
+    }
+    if (t.fixed_degree > 0) {
+      auto grp = pick_group(g, t.fixed_form.degree(), r.group, true);
+      if (!grp.empty()) emit_video(r, t.fixed_form, grp, "fixed");
+      continue;
+    }
+    if (t.deadline_dp || t.knapsack) {
+      auto it = dp_choice.find(r.id);
+      if (it != dp_choice.end()) {
+        auto grp = pick_group(g, it->second.degree(), r.group, true);
+        if (!grp.empty()) {
+          emit_video(r, it->second, grp, "knapsack");
+          continue;
+        }
+      }
+      continue;  // leftovers handled below
+    }
+    // minimal form that meets the deadline, else the fastest that fits
+    Form chosen{0, 0, 0};
+    std::vector<int> grp;
+    std::string reason;
+    for (const auto& f : forms) {
+      if (now + cost.remaining_ms(*r.j, f) > r.deadline) continue;
+      auto cand = pick_group(g, f.degree(), r.group, true);
+      if (cand.empty()) continue;
+      chosen = f;
+      grp = cand;
+      reason = t.best_fit ? "best-fit" : "feasible-min";
+      break;
+    }
+    if (chosen.degree() == 0) {
+      if (t.best_fit) {
+        // largest group that fits
+        for (auto it = forms.rbegin(); it != forms.rend(); ++it) {
+          auto cand = pick_group(g, it->degree(), r.group, true);
+          if (!cand.empty()) {
+            chosen = *it;
+            grp = cand;
+            reason = "best-fit-largest";
+            break;
+          }
+        }
+      } else {
+        chosen = fastest_fit(r, grp);
+        reason = r.feasible ? "fastest-fit" : "late-fastest";
+      }
+    }
+    if (chosen.degree() == 0) continue;
+    // widen while the per-GPU efficiency stays above the threshold and no image is starved
+    if (t.widen > 0 && !t.best_fit) {
+      for (const auto& f : forms) {
+        if (f.degree() <= chosen.degree()) continue;
+        const double base_work = cost.step_ms(r.klass, chosen) * chosen.degree();
+        const double wide_work = cost.step_ms(r.klass, f) * f.degree();
+        if (base_work / wide_work < t.widen) break;
+        if (any_waiting_image_unplaced()) break;
+        give(grp);
+        auto cand = pick_group(g, f.degree(), r.group, true);
+        take(grp);
+        if (cand.empty()) continue;
+        chosen = f;
+        grp = cand;
+        reason = "widened";
+      }
+    }
+    emit_video(r, chosen, grp, reason);
+  }
+
+  // ---- knapsack leftovers: widest-first in EDF order to requests no size saves -------
+  if (t.deadline_dp || t.knapsack) {
+    for (const Req* r : videos) {
+      if (placed.count(r->id) || r->finished_denoise()) continue;
+      std::vector<int> grp;
+      auto forms = forms_for(s, cost, r->klass, video_capacity);
+      for (auto it = forms.rbegin(); it != forms.rend(); ++it) {
+        grp = pick_group(g, it->degree(), r->group, true);
+        if (!grp.empty()) {
+          emit_video(*r, *it, grp, "knapsack-leftover");
+          break;
+        }
+      }
+    }
+  }
+
+  // ---- surplus redistribution (EDF-BF) / idle widening (knapsack baselines) ----------
+  if ((t.best_fit || t.deadline_dp) && !any_waiting_image_unplaced()) {
+    bool grew = true;
+    while (grew) {
+      grew = false;
+      for (auto& pv : placed_videos) {
+        Json& a = assignments.at(pv.index);
+        if (a.at("quantum").is_string() && a.at("quantum").as_string() == "finish") continue;
+        auto forms = forms_for(s, cost, pv.klass, video_capacity);
+        for (const auto& f : forms) {
+          if (f.degree() <= pv.form.degree()) continue;
+          give(pv.group);
+          auto cand = pick_group(g, f.degree(), pv.group, true);
+          if (cand.empty() || cost.step_ms(pv.klass, f) >= cost.step_ms(pv.klass, pv.form)) {
+            take(pv.group);
+            continue;
+          }
+          take(cand);
+          pv.group = cand;
+          pv.form = f;
+          a["group"] = ints(cand);
+          a["degree"] = f.degree();
+          a["form"] = form_name(f);
+          a["reason"] = "surplus";
+          grew = true;
+          break;
+        }
+      }
+    }
+  }
+
+  // ---- lockstep pairing: an unplaced video joins a placed one on its group -----------
+  if (s.pairing && t.elastic) {
+    for (const Req* r : videos) {
+      if (placed.count(r->id) || r->finished_denoise()) continue;
+      for (auto& pv : placed_videos) {
+        Json& a = assignments.at(pv.index);
+        if (a.contains("pair") || !a.at("quantum").is_string() || a.at("quantum").as_string() != "step") continue;
+        const double alone = cost.step_ms(pv.klass, pv.form);
+        const double paired = cost.pair_ms(pv.klass, r->klass, pv.form);
+        if (paired >= alone + cost.step_ms(r->klass, pv.form)) continue;
+        const int left = static_cast<int>(pv.j->integer("steps_total", cost.steps(pv.klass)) - pv.j->integer("steps_done", 0));
+        if (now + left * paired > pv.deadline) continue;
+        a["pair"] = r->id;
+        Json b = Json::object();
+        b["request_id"] = r->id;
+        b["group"] = ints(pv.group);
+        b["degree"] = pv.form.degree();
+        b["form"] = form_name(pv.form);
+        b["quantum"] = "step";
+        b["pair"] = pv.id;
+        b["resize"] = !r->group.empty() && r->group != pv.group;
+        b["reason"] = "paired";
+        placed.insert(r->id);
+        assignments.push_back(b);
+        break;
+      }
+    }
+  }
+
+  Json out = Json::object();
+  out["assignments"] = assignments;
+
+  // ---- sub-step preemption of running video groups for waiting images -----------------
+  Json preempt = Json::array();
+  size_t skips = 0;
+  if (t.blocks && s.preempt && !running.empty()) {
+    std::vector<ImageDemand> demand;
+    for (const Req* im : images) {
+      if (placed.count(im->id)) continue;
+      demand.push_back({im->affinity, im->deadline, im->best_remaining});
+    }
+    if (!demand.empty()) {
+      std::vector<RunningGroup> groups;
+      for (const auto& r : running) {
+        if (!r.video() || r.group.empty()) continue;
+        Form f = r.form.empty() ? Form{1, static_cast<int>(r.group.size()), 1} : parse_form(r.form);
+        const double bms = cost.block_ms(r.klass, f);
+        const double elapsed = std::max(0.0, now - r.j->num("quantum_started_ms", now));
+        auto timing = estimate_preemption_timing(bms, cost.blocks_per_step(r.klass), r.blocks_done, elapsed,
+                                                 std::max(1, s.check_blocks), 1, f.sp > 1);
+        groups.push_back({r.id, r.group, timing.stop_ms, timing.remaining_ms, cost.resume_ms(r.klass),
+                          r.j->flag("rung", false)});
+      }
+      auto sel = select_deadline_preemption(now, demand, groups);
+      for (const auto& id : sel.selected) preempt.push_back(id);
+      skips = sel.deadline_skips;
+    }
+  }
+  out["preempt"] = preempt;
+  out["deadline_skips"] = static_cast<int>(skips);
+  return out;
+}
+
+// ---------------------------------------------------------------------------------------
+PreemptionTiming estimate_preemption_timing(double block_ms, int blocks_total, int blocks_done, double elapsed_ms,
+                                            int check_blocks, int blocks_per_iteration, bool delayed_group_check) {
+  if (!(block_ms > 0) || !std::isfinite(block_ms) || blocks_total <= 0 || blocks_done < 0 || !(elapsed_ms >= 0) ||
+      check_blocks <= 0 || blocks_per_iteration <= 0)
+    throw std::invalid_argument("invalid block preemption timing");
+  PreemptionTiming t;
+  t.stop_ms = block_ms * check_blocks * blocks_per_iteration * (delayed_group_check ? 2 : 1);
+  t.remaining_ms = std::max(block_ms, std::max(0, blocks_total - blocks_done) * block_ms - elapsed_ms);
+  return t;
+}
+
+bool preemption_converts_deadline(double now_ms, double deadline_ms, double service_ms, double stop_ms,
+                                  double boundary_ms) {
+  for (double v : {now_ms, deadline_ms, service_ms, stop_ms, boundary_ms})
+    if (!std::isfinite(v)) throw std::invalid_argument("non-finite preemption input");
+  if (now_ms < 0 || service_ms < 0 || stop_ms < 0 || boundary_ms < 0)
+    throw std::invalid_argument("negative preemption input");
+  const bool late_if_patient = now_ms + boundary_ms + service_ms > deadline_ms;
+  const bool on_time_if_stopped = now_ms + std::min(stop_ms, boundary_ms) + service_ms <= deadline_ms;
+  return late_if_patient && on_time_if_stopped;
+}
+
+namespace {
+void validate_groups(const std::vector<RunningGroup>& running) {
+  std::set<int> used;
+  std::set<std::string> ids;
+  for (const auto& r : running) {
+    if (r.request_id.empty() || !ids.insert(r.request_id).second || r.group.empty())
+      throw std::invalid_argument("invalid running group");
+    for (double v : {r.stop_ms, r.remaining_ms, r.resume_ms})
+      if (!std::isfinite(v) || v < 0) throw std::invalid_argument("invalid running group timing");
+    for (int gpu : r.group)
+      if (gpu < 0 || !used.insert(gpu).second) throw std::invalid_argument("running groups must be disjoint");
+  }
+}
+double displaced(const RunningGroup& r) {
+  return r.group.size() * (std::min(r.stop_ms, r.remaining_ms) + r.resume_ms);
+}
+}  // namespace
+
+std::vector<std::string> select_preemption_groups(const std::vector<int>& affinities,
+                                                  const std::vector<RunningGroup>& running) {
+  validate_groups(running);
+  std::set<int> pinned;
+  size_t flexible = 0;
+  for (int a : affinities) {
+    if (a < -1) throw std::invalid_argument("invalid image affinity");
+    if (a < 0) ++flexible;
+    else pinned.insert(a);
+  }
+  std::vector<std::string> chosen;
+  std::set<int> freed;
+  std::vector<const RunningGroup*> optional;
+  int optional_gpus = 0;
+  for (const auto& r : running) {
+    bool must = r.rung;
+    for (int gpu : r.group) must = must || pinned.count(gpu);
+    if (must) {
+      freed.insert(r.group.begin(), r.group.end());
+      if (!r.rung) chosen.push_back(r.request_id);
+    } else {
+      optional.push_back(&r);
+      optional_gpus += static_cast<int>(r.group.size());
+    }
+  }
+  size_t spare = 0;
+  for (int gpu : freed) spare += !pinned.count(gpu);
+  if (flexible <= spare) return chosen;
+  const int need = static_cast<int>(std::min<size_t>(flexible - spare, optional_gpus));
+  if (need == 0) return chosen;
+  // min displaced GPU-time to free >= need GPUs (fewer interruptions on ties)
+  struct Cell {
+    double cost = kInf;
+    std::vector<std::string> ids;
+  };
+  std::vector<Cell> dp(optional_gpus + 1);
+  dp[0].cost = 0;
+  for (const RunningGroup* r : optional) {
+    const int w = static_cast<int>(r->group.size());
+    for (int c = optional_gpus - w; c >= 0; --c) {
+      if (!std::isfinite(dp[c].cost)) continue;
+      const double v = dp[c].cost + displaced(*r);
+      Cell& dst = dp[c + w];
+      if (v < dst.cost || (v == dst.cost && dp[c].ids.size() + 1 < dst.ids.size())) {
+        dst = dp[c];
+        dst.cost = v;
+        dst.ids.push_back(r->request_id);
+      }
+    }
+  }
+  int best = need;
+  for (int c = need + 1; c <= optional_gpus; ++c)
+    if (dp[c].cost < dp[best].cost) best = c;
+  chosen.insert(chosen.end(), dp[best].ids.begin(), dp[best].ids.end());
+  return chosen;
+}
+
+DeadlinePreemption select_deadline_preemption(double now_ms, const std::vector<ImageDemand>& waiting,
+                                              const std::vector<RunningGroup>& running) {
+  validate_groups(running);
+  auto demand = waiting;
+  for (const auto& d : demand) {
+    if (d.affinity < -1) throw std::invalid_argument("invalid image affinity");
+    preemption_converts_deadline(now_ms, d.deadline_ms, d.service_ms, 0, 0);  // validates
+  }
+  std::stable_sort(demand.begin(), demand.end(), [](const ImageDemand& a, const ImageDemand& b) {
+    if (a.deadline_ms != b.deadline_ms) return a.deadline_ms < b.deadline_ms;
+    return a.affinity >= 0 && b.affinity < 0;
+  });
+  auto groups = running;
+  std::set<int> reserved;
+  DeadlinePreemption out;
+  for (const auto& d : demand) {
+    auto slot = [&](const RunningGroup& r) {
+      for (int gpu : r.group)
+        if (!reserved.count(gpu) && (d.affinity < 0 || gpu == d.affinity)) return gpu;
+      return -1;
+    };
+    // tight SLOs tolerate a doorbell's own latency on an already-rung group
+    const bool tight = d.deadline_ms >= now_ms + 0.85 * d.service_ms && d.deadline_ms - now_ms <= 1.35 * d.service_ms;
+    auto grace = [&](const RunningGroup& r) { return tight ? std::max(1.5 * r.stop_ms, 120.0) : 0.0; };
+    double boundary = kInf;
+    int reuse = -1;
+    double reuse_at = kInf;
+    for (size_t i = 0; i < groups.size(); ++i) {
+      const auto& r = groups[i];
+      if (slot(r) < 0) continue;
+      const double response = r.rung ? std::min(r.stop_ms, r.remaining_ms) : r.remaining_ms;
+      boundary = std::min(boundary, response);
+      if (r.rung && now_ms + response + d.service_ms <= d.deadline_ms + grace(r) && response < reuse_at) {
+        reuse = static_cast<int>(i);
+        reuse_at = response;
+      }
+    }
+    if (reuse >= 0) {
+      reserved.insert(slot(groups[reuse]));
+      continue;
+    }
+    int best = -1;
+    double best_cost = kInf;
+    auto consider = [&](size_t i) {
+      const double c = displaced(groups[i]);
+      if (c < best_cost || (c == best_cost && best >= 0 && groups[i].group.size() < groups[best].group.size())) {
+        best = static_cast<int>(i);
+        best_cost = c;
+      }
+    };
+    if (std::isfinite(boundary) && now_ms + boundary + d.service_ms > d.deadline_ms) {
+      for (size_t i = 0; i < groups.size(); ++i) {
+        const auto& r = groups[i];
+        if (r.rung || slot(r) < 0) continue;
+        if (preemption_converts_deadline(now_ms, d.deadline_ms, d.service_ms, r.stop_ms, r.remaining_ms)) consider(i);
+      }
+      if (best < 0 && tight) {
+        for (size_t i = 0; i < groups.size(); ++i) {
+          const auto& r = groups[i];
+          if (r.rung || slot(r) < 0 || r.stop_ms >= r.remaining_ms) continue;
+          if (now_ms + std::min(r.stop_ms, r.remaining_ms) + d.service_ms > d.deadline_ms + grace(r)) continue;
+          consider(i);
+        }
+      }
+    }
+    if (best < 0) {
+      ++out.deadline_skips;
+      continue;
+    }
+    out.selected.push_back(groups[best].request_id);
+    groups[best].rung = true;
+    reserved.insert(slot(groups[best]));
+  }
+  return out;
+}
+
+}  // namespace ds

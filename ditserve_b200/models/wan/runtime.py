@@ -1,0 +1,217 @@
+"""Wan request state and step engine.
+
+A request is normalised (H, W multiples of 16, frames = 4k+1), seeded on the
+host (CPU generator, so the latent is identical on every device and every SP
+degree), and owns a UniPC flow scheduler with device-resident history.  One
+``step`` = one DiT forward of both CFG branches (batched as B=2 on one SP
+group, or one branch per group under CFG parallelism with a prediction
+exchange) followed by the fused CFG+UniPC update.
+
+Reference behaviour: workers/ditserve/models/wan/runtime.py:117-150 (spec),
+:603-657 (prepare), :673-720 (step), :784-865 (snapshots).
+"""
+from __future__ import annotations
+
+import hashlib
+import io
+from dataclasses import asdict, dataclass, field
+
+import torch
+
+from ...schedulers import UniPCFlowScheduler
+from .config import CONFIGS, WanConfig
+from .model import LocalAttention, WanTransformer
+
+
+@dataclass
+class WanSpec:
+    model: str = "wan2.1-t2v-1.3b"
+    height: int = 480
+    width: int = 832
+    frames: int = 81
+    steps: int = 50
+    guidance: float = 5.0
+    seed: int = 0
+    flow_shift: float | None = None
+    text_len: int | None = None
+    prompt: str = ""
+    negative_prompt: str = ""
+
+    @classmethod
+    def normalize(cls, raw: dict) -> "WanSpec":
+        known = {f for f in cls.__dataclass_fields__}
+        unknown = set(raw) - known
+        if unknown:
+            raise ValueError(f"unknown Wan spec fields: {sorted(unknown)}")
+        spec = cls(**raw)
+        if spec.model not in CONFIGS:
+            raise ValueError(f"unknown Wan model {spec.model!r}")
+        if spec.height % 16 or spec.width % 16:
+            raise ValueError("height and width must be multiples of 16")
+        if spec.frames < 1 or (spec.frames - 1) % 4:
+            raise ValueError("frames must be 4k+1")
+        if spec.steps < 1:
+            raise ValueError("steps must be positive")
+        return spec
+
+    def config(self) -> WanConfig:
+        return CONFIGS[self.model]
+
+    def latent_shape(self) -> tuple[int, int, int, int]:
+        cfg = self.config()
+        st, ss, _ = cfg.vae_stride
+        return (cfg.in_channels, (self.frames - 1) // st + 1, self.height // ss, self.width // ss)
+
+    def to_dict(self) -> dict:
+        return asdict(self)
+
+
+def synthetic_text(seed: int, length: int, dim: int, which: int) -> torch.Tensor:
+    """Seeded N(0,1) text-encoder output standing in for UMT5 (no checkpoint offline)."""
+    g = torch.Generator(device="cpu").manual_seed(int(seed) * 2 + which + 0x5eed)
+    return torch.randn(1, length, dim, generator=g)
+
+
+@dataclass
+class WanRequestState:
+    spec: WanSpec
+    latents: torch.Tensor            # fp32 [1, C, F, H, W], device
+    scheduler: UniPCFlowScheduler
+    context: torch.Tensor            # [1, L, text_dim] model dtype, device
+    negative: torch.Tensor | None    # [1, L, text_dim] or None (guidance <= 1)
+    step: int = 0
+    block: int = 0                   # next block inside the current step (block executor)
+    packets: dict = field(default_factory=dict)
+    metrics: dict = field(default_factory=dict)
+
+    @property
+    def done(self) -> bool:
+        return self.step >= self.spec.steps
+
+    def latent_digest(self) -> str:
+        return hashlib.sha256(self.latents.detach().cpu().contiguous().numpy().tobytes()).hexdigest()
+
+
+class CFGLocal:
+    """Both CFG branches on this SP group (batched as B = 2)."""
+
+    cfg_size = 1
+    cfg_rank = 0
+
+    def exchange(self, pred_mine: torch.Tensor):  # pragma: no cover - unused for local CFG
+        raise RuntimeError("no CFG partner")
+
+
+class WanEngine:
+    def __init__(self, cfg: WanConfig | str, device="cuda", dtype=torch.bfloat16, model: WanTransformer | None = None,
+                 pctx=None, cfg_plan=None, seed: int = 0):
+        self.cfg = CONFIGS[cfg] if isinstance(cfg, str) else cfg
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.model = model or WanTransformer.random_init(self.cfg, device=self.device, dtype=dtype, seed=seed)
+        self.model.eval()
+        self.pctx = pctx or LocalAttention()
+        self.cfg_plan = cfg_plan or CFGLocal()
+
+    # ------------------------------------------------------------------ requests
+    def prepare(self, spec: WanSpec | dict, context: torch.Tensor | None = None,
+                negative: torch.Tensor | None = None) -> WanRequestState:
+        spec = spec if isinstance(spec, WanSpec) else WanSpec.normalize(spec)
+        if spec.model != self.cfg.name:
+            raise ValueError(f"engine hosts {self.cfg.name}, request wants {spec.model}")
+        shape = spec.latent_shape()
+        g = torch.Generator(device="cpu").manual_seed(int(spec.seed))
+        latents = torch.randn((1, *shape), generator=g, dtype=torch.float32).to(self.device)
+        L = spec.text_len or self.cfg.text_len
+        if context is None:
+            context = synthetic_text(spec.seed, L, self.cfg.text_dim, 0)
+        if negative is None and spec.guidance > 1.0:
+            negative = synthetic_text(spec.seed, L, self.cfg.text_dim, 1)
+        sched = UniPCFlowScheduler(spec.steps, spec.flow_shift or self.cfg.flow_shift)
+        return WanRequestState(spec=spec, latents=latents, scheduler=sched,
+                               context=context.to(self.device, self.dtype),
+                               negative=None if negative is None else negative.to(self.device, self.dtype))
+
+    def branches(self, st: WanRequestState) -> list[int]:
+        """CFG branches this rank computes: [0, 1] locally, [cfg_rank] under CFG parallelism."""
+        if st.negative is None:
+            return [0]
+        if self.cfg_plan.cfg_size == 2:
+            return [self.cfg_plan.cfg_rank]
+        return [0, 1]
+
+    def _inputs(self, st: WanRequestState):
+        br = self.branches(st)
+        ctx = torch.cat([st.context if b == 0 else st.negative for b in br], 0)
+        lat = st.latents.expand(len(br), *st.latents.shape[1:])
+        t = torch.full((len(br),), float(st.scheduler.timestep()), device=self.device)
+        return br, lat, t, ctx
+
+    @torch.inference_mode()
+    def predict(self, st: WanRequestState):
+        """Velocity predictions (cond, uncond-or-None) of the current step."""
+        br, lat, t, ctx = self._inputs(st)
+        pred = self.model(lat, t, ctx, self.pctx)
+        return self._split(st, br, pred)
+
+    def _split(self, st, br, pred):
+        if st.negative is None:
+            return pred[0], None
+        if len(br) == 2:
+            return pred[0], pred[1]
+        theirs = self.cfg_plan.exchange(pred[0])
+        return (pred[0], theirs) if br[0] == 0 else (theirs, pred[0])
+
+    @torch.inference_mode()
+    def apply(self, st: WanRequestState, cond: torch.Tensor, uncond: torch.Tensor | None):
+        st.scheduler.step(st.latents.view(-1), cond.reshape(-1), None if uncond is None else uncond.reshape(-1),
+                          st.spec.guidance)
+        st.step += 1
+        st.block = 0
+        st.packets.clear()
+        return st
+
+    def step(self, st: WanRequestState) -> WanRequestState:
+        if st.done:
+            raise RuntimeError("request already finished")
+        cond, uncond = self.predict(st)
+        return self.apply(st, cond, uncond)
+
+    def run(self, st: WanRequestState, steps: int | None = None) -> WanRequestState:
+        n = st.spec.steps - st.step if steps is None else steps
+        for _ in range(n):
+            self.step(st)
+        return st
+
+    # ------------------------------------------------------------------ snapshots
+    def snapshot(self, st: WanRequestState, device="cpu") -> dict:
+        """Exact request state (latents + solver history + text) on ``device`` (pinned when CPU)."""
+        def mv(t):
+            if t is None:
+                return None
+            out = t.detach().to(device, copy=True)
+            return out.pin_memory() if str(device) == "cpu" and torch.cuda.is_available() else out
+        return dict(kind="wan_request.v1", spec=st.spec.to_dict(), step=st.step, latents=mv(st.latents),
+                    context=mv(st.context), negative=mv(st.negative),
+                    scheduler=st.scheduler.state_dict(device=device))
+
+    def restore(self, snap: dict) -> WanRequestState:
+        if snap.get("kind") != "wan_request.v1":
+            raise ValueError("not a Wan request snapshot")
+        spec = WanSpec.normalize(snap["spec"])
+        st = WanRequestState(spec=spec, latents=snap["latents"].to(self.device, copy=True),
+                             scheduler=UniPCFlowScheduler.from_state_dict(snap["scheduler"], self.device),
+                             context=snap["context"].to(self.device, copy=True),
+                             negative=None if snap["negative"] is None else snap["negative"].to(self.device, copy=True),
+                             step=int(snap["step"]))
+        return st
+
+    @staticmethod
+    def pack(snap: dict) -> bytes:
+        buf = io.BytesIO()
+        torch.save(snap, buf)
+        return buf.getvalue()
+
+    @staticmethod
+    def unpack(data: bytes) -> dict:
+        return torch.load(io.BytesIO(data), weights_only=False)

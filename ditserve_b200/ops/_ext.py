@@ -36,6 +36,24 @@ def ext():
     return _ext
 
 
+_launches: dict[str, int] = {}
+
+
+def kernel(name: str):
+    """The bound extension entry point ``name``; counts one launch per call."""
+    fn = getattr(ext(), name)
+    _launches[name] = _launches.get(name, 0) + 1
+    return fn
+
+
+def launch_counts(reset: bool = False) -> dict[str, int]:
+    """Kernel launches issued through this package since the last reset (host-side count)."""
+    out = dict(_launches)
+    if reset:
+        _launches.clear()
+    return out
+
+
 def available() -> bool:
     try:
         ext()

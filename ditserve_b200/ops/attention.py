@@ -11,7 +11,7 @@ import math
 
 import torch
 
-from ._ext import ext, status_word, use_kernels
+from ._ext import kernel, status_word, use_kernels
 
 
 def attention_reference(q, k, v, heads, heads_kv=None, cu_seqlens_q=None, cu_seqlens_k=None, scale=None,
@@ -81,7 +81,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *, 
     ckk = cu_seqlens_k.to(torch.int32) if cu_seqlens_k is not None else None
     if cq is not None and max_seqlen_q is None:
         max_seqlen_q = int((cq[1:] - cq[:-1]).max().item())
-    ext().attention(q2, k2, v2, o2, lse, B, Sq, Sk, cq, ckk, int(max_seqlen_q or 0), heads, heads_kv, d,
+    kernel("attention")(q2, k2, v2, o2, lse, B, Sq, Sk, cq, ckk, int(max_seqlen_q or 0), heads, heads_kv, d,
                     float(scale), status_word(q.device))
     o = out.reshape(*q.shape[:-1], width)
     return (o, lse) if return_lse else o

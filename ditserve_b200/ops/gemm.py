@@ -18,7 +18,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from ._ext import ext, status_word, use_kernels
+from ._ext import kernel, status_word, use_kernels
 
 EPI_NONE, EPI_GELU, EPI_GATED_RES, EPI_RES = 0, 1, 2, 3
 
@@ -79,6 +79,6 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None, *, a
         if gate.stride(-1) != 1:
             raise ValueError("gate must have unit column stride")
         gate_stride = gate.stride(0) if gate.shape[0] > 1 else 0
-    ext().gemm(x2, w, out2, b, epi, r2, gate, gate_stride, int(rows_per_batch or M),
+    kernel("gemm")(x2, w, out2, b, epi, r2, gate, gate_stride, int(rows_per_batch or M),
                status_word(x.device), bn)
     return out2.reshape(*shape[:-1], N)

@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import torch
 
-from ._ext import ext, use_kernels
+from ._ext import kernel, use_kernels
 
 
 def _batch_rows(x2, rows_per_batch, mod):
@@ -63,7 +63,7 @@ def layernorm_modulate(x: torch.Tensor, scale: torch.Tensor | None = None, shift
             assert sh.stride(0) == sc.stride(0) or sh.shape[0] == 1, "scale/shift must share a row stride"
     elif sh is not None:
         mod_stride = sh.stride(0) if sh.shape[0] > 1 else 0
-    ext().layernorm_modulate(x2, y2, sc, sh, mod_stride, int(rows_per_batch or x2.shape[0]), weight, bias,
+    kernel("layernorm_modulate")(x2, y2, sc, sh, mod_stride, int(rows_per_batch or x2.shape[0]), weight, bias,
                              float(eps))
     return y2.reshape(shape)
 
@@ -110,6 +110,6 @@ def rmsnorm_rope_(x: torch.Tensor, weight: torch.Tensor | None, *, groups: int =
         return x
     x2 = x if x.dim() == 2 else x.reshape(-1, x.shape[-1])
     width = x2.shape[1] // groups
-    ext().rmsnorm_rope(x2, weight, width, groups, float(eps), cos, sin, int(rows_per_batch or x2.shape[0]),
+    kernel("rmsnorm_rope")(x2, weight, width, groups, float(eps), cos, sin, int(rows_per_batch or x2.shape[0]),
                        head_dim)
     return x

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import torch
 
-from ._ext import ext, use_kernels
+from ._ext import kernel, use_kernels
 
 
 def sched_step_reference(cond, uncond, guidance, sample, sigma, corrector, predictor, x0_out=None, last_out=None):
@@ -42,7 +42,7 @@ def sched_step(cond: torch.Tensor, uncond: torch.Tensor | None, guidance: float,
     if not use_kernels(sample):
         return sched_step_reference(cond, uncond, guidance, sample, sigma, corrector, predictor, x0_out, last_out)
     c = corrector or {}
-    ext().sched_step(
+    kernel("sched_step")(
         cond.contiguous(), None if uncond is None else uncond.contiguous(), float(guidance), sample, float(sigma),
         corrector is not None, c.get("last"), float(c.get("last_coef", 0.0)), float(c.get("x0_coef", 0.0)),
         list(c.get("hist", [])), [float(v) for v in c.get("hist_coef", [])],

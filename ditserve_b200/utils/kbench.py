@@ -1,0 +1,139 @@
+"""Isolated kernel timing against the measured roofline (CUDA events, warm-up, L2 flush).
+
+    python -m ditserve_b200.utils.kbench [--json out.json]
+
+Times the hot ops of one Wan2.1-1.3B 480p block at the bench shapes (M = 2 x 32 760
+tokens) on our sm_100a kernels and, for context, on cuBLAS (torch.matmul) and
+FlashAttention-2 / torch SDPA when present.  Fractions use MEASURED_PEAKS.json when
+it exists (bf16_tflops burst, hbm_gbs), else the pool's fallback figures.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+from .. import ops
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["bf16_tflops"], d["hbm_gbs"], "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def timeit(fn, iters=10, warmup=3, flush=None):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        if flush is not None:
+            flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--json", default=None)
+    ap.add_argument("--tokens", type=int, default=32760)
+    ap.add_argument("--batch", type=int, default=2)
+    args = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    tflops_peak, hbm_peak, src = peaks()
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)  # 256 MB > L2
+    S, B, D, F, H = args.tokens, args.batch, 1536, 8960, 12
+    M = S * B
+    res = {"peaks": {"bf16_tflops": tflops_peak, "hbm_gbs": hbm_peak, "source": src}, "rows": []}
+
+    def row(name, ms, flops=None, bytes_=None, **kw):
+        r = {"op": name, "ms": round(ms, 4)}
+        if flops:
+            r["tflops"] = round(flops / ms / 1e9, 1)
+            r["frac_of_" + src] = round(flops / ms / 1e9 / tflops_peak, 3)
+        if bytes_:
+            r["gbs"] = round(bytes_ / ms / 1e6, 1)
+            r["hbm_frac_of_" + src] = round(bytes_ / ms / 1e6 / hbm_peak, 3)
+        r.update(kw)
+        res["rows"].append(r)
+        print(json.dumps(r))
+
+    torch.manual_seed(0)
+    x = torch.randn(M, D, device=dev).bfloat16()
+    for name, N, K, kw in [("qkv_proj", 3 * D, D, {}), ("out_proj_gated", D, D, {"gate": True}),
+                           ("ffn_up_gelu", F, D, {"act": "gelu"}), ("ffn_down_gated", D, F, {"gate": True})]:
+        a = torch.randn(M, K, device=dev).bfloat16()
+        w = (torch.randn(N, K, device=dev) / math.sqrt(K)).bfloat16()
+        b = torch.randn(N, device=dev).bfloat16()
+        extra = {}
+        if kw.get("act"):
+            extra["act"] = "gelu"
+        if kw.get("gate"):
+            extra["residual"] = torch.randn(M, N, device=dev).bfloat16()
+            extra["gate"] = torch.randn(B, N, device=dev)
+            extra["rows_per_batch"] = S
+        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        ms = timeit(lambda: ops.linear(a, w, b, out=out, **extra), flush=flush)
+        row(name, ms, flops=2.0 * M * N * K, impl="ours", shape=[M, N, K])
+        ms_cb = timeit(lambda: torch.matmul(a, w.t()), flush=flush)
+        row(name + "_cublas_plain", ms_cb, flops=2.0 * M * N * K, impl="cublas", shape=[M, N, K])
+        del a, w, out, extra
+    # attention
+    qkv = torch.randn(M, 3 * D, device=dev).bfloat16()
+    q, k, v = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
+    o = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
+    fl = 4.0 * B * H * S * S * 128
+    ms = timeit(lambda: ops.attention(q.view(B, S, D), k.view(B, S, D), v.view(B, S, D), H, out=o), iters=5)
+    row("self_attention", ms, flops=fl, impl="ours", shape=[B, S, H, 128])
+    qh = q.reshape(B, S, H, 128)
+    kh = k.reshape(B, S, H, 128)
+    vh = v.reshape(B, S, H, 128)
+    try:
+        from flash_attn import flash_attn_func
+        qc, kc, vc = qh.contiguous(), kh.contiguous(), vh.contiguous()
+        ms = timeit(lambda: flash_attn_func(qc, kc, vc), iters=5)
+        row("self_attention_fa2", ms, flops=fl, impl="flash_attn 2 (library)")
+    except Exception as exc:  # pragma: no cover
+        print("fa2 unavailable", exc)
+    try:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        qt, kt, vt = (t.transpose(1, 2).contiguous() for t in (qh, kh, vh))
+        with sdpa_kernel(SDPBackend.FLASH_ATTENTION):
+            ms = timeit(lambda: torch.nn.functional.scaled_dot_product_attention(qt, kt, vt), iters=5)
+        row("self_attention_sdpa_flash", ms, flops=fl, impl="torch SDPA flash (reference path)")
+    except Exception as exc:  # pragma: no cover
+        print("sdpa flash unavailable", exc)
+    # cross attention against 512 text tokens
+    kv = torch.randn(B * 512, 2 * D, device=dev).bfloat16()
+    ms = timeit(lambda: ops.attention(q.view(B, S, D), kv[:, :D].view(B, 512, D), kv[:, D:].view(B, 512, D), H), iters=5)
+    row("cross_attention", ms, flops=4.0 * B * H * S * 512 * 128, impl="ours")
+    # memory-bound fused kernels
+    mod = torch.randn(B, 6, D, device=dev)
+    y = torch.empty_like(x)
+    ms = timeit(lambda: ops.layernorm_modulate(x, scale=mod[:, 1], shift=mod[:, 0], rows_per_batch=S, out=y), flush=flush)
+    row("layernorm_modulate", ms, bytes_=2 * M * D * 2, impl="ours")
+    w = torch.ones(D, device=dev).bfloat16()
+    ang = torch.rand(S, 64, device=dev)
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    ms = timeit(lambda: ops.rmsnorm_rope_(q, w, cos=cos, sin=sin, rows_per_batch=S), flush=flush)
+    row("rmsnorm_rope_q", ms, bytes_=2 * M * D * 2, impl="ours")
+    if args.json:
+        json.dump(res, open(args.json, "w"), indent=1)
+
+
+if __name__ == "__main__":
+    main()

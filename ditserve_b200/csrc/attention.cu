@@ -30,6 +30,8 @@
 #include "tma_host.h"
 #include "kernels.h"
 
+#include <cstdlib>
+
 namespace ds {
 namespace {
 
@@ -342,6 +344,367 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// v2: two 128-row query tiles per CTA (A, B) and two softmax warpgroups.
+//   WG0  warp 0: TMA producer (Q_A, Q_B once; K one tile ahead of V)
+//        warp 1: TMEM owner + MMA issuer, order  S_A0 S_B0 | PV_A0 S_A1 PV_B0 S_B1 | ...
+//   WG1  softmax of tile A (thread = row),  WG2 softmax of tile B.
+// While WG1 turns S_A(j) into P_A(j) the tensor core runs S_B(j) / PV_B(j-1), and the
+// other way round, so MUFU work and MMA overlap.  TMEM: S_A [0,128), S_B [128,256),
+// O_A [256, 256+D), O_B [384, 384+D).  The row max takes a first pass over S in
+// 64-column halves and the exponentials a second, which keeps each softmax thread
+// under the 168-register budget of a 384-thread CTA.
+constexpr int kAttn2Threads = 384;
+
+template <int D>
+struct Attn2Cfg {
+  static constexpr int kAtoms = D / 64;
+  static constexpr int kQBytes = kQT * D * 2;
+  static constexpr int kKBytes = kKT * D * 2;
+  static constexpr int kVBytes = kKT * D * 2;
+  static constexpr int kPBytes = kQT * kKT * 2;
+  static constexpr int KS = 2;
+  static constexpr int VS = D == 64 ? 2 : 1;
+  static constexpr int kSmemBytes =
+      2 * kQBytes + KS * kKBytes + VS * kVBytes + 2 * kPBytes + 1024 /*align*/ + 512 /*barriers*/;
+  static constexpr int kTmemCols = 512;
+};
+
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  lo = __uint_as_float(static_cast<uint32_t>(v));
+  hi = __uint_as_float(static_cast<uint32_t>(v >> 32));
+}
+// (a0, a1) * (b, b) + (c, c) on the packed fp32x2 datapath
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kAttn2Threads, 1)
+    attention2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+  using Cfg = Attn2Cfg<D>;
+  constexpr int KS = Cfg::KS;
+  constexpr int VS = Cfg::VS;
+  const int qt = blockIdx.x;  // 256-row query block
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  int q_start, q_len, k_start, k_len;
+  if (p.cu_q != nullptr) {
+    q_start = p.cu_q[b];
+    q_len = p.cu_q[b + 1] - q_start;
+    k_start = p.cu_k[b];
+    k_len = p.cu_k[b + 1] - k_start;
+  } else {
+    q_start = b * p.seq_q;
+    q_len = p.seq_q;
+    k_start = b * p.seq_k;
+    k_len = p.seq_k;
+  }
+  if (qt * 2 * kQT >= q_len || k_len <= 0) return;
+  const int hk = h / (p.heads / p.heads_kv);
+  const int n_tiles = (k_len + kKT - 1) / kKT;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                                   // [2][kQBytes]
+  uint8_t* sK = sQ + 2 * Cfg::kQBytes;                  // [KS][kKBytes]
+  uint8_t* sV = sK + KS * Cfg::kKBytes;                 // [VS][kVBytes]
+  uint8_t* sP = sV + VS * Cfg::kVBytes;                 // [2][kPBytes]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::kPBytes);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + VS;
+  uint64_t* s_full = v_empty + VS;  // [2] per tile
+  uint64_t* p_full = s_full + 2;    // [2]
+  uint64_t* pv_done = p_full + 2;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int wg = warp >> 2;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < KS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VS; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc<Cfg::kTmemCols>(tmem_slot);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int q0 = q_start + qt * 2 * kQT;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer: K runs one tile ahead of V ----------------
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, 2 * Cfg::kQBytes);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int a = 0; a < Cfg::kAtoms; ++a)
+          tma_load_2d(sQ + t * Cfg::kQBytes + a * (kQT * 128), &tmQ, h * D + a * 64, q0 + t * kQT, q_full);
+      auto load_k = [&](int j) -> bool {
+        const int st = j % KS;
+        if (!mbar_wait(&k_empty[st], ((j / KS) & 1) ^ 1, abort_flag, p.status, 210)) return false;
+        mbar_arrive_expect_tx(&k_full[st], Cfg::kKBytes);
+#pragma unroll
+        for (int a = 0; a < Cfg::kAtoms; ++a)
+          tma_load_2d(sK + st * Cfg::kKBytes + a * (kKT * 128), &tmK, hk * D + a * 64, k_start + j * kKT,
+                      &k_full[st]);
+        return true;
+      };
+      bool ok = load_k(0);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles && !load_k(j + 1)) break;
+        const int st = j % VS;
+        if (!mbar_wait(&v_empty[st], ((j / VS) & 1) ^ 1, abort_flag, p.status, 211)) break;
+        mbar_arrive_expect_tx(&v_full[st], Cfg::kVBytes);
+#pragma unroll
+        for (int a = 0; a < Cfg::kAtoms; ++a)
+          tma_load_2d(sV + st * Cfg::kVBytes + a * (kKT * 128), &tmV, hk * D + a * 64, k_start + j * kKT,
+                      &v_full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc_s = umma_idesc_bf16(kQT, kKT, false);
+      constexpr uint32_t idesc_o = umma_idesc_bf16(kQT, D, true);
+      auto issue_s = [&](int t, int j) {
+        const int st = j % KS;
+        const uint32_t d = tmem_base + t * kKT;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (kQT * 128) + (kk & 3) * 32;
+          const uint64_t da = umma_desc_sw128(smem_u32(sQ + t * Cfg::kQBytes) + off, 16, 1024);
+          const uint64_t db = umma_desc_sw128(smem_u32(sK + st * Cfg::kKBytes) + off, 16, 1024);
+          umma_bf16_ss(d, da, db, idesc_s, kk != 0);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, 222 + t)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem_base + 256 + t * 128;
+        const uint32_t p_base = smem_u32(sP + t * Cfg::kPBytes);
+        const uint32_t v_base = smem_u32(sV + (j % VS) * Cfg::kVBytes);
+#pragma unroll
+        for (int kk = 0; kk < kKT / 16; ++kk) {
+          const uint64_t da = umma_desc_sw128(p_base + (kk >> 2) * (kQT * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t db = umma_desc_sw128(v_base + kk * (16 * 128), kKT * 128, 1024);
+          umma_bf16_ss(d, da, db, idesc_o, (j | kk) != 0);
+        }
+        umma_commit(&pv_done[t]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 220) &&
+                mbar_wait(&k_full[0], 0, abort_flag, p.status, 221);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (!mbar_wait(&v_full[j % VS], (j / VS) & 1, abort_flag, p.status, 224)) break;
+        tc_fence_after();
+        if (!issue_pv(0, j)) break;
+        const bool more = j + 1 < n_tiles;
+        if (more) {
+          const int st = (j + 1) % KS;
+          if (!mbar_wait(&k_full[st], ((j + 1) / KS) & 1, abort_flag, p.status, 225)) break;
+          tc_fence_after();
+          issue_s(0, j + 1);
+        }
+        if (!issue_pv(1, j)) break;
+        umma_commit(&v_empty[j % VS]);
+        if (more) {
+          issue_s(1, j + 1);
+          umma_commit(&k_empty[(j + 1) % KS]);
+        }
+      }
+    }
+  } else if (wg >= 1) {
+    // ---------------- softmax warpgroups (tile t = wg - 1) ----------------
+    const int t = wg - 1;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_col = tmem_base + lane_addr + t * kKT;
+    const uint32_t o_col = tmem_base + lane_addr + 256 + t * 128;
+    const float sl2 = p.scale_log2;
+    const uint64_t sl2x2 = f2_pack(sl2, sl2);
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+    uint8_t* prow = sP + t * Cfg::kPBytes + row * 128;
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.status, 230 + t)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int valid = k_len - j * kKT;  // columns >= valid are outside the segment
+      const bool masked = valid < kKT;
+      // pass 1: row max
+      float mx = -INFINITY;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t s[64];
+        tmem_ld32(s_col + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+        tmem_ld32(s_col + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+        tmem_wait_ld();
+        if (masked) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (half * 64 + c < valid) mx = fmaxf(mx, __uint_as_float(s[c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) mx = fmaxf(mx, fmaxf(__uint_as_float(s[c]), __uint_as_float(s[c + 1])));
+        }
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const bool need = (m_new - m_run) * sl2 > 8.0f;  // always true on the first tile
+      float alpha = 1.f;
+      if (need) {
+        alpha = ex2_approx((m_run - m_new) * sl2);
+        m_run = m_new;
+      }
+      if (j > 0) {
+        // PV(j-1) has completed (the commit behind S(j) covers it); wait formally so the
+        // O rescale and the P overwrite below are ordered after it
+        if (!mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status, 232 + t)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(o_col + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(o_col + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      l_run *= alpha;
+      const float neg = -m_run * sl2;
+      const uint64_t negx2 = f2_pack(neg, neg);
+      float lsum0 = 0.f, lsum1 = 0.f;
+      // pass 2: exponentials, row sum, bf16 P into shared memory (128-byte swizzle)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t s[64];
+        tmem_ld32(s_col + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+        tmem_ld32(s_col + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+        tmem_wait_ld();
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          float e8[8];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            const int c = ch * 8 + e;
+            uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2x2, negx2);
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            if (masked) {
+              if (half * 64 + c >= valid) x0 = -INFINITY;
+              if (half * 64 + c + 1 >= valid) x1 = -INFINITY;
+            }
+            e8[e] = ex2_approx(x0);
+            e8[e + 1] = ex2_approx(x1);
+            lsum0 += e8[e];
+            lsum1 += e8[e + 1];
+          }
+          uint4 pk;
+          pk.x = pack_bf16x2(e8[0], e8[1]);
+          pk.y = pack_bf16x2(e8[2], e8[3]);
+          pk.z = pack_bf16x2(e8[4], e8[5]);
+          pk.w = pack_bf16x2(e8[6], e8[7]);
+          const int phys = ch ^ (row & 7);
+          *reinterpret_cast<uint4*>(prow + half * (kQT * 128) + phys * 16) = pk;
+        }
+      }
+      l_run += lsum0 + lsum1;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    if (ok) ok = mbar_wait(&pv_done[t], (n_tiles - 1) & 1, abort_flag, p.status, 234 + t);
+    if (ok) {
+      tc_fence_after();
+      const int qrow = qt * 2 * kQT + t * kQT + row;
+      const bool row_ok = qrow < q_len;
+      const float inv_l = 1.0f / l_run;
+      __nv_bfloat16* orow = p.o + static_cast<int64_t>(q_start + qrow) * p.o_stride + h * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_col + c * 32, o);
+        tmem_wait_ld();
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(o[q * 8 + 0]) * inv_l, __uint_as_float(o[q * 8 + 1]) * inv_l);
+            w.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv_l, __uint_as_float(o[q * 8 + 3]) * inv_l);
+            w.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv_l, __uint_as_float(o[q * 8 + 5]) * inv_l);
+            w.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv_l, __uint_as_float(o[q * 8 + 7]) * inv_l);
+            dst[q] = w;
+          }
+        }
+      }
+      if (row_ok && p.lse != nullptr)
+        p.lse[static_cast<int64_t>(h) * p.lse_stride + q_start + qrow] = m_run * p.scale + logf(l_run);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0) {
+    const unsigned long long t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 1000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<Cfg::kTmemCols>(tmem_base);
+  }
+}
+
 template <int D>
 void launch_d(const AttnArgs& a, cudaStream_t stream) {
   using Cfg = AttnCfg<D>;
@@ -366,8 +729,16 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
   p.lse_stride = a.lse_stride;
   p.status = a.status;
   const int max_q = a.cu_seqlens_q ? a.max_seq_q : a.seq_q;
-  dim3 grid((max_q + kQT - 1) / kQT, a.heads, a.batch);
-  kern<<<grid, kAttnThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, p);
+  static const bool use_v1 = std::getenv("DS_ATTN_V1") != nullptr;
+  if (use_v1) {
+    dim3 grid((max_q + kQT - 1) / kQT, a.heads, a.batch);
+    kern<<<grid, kAttnThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, p);
+  } else {
+    auto kern2 = attention2_kernel<D>;
+    cudaFuncSetAttribute(kern2, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Cfg<D>::kSmemBytes);
+    dim3 grid((max_q + 2 * kQT - 1) / (2 * kQT), a.heads, a.batch);
+    kern2<<<grid, kAttn2Threads, Attn2Cfg<D>::kSmemBytes, stream>>>(tq, tk, tv, p);
+  }
 }
 
 }  // namespace

@@ -44,7 +44,7 @@ class UlyssesNCCL:
 
     def gather_sequence(self, y: torch.Tensor, batch: int, seq_local: int) -> torch.Tensor:
         P = self.sp_size
-        parts = torch.empty((P, batch * seq_local, y.shape[1]), device=y.device, dtype=y.dtype)
+        parts = torch.empty((P * batch * seq_local, y.shape[1]), device=y.device, dtype=y.dtype)
         dist.all_gather_into_tensor(parts, y.contiguous(), group=self.group)
         return parts.view(P, batch, seq_local, -1).permute(1, 0, 2, 3).reshape(batch * P * seq_local, -1)
 
@@ -56,6 +56,7 @@ class CFGExchangeNCCL:
         self.cfg_rank = cfg_rank
 
     def exchange(self, mine: torch.Tensor) -> torch.Tensor:
-        both = torch.empty((2, *mine.shape), device=mine.device, dtype=mine.dtype)
-        dist.all_gather_into_tensor(both, mine.contiguous(), group=self.group)
-        return both[1 - self.cfg_rank]
+        flat = mine.contiguous().reshape(1, -1)
+        both = torch.empty((2, flat.shape[1]), device=mine.device, dtype=mine.dtype)
+        dist.all_gather_into_tensor(both, flat, group=self.group)
+        return both[1 - self.cfg_rank].view(mine.shape)

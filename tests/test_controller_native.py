@@ -1,0 +1,65 @@
+"""The C++ controller: ctest suites and an end-to-end CPU study through the CLI."""
+import json
+import os
+import shutil
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CTL = os.path.join(ROOT, "cpp", "controller")
+BUILD = os.path.join(CTL, "build")
+BIN = os.path.join(BUILD, "ditserve-b200")
+
+
+@pytest.fixture(scope="module")
+def controller():
+    if shutil.which("cmake") is None:
+        pytest.skip("cmake unavailable")
+    subprocess.run(["cmake", "-S", CTL, "-B", BUILD, "-DCMAKE_BUILD_TYPE=Release"], check=True,
+                   capture_output=True)
+    subprocess.run(["cmake", "--build", BUILD, "-j", str(os.cpu_count() or 4)], check=True, capture_output=True)
+    return BIN
+
+
+def test_ctest_suites(controller):
+    r = subprocess.run(["ctest", "--output-on-failure"], cwd=BUILD, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
+def test_rpc_needs_no_python(controller):
+    req = {"state": {"now_ms": 0, "gpus": 8, "requests": [
+        {"request_id": "v", "kind": "video", "class": "wan21_480p", "arrival_ms": 0, "deadline_ms": 1e9}]},
+           "policy": "ditserve"}
+    r = subprocess.run([controller, "rpc", "plan"], input=json.dumps(req), capture_output=True, text=True,
+                       env={"PATH": "/usr/bin:/bin"})
+    assert r.returncode == 0, r.stderr
+    plan = json.loads(r.stdout)
+    assert plan["assignments"][0]["request_id"] == "v"
+    cat = json.loads(subprocess.run([controller, "rpc", "policies"], input="{}", capture_output=True,
+                                    text=True).stdout)
+    assert {"ditserve", "tetriserve", "edf-bestfit"} <= {p["id"] for p in cat}
+    bad = subprocess.run([controller, "rpc", "nope"], input="{}", capture_output=True, text=True)
+    assert bad.returncode == 2
+
+
+def test_mock_study_end_to_end(controller, tmp_path):
+    env = dict(os.environ, DITSERVE_PYTHON=sys.executable, DITSERVE_PACKAGE_ROOT=ROOT)
+    cfg = os.path.join(ROOT, "configs", "studies", "mock.json")
+    r = subprocess.run([controller, "--json", "run", "--config", cfg, "--run-id", "t1", "--work-dir", str(tmp_path)],
+                       capture_output=True, text=True, env=env, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    rep = json.loads(r.stdout)
+    assert rep["status"] == "ok"
+    for pid in ("online", "cluster"):
+        assert rep["phases"][pid]["gates"]["pass"], rep["phases"][pid]["gates"]
+    sims = rep["phases"]["whatif"]["last"]
+    assert set(sims) == {"ditserve", "edf-bestfit", "static-cfg2sp4", "xdit-sp1"}
+    # resume refuses a changed config and skips finished phases otherwise
+    again = subprocess.run([controller, "--json", "run", "--config", cfg, "--run-id", "t1", "--work-dir",
+                            str(tmp_path), "--resume"], capture_output=True, text=True, env=env, timeout=600)
+    assert again.returncode == 0 and json.loads(again.stdout)["phases"]["ops"]["resumed"]
+    no = subprocess.run([controller, "run", "--config", cfg, "--run-id", "t1", "--work-dir", str(tmp_path)],
+                        capture_output=True, text=True, env=env)
+    assert no.returncode == 1

@@ -151,7 +151,7 @@ def main():
         from ditserve_b200.parallel.runtime import build_parallel
         pctx, cfg_plan = build_parallel(layout, rank, dev, attention=args.attention,
                                         seq_local=WAN21_T2V_1_3B.tokens((16, 21, 60, 104)) // form.sp,
-                                        cfg=WAN21_T2V_1_3B)
+                                        cfg=WAN21_T2V_1_3B, pred_numel=16 * 21 * 60 * 104)
 
     engine = WanEngine(WAN21_T2V_1_3B, device=dev, pctx=pctx, cfg_plan=cfg_plan, seed=0)
     spec = WanSpec(model=WAN21_T2V_1_3B.name, height=480, width=832, frames=81, steps=50, guidance=5.0, seed=42)

@@ -5,23 +5,16 @@
 // Segments are uniform (batch x seq) or ragged through cu_seqlens (token
 // packing for SD3.5 continuous batching).
 //
-// One CTA computes a 128-row query tile of one head of one segment:
-//   warp 0      TMA producer: Q once, then K_j / V_j tiles (128 rows) into a
-//               two-stage ring (128-byte swizzle; no multicast).
-//   warp 1      TMEM owner + MMA issuer (one lane):
-//                 S_j = Q K_j^T     -> TMEM columns [128*(j%2), +128)
-//                 O  += P_j V_j      -> TMEM columns [256, 256+D)
-//               S_{j+1} is issued before P_j is ready so the tensor core works
-//               while the softmax warps compute.
-//   warps 2..5  softmax: thread t owns query row t (TMEM lane t).  It loads
-//               S_j from TMEM, applies the column mask, updates the running
-//               max and sum, writes P_j (bf16) into a double-buffered
-//               shared-memory tile in the UMMA K-major layout and signals the
-//               MMA warp.  O is rescaled in TMEM only when the running max
-//               grows by more than 2^8 (the stale max keeps P <= 256, exact in
-//               the fp32 accumulators), so the common iteration never touches O.
-//   Final: O / l is stored as bf16; optionally the natural-log LSE (for the
-//   ring-attention merge).
+// Segments: uniform (batch x seq), ragged through cu_seqlens, or a dual-range
+// table where a segment's queries and keys each come from two row ranges of the
+// same buffers (MMDiT joint attention over an image block and a text block).
+//
+// One CTA computes two 128-row query tiles of one head of one segment (see the
+// v2 comment below for the warp roles).  Softmax threads own one query row
+// each (TMEM lane); O is rescaled in TMEM only when the running max grows by
+// more than 2^8 (the stale max keeps P <= 256, exact in the fp32 accumulators),
+// so the common iteration never touches O.  Final: O / l stored as bf16,
+// optionally the natural-log LSE (ring-attention merge) or peer stores.
 //
 // Replaces torch SDPA (FLASH) / flash_attn_varlen_func of the reference
 // (workers/ditserve/models/wan/runtime.py:442-445,
@@ -30,8 +23,6 @@
 #include "tma_host.h"
 #include "kernels.h"
 
-#include <cstdlib>
-
 namespace ds {
 namespace {
 
@@ -39,24 +30,11 @@ constexpr int kQT = 128;  // query rows per CTA
 constexpr int kKT = 128;  // key rows per tile
 constexpr int kAttnThreads = 192;
 
-template <int D>
-struct AttnCfg {
-  static constexpr int kAtoms = D / 64;
-  static constexpr int kQBytes = kQT * D * 2;
-  static constexpr int kKBytes = kKT * D * 2;
-  static constexpr int kVBytes = kKT * D * 2;
-  static constexpr int kPBytes = kQT * kKT * 2;
-  static constexpr int kKVStages = 2;
-  static constexpr int kSmemBytes =
-      kQBytes + kKVStages * (kKBytes + kVBytes) + 2 * kPBytes + 1024 /*align*/ + 512 /*barriers*/;
-  static constexpr int kTmemCols = 512;
-  static constexpr int kOCol = 256;
-};
-
 struct AttnParams {
   int batch, seq_q, seq_k;
   const int* cu_q;
   const int* cu_k;
+  const int* seg;  // [batch][8] dual-range table (qa0 qa1 qb0 qb1 ka0 ka1 kb0 kb1) or null
   int heads, heads_kv;
   float scale_log2;  // softmax_scale * log2(e)
   float scale;
@@ -65,285 +43,13 @@ struct AttnParams {
   float* lse;
   int64_t lse_stride;
   int* status;
+  int o_scatter;
+  PeerGroup o_group;
+  int64_t o_off;
+  int o_seq_local;
+  int o_head_offset;
+  int64_t o_peer_stride;
 };
-
-template <int D>
-__global__ void __launch_bounds__(kAttnThreads, 1)
-    attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV, AttnParams p) {
-  using Cfg = AttnCfg<D>;
-  constexpr int KS = Cfg::kKVStages;
-  const int qt = blockIdx.x;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  int q_start, q_len, k_start, k_len;
-  if (p.cu_q != nullptr) {
-    q_start = p.cu_q[b];
-    q_len = p.cu_q[b + 1] - q_start;
-    k_start = p.cu_k[b];
-    k_len = p.cu_k[b + 1] - k_start;
-  } else {
-    q_start = b * p.seq_q;
-    q_len = p.seq_q;
-    k_start = b * p.seq_k;
-    k_len = p.seq_k;
-  }
-  if (qt * kQT >= q_len || k_len <= 0) return;  // uniform across the CTA
-  const int hk = h / (p.heads / p.heads_kv);
-  const int n_tiles = (k_len + kKT - 1) / kKT;
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + Cfg::kQBytes;
-  uint8_t* sV = sK + KS * Cfg::kKBytes;
-  uint8_t* sP = sV + KS * Cfg::kVBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::kPBytes);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + KS;
-  uint64_t* v_full = k_empty + KS;
-  uint64_t* v_empty = v_full + KS;
-  uint64_t* s_full = v_empty + KS;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* pv_done = p_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int i = 0; i < KS; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&pv_done[i], 1);
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) tmem_alloc<Cfg::kTmemCols>(tmem_slot);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, Cfg::kQBytes);
-#pragma unroll
-      for (int a = 0; a < Cfg::kAtoms; ++a)
-        tma_load_2d(sQ + a * (kQT * 128), &tmQ, h * D + a * 64, q_start + qt * kQT, q_full);
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j % KS;
-        const uint32_t ph = (j / KS) & 1;
-        const int krow = k_start + j * kKT;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, p.status, 110)) break;
-        mbar_arrive_expect_tx(&k_full[st], Cfg::kKBytes);
-#pragma unroll
-        for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_2d(sK + st * Cfg::kKBytes + a * (kKT * 128), &tmK, hk * D + a * 64, krow, &k_full[st]);
-        if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, p.status, 111)) break;
-        mbar_arrive_expect_tx(&v_full[st], Cfg::kVBytes);
-#pragma unroll
-        for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_2d(sV + st * Cfg::kVBytes + a * (kKT * 128), &tmV, hk * D + a * 64, krow, &v_full[st]);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc_s = umma_idesc_bf16(kQT, kKT, false);
-      constexpr uint32_t idesc_o = umma_idesc_bf16(kQT, D, true);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % KS;
-        if (!mbar_wait(&k_full[st], (j / KS) & 1, abort_flag, p.status, 120)) return false;
-        tc_fence_after();
-        const uint32_t d = tmem_base + (j & 1) * kKT;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (kQT * 128) + (kk & 3) * 32;
-          const uint64_t da = umma_desc_sw128(smem_u32(sQ) + off, 16, 1024);
-          const uint64_t db = umma_desc_sw128(smem_u32(sK + st * Cfg::kKBytes) + off, 16, 1024);
-          umma_bf16_ss(d, da, db, idesc_s, kk != 0);
-        }
-        umma_commit(&s_full[j & 1]);
-        umma_commit(&k_empty[st]);
-        return true;
-      };
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 121);
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        if (j + 1 < n_tiles) {
-          if (!issue_s(j + 1)) break;
-        }
-        const int st = j % KS;
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, abort_flag, p.status, 122)) break;
-        if (!mbar_wait(&v_full[st], (j / KS) & 1, abort_flag, p.status, 123)) break;
-        tc_fence_after();
-        const uint32_t d = tmem_base + Cfg::kOCol;
-        const uint32_t p_base = smem_u32(sP + (j & 1) * Cfg::kPBytes);
-        const uint32_t v_base = smem_u32(sV + st * Cfg::kVBytes);
-#pragma unroll
-        for (int kk = 0; kk < kKT / 16; ++kk) {
-          const uint64_t da = umma_desc_sw128(p_base + (kk >> 2) * (kQT * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t db = umma_desc_sw128(v_base + kk * (16 * 128), kKT * 128, 1024);
-          umma_bf16_ss(d, da, db, idesc_o, (j | kk) != 0);
-        }
-        umma_commit(&pv_done[j & 1]);
-        umma_commit(&v_empty[st]);
-      }
-    }
-  } else {
-    // ---------------- softmax warps 2..5 ----------------
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    const float sl2 = p.scale_log2;
-    float m_run = -INFINITY;
-    float l_run = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag, p.status, 130)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t s[kKT];
-#pragma unroll
-      for (int c = 0; c < kKT / 32; ++c)
-        tmem_ld32(tmem_base + lane_addr + (j & 1) * kKT + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
-      tmem_wait_ld();
-      const int valid = k_len - j * kKT;  // columns >= valid are outside the segment
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kKT; ++c) {
-        if (c >= valid) s[c] = __float_as_uint(-INFINITY);
-        mx = fmaxf(mx, __uint_as_float(s[c]));
-      }
-      const float m_new = fmaxf(m_run, mx);
-      const bool need = (m_new - m_run) * sl2 > 8.0f;  // true on the first tile (m_run = -inf)
-      float alpha = 1.f;
-      if (need) {
-        alpha = ex2_approx((m_run - m_new) * sl2);  // 0 on the first tile
-        m_run = m_new;
-      }
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O must hold PV_{j-1} before it can be rescaled
-        const int pj = j - 1;
-        if (!mbar_wait(&pv_done[pj & 1], (pj >> 1) & 1, abort_flag, p.status, 131)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          const uint32_t addr = tmem_base + lane_addr + Cfg::kOCol + c * 32;
-          tmem_ld32(addr, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(addr, o);
-        }
-        tmem_wait_st();
-      }
-      l_run *= alpha;
-      if (j >= 2) {
-        // P buffer (j&1) is free once PV_{j-2} has completed
-        const int pj = j - 2;
-        if (!mbar_wait(&pv_done[pj & 1], (pj >> 1) & 1, abort_flag, p.status, 132)) {
-          ok = false;
-          break;
-        }
-      }
-      const float neg = -m_run * sl2;
-      float lsum = 0.f;
-      uint8_t* prow = sP + (j & 1) * Cfg::kPBytes + row * 128;
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          float e8[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float x = __uint_as_float(s[a * 64 + ch * 8 + e]);
-            e8[e] = ex2_approx(fmaf(x, sl2, neg));
-            lsum += e8[e];
-          }
-          uint4 pk;
-          pk.x = pack_bf16x2(e8[0], e8[1]);
-          pk.y = pack_bf16x2(e8[2], e8[3]);
-          pk.z = pack_bf16x2(e8[4], e8[5]);
-          pk.w = pack_bf16x2(e8[6], e8[7]);
-          const int phys = ch ^ (row & 7);  // 128-byte swizzle
-          *reinterpret_cast<uint4*>(prow + a * (kQT * 128) + phys * 16) = pk;
-        }
-      }
-      l_run += lsum;
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&p_full[j & 1]);
-    }
-    if (ok) {
-      const int pj = n_tiles - 1;
-      ok = mbar_wait(&pv_done[pj & 1], (pj >> 1) & 1, abort_flag, p.status, 133);
-    }
-    if (ok) {
-      tc_fence_after();
-      const int qrow = qt * kQT + row;
-      const bool row_ok = qrow < q_len;
-      const float inv_l = 1.0f / l_run;
-      __nv_bfloat16* orow = p.o + static_cast<int64_t>(q_start + qrow) * p.o_stride + h * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tmem_base + lane_addr + Cfg::kOCol + c * 32, o);
-        tmem_wait_ld();
-        if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(o[q * 8 + 0]) * inv_l, __uint_as_float(o[q * 8 + 1]) * inv_l);
-            w.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv_l, __uint_as_float(o[q * 8 + 3]) * inv_l);
-            w.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv_l, __uint_as_float(o[q * 8 + 5]) * inv_l);
-            w.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv_l, __uint_as_float(o[q * 8 + 7]) * inv_l);
-            dst[q] = w;
-          }
-        }
-      }
-      if (row_ok && p.lse != nullptr) {
-        p.lse[static_cast<int64_t>(h) * p.lse_stride + q_start + qrow] = m_run * p.scale + logf(l_run);
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (*abort_flag && threadIdx.x == 0) {
-    const unsigned long long t0 = globaltimer_ns();
-    while (globaltimer_ns() - t0 < 1000000ull) {
-    }
-  }
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc<Cfg::kTmemCols>(tmem_base);
-  }
-}
-
 
 // ---------------------------------------------------------------------------
 // v2: two 128-row query tiles per CTA (A, B) and two softmax warpgroups.
@@ -392,24 +98,42 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   using Cfg = Attn2Cfg<D>;
   constexpr int KS = Cfg::KS;
   constexpr int VS = Cfg::VS;
-  const int qt = blockIdx.x;  // 256-row query block
   const int h = blockIdx.y;
   const int b = blockIdx.z;
-  int q_start, q_len, k_start, k_len;
-  if (p.cu_q != nullptr) {
-    q_start = p.cu_q[b];
-    q_len = p.cu_q[b + 1] - q_start;
-    k_start = p.cu_k[b];
-    k_len = p.cu_k[b + 1] - k_start;
+  // segment = query rows [qa0,qa1) u [qb0,qb1) attending to keys [ka0,ka1) u [kb0,kb1)
+  int qa0, qa1, qb0, qb1, ka0, ka1, kb0, kb1;
+  if (p.seg != nullptr) {
+    const int* sg = p.seg + 8 * b;
+    qa0 = sg[0]; qa1 = sg[1]; qb0 = sg[2]; qb1 = sg[3];
+    ka0 = sg[4]; ka1 = sg[5]; kb0 = sg[6]; kb1 = sg[7];
+  } else if (p.cu_q != nullptr) {
+    qa0 = p.cu_q[b]; qa1 = p.cu_q[b + 1];
+    ka0 = p.cu_k[b]; ka1 = p.cu_k[b + 1];
+    qb0 = qb1 = kb0 = kb1 = 0;
   } else {
-    q_start = b * p.seq_q;
-    q_len = p.seq_q;
-    k_start = b * p.seq_k;
-    k_len = p.seq_k;
+    qa0 = b * p.seq_q; qa1 = qa0 + p.seq_q;
+    ka0 = b * p.seq_k; ka1 = ka0 + p.seq_k;
+    qb0 = qb1 = kb0 = kb1 = 0;
   }
-  if (qt * 2 * kQT >= q_len || k_len <= 0) return;
+  const int nqa = (qa1 - qa0 + 2 * kQT - 1) / (2 * kQT);
+  const int nqb = (qb1 - qb0 + 2 * kQT - 1) / (2 * kQT);
+  int q0, q_end;
+  if (static_cast<int>(blockIdx.x) < nqa) {
+    q0 = qa0 + blockIdx.x * 2 * kQT;
+    q_end = qa1;
+  } else if (static_cast<int>(blockIdx.x) < nqa + nqb) {
+    q0 = qb0 + (blockIdx.x - nqa) * 2 * kQT;
+    q_end = qb1;
+  } else {
+    return;
+  }
+  const int nka = (ka1 - ka0 + kKT - 1) / kKT;
+  const int n_tiles = nka + (kb1 - kb0 + kKT - 1) / kKT;
+  if (n_tiles <= 0) return;  // uniform across the CTA
+  // first key row of tile j and how many of its rows belong to the segment
+  auto ktile_row = [&](int j) { return j < nka ? ka0 + j * kKT : kb0 + (j - nka) * kKT; };
+  auto ktile_valid = [&](int j) { return j < nka ? ka1 - (ka0 + j * kKT) : kb1 - (kb0 + (j - nka) * kKT); };
   const int hk = h / (p.heads / p.heads_kv);
-  const int n_tiles = (k_len + kKT - 1) / kKT;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -456,7 +180,6 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int q0 = q_start + qt * 2 * kQT;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -476,8 +199,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         mbar_arrive_expect_tx(&k_full[st], Cfg::kKBytes);
 #pragma unroll
         for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_2d(sK + st * Cfg::kKBytes + a * (kKT * 128), &tmK, hk * D + a * 64, k_start + j * kKT,
-                      &k_full[st]);
+          tma_load_2d(sK + st * Cfg::kKBytes + a * (kKT * 128), &tmK, hk * D + a * 64, ktile_row(j), &k_full[st]);
         return true;
       };
       bool ok = load_k(0);
@@ -488,8 +210,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         mbar_arrive_expect_tx(&v_full[st], Cfg::kVBytes);
 #pragma unroll
         for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_2d(sV + st * Cfg::kVBytes + a * (kKT * 128), &tmV, hk * D + a * 64, k_start + j * kKT,
-                      &v_full[st]);
+          tma_load_2d(sV + st * Cfg::kVBytes + a * (kKT * 128), &tmV, hk * D + a * 64, ktile_row(j), &v_full[st]);
       }
     }
   } else if (warp == 1) {
@@ -571,7 +292,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         break;
       }
       tc_fence_after();
-      const int valid = k_len - j * kKT;  // columns >= valid are outside the segment
+      const int valid = ktile_valid(j);  // columns >= valid are outside the segment
       const bool masked = valid < kKT;
       // pass 1: row max
       float mx = -INFINITY;
@@ -664,10 +385,21 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
     if (ok) ok = mbar_wait(&pv_done[t], (n_tiles - 1) & 1, abort_flag, p.status, 234 + t);
     if (ok) {
       tc_fence_after();
-      const int qrow = qt * 2 * kQT + t * kQT + row;
-      const bool row_ok = qrow < q_len;
+      const int qabs = q0 + t * kQT + row;  // absolute row of q / o
+      const bool row_ok = qabs < q_end;
       const float inv_l = 1.0f / l_run;
-      __nv_bfloat16* orow = p.o + static_cast<int64_t>(q_start + qrow) * p.o_stride + h * D;
+      __nv_bfloat16* orow;
+      if (p.o_scatter) {
+        // Ulysses head->sequence all-to-all: the row goes straight to the token's owner
+        const int qrow = qabs - qa0;
+        const int owner = qrow / p.o_seq_local;
+        const int local = qrow - owner * p.o_seq_local;
+        __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(
+            reinterpret_cast<uint8_t*>(p.o_group.base[owner < p.o_group.size ? owner : 0]) + p.o_off);
+        orow = base + (static_cast<int64_t>(b) * p.o_seq_local + local) * p.o_peer_stride + (p.o_head_offset + h) * D;
+      } else {
+        orow = p.o + static_cast<int64_t>(qabs) * p.o_stride + h * D;
+      }
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
@@ -687,7 +419,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         }
       }
       if (row_ok && p.lse != nullptr)
-        p.lse[static_cast<int64_t>(h) * p.lse_stride + q_start + qrow] = m_run * p.scale + logf(l_run);
+        p.lse[static_cast<int64_t>(h) * p.lse_stride + qabs] = m_run * p.scale + logf(l_run);
     }
   }
 
@@ -707,9 +439,6 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
 
 template <int D>
 void launch_d(const AttnArgs& a, cudaStream_t stream) {
-  using Cfg = AttnCfg<D>;
-  auto kern = attention_kernel<D>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   CUtensorMap tq = make_tmap_bf16_2d(a.q, a.total_q, static_cast<uint64_t>(a.heads) * D, a.q_row_stride, kQT);
   CUtensorMap tk = make_tmap_bf16_2d(a.k, a.total_k, static_cast<uint64_t>(a.heads_kv) * D, a.k_row_stride, kKT);
   CUtensorMap tv = make_tmap_bf16_2d(a.v, a.total_k, static_cast<uint64_t>(a.heads_kv) * D, a.v_row_stride, kKT);
@@ -719,6 +448,7 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
   p.seq_k = a.seq_k;
   p.cu_q = a.cu_seqlens_q;
   p.cu_k = a.cu_seqlens_k;
+  p.seg = a.seg_table;
   p.heads = a.heads;
   p.heads_kv = a.heads_kv;
   p.scale = a.softmax_scale;
@@ -728,17 +458,19 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
   p.lse = a.lse;
   p.lse_stride = a.lse_stride;
   p.status = a.status;
-  const int max_q = a.cu_seqlens_q ? a.max_seq_q : a.seq_q;
-  static const bool use_v1 = std::getenv("DS_ATTN_V1") != nullptr;
-  if (use_v1) {
-    dim3 grid((max_q + kQT - 1) / kQT, a.heads, a.batch);
-    kern<<<grid, kAttnThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, p);
-  } else {
-    auto kern2 = attention2_kernel<D>;
-    cudaFuncSetAttribute(kern2, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Cfg<D>::kSmemBytes);
-    dim3 grid((max_q + 2 * kQT - 1) / (2 * kQT), a.heads, a.batch);
-    kern2<<<grid, kAttn2Threads, Attn2Cfg<D>::kSmemBytes, stream>>>(tq, tk, tv, p);
-  }
+  p.o_scatter = a.o_scatter;
+  p.o_group = a.o_group;
+  p.o_off = a.o_off;
+  p.o_seq_local = a.o_seq_local;
+  p.o_head_offset = a.o_head_offset;
+  p.o_peer_stride = a.o_peer_stride;
+  // grid.x: 256-row query blocks of the longest segment (both ranges in dual-range mode)
+  const int max_q = (a.cu_seqlens_q || a.seg_table) ? a.max_seq_q : a.seq_q;
+  const int blocks = a.seg_table ? a.max_q_blocks : (max_q + 2 * kQT - 1) / (2 * kQT);
+  auto kern = attention2_kernel<D>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Cfg<D>::kSmemBytes);
+  dim3 grid(blocks, a.heads, a.batch);
+  kern<<<grid, kAttn2Threads, Attn2Cfg<D>::kSmemBytes, stream>>>(tq, tk, tv, p);
 }
 
 }  // namespace
@@ -750,6 +482,7 @@ void launch_attention(const AttnArgs& a, cudaStream_t stream) {
   if ((a.cu_seqlens_q == nullptr) != (a.cu_seqlens_k == nullptr))
     throw std::runtime_error("attention: give both cu_seqlens or neither");
   if (a.cu_seqlens_q != nullptr && a.max_seq_q <= 0) throw std::runtime_error("attention: max_seq_q required");
+  if (a.seg_table != nullptr && a.max_q_blocks <= 0) throw std::runtime_error("attention: max_q_blocks required");
   switch (a.head_dim) {
     case 128: launch_d<128>(a, stream); break;
     case 64: launch_d<64>(a, stream); break;

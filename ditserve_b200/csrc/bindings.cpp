@@ -5,6 +5,9 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAException.h>
+
+#include <cstring>
 
 #include "kernels.h"
 
@@ -28,7 +31,8 @@ int* status_ptr(const at::Tensor& status) {
 
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c10::optional<at::Tensor>& bias,
           int64_t epilogue, const c10::optional<at::Tensor>& R, const c10::optional<at::Tensor>& gate,
-          int64_t gate_stride, int64_t rows_per_batch, const at::Tensor& status, int64_t bn_override) {
+          int64_t gate_stride, int64_t rows_per_batch, const at::Tensor& status, int64_t bn_override,
+          const c10::optional<at::Tensor>& row_batch) {
   check_cuda_bf16_2d(A, "A");
   check_cuda_bf16_2d(B, "B");
   check_cuda_bf16_2d(C, "C");
@@ -65,13 +69,19 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c10::op
   a.rows_per_batch = static_cast<int>(rows_per_batch);
   a.status = status_ptr(status);
   a.bn_override = static_cast<int>(bn_override);
+  if (row_batch.has_value()) {
+    TORCH_CHECK(row_batch->scalar_type() == at::kInt && row_batch->numel() >= A.size(0) && row_batch->is_cuda(),
+                "gemm: row_batch must be int32 CUDA with one entry per row");
+    a.row_batch = row_batch->data_ptr<int>();
+  }
   ds::launch_gemm(a, at::cuda::getCurrentCUDAStream());
 }
 
 void attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
                const c10::optional<at::Tensor>& lse, int64_t batch, int64_t seq_q, int64_t seq_k,
                const c10::optional<at::Tensor>& cu_q, const c10::optional<at::Tensor>& cu_k, int64_t max_seq_q,
-               int64_t heads, int64_t heads_kv, int64_t head_dim, double scale, const at::Tensor& status) {
+               int64_t heads, int64_t heads_kv, int64_t head_dim, double scale, const at::Tensor& status,
+               const c10::optional<at::Tensor>& seg, int64_t max_q_blocks) {
   check_cuda_bf16_2d(q, "q");
   check_cuda_bf16_2d(k, "k");
   check_cuda_bf16_2d(v, "v");
@@ -80,7 +90,11 @@ void attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
   TORCH_CHECK(k.size(1) == heads_kv * head_dim && v.size(1) == heads_kv * head_dim, "attention: kv width");
   TORCH_CHECK(o.size(0) == q.size(0) && o.size(1) == q.size(1), "attention: o shape");
   TORCH_CHECK(k.size(0) == v.size(0), "attention: k/v rows");
-  if (!cu_q.has_value()) {
+  if (seg.has_value()) {
+    TORCH_CHECK(seg->is_cuda() && seg->scalar_type() == at::kInt && seg->is_contiguous() && seg->numel() == 8 * batch,
+                "attention: seg table must be int32 [batch, 8] on the device");
+    TORCH_CHECK(max_q_blocks > 0, "attention: max_q_blocks required with a seg table");
+  } else if (!cu_q.has_value()) {
     TORCH_CHECK(batch * seq_q == q.size(0) && batch * seq_k == k.size(0), "attention: uniform segment sizes");
   } else {
     TORCH_CHECK(cu_q->scalar_type() == at::kInt && cu_k.has_value() && cu_k->scalar_type() == at::kInt,
@@ -117,13 +131,15 @@ void attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
   a.head_dim = static_cast<int>(head_dim);
   a.softmax_scale = static_cast<float>(scale);
   a.status = status_ptr(status);
+  a.seg_table = seg.has_value() ? seg->data_ptr<int>() : nullptr;
+  a.max_q_blocks = static_cast<int>(max_q_blocks);
   ds::launch_attention(a, at::cuda::getCurrentCUDAStream());
 }
 
 void layernorm_modulate(const at::Tensor& x, at::Tensor& y, const c10::optional<at::Tensor>& scale,
                         const c10::optional<at::Tensor>& shift, int64_t mod_stride, int64_t rows_per_batch,
                         const c10::optional<at::Tensor>& weight, const c10::optional<at::Tensor>& bias,
-                        double eps) {
+                        double eps, const c10::optional<at::Tensor>& row_batch) {
   check_cuda_bf16_2d(x, "x");
   check_cuda_bf16_2d(y, "y");
   TORCH_CHECK(x.sizes() == y.sizes(), "layernorm_modulate: shape mismatch");
@@ -146,6 +162,11 @@ void layernorm_modulate(const at::Tensor& x, at::Tensor& y, const c10::optional<
   a.rows_per_batch = static_cast<int>(rows_per_batch);
   a.weight = opt_ptr(weight);
   a.bias = opt_ptr(bias);
+  if (row_batch.has_value()) {
+    TORCH_CHECK(row_batch->scalar_type() == at::kInt && row_batch->numel() >= x.size(0) && row_batch->is_cuda(),
+                "layernorm_modulate: row_batch must be int32 CUDA with one entry per row");
+    a.row_batch = row_batch->data_ptr<int>();
+  }
   ds::launch_layernorm_modulate(a, at::cuda::getCurrentCUDAStream());
 }
 
@@ -229,6 +250,160 @@ void sched_step(const at::Tensor& cond, const c10::optional<at::Tensor>& uncond,
   ds::launch_sched_step(a, at::cuda::getCurrentCUDAStream());
 }
 
+// ---------------------------------------------------------------- symmetric heap + fused collectives
+std::tuple<at::Tensor, py::bytes> symm_alloc(int64_t nbytes, int64_t device) {
+  TORCH_CHECK(nbytes > ds::kFlagBytes, "symmetric heap too small");
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  void* ptr = nullptr;
+  C10_CUDA_CHECK(cudaMalloc(&ptr, static_cast<size_t>(nbytes)));
+  C10_CUDA_CHECK(cudaMemset(ptr, 0, static_cast<size_t>(nbytes)));
+  C10_CUDA_CHECK(cudaDeviceSynchronize());
+  cudaIpcMemHandle_t h;
+  C10_CUDA_CHECK(cudaIpcGetMemHandle(&h, ptr));
+  auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device);
+  at::Tensor t = torch::from_blob(ptr, {nbytes}, [](void* p) { cudaFree(p); }, opts);
+  return {t, py::bytes(reinterpret_cast<const char*>(&h), sizeof(h))};
+}
+
+int64_t symm_open(const py::bytes& handle, int64_t device) {
+  std::string s = handle;
+  TORCH_CHECK(s.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle");
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, s.data(), sizeof(h));
+  void* p = nullptr;
+  C10_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void symm_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
+
+ds::PeerGroup make_group(int64_t rank, const std::vector<int64_t>& bases, int64_t timeout_ns) {
+  TORCH_CHECK(!bases.empty() && bases.size() <= static_cast<size_t>(ds::kMaxPeers), "group size out of range");
+  TORCH_CHECK(rank >= 0 && rank < static_cast<int64_t>(bases.size()), "rank outside the group");
+  ds::PeerGroup g;
+  g.rank = static_cast<int>(rank);
+  g.size = static_cast<int>(bases.size());
+  for (size_t i = 0; i < bases.size(); ++i) {
+    g.base[i] = reinterpret_cast<void*>(bases[i]);
+    g.flags[i] = reinterpret_cast<uint64_t*>(bases[i]);
+  }
+  g.timeout_ns = static_cast<unsigned long long>(timeout_ns);
+  return g;
+}
+
+void group_barrier(int64_t rank, const std::vector<int64_t>& bases, int64_t timeout_ns, int64_t channel,
+                   int64_t epoch, const at::Tensor& status) {
+  ds::launch_group_barrier(make_group(rank, bases, timeout_ns), static_cast<int>(channel),
+                           static_cast<uint64_t>(epoch), status_ptr(status), at::cuda::getCurrentCUDAStream());
+}
+
+void cfg_step_peer(const at::Tensor& mine, int64_t theirs_off, int64_t role, double guidance, at::Tensor& sample,
+                   double sigma, bool do_corrector, const c10::optional<at::Tensor>& last, double c_last,
+                   double c_x0, std::vector<c10::optional<at::Tensor>> c_hist, std::vector<double> c_coef,
+                   double p_x, double p_x0, double p_v, std::vector<c10::optional<at::Tensor>> p_hist,
+                   std::vector<double> p_coef, const c10::optional<at::Tensor>& x0_out,
+                   const c10::optional<at::Tensor>& last_out, int64_t rank, const std::vector<int64_t>& bases,
+                   int64_t timeout_ns, int64_t channel, int64_t epoch, const at::Tensor& status) {
+  TORCH_CHECK(mine.scalar_type() == at::kBFloat16 && mine.is_contiguous() && mine.numel() == sample.numel(),
+              "cfg_step_peer: prediction must be contiguous bf16 of the latent size");
+  TORCH_CHECK(sample.scalar_type() == at::kFloat && sample.is_contiguous(), "cfg_step_peer: sample fp32");
+  const c10::cuda::CUDAGuard guard(sample.device());
+  ds::SchedStepArgs a;
+  a.guidance = static_cast<float>(guidance);
+  a.n = sample.numel();
+  a.sample = sample.data_ptr<float>();
+  a.sigma = static_cast<float>(sigma);
+  a.do_corrector = do_corrector ? 1 : 0;
+  a.last = opt_f32(last);
+  a.c_last = static_cast<float>(c_last);
+  a.c_x0 = static_cast<float>(c_x0);
+  for (size_t i = 0; i < c_hist.size() && i < 3; ++i) {
+    a.c_hist_ptr[i] = opt_f32(c_hist[i]);
+    a.c_hist[i] = static_cast<float>(c_coef[i]);
+  }
+  a.p_x = static_cast<float>(p_x);
+  a.p_x0 = static_cast<float>(p_x0);
+  a.p_v = static_cast<float>(p_v);
+  for (size_t i = 0; i < p_hist.size() && i < 3; ++i) {
+    a.p_hist_ptr[i] = opt_f32(p_hist[i]);
+    a.p_hist[i] = static_cast<float>(p_coef[i]);
+  }
+  a.x0_out = x0_out.has_value() ? const_cast<float*>(opt_f32(x0_out)) : nullptr;
+  a.last_out = last_out.has_value() ? const_cast<float*>(opt_f32(last_out)) : nullptr;
+  ds::launch_cfg_step_peer(a, make_group(rank, bases, timeout_ns), static_cast<int>(channel),
+                           static_cast<uint64_t>(epoch), mine.data_ptr(), theirs_off, static_cast<int>(role),
+                           status_ptr(status), at::cuda::getCurrentCUDAStream());
+}
+
+void qkv_scatter(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk, double eps,
+                 const c10::optional<at::Tensor>& cos, const c10::optional<at::Tensor>& sin, int64_t seq_local,
+                 int64_t heads, int64_t head_dim, int64_t rank, const std::vector<int64_t>& bases, int64_t timeout_ns,
+                 int64_t recv_off) {
+  check_cuda_bf16_2d(qkv, "qkv");
+  TORCH_CHECK(qkv.size(1) >= 3 * heads * head_dim, "qkv_scatter: qkv too narrow");
+  TORCH_CHECK(qkv.size(0) % seq_local == 0, "qkv_scatter: rows must be batch * seq_local");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  ds::QkvScatterArgs a;
+  a.qkv = qkv.data_ptr();
+  a.qkv_stride = qkv.stride(0);
+  a.rows = static_cast<int>(qkv.size(0));
+  a.seq_local = static_cast<int>(seq_local);
+  a.heads = static_cast<int>(heads);
+  a.head_dim = static_cast<int>(head_dim);
+  a.wq = wq.data_ptr();
+  a.wk = wk.data_ptr();
+  a.eps = static_cast<float>(eps);
+  a.rope_cos = cos.has_value() ? cos->data_ptr<float>() : nullptr;
+  a.rope_sin = sin.has_value() ? sin->data_ptr<float>() : nullptr;
+  a.group = make_group(rank, bases, timeout_ns);
+  a.recv_off = recv_off;
+  ds::launch_qkv_scatter(a, at::cuda::getCurrentCUDAStream());
+}
+
+void attention_scatter(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t batch, int64_t seq,
+                       int64_t heads, int64_t head_dim, double scale, int64_t rank, const std::vector<int64_t>& bases,
+                       int64_t timeout_ns, int64_t o_off, int64_t seq_local, int64_t head_offset,
+                       int64_t peer_stride, const at::Tensor& status) {
+  check_cuda_bf16_2d(q, "q");
+  check_cuda_bf16_2d(k, "k");
+  check_cuda_bf16_2d(v, "v");
+  TORCH_CHECK(q.size(0) == batch * seq && k.size(0) == batch * seq, "attention_scatter: rows");
+  const c10::cuda::CUDAGuard guard(q.device());
+  ds::AttnArgs a;
+  a.q = q.data_ptr();
+  a.q_row_stride = q.stride(0);
+  a.k = k.data_ptr();
+  a.k_row_stride = k.stride(0);
+  a.v = v.data_ptr();
+  a.v_row_stride = v.stride(0);
+  a.o = nullptr;
+  a.total_q = static_cast<int>(q.size(0));
+  a.total_k = static_cast<int>(k.size(0));
+  a.batch = static_cast<int>(batch);
+  a.seq_q = a.seq_k = static_cast<int>(seq);
+  a.heads = a.heads_kv = static_cast<int>(heads);
+  a.head_dim = static_cast<int>(head_dim);
+  a.softmax_scale = static_cast<float>(scale);
+  a.status = status_ptr(status);
+  a.o_scatter = 1;
+  a.o_group = make_group(rank, bases, timeout_ns);
+  a.o_off = o_off;
+  a.o_seq_local = static_cast<int>(seq_local);
+  a.o_head_offset = static_cast<int>(head_offset);
+  a.o_peer_stride = peer_stride;
+  ds::launch_attention(a, at::cuda::getCurrentCUDAStream());
+}
+
+void allgather_rows(const at::Tensor& src, int64_t dst_off, int64_t rank, const std::vector<int64_t>& bases,
+                    int64_t timeout_ns) {
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous(), "allgather_rows: contiguous CUDA source");
+  const c10::cuda::CUDAGuard guard(src.device());
+  ds::launch_allgather_rows(make_group(rank, bases, timeout_ns), src.data_ptr(),
+                            static_cast<int64_t>(src.numel() * src.element_size()), dst_off,
+                            at::cuda::getCurrentCUDAStream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -239,4 +414,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("layernorm_modulate", &layernorm_modulate, "LayerNorm + adaLN modulation");
   m.def("rmsnorm_rope", &rmsnorm_rope, "RMS norm + interleaved RoPE, in place");
   m.def("sched_step", &sched_step, "CFG combine + UniPC/Euler latent update");
+  m.def("symm_alloc", &symm_alloc, "allocate a zeroed symmetric heap and its IPC handle");
+  m.def("symm_open", &symm_open, "open a peer heap from its IPC handle");
+  m.def("symm_close", &symm_close);
+  m.def("group_barrier", &group_barrier, "bounded flag barrier over peer memory");
+  m.def("cfg_step_peer", &cfg_step_peer, "CFG exchange over NVLink fused with guidance + latent update");
+  m.def("qkv_scatter", &qkv_scatter, "RMS qk-norm + RoPE + Ulysses all-to-all scatter");
+  m.def("attention_scatter", &attention_scatter, "attention with the head->sequence all-to-all in its epilogue");
+  m.def("allgather_rows", &allgather_rows, "sequence all-gather by peer stores");
+  m.attr("FLAG_BYTES") = ds::kFlagBytes;
+  m.attr("MAX_PEERS") = ds::kMaxPeers;
+  m.attr("CHANNELS") = ds::kChannels;
 }

@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(256) layernorm_modulate_kernel(LayerNormArgs a
       ss += d * d;
     }
   const float rstd = rsqrtf(warp_sum(ss) * inv_dim + a.eps);
-  const int b = a.rows_per_batch > 0 ? warp / a.rows_per_batch : 0;
+  const int b = a.row_batch != nullptr ? a.row_batch[warp] : (a.rows_per_batch > 0 ? warp / a.rows_per_batch : 0);
   const float* scale = a.scale ? a.scale + static_cast<int64_t>(b) * a.mod_stride : nullptr;
   const float* shift = a.shift ? a.shift + static_cast<int64_t>(b) * a.mod_stride : nullptr;
 #pragma unroll

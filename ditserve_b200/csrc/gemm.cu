@@ -55,6 +55,7 @@ struct EpiParams {
   const float* gate;
   int64_t gate_stride;
   int rows_per_batch;
+  const int* row_batch;
   int* status;
 };
 
@@ -172,7 +173,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = m0 + row_in_tile;
       const bool row_ok = m < p.M;
       const float* gate_row = nullptr;
-      if (EPI == kEpiGatedRes) gate_row = p.gate + static_cast<int64_t>(m / p.rows_per_batch) * p.gate_stride;
+      if (EPI == kEpiGatedRes && row_ok) {
+        const int bidx = p.row_batch != nullptr ? __ldg(p.row_batch + m) : m / p.rows_per_batch;
+        gate_row = p.gate + static_cast<int64_t>(bidx) * p.gate_stride;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -273,6 +277,7 @@ void launch_bn_epi(const GemmArgs& a, cudaStream_t stream) {
   p.gate = a.gate;
   p.gate_stride = a.gate_stride;
   p.rows_per_batch = a.rows_per_batch > 0 ? a.rows_per_batch : a.M;
+  p.row_batch = a.row_batch;
   p.status = a.status;
   const int tiles = ((a.M + kBM - 1) / kBM) * (a.N / BN);
   const int sms = a.num_sms > 0 ? a.num_sms : device_sm_count();

@@ -8,6 +8,20 @@
 
 namespace ds {
 
+constexpr int kMaxPeers = 8;
+constexpr int kChannels = 16;
+// Flag area at the head of every symmetric heap: uint64 flags[kChannels][kMaxPeers].
+constexpr int64_t kFlagBytes = static_cast<int64_t>(kChannels) * kMaxPeers * 8;
+
+// A rank group over symmetric heaps: base[i] is member i's heap (peer-mapped),
+// flags[i] its flag area (= base[i]).  rank/size are positions inside the group.
+struct PeerGroup {
+  int rank = 0, size = 1;
+  void* base[kMaxPeers] = {};
+  uint64_t* flags[kMaxPeers] = {};
+  unsigned long long timeout_ns = 10000000000ull;
+};
+
 enum GemmEpilogue : int { kEpiNone = 0, kEpiGelu = 1, kEpiGatedRes = 2, kEpiRes = 3 };
 
 struct GemmArgs {
@@ -25,6 +39,7 @@ struct GemmArgs {
   const float* gate = nullptr;  // gate[b * gate_stride + n], b = row / rows_per_batch
   int64_t gate_stride = 0;
   int rows_per_batch = 0;
+  const int* row_batch = nullptr;  // optional per-row batch index (packed ragged batches)
   int* status = nullptr;  // device status word pair (code, site)
   int num_sms = 0;        // 0: all SMs of the current device
   int bn_override = 0;    // 0: heuristic
@@ -52,9 +67,21 @@ struct AttnArgs {
   const int* cu_seqlens_q = nullptr;
   const int* cu_seqlens_k = nullptr;
   int max_seq_q = 0;
+  const int* seg_table = nullptr;  // [batch][8]: qa0 qa1 qb0 qb1 ka0 ka1 kb0 kb1 (dual-range segments)
+  int max_q_blocks = 0;            // grid.x in dual-range mode: max over segments of 256-row query blocks
   int heads = 0, heads_kv = 0, head_dim = 128;
   float softmax_scale = 0.f;
   int* status = nullptr;
+  // peer-store epilogue (Ulysses head->sequence all-to-all): when o_scatter is set, the
+  // output row of query token t (of S = size*o_seq_local) is stored on group member
+  // t / o_seq_local at heap offset o_off, row (b*o_seq_local + t % o_seq_local), column
+  // (o_head_offset + h) * head_dim, row stride o_peer_stride elements.
+  int o_scatter = 0;
+  PeerGroup o_group;
+  int64_t o_off = 0;
+  int o_seq_local = 0;
+  int o_head_offset = 0;
+  int64_t o_peer_stride = 0;
 };
 void launch_attention(const AttnArgs& a, cudaStream_t stream);
 
@@ -72,6 +99,7 @@ struct LayerNormArgs {
   const float* shift = nullptr;
   int64_t mod_stride = 0;
   int rows_per_batch = 0;
+  const int* row_batch = nullptr;  // optional per-row batch index (packed ragged batches)
   const void* weight = nullptr;  // bf16 [dim]
   const void* bias = nullptr;    // bf16 [dim]
 };
@@ -123,5 +151,24 @@ struct SchedStepArgs {
   float* last_out = nullptr;
 };
 void launch_sched_step(const SchedStepArgs& a, cudaStream_t stream);
+
+// ---- fused collectives over peer memory (comm.cu) ----
+struct QkvScatterArgs {
+  const void* qkv = nullptr;  // [rows = B*Sl, >= 3*H*D] bf16
+  int64_t qkv_stride = 0;
+  int rows = 0, seq_local = 0, heads = 0, head_dim = 128;
+  const void* wq = nullptr;  // bf16 [H*D] RMS weights
+  const void* wk = nullptr;
+  float eps = 1e-6f;
+  const float* rope_cos = nullptr;  // [S_full, D/2] (global positions)
+  const float* rope_sin = nullptr;
+  PeerGroup group;
+  int64_t recv_off = 0;  // heap offset of every member's receive buffer [B*S, 3*Hl*D]
+};
+void launch_group_barrier(const PeerGroup& g, int channel, uint64_t epoch, int* status, cudaStream_t s);
+void launch_cfg_step_peer(const SchedStepArgs& a, const PeerGroup& g, int channel, uint64_t epoch,
+                          const void* mine, int64_t theirs_off, int my_role, int* status, cudaStream_t s);
+void launch_qkv_scatter(const QkvScatterArgs& a, cudaStream_t s);
+void launch_allgather_rows(const PeerGroup& g, const void* src, int64_t bytes, int64_t dst_off, cudaStream_t s);
 
 }  // namespace ds

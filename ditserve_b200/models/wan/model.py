@@ -184,6 +184,8 @@ class WanPacket:
     grid: tuple
     text_len: int
     next_block: int = 0
+    cos_full: torch.Tensor | None = None   # whole-sequence tables (fused SP kernels use global positions)
+    sin_full: torch.Tensor | None = None
 
     def tensors(self) -> dict:
         return dict(x=self.x, mod=self.mod, temb=self.temb, ctx=self.ctx, cos=self.cos, sin=self.sin)
@@ -321,11 +323,11 @@ class WanTransformer(nn.Module):
         if timestep.dim() == 2:  # per-token timesteps: keep this rank's rows
             temb = temb[:, r * Sl:(r + 1) * Sl].reshape(B * Sl, -1)
             mod = mod[:, r * Sl:(r + 1) * Sl].reshape(B * Sl, 6, -1)
-        cos, sin = self.rope(grid, latents.device)
-        cos, sin = cos[r * Sl:(r + 1) * Sl], sin[r * Sl:(r + 1) * Sl]
+        cos_full, sin_full = self.rope(grid, latents.device)
+        cos, sin = cos_full[r * Sl:(r + 1) * Sl], sin_full[r * Sl:(r + 1) * Sl]
         return WanPacket(x=x.contiguous(), mod=mod.contiguous(), temb=temb.contiguous(), ctx=ctx.contiguous(),
                          cos=cos.contiguous(), sin=sin.contiguous(), batch=B, seq_local=Sl, seq=S, grid=grid,
-                         text_len=context.shape[1])
+                         text_len=context.shape[1], cos_full=cos_full, sin_full=sin_full)
 
     def forward_block(self, i: int, pk: WanPacket, pctx=None) -> WanPacket:
         pctx = pctx or LocalAttention()
@@ -339,12 +341,17 @@ class WanTransformer(nn.Module):
         h = ops.layernorm_modulate(x, scale=m[:, 1], shift=m[:, 0], eps=cfg.eps, rows_per_batch=rpb)
         a1 = blk.attn1
         qkv = ops.linear(h, a1.w_qkv, a1.b_qkv)
-        q, k, v = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
-        ops.rmsnorm_rope_(q, a1.norm_q.weight, eps=cfg.eps, cos=pk.cos, sin=pk.sin, rows_per_batch=pk.seq_local,
-                          head_dim=hd)
-        ops.rmsnorm_rope_(k, a1.norm_k.weight, eps=cfg.eps, cos=pk.cos, sin=pk.sin, rows_per_batch=pk.seq_local,
-                          head_dim=hd)
-        o = pctx.self_attention_qkv(qkv, Hh, pk.batch, pk.seq_local)
+        if hasattr(pctx, "fused_qkv_attention") and qkv.is_cuda:
+            # qk-norm + RoPE + all-to-all in one kernel, attention epilogue scatters O back
+            o = pctx.fused_qkv_attention(qkv, a1.norm_q.weight, a1.norm_k.weight, cfg.eps, pk.cos_full, pk.sin_full,
+                                         Hh, pk.batch, pk.seq_local)
+        else:
+            q, k, v = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
+            ops.rmsnorm_rope_(q, a1.norm_q.weight, eps=cfg.eps, cos=pk.cos, sin=pk.sin,
+                              rows_per_batch=pk.seq_local, head_dim=hd)
+            ops.rmsnorm_rope_(k, a1.norm_k.weight, eps=cfg.eps, cos=pk.cos, sin=pk.sin,
+                              rows_per_batch=pk.seq_local, head_dim=hd)
+            o = pctx.self_attention_qkv(qkv, Hh, pk.batch, pk.seq_local)
         x = ops.linear(o, a1.to_out[0].weight, a1.to_out[0].bias, residual=x, gate=m[:, 2], rows_per_batch=rpb,
                        out=x if x.is_cuda else None)
         # --- cross attention (no sequence parallelism: local queries against the full text)

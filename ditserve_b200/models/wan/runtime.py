@@ -174,6 +174,16 @@ class WanEngine:
     def step(self, st: WanRequestState) -> WanRequestState:
         if st.done:
             raise RuntimeError("request already finished")
+        if st.negative is not None and hasattr(self.cfg_plan, "fused_step"):
+            # CFG parallelism over peer memory: exchange + guidance + update in one kernel
+            with torch.inference_mode():
+                br, lat, t, ctx = self._inputs(st)
+                mine = self.model(lat, t, ctx, self.pctx)[0]
+                self.cfg_plan.fused_step(st.scheduler, st.latents.view(-1), mine, st.spec.guidance)
+            st.step += 1
+            st.block = 0
+            st.packets.clear()
+            return st
         cond, uncond = self.predict(st)
         return self.apply(st, cond, uncond)
 

@@ -53,6 +53,50 @@ def attention_reference(q, k, v, heads, heads_kv=None, cu_seqlens_q=None, cu_seq
     return (o, torch.cat(lses, -1)) if return_lse else o
 
 
+def segments_reference(q, k, v, heads, seg_table, scale=None, heads_kv=None):
+    """Dual-range segments: rows [qa0,qa1) u [qb0,qb1) attend to [ka0,ka1) u [kb0,kb1)."""
+    out = torch.zeros(q.shape[0], q.shape[1], dtype=q.dtype)
+    for row in seg_table.tolist():
+        qa0, qa1, qb0, qb1, ka0, ka1, kb0, kb1 = row
+        qi = torch.cat([torch.arange(qa0, qa1), torch.arange(qb0, qb1)])
+        ki = torch.cat([torch.arange(ka0, ka1), torch.arange(kb0, kb1)])
+        if len(qi) == 0 or len(ki) == 0:
+            continue
+        o = attention_reference(q[qi], k[ki], v[ki], heads, heads_kv, scale=scale)
+        out[qi] = o.to(out.dtype)
+    return out
+
+
+def segment_table(segments) -> torch.Tensor:
+    """[(qa0, qa1, qb0, qb1, ka0, ka1, kb0, kb1), ...] -> int32 [n, 8]."""
+    return torch.tensor([list(s) for s in segments], dtype=torch.int32)
+
+
+def attention_segments(q, k, v, heads, seg_table: torch.Tensor, *, scale=None, out=None, heads_kv=None):
+    """Attention over dual-range segments of one packed buffer (MMDiT joint attention)."""
+    heads_kv = heads_kv or heads
+    if not use_kernels(q, k, v):
+        o = segments_reference(q, k, v, heads, seg_table, scale, heads_kv)
+        if out is not None:
+            rows = torch.zeros(q.shape[0], dtype=torch.bool)
+            for r in seg_table.tolist():
+                rows[r[0]:r[1]] = True
+                rows[r[2]:r[3]] = True
+            out[rows] = o[rows]
+            return out
+        return o
+    d = q.shape[-1] // heads
+    scale = scale if scale is not None else 1.0 / math.sqrt(d)
+    tbl = seg_table.to(torch.int32)
+    cpu = tbl.cpu()
+    blocks = int(((cpu[:, 1] - cpu[:, 0] + 255) // 256 + (cpu[:, 3] - cpu[:, 2] + 255) // 256).max().item())
+    if out is None:
+        out = torch.empty(q.shape[0], q.shape[1], device=q.device, dtype=torch.bfloat16)
+    kernel("attention")(q, k, v, out, None, tbl.shape[0], 0, 0, None, None, 0, heads, heads_kv, d, float(scale),
+                        status_word(q.device), tbl.to(q.device).contiguous(), blocks)
+    return out
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *, heads_kv: int | None = None,
               cu_seqlens_q: torch.Tensor | None = None, cu_seqlens_k: torch.Tensor | None = None,
               max_seqlen_q: int | None = None, scale: float | None = None, out: torch.Tensor | None = None,
@@ -82,6 +126,6 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *, 
     if cq is not None and max_seqlen_q is None:
         max_seqlen_q = int((cq[1:] - cq[:-1]).max().item())
     kernel("attention")(q2, k2, v2, o2, lse, B, Sq, Sk, cq, ckk, int(max_seqlen_q or 0), heads, heads_kv, d,
-                    float(scale), status_word(q.device))
+                        float(scale), status_word(q.device), None, 0)
     o = out.reshape(*q.shape[:-1], width)
     return (o, lse) if return_lse else o

@@ -27,7 +27,17 @@ def gelu_tanh_ref(x: torch.Tensor) -> torch.Tensor:
     return F.gelu(x, approximate="tanh")
 
 
-def linear_reference(x, w, b=None, act=None, residual=None, gate=None, rows_per_batch=None):
+def _row_gate(gate, rows, rows_per_batch, row_batch):
+    g = gate.float()
+    if g.dim() == 1:
+        g = g.unsqueeze(0)
+    if row_batch is not None:
+        return g[row_batch.long().cpu()] if not g.is_cuda else g[row_batch.long()]
+    rpb = rows_per_batch or rows
+    return g.repeat_interleave(rpb, dim=0)[:rows]
+
+
+def linear_reference(x, w, b=None, act=None, residual=None, gate=None, rows_per_batch=None, row_batch=None):
     """fp32 PyTorch statement of the fused op (CPU path and test oracle)."""
     shape = x.shape
     x2 = x.reshape(-1, shape[-1]).float()
@@ -39,9 +49,7 @@ def linear_reference(x, w, b=None, act=None, residual=None, gate=None, rows_per_
     if residual is not None:
         r = residual.reshape(-1, y.shape[-1]).float()
         if gate is not None:
-            rpb = rows_per_batch or y.shape[0]
-            g = gate.float().repeat_interleave(rpb, dim=0)[: y.shape[0]]
-            y = r + g * y
+            y = r + _row_gate(gate, y.shape[0], rows_per_batch, row_batch) * y
         else:
             y = r + y
     return y.to(x.dtype).reshape(*shape[:-1], w.shape[0])
@@ -50,9 +58,13 @@ def linear_reference(x, w, b=None, act=None, residual=None, gate=None, rows_per_
 def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None, *, act: str | None = None,
            residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
            rows_per_batch: int | None = None, out: torch.Tensor | None = None,
-           bn: int = 0) -> torch.Tensor:
+           bn: int = 0, row_batch: torch.Tensor | None = None) -> torch.Tensor:
     if not use_kernels(x, w):
-        return linear_reference(x, w, b, act, residual, gate, rows_per_batch)
+        y = linear_reference(x, w, b, act, residual, gate, rows_per_batch, row_batch)
+        if out is not None:
+            out.copy_(y.reshape(out.shape))
+            return out
+        return y
     shape = x.shape
     x2 = x.reshape(-1, shape[-1])
     if x2.stride(-1) != 1:
@@ -80,5 +92,5 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None, *, a
             raise ValueError("gate must have unit column stride")
         gate_stride = gate.stride(0) if gate.shape[0] > 1 else 0
     kernel("gemm")(x2, w, out2, b, epi, r2, gate, gate_stride, int(rows_per_batch or M),
-               status_word(x.device), bn)
+                   status_word(x.device), bn, row_batch)
     return out2.reshape(*shape[:-1], N)

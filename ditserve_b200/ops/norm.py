@@ -12,17 +12,20 @@ import torch
 from ._ext import kernel, use_kernels
 
 
-def _batch_rows(x2, rows_per_batch, mod):
+def _batch_rows(x2, rows_per_batch, mod, row_batch=None):
     if mod is None:
         return None
-    rpb = rows_per_batch or x2.shape[0]
     m = mod.float()
     if m.dim() == 1:
         m = m.unsqueeze(0)
+    if row_batch is not None:
+        return m[row_batch.long().to(m.device)]
+    rpb = rows_per_batch or x2.shape[0]
     return m.repeat_interleave(rpb, dim=0)[: x2.shape[0]]
 
 
-def layernorm_modulate_reference(x, scale=None, shift=None, weight=None, bias=None, eps=1e-6, rows_per_batch=None):
+def layernorm_modulate_reference(x, scale=None, shift=None, weight=None, bias=None, eps=1e-6, rows_per_batch=None,
+                                 row_batch=None):
     shape = x.shape
     x2 = x.reshape(-1, shape[-1]).float()
     y = torch.nn.functional.layer_norm(x2, (x2.shape[-1],), eps=eps)
@@ -30,8 +33,8 @@ def layernorm_modulate_reference(x, scale=None, shift=None, weight=None, bias=No
         y = y * weight.float()
     if bias is not None:
         y = y + bias.float()
-    sc = _batch_rows(x2, rows_per_batch, scale)
-    sh = _batch_rows(x2, rows_per_batch, shift)
+    sc = _batch_rows(x2, rows_per_batch, scale, row_batch)
+    sh = _batch_rows(x2, rows_per_batch, shift, row_batch)
     if sc is not None:
         y = y * (1 + sc)
     if sh is not None:
@@ -41,10 +44,16 @@ def layernorm_modulate_reference(x, scale=None, shift=None, weight=None, bias=No
 
 def layernorm_modulate(x: torch.Tensor, scale: torch.Tensor | None = None, shift: torch.Tensor | None = None,
                        weight: torch.Tensor | None = None, bias: torch.Tensor | None = None, eps: float = 1e-6,
-                       rows_per_batch: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-    """y = LN(x) [* w + b] [* (1 + scale[b]) + shift[b]]; scale/shift fp32 [B, D]."""
+                       rows_per_batch: int | None = None, out: torch.Tensor | None = None,
+                       row_batch: torch.Tensor | None = None) -> torch.Tensor:
+    """y = LN(x) [* w + b] [* (1 + scale[b]) + shift[b]]; scale/shift fp32 [B, D]; the batch index of a
+    row is row // rows_per_batch, or row_batch[row] for packed ragged batches."""
     if not use_kernels(x):
-        return layernorm_modulate_reference(x, scale, shift, weight, bias, eps, rows_per_batch)
+        y = layernorm_modulate_reference(x, scale, shift, weight, bias, eps, rows_per_batch, row_batch)
+        if out is not None:
+            out.copy_(y.reshape(out.shape))
+            return out
+        return y
     shape = x.shape
     x2 = x.reshape(-1, shape[-1])
     y = out if out is not None else torch.empty_like(x2)
@@ -64,7 +73,7 @@ def layernorm_modulate(x: torch.Tensor, scale: torch.Tensor | None = None, shift
     elif sh is not None:
         mod_stride = sh.stride(0) if sh.shape[0] > 1 else 0
     kernel("layernorm_modulate")(x2, y2, sc, sh, mod_stride, int(rows_per_batch or x2.shape[0]), weight, bias,
-                             float(eps))
+                                 float(eps), row_batch)
     return y2.reshape(shape)
 
 

@@ -1,0 +1,138 @@
+"""Fused peer-memory replacements of the NCCL collectives (the product path).
+
+* ``FusedUlysses`` — Ulysses sequence parallelism with
+  (1) RMS qk-norm + RoPE + head-scatter all-to-all in one kernel (qkv_scatter),
+  (2) a bounded flag barrier,
+  (3) attention on the gathered full sequence whose epilogue stores each output
+      row into the owning rank's O buffer (the inverse all-to-all),
+  (4) a second barrier before the output projection reads O.
+* ``FusedCFG`` — CFG parallelism: each rank writes its branch prediction into
+  its heap; one kernel signals the partner, waits (bounded), reads the partner's
+  prediction over NVLink and applies guidance + the UniPC/Euler update.
+Reference collectives replaced: usp.py:207-270/:368-381 (all_to_all_single) and
+xdit/wan.py:187-203 (prediction all_gather).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import ops
+from ..ops._ext import ext, status_word
+from .symm import PeerGroup, SymmetricHeap
+
+CH_SP, CH_CFG, CH_GATHER = 0, 1, 2
+
+
+class FusedUlysses:
+    def __init__(self, heap: SymmetricHeap, members: tuple, seq_local: int, heads: int, head_dim: int,
+                 batch: int, gather_cols: int = 64):
+        self.group = PeerGroup(heap, members, CH_SP)
+        self.gather_group = PeerGroup(heap, members, CH_GATHER)
+        self.heap = heap
+        self.sp_size = self.group.size
+        self.sp_rank = self.group.rank
+        self.seq_local = seq_local
+        self.heads = heads
+        self.head_dim = head_dim
+        self.batch = batch
+        P = self.sp_size
+        hl = heads // P
+        S = seq_local * P
+        self.recv_off, self.recv = heap.alloc_view((batch * S, 3 * hl * head_dim))
+        self.o_off, self.o = heap.alloc_view((batch * seq_local, heads * head_dim))
+        self.gather_off, self.gathered = heap.alloc_view((P * batch * seq_local, gather_cols))
+        self.gather_cols = gather_cols
+
+    def fused_qkv_attention(self, qkv, wq, wk, eps, cos_full, sin_full, heads, batch, seq_local):
+        assert batch == self.batch and seq_local == self.seq_local and heads == self.heads
+        st = status_word(qkv.device)
+        r, bases, tmo = self.group.args()
+        ext().qkv_scatter(qkv, wq, wk, float(eps), cos_full, sin_full, seq_local, heads, self.head_dim, r, bases,
+                          tmo, self.recv_off)
+        self.group.barrier(st)
+        hl = heads // self.sp_size
+        w = hl * self.head_dim
+        q, k, v = self.recv[:, :w], self.recv[:, w:2 * w], self.recv[:, 2 * w:]
+        ext().attention_scatter(q, k, v, batch, seq_local * self.sp_size, hl, self.head_dim,
+                                1.0 / math.sqrt(self.head_dim), r, bases, tmo, self.o_off, seq_local,
+                                self.sp_rank * hl, heads * self.head_dim, st)
+        self.group.barrier(st)
+        return self.o
+
+    def gather_sequence(self, y, batch, seq_local):
+        if y.shape[1] != self.gather_cols:
+            raise ValueError("gather width differs from the reserved buffer")
+        r, bases, tmo = self.gather_group.args()
+        ext().allgather_rows(y.contiguous(), self.gather_off, r, bases, tmo)
+        self.gather_group.barrier(status_word(y.device))
+        P = self.sp_size
+        return self.gathered.view(P, batch, seq_local, -1).permute(1, 0, 2, 3).reshape(batch * P * seq_local, -1)
+
+
+class FusedCFG:
+    """CFG pair over peer memory; cfg_rank 0 computes the conditional branch."""
+
+    def __init__(self, heap: SymmetricHeap, members: tuple, numel: int):
+        self.group = PeerGroup(heap, members, CH_CFG)
+        self.heap = heap
+        self.cfg_size = 2
+        self.cfg_rank = self.group.rank
+        self.numel = numel
+        # double-buffered prediction slots (parity of the exchange epoch)
+        self.slots = [heap.alloc_view((numel,)) for _ in range(2)]
+        self.calls = 0
+
+    def exchange(self, mine):  # pragma: no cover - the fused step never exchanges separately
+        raise RuntimeError("FusedCFG applies guidance inside the exchange kernel")
+
+    def fused_step(self, scheduler, sample: torch.Tensor, mine: torch.Tensor, guidance: float):
+        n = mine.numel()
+        if n > self.numel:
+            raise ValueError(f"prediction of {n} elements exceeds the reserved CFG slot ({self.numel})")
+        slot_off, slot = self.slots[self.calls & 1]
+        slot = slot[:n]
+        self.calls += 1
+        slot.copy_(mine.reshape(-1))
+        r, bases, tmo = self.group.args()
+        epoch = self.heap.next_epoch(self.group.channel)
+        st = status_word(sample.device)
+
+        def kernel(cond, uncond, g, x, sigma, corr, pred, x0_out=None, last_out=None):
+            c = corr or {}
+            ext().cfg_step_peer(
+                slot, slot_off, self.cfg_rank, float(g), x, float(sigma), corr is not None, c.get("last"),
+                float(c.get("last_coef", 0.0)), float(c.get("x0_coef", 0.0)), list(c.get("hist", [])),
+                [float(v) for v in c.get("hist_coef", [])], float(pred.get("x", 1.0)), float(pred.get("x0", 0.0)),
+                float(pred.get("v", 0.0)), list(pred.get("hist", [])), [float(v) for v in pred.get("hist_coef", [])],
+                x0_out, last_out, r, bases, tmo, self.group.channel, epoch, st)
+            return x
+
+        return scheduler.step(sample, mine.reshape(-1), None, guidance, kernel=kernel)
+
+
+def upgrade(layout, rank, device, pctx, cfg_plan, sp_groups, cfg_groups, seq_local=None, cfg=None,
+            heap_bytes: int | None = None, pred_numel: int | None = None):
+    """Replace the NCCL plans of ``build_parallel`` by fused peer-memory ones (same layout)."""
+    if device.type != "cuda" or cfg is None or seq_local is None:
+        return pctx, cfg_plan
+    form = layout.form
+    batch = 1 if form.cfg == 2 else 2
+    P = form.sp
+    hl = cfg.heads // P
+    need = 0
+    if P > 1:
+        need += batch * seq_local * P * 3 * hl * cfg.head_dim * 2 + batch * seq_local * cfg.dim * 2
+        need += P * batch * seq_local * cfg.out_channels * 4 * 2
+    pred_numel = pred_numel or 8 * 1024 * 1024
+    need += 2 * pred_numel * 2  # double-buffered bf16 prediction slots
+    heap = SymmetricHeap(heap_bytes or int(need * 1.2) + (64 << 20), device)
+    if P > 1:
+        pctx = FusedUlysses(heap, layout.sp_ranks(rank), seq_local, cfg.heads, cfg.head_dim, batch,
+                            gather_cols=cfg.out_channels * math.prod(cfg.patch))
+    if form.cfg == 2:
+        partner = layout.cfg_partner(rank)
+        members = (rank, partner) if layout.cfg_role(rank) == 0 else (partner, rank)
+        cfg_plan = FusedCFG(heap, members, numel=pred_numel)
+    return pctx, cfg_plan

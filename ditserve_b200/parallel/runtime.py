@@ -18,7 +18,7 @@ from .nccl import CFGExchangeNCCL, UlyssesNCCL
 
 
 def build_parallel(layout: FixedLayout, rank: int, device: torch.device, attention: str = "fused",
-                   seq_local: int | None = None, cfg=None):
+                   seq_local: int | None = None, cfg=None, pred_numel: int | None = None):
     form = layout.form
     sp_groups, cfg_groups = {}, {}
     n_sp = len(layout.ranks) // form.sp
@@ -46,5 +46,5 @@ def build_parallel(layout: FixedLayout, rank: int, device: torch.device, attenti
             fused = None
         if fused is not None:
             pctx, cfg_plan = fused.upgrade(layout, rank, device, pctx, cfg_plan, sp_groups, cfg_groups,
-                                           seq_local=seq_local, cfg=cfg)
+                                           seq_local=seq_local, cfg=cfg, pred_numel=pred_numel)
     return pctx, cfg_plan

@@ -58,11 +58,11 @@ class FlowMatchEulerScheduler:
         return self.step_index >= self.steps
 
     def step(self, sample: torch.Tensor, cond: torch.Tensor, uncond: torch.Tensor | None = None,
-             guidance: float = 1.0) -> torch.Tensor:
+             guidance: float = 1.0, kernel=None) -> torch.Tensor:
         if self.done:
             raise RuntimeError("scheduler already finished")
         s, s_next = self.sigmas[self.step_index], self.sigmas[self.step_index + 1]
-        ops.sched_step(cond, uncond, guidance, sample, s, None, dict(x=1.0, x0=0.0, v=s_next - s))
+        (kernel or ops.sched_step)(cond, uncond, guidance, sample, s, None, dict(x=1.0, x0=0.0, v=s_next - s))
         self.step_index += 1
         return sample
 

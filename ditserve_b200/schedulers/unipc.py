@@ -151,7 +151,7 @@ class UniPCFlowScheduler:
         return s_cur, corr, pred
 
     def step(self, sample: torch.Tensor, cond: torch.Tensor, uncond: torch.Tensor | None = None,
-             guidance: float = 1.0) -> torch.Tensor:
+             guidance: float = 1.0, kernel=None) -> torch.Tensor:
         """Advance ``sample`` (fp32, in place) by one step from the model's velocity."""
         if self.done:
             raise RuntimeError("scheduler already finished")
@@ -170,8 +170,8 @@ class UniPCFlowScheduler:
         pred_args = dict(x=pred["x"], x0=pred["x0"],
                          hist=[self.hist[-(i + 1)] for i in range(pred["order"] - 1)],
                          hist_coef=pred["hist_coef"])
-        ops.sched_step(cond, uncond, guidance, sample, s_cur, corr_args, pred_args, x0_out=x0_new,
-                       last_out=last_out)
+        (kernel or ops.sched_step)(cond, uncond, guidance, sample, s_cur, corr_args, pred_args, x0_out=x0_new,
+                                   last_out=last_out)
         self.last = last_out
         self.hist.append(x0_new)
         self.hist_sigmas.append(s_cur)

@@ -178,3 +178,26 @@ def test_sched_step_matches_reference():
     torch.testing.assert_close(x.cpu(), xr, rtol=1e-5, atol=1e-4)
     torch.testing.assert_close(x0o.cpu(), x0r, rtol=1e-5, atol=1e-4)
     torch.testing.assert_close(lo.cpu(), lr, rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_attention_dual_range_segments(D):
+    """MMDiT joint attention: each segment = an image block range + a text block range."""
+    torch.manual_seed(10)
+    d = _dev()
+    H = 3
+    img = [1024, 256, 4096]
+    txt = [333, 333, 77]
+    Ti, Tt = sum(img), sum(txt)
+    qkv = torch.randn(Ti + Tt, 3 * H * D, device=d).bfloat16()
+    q, k, v = qkv[:, :H * D], qkv[:, H * D:2 * H * D], qkv[:, 2 * H * D:]
+    segs, io, to = [], 0, Ti
+    for a, b in zip(img, txt):
+        segs.append((io, io + a, to, to + b, io, io + a, to, to + b))
+        io += a
+        to += b
+    tbl = ops.segment_table(segs)
+    o = ops.attention_segments(q, k, v, H, tbl)
+    ro = ops.segments_reference(q.cpu(), k.cpu(), v.cpu(), H, tbl)
+    ops.check_status(d)
+    assert _rel(o.cpu(), ro) < 2e-2

@@ -1,0 +1,102 @@
+"""SD3.5 worker backend: atomic requests and step-level continuous batches.
+
+ops: hello, prepare, advance (steps), advance_batch (one denoising step for a list of
+state_ids: late joins and early exits allowed), generate_batch (atomic), finish, release,
+snapshot, restore.  Reference: workers/ditserve/models/sd35.py:25-1634.
+"""
+from __future__ import annotations
+
+import time
+
+import torch
+
+from ..base import Backend, progress
+from .model import SD35_MEDIUM, SD35_TINY
+from .runtime import SD35Engine, SD35Spec
+
+CONFIGS = {c.name: c for c in (SD35_MEDIUM, SD35_TINY)}
+
+
+class SD35Backend(Backend):
+    operations = Backend.operations + ("advance_batch", "generate_batch", "snapshot", "restore", "inventory")
+
+    def __init__(self, config):
+        super().__init__(config)
+        cfg = CONFIGS[config.get("model", "sd3.5-medium")]
+        dev = config.get("device") or ("cuda:0" if torch.cuda.is_available() else "cpu")
+        self.device = torch.device(dev)
+        dtype = torch.bfloat16 if self.device.type == "cuda" else torch.float32
+        self.engine = SD35Engine(cfg, device=self.device, dtype=dtype, seed=int(config.get("seed", 0)),
+                                 max_batch=int(config.get("max_batch", 8)))
+        self.snapshots: dict = {}
+
+    def capabilities(self):
+        return dict(quanta=["step", "atomic"], continuous_batch=self.engine.max_batch, sequence_packing=True,
+                    model=self.engine.cfg.name)
+
+    def prepare(self, request):
+        key = self.new_id(request)
+        spec = {k: v for k, v in request.get("spec", {}).items() if k in SD35Spec.__dataclass_fields__}
+        self.states[key] = self.engine.prepare(spec)
+        st = self.states[key]
+        return dict(state_id=key, progress=progress(st.step, st.spec.steps))
+
+    def _sync(self):
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+
+    def advance(self, request):
+        st = self.state(request)
+        t0 = time.perf_counter()
+        for _ in range(min(int(request.get("steps", 1)), st.spec.steps - st.step)):
+            self.engine.advance_batch([st])
+        self._sync()
+        return dict(state_id=request["state_id"], progress=progress(st.step, st.spec.steps),
+                    model_ms=(time.perf_counter() - t0) * 1000)
+
+    def advance_batch(self, request):
+        ids = list(request["state_ids"])
+        states = [self.state(dict(state_id=i)) for i in ids]
+        t0 = time.perf_counter()
+        self.engine.advance_batch(states)
+        self._sync()
+        return dict(members=[dict(state_id=i, progress=progress(s.step, s.spec.steps)) for i, s in zip(ids, states)],
+                    batch=len(ids), model_ms=(time.perf_counter() - t0) * 1000)
+
+    def generate_batch(self, request):
+        out = []
+        states = []
+        for spec in request["specs"]:
+            sid = spec["request_id"]
+            self.prepare(dict(id=request["id"], state_id=sid, spec=spec))
+            states.append(sid)
+        while any(not self.states[s].done for s in states):
+            self.engine.advance_batch([self.states[s] for s in states])
+        for s in states:
+            out.append(self.finish(dict(request, state_id=s)))
+            self.release(dict(state_id=s))
+        return dict(results=out)
+
+    def finish(self, request):
+        st = self.state(request)
+        if not st.done:
+            raise ValueError("request is not complete")
+        art = self.persist(st.latents.float(), request)
+        return dict(state_id=request["state_id"], artifact=art, value=art.get("array_sha256"))
+
+    def snapshot(self, request):
+        st = self.state(request)
+        self.snapshots[request["state_id"]] = self.engine.snapshot(st)
+        if request.get("mode", "hot") != "keep":
+            del self.states[request["state_id"]]
+        return dict(state_id=request["state_id"], step=st.step)
+
+    def restore(self, request):
+        snap = self.snapshots.pop(request["state_id"], None)
+        if snap is None:
+            raise ValueError("no snapshot for state_id")
+        self.states[request["state_id"]] = self.engine.restore(snap)
+        return dict(state_id=request["state_id"])
+
+    def inventory(self, request):
+        return dict(states={k: dict(step=v.step, steps=v.spec.steps) for k, v in self.states.items()})

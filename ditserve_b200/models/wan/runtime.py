@@ -92,6 +92,19 @@ class WanRequestState:
         return hashlib.sha256(self.latents.detach().cpu().contiguous().numpy().tobytes()).hexdigest()
 
 
+def _tensor_items(tree, prefix=""):
+    if isinstance(tree, torch.Tensor):
+        yield prefix, tree.detach().cpu()
+    elif isinstance(tree, dict):
+        for k in sorted(tree):
+            if k == "manifest":
+                continue
+            yield from _tensor_items(tree[k], f"{prefix}/{k}")
+    elif isinstance(tree, (list, tuple)):
+        for i, v in enumerate(tree):
+            yield from _tensor_items(v, f"{prefix}/{i}")
+
+
 class CFGLocal:
     """Both CFG branches on this SP group (batched as B = 2)."""
 
@@ -171,21 +184,88 @@ class WanEngine:
         st.packets.clear()
         return st
 
-    def step(self, st: WanRequestState) -> WanRequestState:
-        if st.done:
-            raise RuntimeError("request already finished")
+    # ------------------------------------------------------------------ block executor
+    def _begin(self, st: WanRequestState):
+        br, lat, t, ctx = self._inputs(st)
+        st.packets["pk"] = self.model.begin(lat, t, ctx, self.pctx)
+        st.packets["branches"] = br
+
+    def _finish_step(self, st: WanRequestState):
+        pk = st.packets["pk"]
+        pred = self.model.predict(pk, self.pctx)
         if st.negative is not None and hasattr(self.cfg_plan, "fused_step"):
             # CFG parallelism over peer memory: exchange + guidance + update in one kernel
-            with torch.inference_mode():
-                br, lat, t, ctx = self._inputs(st)
-                mine = self.model(lat, t, ctx, self.pctx)[0]
-                self.cfg_plan.fused_step(st.scheduler, st.latents.view(-1), mine, st.spec.guidance)
+            self.cfg_plan.fused_step(st.scheduler, st.latents.view(-1), pred[0], st.spec.guidance)
             st.step += 1
             st.block = 0
             st.packets.clear()
-            return st
-        cond, uncond = self.predict(st)
-        return self.apply(st, cond, uncond)
+            return
+        cond, uncond = self._split(st, st.packets["branches"], pred)
+        self.apply(st, cond, uncond)
+
+    @torch.inference_mode()
+    def advance(self, st: WanRequestState, blocks: int | None = None, *, bell=None, check_every: int = 1,
+                group_flag=None, timing: bool = False) -> dict:
+        """Run up to ``blocks`` transformer blocks (default: to the end of the current step).
+
+        The quantum never crosses a solver-step boundary.  With a doorbell predicate the
+        host enqueues ``check_every`` blocks at a time, waits for the previous interval's
+        event (one interval of lead) and stops once the bell has rung; ``group_flag`` (a
+        callable taking and returning an int) makes every rank of an SP group agree on the
+        stop (MAX over the group) so all ranks stop after the same block.
+        """
+        if st.done:
+            raise RuntimeError("request already finished")
+        L = self.cfg.layers
+        if not st.packets:
+            self._begin(st)
+        want = L - st.block if blocks is None else min(int(blocks), L - st.block)
+        done = 0
+        stopped = False
+        prev_evt = None
+        t0 = t1 = None
+        if timing and st.latents.is_cuda:
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record()
+        pk = st.packets["pk"]
+        while done < want:
+            chunk = min(max(1, check_every), want - done)
+            for _ in range(chunk):
+                self.model.forward_block(st.block, pk, self.pctx)
+                st.block += 1
+                done += 1
+            if bell is None or done >= want:
+                continue
+            evt = None
+            if st.latents.is_cuda:
+                evt = torch.cuda.Event()
+                evt.record()
+            if prev_evt is not None:
+                prev_evt.synchronize()  # at most one interval of host lead
+            prev_evt = evt
+            flag = 1 if bell() else 0
+            if group_flag is not None:
+                flag = group_flag(flag)
+            if flag:
+                stopped = True
+                break
+        step_completed = False
+        if st.block >= L:
+            self._finish_step(st)
+            step_completed = True
+        out = dict(blocks=done, next_block=st.block, step_completed=step_completed, doorbell_stop=stopped,
+                   step=st.step, steps=st.spec.steps)
+        if t0 is not None:
+            t1.record()
+            t1.synchronize()
+            out["block_cuda_ms"] = t0.elapsed_time(t1)
+        return out
+
+    def step(self, st: WanRequestState) -> WanRequestState:
+        if st.done:
+            raise RuntimeError("request already finished")
+        self.advance(st)
+        return st
 
     def run(self, st: WanRequestState, steps: int | None = None) -> WanRequestState:
         n = st.spec.steps - st.step if steps is None else steps
@@ -214,6 +294,45 @@ class WanEngine:
                              context=snap["context"].to(self.device, copy=True),
                              negative=None if snap["negative"] is None else snap["negative"].to(self.device, copy=True),
                              step=int(snap["step"]))
+        return st
+
+    def export_packet(self, st: WanRequestState) -> tuple[bytes, str]:
+        """Serialise a request mid-step (continuation packet) with a SHA-256 manifest."""
+        snap = self.snapshot(st)
+        snap["block"] = st.block
+        if st.packets:
+            pk = st.packets["pk"]
+            snap["packet"] = {k: v.detach().cpu().clone() for k, v in pk.tensors().items()}
+            snap["packet_meta"] = dict(batch=pk.batch, seq_local=pk.seq_local, seq=pk.seq, grid=list(pk.grid),
+                                       text_len=pk.text_len, next_block=pk.next_block,
+                                       branches=list(st.packets["branches"]))
+        manifest = {}
+        for name, t in _tensor_items(snap):
+            manifest[name] = hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
+        snap["manifest"] = manifest
+        blob = self.pack(snap)
+        return blob, hashlib.sha256(blob).hexdigest()
+
+    def import_packet(self, blob: bytes, digest: str) -> WanRequestState:
+        if hashlib.sha256(blob).hexdigest() != digest:
+            raise ValueError("packet digest mismatch (tampered or truncated transfer)")
+        snap = self.unpack(blob)
+        manifest = snap.pop("manifest")
+        for name, t in _tensor_items(snap):
+            if hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).hexdigest() != manifest.get(name):
+                raise ValueError(f"tensor {name} does not match its manifest")
+        st = self.restore(snap)
+        st.block = int(snap.get("block", 0))
+        if "packet" in snap:
+            from .model import WanPacket
+            meta = snap["packet_meta"]
+            t = {k: v.to(self.device) for k, v in snap["packet"].items()}
+            cos_full, sin_full = self.model.rope(tuple(meta["grid"]), self.device)
+            pk = WanPacket(x=t["x"], mod=t["mod"], temb=t["temb"], ctx=t["ctx"], cos=t["cos"], sin=t["sin"],
+                           batch=meta["batch"], seq_local=meta["seq_local"], seq=meta["seq"], grid=tuple(meta["grid"]),
+                           text_len=meta["text_len"], next_block=meta["next_block"], cos_full=cos_full,
+                           sin_full=sin_full)
+            st.packets = {"pk": pk, "branches": meta["branches"]}
         return st
 
     @staticmethod

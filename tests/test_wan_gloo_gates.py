@@ -102,3 +102,28 @@ def test_gloo_world2_gates(mode):
     assert torch.equal(out["full"], out["segmented"]), "segmented run differs bitwise"
     cos, rel = _cos_rel(out["full"], ref)
     assert cos >= 0.95 and rel <= 0.25, (cos, rel)
+
+
+def test_block_quanta_and_packets_are_bitwise():
+    """Sub-step quanta of any size, a doorbell stop and a mid-step export/import all end on the
+    same latent as an uninterrupted run."""
+    e = _engine()
+    full = e.run(e.prepare(SPEC))
+    st = e.prepare(SPEC)
+    rung = {"n": 0}
+
+    def bell():
+        rung["n"] += 1
+        return rung["n"] == 1  # rings once, at the first check
+
+    r = e.advance(st, bell=bell, check_every=1)
+    assert r["doorbell_stop"] and r["blocks"] == 1 and not r["step_completed"]
+    blob, digest = e.export_packet(st)
+    with pytest.raises(ValueError):
+        e.import_packet(blob[:-1] + bytes([blob[-1] ^ 1]), digest)
+    st2 = e.import_packet(blob, digest)
+    assert st2.block == 1
+    e.advance(st2, blocks=1)
+    while not st2.done:
+        e.advance(st2)
+    assert torch.equal(st2.latents, full.latents)

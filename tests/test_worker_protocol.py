@@ -85,3 +85,32 @@ def test_fault_injection_and_doorbell(tmp_path):
     r = b2.advance(dict(id=2, state_id="s", quantum="step", check_blocks=2,
                         doorbell=dict(path=bell.path, epoch=4)))
     assert r["doorbell_stop"] and r["executed"] == 2
+
+
+def test_wan_and_sd35_backends_on_cpu(tmp_path):
+    """The model backends speak the same op surface as the mock (tiny models, CPU)."""
+    from ditserve_b200.models.sd35.backend import SD35Backend
+    from ditserve_b200.models.wan.backend import WanBackend
+    w = WanBackend({"model": "wan-tiny", "device": "cpu", "transfer_dir": str(tmp_path)})
+    spec = dict(request_id="v", height=64, width=64, frames=13, steps=2, seed=1)
+    w.prepare(dict(id=1, spec=spec))
+    r = w.advance(dict(id=2, state_id="v", blocks=1))
+    assert r["progress"]["block"] == 1
+    pk = w.block_export(dict(id=3, state_id="v"))
+    w.release(dict(state_id="v"))
+    w.block_import(dict(id=4, state_id="v", path=pk["path"], manifest=pk["manifest"]))
+    while not w.states["v"].done:
+        w.advance(dict(id=5, state_id="v", quantum="step"))
+    out = w.finish(dict(id=6, state_id="v", output_mode="digest"))
+    w2 = WanBackend({"model": "wan-tiny", "device": "cpu"})
+    w2.prepare(dict(id=1, spec=spec))
+    w2.advance(dict(id=2, state_id="v", steps=2))
+    assert w2.finish(dict(id=3, state_id="v", output_mode="digest"))["value"] == out["value"]
+    s = SD35Backend({"model": "sd3.5-tiny", "device": "cpu"})
+    for k in ("a", "b"):
+        s.prepare(dict(id=1, spec=dict(request_id=k, height=64, width=64, steps=2, seed=3)))
+    s.advance_batch(dict(id=2, state_ids=["a", "b"]))
+    s.advance_batch(dict(id=3, state_ids=["a", "b"]))
+    fa = s.finish(dict(id=4, state_id="a", output_mode="digest"))
+    fb = s.finish(dict(id=5, state_id="b", output_mode="digest"))
+    assert fa["value"] == fb["value"]  # same seed and spec

@@ -78,7 +78,7 @@ class Worker:
             return process_memory()
         if op == "mps_control":
             from .green_context import mps_control
-            return mps_control(request)
+            return mps_control(request, allowed=bool(self.config.get("allow_mps_control", False)))
         if op == "shutdown":
             if self.backend is not None and hasattr(self.backend, "close"):
                 self.backend.close()

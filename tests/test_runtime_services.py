@@ -1,0 +1,94 @@
+"""Host services of the worker runtime (CPU): SM partition math, MPS control gating,
+remote bridge over localhost TCP with doorbell mirroring, model integrity, client."""
+import json
+import os
+import stat
+import subprocess
+import sys
+import threading
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_partition_sms():
+    from ditserve_b200.runtime.green_context import partition_sms
+    assert partition_sms(148, [3, 1]) == [112, 32] or sum(partition_sms(148, [3, 1])) == 144
+    s = partition_sms(148, [2, 1, 1])
+    assert sum(s) <= 148 and all(x % 8 == 0 and x >= 8 for x in s)
+    assert partition_sms(108, [72, 36]) == [72, 32] or sum(partition_sms(108, [72, 36])) <= 108
+    with pytest.raises(ValueError):
+        partition_sms(16, [1, 1, 1])
+
+
+def test_mps_control_is_refused_by_default(tmp_path):
+    from ditserve_b200.runtime.green_context import mps_control
+    fake = tmp_path / "fake-mps"
+    log = tmp_path / "calls"
+    fake.write_text(f"#!/bin/sh\ncat >> {log}\nexit 0\n")
+    fake.chmod(fake.stat().st_mode | stat.S_IEXEC)
+    with pytest.raises(PermissionError):
+        mps_control({"action": "quit"}, binary=str(fake))
+    out = mps_control({"action": "quit"}, binary=str(fake), allowed=True)
+    assert out["quit"] and "quit" in log.read_text()
+
+
+def test_remote_bridge_relays_ops_and_mirrors_doorbells(tmp_path):
+    from ditserve_b200.runtime.doorbell import Doorbell
+    from ditserve_b200.runtime.remote_bridge import BridgeDaemon
+    daemon = BridgeDaemon("127.0.0.1", 0)
+    t = threading.Thread(target=daemon.serve_forever, daemon=True)
+    t.start()
+    cfg = {"options": {"costs": {"step_ms": 400}}}
+    proxy = subprocess.Popen([sys.executable, "-m", "ditserve_b200.runtime.remote_bridge", "proxy", "--connect",
+                              f"127.0.0.1:{daemon.port}", "--backend", "mock", "--config", json.dumps(cfg)],
+                             cwd=ROOT, stdin=subprocess.PIPE, stdout=subprocess.PIPE, text=True)
+
+    def call(i, op, **kw):
+        proxy.stdin.write(json.dumps(dict(version=1, id=i, op=op, **kw)) + "\n")
+        proxy.stdin.flush()
+        return json.loads(proxy.stdout.readline())
+
+    try:
+        assert call(1, "hello")["ok"]
+        assert call(2, "prepare", spec=dict(request_id="r", steps=1, blocks_per_step=8, seed=0))["ok"]
+        bell = Doorbell(str(tmp_path / "bell0"), create=True)
+        timer = threading.Timer(0.25, lambda: bell.ring(1))
+        timer.start()
+        r = call(3, "advance", state_id="r", quantum="step", check_blocks=1, doorbell=dict(path=bell.path, epoch=0))
+        assert r["ok"] and r["result"]["doorbell_stop"], r
+        assert r["result"]["executed"] < 8
+    finally:
+        proxy.stdin.close()
+        proxy.wait(timeout=10)
+        daemon.stop()
+
+
+def test_snapshot_integrity(tmp_path):
+    from ditserve_b200.runtime.model_integrity import IntegrityError, build_manifest, verify_snapshot
+    (tmp_path / "transformer").mkdir()
+    (tmp_path / "transformer" / "a.bin").write_bytes(b"abc")
+    (tmp_path / "model_index.json").write_text("{}")
+    man = build_manifest(tmp_path)
+    assert verify_snapshot(tmp_path, man)["verified"]
+    (tmp_path / "transformer" / "a.bin").write_bytes(b"abd")
+    with pytest.raises(IntegrityError):
+        verify_snapshot(tmp_path, man)
+
+
+def test_diffusers_layout_round_trip(tmp_path):
+    import torch
+    from safetensors.torch import save_file
+    from ditserve_b200.models.wan.config import WAN_TINY
+    from ditserve_b200.models.wan.model import WanTransformer
+    from ditserve_b200.runtime.model_integrity import load_diffusers_transformer
+    a = WanTransformer.random_init(WAN_TINY, dtype=torch.float32, seed=1)
+    (tmp_path / "transformer").mkdir()
+    save_file({k: v.contiguous() for k, v in a.state_dict().items()},
+              str(tmp_path / "transformer" / "diffusion_pytorch_model.safetensors"))
+    b = WanTransformer.random_init(WAN_TINY, dtype=torch.float32, seed=2)
+    info = load_diffusers_transformer(b, tmp_path)
+    assert info["tensors"] == len(a.state_dict())
+    for k, v in a.state_dict().items():
+        assert torch.equal(v, b.state_dict()[k])

@@ -30,7 +30,16 @@ constexpr int kQT = 128;  // query rows per CTA
 constexpr int kKT = 128;  // key rows per tile
 constexpr int kAttnThreads = 192;
 
+// K/V descriptors of up to kMaxKvSources key/value sources (ring attention: the local
+// chunk plus the chunks held by the ring peers, read in place over NVLink).
+constexpr int kMaxKvSources = 4;
+struct alignas(64) KvMaps {
+  CUtensorMap k[kMaxKvSources];
+  CUtensorMap v[kMaxKvSources];
+};
+
 struct AttnParams {
+  int kv_sources;
   int batch, seq_q, seq_k;
   const int* cu_q;
   const int* cu_k;
@@ -93,8 +102,8 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 
 template <int D>
 __global__ void __launch_bounds__(kAttn2Threads, 1)
-    attention2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                      const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+    attention2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ KvMaps kv,
+                      AttnParams p) {
   using Cfg = Attn2Cfg<D>;
   constexpr int KS = Cfg::KS;
   constexpr int VS = Cfg::VS;
@@ -128,11 +137,18 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
     return;
   }
   const int nka = (ka1 - ka0 + kKT - 1) / kKT;
-  const int n_tiles = nka + (kb1 - kb0 + kKT - 1) / kKT;
+  const int per_source = nka + (kb1 - kb0 + kKT - 1) / kKT;
+  const int n_tiles = per_source * p.kv_sources;
   if (n_tiles <= 0) return;  // uniform across the CTA
-  // first key row of tile j and how many of its rows belong to the segment
-  auto ktile_row = [&](int j) { return j < nka ? ka0 + j * kKT : kb0 + (j - nka) * kKT; };
-  auto ktile_valid = [&](int j) { return j < nka ? ka1 - (ka0 + j * kKT) : kb1 - (kb0 + (j - nka) * kKT); };
+  // tile j reads source j / per_source; within a source the segment's key ranges repeat
+  auto ktile_row = [&](int j) {
+    const int jj = j % per_source;
+    return jj < nka ? ka0 + jj * kKT : kb0 + (jj - nka) * kKT;
+  };
+  auto ktile_valid = [&](int j) {
+    const int jj = j % per_source;
+    return jj < nka ? ka1 - (ka0 + jj * kKT) : kb1 - (kb0 + (jj - nka) * kKT);
+  };
   const int hk = h / (p.heads / p.heads_kv);
 
   extern __shared__ uint8_t smem_raw[];
@@ -185,8 +201,10 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
     if (lane == 0) {
       // ---------------- TMA producer: K runs one tile ahead of V ----------------
       tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
+      for (int src = 0; src < p.kv_sources; ++src) {
+        tma_prefetch_desc(&kv.k[src]);
+        tma_prefetch_desc(&kv.v[src]);
+      }
       mbar_arrive_expect_tx(q_full, 2 * Cfg::kQBytes);
 #pragma unroll
       for (int t = 0; t < 2; ++t)
@@ -199,7 +217,8 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         mbar_arrive_expect_tx(&k_full[st], Cfg::kKBytes);
 #pragma unroll
         for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_2d(sK + st * Cfg::kKBytes + a * (kKT * 128), &tmK, hk * D + a * 64, ktile_row(j), &k_full[st]);
+          tma_load_2d(sK + st * Cfg::kKBytes + a * (kKT * 128), &kv.k[j / per_source], hk * D + a * 64, ktile_row(j),
+                      &k_full[st]);
         return true;
       };
       bool ok = load_k(0);
@@ -210,7 +229,8 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         mbar_arrive_expect_tx(&v_full[st], Cfg::kVBytes);
 #pragma unroll
         for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_2d(sV + st * Cfg::kVBytes + a * (kKT * 128), &tmV, hk * D + a * 64, ktile_row(j), &v_full[st]);
+          tma_load_2d(sV + st * Cfg::kVBytes + a * (kKT * 128), &kv.v[j / per_source], hk * D + a * 64, ktile_row(j),
+                      &v_full[st]);
       }
     }
   } else if (warp == 1) {
@@ -440,9 +460,17 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
 template <int D>
 void launch_d(const AttnArgs& a, cudaStream_t stream) {
   CUtensorMap tq = make_tmap_bf16_2d(a.q, a.total_q, static_cast<uint64_t>(a.heads) * D, a.q_row_stride, kQT);
-  CUtensorMap tk = make_tmap_bf16_2d(a.k, a.total_k, static_cast<uint64_t>(a.heads_kv) * D, a.k_row_stride, kKT);
-  CUtensorMap tv = make_tmap_bf16_2d(a.v, a.total_k, static_cast<uint64_t>(a.heads_kv) * D, a.v_row_stride, kKT);
+  if (a.kv_sources < 1 || a.kv_sources > kMaxKvSources) throw std::runtime_error("attention: 1..4 KV sources");
+  KvMaps kv;
+  for (int src = 0; src < a.kv_sources; ++src) {
+    const void* kp = src == 0 ? a.k : a.k_extra[src - 1];
+    const void* vp = src == 0 ? a.v : a.v_extra[src - 1];
+    if (kp == nullptr || vp == nullptr) throw std::runtime_error("attention: missing KV source pointer");
+    kv.k[src] = make_tmap_bf16_2d(kp, a.total_k, static_cast<uint64_t>(a.heads_kv) * D, a.k_row_stride, kKT);
+    kv.v[src] = make_tmap_bf16_2d(vp, a.total_k, static_cast<uint64_t>(a.heads_kv) * D, a.v_row_stride, kKT);
+  }
   AttnParams p;
+  p.kv_sources = a.kv_sources;
   p.batch = a.batch;
   p.seq_q = a.seq_q;
   p.seq_k = a.seq_k;
@@ -470,7 +498,7 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
   auto kern = attention2_kernel<D>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Cfg<D>::kSmemBytes);
   dim3 grid(blocks, a.heads, a.batch);
-  kern<<<grid, kAttn2Threads, Attn2Cfg<D>::kSmemBytes, stream>>>(tq, tk, tv, p);
+  kern<<<grid, kAttn2Threads, Attn2Cfg<D>::kSmemBytes, stream>>>(tq, kv, p);
 }
 
 }  // namespace

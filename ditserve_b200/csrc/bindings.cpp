@@ -81,7 +81,8 @@ void attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
                const c10::optional<at::Tensor>& lse, int64_t batch, int64_t seq_q, int64_t seq_k,
                const c10::optional<at::Tensor>& cu_q, const c10::optional<at::Tensor>& cu_k, int64_t max_seq_q,
                int64_t heads, int64_t heads_kv, int64_t head_dim, double scale, const at::Tensor& status,
-               const c10::optional<at::Tensor>& seg, int64_t max_q_blocks) {
+               const c10::optional<at::Tensor>& seg, int64_t max_q_blocks, std::vector<at::Tensor> k_extra,
+               std::vector<at::Tensor> v_extra) {
   check_cuda_bf16_2d(q, "q");
   check_cuda_bf16_2d(k, "k");
   check_cuda_bf16_2d(v, "v");
@@ -133,6 +134,17 @@ void attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
   a.status = status_ptr(status);
   a.seg_table = seg.has_value() ? seg->data_ptr<int>() : nullptr;
   a.max_q_blocks = static_cast<int>(max_q_blocks);
+  TORCH_CHECK(k_extra.size() == v_extra.size() && k_extra.size() <= 3, "attention: up to 3 extra KV sources");
+  a.kv_sources = 1 + static_cast<int>(k_extra.size());
+  for (size_t i = 0; i < k_extra.size(); ++i) {
+    check_cuda_bf16_2d(k_extra[i], "k_extra");
+    check_cuda_bf16_2d(v_extra[i], "v_extra");
+    TORCH_CHECK(k_extra[i].sizes() == k.sizes() && k_extra[i].stride(0) == k.stride(0) &&
+                    v_extra[i].sizes() == v.sizes() && v_extra[i].stride(0) == v.stride(0),
+                "attention: extra KV sources must match k/v in shape and stride");
+    a.k_extra[i] = k_extra[i].data_ptr();
+    a.v_extra[i] = v_extra[i].data_ptr();
+  }
   ds::launch_attention(a, at::cuda::getCurrentCUDAStream());
 }
 
@@ -339,7 +351,7 @@ void cfg_step_peer(const at::Tensor& mine, int64_t theirs_off, int64_t role, dou
 void qkv_scatter(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk, double eps,
                  const c10::optional<at::Tensor>& cos, const c10::optional<at::Tensor>& sin, int64_t seq_local,
                  int64_t heads, int64_t head_dim, int64_t rank, const std::vector<int64_t>& bases, int64_t timeout_ns,
-                 int64_t recv_off) {
+                 int64_t recv_off, int64_t pos_base) {
   check_cuda_bf16_2d(qkv, "qkv");
   TORCH_CHECK(qkv.size(1) >= 3 * heads * head_dim, "qkv_scatter: qkv too narrow");
   TORCH_CHECK(qkv.size(0) % seq_local == 0, "qkv_scatter: rows must be batch * seq_local");
@@ -358,13 +370,15 @@ void qkv_scatter(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& 
   a.rope_sin = sin.has_value() ? sin->data_ptr<float>() : nullptr;
   a.group = make_group(rank, bases, timeout_ns);
   a.recv_off = recv_off;
+  a.pos_base = static_cast<int>(pos_base);
   ds::launch_qkv_scatter(a, at::cuda::getCurrentCUDAStream());
 }
 
 void attention_scatter(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t batch, int64_t seq,
                        int64_t heads, int64_t head_dim, double scale, int64_t rank, const std::vector<int64_t>& bases,
                        int64_t timeout_ns, int64_t o_off, int64_t seq_local, int64_t head_offset,
-                       int64_t peer_stride, const at::Tensor& status) {
+                       int64_t peer_stride, const at::Tensor& status, std::vector<int64_t> k_extra_ptrs,
+                       std::vector<int64_t> v_extra_ptrs) {
   check_cuda_bf16_2d(q, "q");
   check_cuda_bf16_2d(k, "k");
   check_cuda_bf16_2d(v, "v");
@@ -392,6 +406,12 @@ void attention_scatter(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   a.o_seq_local = static_cast<int>(seq_local);
   a.o_head_offset = static_cast<int>(head_offset);
   a.o_peer_stride = peer_stride;
+  TORCH_CHECK(k_extra_ptrs.size() == v_extra_ptrs.size() && k_extra_ptrs.size() <= 3, "up to 3 ring peers");
+  a.kv_sources = 1 + static_cast<int>(k_extra_ptrs.size());
+  for (size_t i = 0; i < k_extra_ptrs.size(); ++i) {
+    a.k_extra[i] = reinterpret_cast<const void*>(k_extra_ptrs[i]);
+    a.v_extra[i] = reinterpret_cast<const void*>(v_extra_ptrs[i]);
+  }
   ds::launch_attention(a, at::cuda::getCurrentCUDAStream());
 }
 

@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(256) qkv_scatter_kernel(QkvScatterArgs a) {
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       const float r = rsqrtf(ss / static_cast<float>(width) + a.eps);
       const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(part == 0 ? a.wq : a.wk);
-      const int pos = t + a.group.rank * a.seq_local;  // global position in the sequence
+      const int pos = a.pos_base + t + a.group.rank * a.seq_local;  // global position in the sequence
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
         const int col = c * 256 + lane * 8;

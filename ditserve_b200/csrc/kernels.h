@@ -67,6 +67,11 @@ struct AttnArgs {
   const int* cu_seqlens_q = nullptr;
   const int* cu_seqlens_k = nullptr;
   int max_seq_q = 0;
+  // extra key/value sources with the same shape and strides as k/v (ring attention: the
+  // chunks of the ring peers, read in place); every segment attends to all sources
+  int kv_sources = 1;
+  const void* k_extra[3] = {nullptr, nullptr, nullptr};
+  const void* v_extra[3] = {nullptr, nullptr, nullptr};
   const int* seg_table = nullptr;  // [batch][8]: qa0 qa1 qb0 qb1 ka0 ka1 kb0 kb1 (dual-range segments)
   int max_q_blocks = 0;            // grid.x in dual-range mode: max over segments of 256-row query blocks
   int heads = 0, heads_kv = 0, head_dim = 128;
@@ -164,6 +169,7 @@ struct QkvScatterArgs {
   const float* rope_sin = nullptr;
   PeerGroup group;
   int64_t recv_off = 0;  // heap offset of every member's receive buffer [B*S, 3*Hl*D]
+  int pos_base = 0;      // global position of this group's first token (ring chunk offset)
 };
 void launch_group_barrier(const PeerGroup& g, int channel, uint64_t epoch, int* status, cudaStream_t s);
 void launch_cfg_step_peer(const SchedStepArgs& a, const PeerGroup& g, int channel, uint64_t epoch,

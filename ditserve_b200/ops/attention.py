@@ -93,16 +93,22 @@ def attention_segments(q, k, v, heads, seg_table: torch.Tensor, *, scale=None, o
     if out is None:
         out = torch.empty(q.shape[0], q.shape[1], device=q.device, dtype=torch.bfloat16)
     kernel("attention")(q, k, v, out, None, tbl.shape[0], 0, 0, None, None, 0, heads, heads_kv, d, float(scale),
-                        status_word(q.device), tbl.to(q.device).contiguous(), blocks)
+                        status_word(q.device), tbl.to(q.device).contiguous(), blocks, [], [])
     return out
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *, heads_kv: int | None = None,
               cu_seqlens_q: torch.Tensor | None = None, cu_seqlens_k: torch.Tensor | None = None,
               max_seqlen_q: int | None = None, scale: float | None = None, out: torch.Tensor | None = None,
-              return_lse: bool = False):
+              return_lse: bool = False, kv_extra: list | None = None):
+    """``kv_extra`` = [(k_i, v_i), ...]: extra key/value sources laid out like k/v (ring chunks);
+    every query attends to the keys of all sources."""
     heads_kv = heads_kv or heads
     if not use_kernels(q, k, v):
+        if kv_extra:
+            cat = 1 if k.dim() == 3 else 0
+            k = torch.cat([k] + [e[0] for e in kv_extra], cat)
+            v = torch.cat([v] + [e[1] for e in kv_extra], cat)
         return attention_reference(q, k, v, heads, heads_kv, cu_seqlens_q, cu_seqlens_k, scale, return_lse)
     width = q.shape[-1]
     d = width // heads
@@ -125,7 +131,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, *, 
     ckk = cu_seqlens_k.to(torch.int32) if cu_seqlens_k is not None else None
     if cq is not None and max_seqlen_q is None:
         max_seqlen_q = int((cq[1:] - cq[:-1]).max().item())
+    ke = [e[0].reshape(k2.shape) for e in (kv_extra or [])]
+    ve = [e[1].reshape(v2.shape) for e in (kv_extra or [])]
     kernel("attention")(q2, k2, v2, o2, lse, B, Sq, Sk, cq, ckk, int(max_seqlen_q or 0), heads, heads_kv, d,
-                        float(scale), status_word(q.device), None, 0)
+                        float(scale), status_word(q.device), None, 0, ke, ve)
     o = out.reshape(*q.shape[:-1], width)
     return (o, lse) if return_lse else o

@@ -22,7 +22,7 @@ from .. import ops
 from ..ops._ext import ext, status_word
 from .symm import PeerGroup, SymmetricHeap
 
-CH_SP, CH_CFG, CH_GATHER = 0, 1, 2
+CH_SP, CH_CFG, CH_GATHER, CH_USP_ADDR = 0, 1, 2, 3
 
 
 class FusedUlysses:
@@ -50,14 +50,14 @@ class FusedUlysses:
         st = status_word(qkv.device)
         r, bases, tmo = self.group.args()
         ext().qkv_scatter(qkv, wq, wk, float(eps), cos_full, sin_full, seq_local, heads, self.head_dim, r, bases,
-                          tmo, self.recv_off)
+                          tmo, self.recv_off, 0)
         self.group.barrier(st)
         hl = heads // self.sp_size
         w = hl * self.head_dim
         q, k, v = self.recv[:, :w], self.recv[:, w:2 * w], self.recv[:, 2 * w:]
         ext().attention_scatter(q, k, v, batch, seq_local * self.sp_size, hl, self.head_dim,
                                 1.0 / math.sqrt(self.head_dim), r, bases, tmo, self.o_off, seq_local,
-                                self.sp_rank * hl, heads * self.head_dim, st)
+                                self.sp_rank * hl, heads * self.head_dim, st, [], [])
         self.group.barrier(st)
         return self.o
 
@@ -69,6 +69,51 @@ class FusedUlysses:
         self.gather_group.barrier(status_word(y.device))
         P = self.sp_size
         return self.gathered.view(P, batch, seq_local, -1).permute(1, 0, 2, 3).reshape(batch * P * seq_local, -1)
+
+
+class FusedUSP(FusedUlysses):
+    """Ulysses x ring (2D USP): heads exchanged inside the U-group, keys/values of the ring
+    peers read in place by the attention mainloop (multi-source TMA over peer memory)."""
+
+    def __init__(self, heap: SymmetricHeap, sp_members: tuple, ring: int, seq_local: int, heads: int, head_dim: int,
+                 batch: int, gather_cols: int = 64):
+        P = len(sp_members)
+        U = P // ring
+        m = sp_members.index(heap.rank)
+        self.r, self.u, self.U, self.R = m // U, m % U, U, ring
+        self.sp_group = PeerGroup(heap, sp_members, CH_SP)
+        self.gather_group = PeerGroup(heap, sp_members, CH_GATHER)
+        self.ugroup = PeerGroup(heap, sp_members[self.r * U:(self.r + 1) * U], CH_USP_ADDR)
+        self.ring_members = [sp_members[rr * U + self.u] for rr in range(ring)]
+        self.heap = heap
+        self.sp_size, self.sp_rank = P, m
+        self.seq_local, self.heads, self.head_dim, self.batch = seq_local, heads, head_dim, batch
+        hl = heads // U
+        chunk = seq_local * U  # tokens of one ring chunk
+        self.recv_off, self.recv = heap.alloc_view((batch * chunk, 3 * hl * head_dim))
+        self.o_off, self.o = heap.alloc_view((batch * seq_local, heads * head_dim))
+        self.gather_off, self.gathered = heap.alloc_view((P * batch * seq_local, gather_cols))
+        self.gather_cols = gather_cols
+        self.group = self.sp_group
+
+    def fused_qkv_attention(self, qkv, wq, wk, eps, cos_full, sin_full, heads, batch, seq_local):
+        st = status_word(qkv.device)
+        ur, ub, utmo = self.ugroup.args()
+        chunk = seq_local * self.U
+        ext().qkv_scatter(qkv, wq, wk, float(eps), cos_full, sin_full, seq_local, heads, self.head_dim, ur, ub,
+                          utmo, self.recv_off, self.r * chunk)
+        self.sp_group.barrier(st)
+        hl = heads // self.U
+        w = hl * self.head_dim
+        q, k, v = self.recv[:, :w], self.recv[:, w:2 * w], self.recv[:, 2 * w:]
+        peers = [m for m in self.ring_members if m != self.heap.rank]
+        k_extra = [self.heap.bases[m] + self.recv_off + w * 2 for m in peers]
+        v_extra = [self.heap.bases[m] + self.recv_off + 2 * w * 2 for m in peers]
+        ext().attention_scatter(q, k, v, batch, chunk, hl, self.head_dim, 1.0 / math.sqrt(self.head_dim), ur, ub,
+                                utmo, self.o_off, seq_local, self.u * hl, heads * self.head_dim, st, k_extra,
+                                v_extra)
+        self.sp_group.barrier(st)
+        return self.o
 
 
 class FusedCFG:
@@ -123,12 +168,16 @@ def upgrade(layout, rank, device, pctx, cfg_plan, sp_groups, cfg_groups, seq_loc
     hl = cfg.heads // P
     need = 0
     if P > 1:
-        need += batch * seq_local * P * 3 * hl * cfg.head_dim * 2 + batch * seq_local * cfg.dim * 2
+        hl = cfg.heads // form.ulysses
+        need += batch * seq_local * form.ulysses * 3 * hl * cfg.head_dim * 2 + batch * seq_local * cfg.dim * 2
         need += P * batch * seq_local * cfg.out_channels * 4 * 2
     pred_numel = pred_numel or 8 * 1024 * 1024
     need += 2 * pred_numel * 2  # double-buffered bf16 prediction slots
     heap = SymmetricHeap(heap_bytes or int(need * 1.2) + (64 << 20), device)
-    if P > 1:
+    if P > 1 and form.ring > 1:
+        pctx = FusedUSP(heap, layout.sp_ranks(rank), form.ring, seq_local, cfg.heads, cfg.head_dim, batch,
+                        gather_cols=cfg.out_channels * math.prod(cfg.patch))
+    elif P > 1:
         pctx = FusedUlysses(heap, layout.sp_ranks(rank), seq_local, cfg.heads, cfg.head_dim, batch,
                             gather_cols=cfg.out_channels * math.prod(cfg.patch))
     if form.cfg == 2:

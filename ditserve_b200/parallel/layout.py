@@ -96,6 +96,20 @@ class FixedLayout:
     def sp_rank(self, rank: int) -> int:
         return self.sp_ranks(rank).index(rank)
 
+    # Ulysses x ring inside one SP group: member m = r * U + u holds token shard m of the
+    # sequence; the U-group (same r) exchanges heads, the ring group (same u) shares keys.
+    def ulysses_ranks(self, rank: int) -> tuple:
+        sp = self.sp_ranks(rank)
+        U = self.form.ulysses
+        r = sp.index(rank) // U
+        return tuple(sp[r * U:(r + 1) * U])
+
+    def ring_ranks(self, rank: int) -> tuple:
+        sp = self.sp_ranks(rank)
+        U = self.form.ulysses
+        u = sp.index(rank) % U
+        return tuple(sp[rr * U + u] for rr in range(self.form.ring))
+
 
 def default_form(n_gpus: int, cfg: bool = True) -> Form:
     """Best single-request form on NVSwitch: CFG parallelism first, then Ulysses."""

@@ -60,3 +60,48 @@ class CFGExchangeNCCL:
         both = torch.empty((2, flat.shape[1]), device=mine.device, dtype=mine.dtype)
         dist.all_gather_into_tensor(both, flat, group=self.group)
         return both[1 - self.cfg_rank].view(mine.shape)
+
+
+class UlyssesRingNCCL(UlyssesNCCL):
+    """NCCL baseline of Ulysses x ring: all-to-all inside the U-group, then the ring
+    group's key/value chunks gathered and attended to in one pass (the exact result of a
+    ring rotation with log-sum-exp merging)."""
+
+    def __init__(self, sp_group, u_group, ring_group, sp_size, sp_rank, ulysses, ring):
+        self.group = u_group
+        self.u_size = ulysses
+        self.sp_group = sp_group
+        self.ring_group = ring_group
+        self.ring = ring
+        self.sp_size = sp_size          # the model shards the sequence over the whole SP group
+        self.sp_rank = sp_rank
+        self.sp_size_total = sp_size
+
+    def self_attention_qkv(self, qkv, heads, batch, seq_local):
+        U = self.u_size
+        hd = qkv.shape[1] // (3 * heads)
+        hl = heads // U
+        if U > 1:
+            send = qkv.view(batch, seq_local, 3, U, hl, hd).permute(3, 0, 1, 2, 4, 5).contiguous()
+            recv = torch.empty_like(send)
+            dist.all_to_all_single(recv, send, group=self.group)
+            chunk = recv.permute(1, 0, 2, 3, 4, 5).reshape(batch, U * seq_local, 3, hl * hd)
+        else:
+            chunk = qkv.view(batch, seq_local, 3, heads * hd)
+        kv = chunk[:, :, 1:].contiguous()
+        parts = torch.empty((self.ring, *kv.shape), device=kv.device, dtype=kv.dtype)
+        dist.all_gather_into_tensor(parts.view(self.ring * kv.shape[0], *kv.shape[1:]), kv, group=self.ring_group)
+        keys = parts.permute(1, 0, 2, 3, 4).reshape(batch, self.ring * U * seq_local, 2, hl * hd)
+        o = ops.attention(chunk[:, :, 0], keys[:, :, 0], keys[:, :, 1], hl)
+        if U == 1:
+            return o.reshape(batch * seq_local, heads * hd)
+        send2 = o.view(batch, U, seq_local, hl * hd).permute(1, 0, 2, 3).contiguous()
+        recv2 = torch.empty_like(send2)
+        dist.all_to_all_single(recv2, send2, group=self.group)
+        return recv2.permute(1, 2, 0, 3).reshape(batch * seq_local, heads * hd)
+
+    def gather_sequence(self, y, batch, seq_local):
+        P = self.sp_size_total
+        parts = torch.empty((P * batch * seq_local, y.shape[1]), device=y.device, dtype=y.dtype)
+        dist.all_gather_into_tensor(parts, y.contiguous(), group=self.sp_group)
+        return parts.view(P, batch, seq_local, -1).permute(1, 0, 2, 3).reshape(batch * P * seq_local, -1)

@@ -14,7 +14,7 @@ import torch.distributed as dist
 from ..models.wan.model import LocalAttention
 from ..models.wan.runtime import CFGLocal
 from .layout import FixedLayout
-from .nccl import CFGExchangeNCCL, UlyssesNCCL
+from .nccl import CFGExchangeNCCL, UlyssesNCCL, UlyssesRingNCCL
 
 
 def build_parallel(layout: FixedLayout, rank: int, device: torch.device, attention: str = "fused",
@@ -30,10 +30,25 @@ def build_parallel(layout: FixedLayout, rank: int, device: torch.device, attenti
         for j in range(form.sp):
             pair = (layout.ranks[j], layout.ranks[j + form.sp])
             cfg_groups[pair] = dist.new_group(list(pair))
+    u_groups, ring_groups = {}, {}
+    if form.ring > 1:
+        U, R = form.ulysses, form.ring
+        for i in range(n_sp):
+            sp = layout.ranks[i * form.sp:(i + 1) * form.sp]
+            for r in range(R):
+                g = tuple(sp[r * U:(r + 1) * U])
+                u_groups[g] = dist.new_group(list(g)) if U > 1 else None
+            for u in range(U):
+                g = tuple(sp[rr * U + u] for rr in range(R))
+                ring_groups[g] = dist.new_group(list(g))
     pctx = LocalAttention()
     cfg_plan = CFGLocal()
     my_sp = layout.sp_ranks(rank)
-    if form.sp > 1:
+    if form.sp > 1 and form.ring > 1:
+        pctx = UlyssesRingNCCL(sp_groups[my_sp], u_groups[layout.ulysses_ranks(rank)],
+                               ring_groups[layout.ring_ranks(rank)], form.sp, layout.sp_rank(rank), form.ulysses,
+                               form.ring)
+    elif form.sp > 1:
         pctx = UlyssesNCCL(sp_groups[my_sp], form.sp, layout.sp_rank(rank))
     if form.cfg == 2:
         partner = layout.cfg_partner(rank)

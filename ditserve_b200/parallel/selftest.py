@@ -23,6 +23,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--tiny", action="store_true", help="small 2-block model at 240p (fast)")
+    ap.add_argument("--form", default=None, help="parallel form (default: cfg2 x Ulysses over the world)")
     args = ap.parse_args()
     from ..models.wan.config import WAN21_T2V_1_3B, WanConfig
     from ..models.wan import config as wcfg
@@ -42,7 +43,8 @@ def main():
     spec = WanSpec(model=cfg.name, height=240 if args.tiny else 480, width=416 if args.tiny else 832, frames=81,
                    steps=10, guidance=5.0, seed=3)
     lat = spec.latent_shape()
-    form = default_form(world)
+    from .layout import Form
+    form = Form.parse(args.form) if args.form else default_form(world)
     layout = FixedLayout(tuple(range(world)), form)
     out = {}
     for path in ("nccl", "fused"):

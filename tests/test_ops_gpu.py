@@ -201,3 +201,19 @@ def test_attention_dual_range_segments(D):
     ro = ops.segments_reference(q.cpu(), k.cpu(), v.cpu(), H, tbl)
     ops.check_status(d)
     assert _rel(o.cpu(), ro) < 2e-2
+
+
+@pytest.mark.parametrize("sources", [2, 3, 4])
+def test_attention_multi_source_kv_equals_concatenated(sources):
+    """Ring mainloop on one GPU: keys/values split over several sources (as ring peers hold
+    them) give the same result as one concatenated key/value set."""
+    torch.manual_seed(11)
+    d = _dev()
+    B, S, H, D = 2, 640, 4, 128
+    q = torch.randn(B, S, H * D, device=d).bfloat16()
+    ks = [torch.randn(B, S, H * D, device=d).bfloat16() for _ in range(sources)]
+    vs = [torch.randn(B, S, H * D, device=d).bfloat16() for _ in range(sources)]
+    o = ops.attention(q, ks[0], vs[0], H, kv_extra=list(zip(ks[1:], vs[1:])))
+    ref = ops.attention_reference(q.cpu(), torch.cat([k.cpu() for k in ks], 1), torch.cat([v.cpu() for v in vs], 1), H)
+    ops.check_status(d)
+    assert _rel(o.cpu(), ref) < 2e-2

@@ -48,8 +48,8 @@ def _worker(rank, world, port, mode, out):
     try:
         from ditserve_b200.parallel.layout import Form, FixedLayout
         from ditserve_b200.parallel.runtime import build_parallel
-        form = Form(1, 2, 1) if mode == "sp2" else Form(2, 1, 1)
-        layout = FixedLayout((0, 1), form)
+        form = {"sp2": Form(1, 2, 1), "cfg2": Form(2, 1, 1), "u2r2": Form(1, 4, 2)}[mode]
+        layout = FixedLayout(tuple(range(world)), form)
         pctx, cfg_plan = build_parallel(layout, rank, torch.device("cpu"), attention="nccl")
         e = _engine(pctx, cfg_plan)
         st = e.prepare(SPEC)
@@ -73,7 +73,8 @@ def _run_world(mode):
     port = _free_port()
     mgr = mp.Manager()
     out = mgr.dict()
-    mp.spawn(_worker, args=(2, port, mode, out), nprocs=2, join=True)
+    world = 4 if mode == "u2r2" else 2
+    mp.spawn(_worker, args=(world, port, mode, out), nprocs=world, join=True)
     return dict(out)
 
 
@@ -95,7 +96,7 @@ def test_single_rank_pause_resume_is_bitwise():
     assert torch.equal(st.latents, st3.latents)
 
 
-@pytest.mark.parametrize("mode", ["sp2", "cfg2"])
+@pytest.mark.parametrize("mode", ["sp2", "cfg2", "u2r2"])
 def test_gloo_world2_gates(mode):
     ref = _sp1_run()
     out = _run_world(mode)

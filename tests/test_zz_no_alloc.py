@@ -38,7 +38,7 @@ def _existing_path(qkv, wq, wk, eps, cos, sin, batch, seq, heads, hd):
     width = heads * hd
     heap, _ = ext.symm_alloc(int(ext.FLAG_BYTES) + batch * seq * 3 * width * 2 + 4096, 0)
     off = 4096 if int(ext.FLAG_BYTES) <= 4096 else int(ext.FLAG_BYTES)
-    ext.qkv_scatter(qkv, wq, wk, float(eps), cos, sin, seq, heads, hd, 0, [heap.data_ptr()], int(1e9), off)
+    ext.qkv_scatter(qkv, wq, wk, float(eps), cos, sin, seq, heads, hd, 0, [heap.data_ptr()], int(1e9), off, 0)
     staged = heap[off:off + batch * seq * 3 * width * 2].view(torch.bfloat16).view(batch * seq, 3 * width)
     q, k, v = staged[:, :width], staged[:, width:2 * width], staged[:, 2 * width:]
     out = ops.attention(q.view(batch, seq, width), k.view(batch, seq, width), v.view(batch, seq, width), heads)

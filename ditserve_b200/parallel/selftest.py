@@ -40,7 +40,8 @@ def main():
     if args.tiny:
         cfg = WanConfig("wan-selftest", dim=1536, heads=12, ffn_dim=2048, layers=2, in_channels=16, out_channels=16)
         wcfg.CONFIGS[cfg.name] = cfg
-    spec = WanSpec(model=cfg.name, height=240 if args.tiny else 480, width=416 if args.tiny else 832, frames=81,
+    # tiny: 21 x 16 x 28 = 9408 tokens, divisible by every SP degree up to 8
+    spec = WanSpec(model=cfg.name, height=256 if args.tiny else 480, width=448 if args.tiny else 832, frames=81,
                    steps=10, guidance=5.0, seed=3)
     lat = spec.latent_shape()
     from .layout import Form

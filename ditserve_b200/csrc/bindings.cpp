@@ -424,6 +424,22 @@ void allgather_rows(const at::Tensor& src, int64_t dst_off, int64_t rank, const 
                             at::cuda::getCurrentCUDAStream());
 }
 
+void strided_put(const at::Tensor& src, int64_t peer, int64_t dst_off, int64_t rank,
+                 const std::vector<int64_t>& bases, int64_t timeout_ns) {
+  TORCH_CHECK(src.is_cuda() && src.dim() <= 4, "strided_put: CUDA tensor of at most 4 dims");
+  TORCH_CHECK(src.element_size() == 2 || src.element_size() == 4, "strided_put: 2- or 4-byte elements");
+  const c10::cuda::CUDAGuard guard(src.device());
+  ds::StridedSlice sl;
+  sl.esize = static_cast<int>(src.element_size());
+  const int off = 4 - static_cast<int>(src.dim());
+  for (int d = 0; d < src.dim(); ++d) {
+    sl.size[off + d] = src.size(d);
+    sl.stride[off + d] = src.stride(d) * src.element_size();
+  }
+  ds::launch_strided_put(make_group(rank, bases, timeout_ns), static_cast<int>(peer), src.data_ptr(), sl, dst_off,
+                         at::cuda::getCurrentCUDAStream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -442,6 +458,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_scatter", &qkv_scatter, "RMS qk-norm + RoPE + Ulysses all-to-all scatter");
   m.def("attention_scatter", &attention_scatter, "attention with the head->sequence all-to-all in its epilogue");
   m.def("allgather_rows", &allgather_rows, "sequence all-gather by peer stores");
+  m.def("strided_put", &strided_put, "strided slice -> contiguous buffer of a group member (halo exchange)");
   m.attr("FLAG_BYTES") = ds::kFlagBytes;
   m.attr("MAX_PEERS") = ds::kMaxPeers;
   m.attr("CHANNELS") = ds::kChannels;

@@ -249,7 +249,44 @@ __global__ void __launch_bounds__(256) allgather_rows_kernel(PeerGroup g, const 
   }
 }
 
+// Copy a strided 4-D slice (elements of `esize` bytes) into a contiguous buffer of one
+// group member (halo exchange of the patch-parallel VAE: a boundary row/column of this
+// rank's feature map lands directly in the neighbour's halo buffer).
+__global__ void __launch_bounds__(256) strided_put_kernel(PeerGroup g, int peer, const uint8_t* src, StridedSlice sl,
+                                                          int64_t dst_off) {
+  const int64_t n = static_cast<int64_t>(sl.size[0]) * sl.size[1] * sl.size[2] * sl.size[3];
+  uint8_t* dst = reinterpret_cast<uint8_t*>(g.base[peer]) + dst_off;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t r = i;
+    const int64_t i3 = r % sl.size[3];
+    r /= sl.size[3];
+    const int64_t i2 = r % sl.size[2];
+    r /= sl.size[2];
+    const int64_t i1 = r % sl.size[1];
+    const int64_t i0 = r / sl.size[1];
+    const uint8_t* s = src + i0 * sl.stride[0] + i1 * sl.stride[1] + i2 * sl.stride[2] + i3 * sl.stride[3];
+    if (sl.esize == 2) {
+      reinterpret_cast<uint16_t*>(dst)[i] = *reinterpret_cast<const uint16_t*>(s);
+    } else {
+      reinterpret_cast<uint32_t*>(dst)[i] = *reinterpret_cast<const uint32_t*>(s);
+    }
+  }
+}
+
 }  // namespace
+
+void launch_strided_put(const PeerGroup& g, int peer, const void* src, const StridedSlice& sl, int64_t dst_off,
+                        cudaStream_t s) {
+  if (peer < 0 || peer >= g.size) throw std::runtime_error("strided_put: peer outside the group");
+  if (sl.esize != 2 && sl.esize != 4) throw std::runtime_error("strided_put: element size must be 2 or 4");
+  const int64_t n = static_cast<int64_t>(sl.size[0]) * sl.size[1] * sl.size[2] * sl.size[3];
+  if (n <= 0) return;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  strided_put_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(g, peer, reinterpret_cast<const uint8_t*>(src), sl,
+                                                              dst_off);
+}
 
 void launch_group_barrier(const PeerGroup& g, int channel, uint64_t epoch, int* status, cudaStream_t s) {
   if (g.size < 1 || g.size > kMaxPeers || channel < 0 || channel >= kChannels) throw std::runtime_error("bad group");

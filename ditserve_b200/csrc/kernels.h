@@ -176,5 +176,12 @@ void launch_cfg_step_peer(const SchedStepArgs& a, const PeerGroup& g, int channe
                           const void* mine, int64_t theirs_off, int my_role, int* status, cudaStream_t s);
 void launch_qkv_scatter(const QkvScatterArgs& a, cudaStream_t s);
 void launch_allgather_rows(const PeerGroup& g, const void* src, int64_t bytes, int64_t dst_off, cudaStream_t s);
+struct StridedSlice {
+  int64_t size[4] = {1, 1, 1, 1};
+  int64_t stride[4] = {0, 0, 0, 0};  // bytes
+  int esize = 2;
+};
+void launch_strided_put(const PeerGroup& g, int peer, const void* src, const StridedSlice& sl, int64_t dst_off,
+                        cudaStream_t s);
 
 }  // namespace ds

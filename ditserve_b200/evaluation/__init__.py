@@ -1,0 +1,98 @@
+"""Quality metrics, dataset splits and telemetry parsers.
+
+* ``psnr``, ``ssim`` (Gaussian-window SSIM, Wang et al. 2004) on [-1, 1] or [0, 1] video/image
+  tensors; ``drift`` = cosine + relative L2 (the cross-parallelism gate: cos >= 0.95, relL2 <= 0.25).
+* ``lpips`` needs pretrained AlexNet/VGG weights, which are not available offline; the function
+  takes a feature network and raises a clear error without one.
+* ``hash_bucket_split`` — deterministic train/val/test assignment by SHA-256 of an item id.
+* ``kineto_summary`` — aggregate GPU kernel time by name from a torch.profiler chrome trace.
+Reference: workers/ditserve/evaluation/{quality.py:39-125, artifacts.py:186-345, datasets.py,
+cuda_profile.py}.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import math
+from collections import defaultdict
+
+import torch
+import torch.nn.functional as F
+
+
+def _unit(x: torch.Tensor, value_range) -> torch.Tensor:
+    lo, hi = value_range
+    return (x.float() - lo) / (hi - lo)
+
+
+def psnr(a: torch.Tensor, b: torch.Tensor, value_range=(-1.0, 1.0)) -> float:
+    mse = F.mse_loss(_unit(a, value_range), _unit(b, value_range)).item()
+    return float("inf") if mse == 0 else 10.0 * math.log10(1.0 / mse)
+
+
+def _gauss(size=11, sigma=1.5, device=None):
+    x = torch.arange(size, dtype=torch.float32, device=device) - size // 2
+    g = torch.exp(-x ** 2 / (2 * sigma ** 2))
+    g = g / g.sum()
+    return g[:, None] * g[None, :]
+
+
+def ssim(a: torch.Tensor, b: torch.Tensor, value_range=(-1.0, 1.0)) -> float:
+    """Mean SSIM over frames/channels; inputs [..., H, W] (video [B, C, T, H, W] allowed)."""
+    x = _unit(a, value_range).reshape(-1, 1, *a.shape[-2:])
+    y = _unit(b, value_range).reshape(-1, 1, *b.shape[-2:])
+    w = _gauss(device=x.device)[None, None]
+    pad = w.shape[-1] // 2
+    mu_x, mu_y = F.conv2d(x, w, padding=pad), F.conv2d(y, w, padding=pad)
+    sxx = F.conv2d(x * x, w, padding=pad) - mu_x ** 2
+    syy = F.conv2d(y * y, w, padding=pad) - mu_y ** 2
+    sxy = F.conv2d(x * y, w, padding=pad) - mu_x * mu_y
+    c1, c2 = 0.01 ** 2, 0.03 ** 2
+    s = ((2 * mu_x * mu_y + c1) * (2 * sxy + c2)) / ((mu_x ** 2 + mu_y ** 2 + c1) * (sxx + syy + c2))
+    return s.mean().item()
+
+
+def drift(a: torch.Tensor, b: torch.Tensor) -> dict:
+    x, y = a.double().flatten(), b.double().flatten()
+    cos = (x @ y / (x.norm() * y.norm()).clamp_min(1e-300)).item()
+    rel = ((x - y).norm() / y.norm().clamp_min(1e-300)).item()
+    return dict(cos=cos, rel_l2=rel, passes=cos >= 0.95 and rel <= 0.25)
+
+
+def lpips(a, b, feature_net=None):
+    if feature_net is None:
+        raise RuntimeError("LPIPS needs pretrained AlexNet/VGG features, which are not available offline")
+    fa, fb = feature_net(a), feature_net(b)
+    return sum(((F.normalize(x, dim=1) - F.normalize(y, dim=1)) ** 2).mean().item() for x, y in zip(fa, fb))
+
+
+def hash_bucket_split(ids, fractions=(("train", 0.8), ("val", 0.1), ("test", 0.1)), salt: str = "ditserve"):
+    total = sum(f for _, f in fractions)
+    out = defaultdict(list)
+    for i in ids:
+        h = int(hashlib.sha256(f"{salt}:{i}".encode()).hexdigest()[:15], 16) / float(1 << 60)
+        acc = 0.0
+        for name, f in fractions:
+            acc += f / total
+            if h < acc:
+                out[name].append(i)
+                break
+        else:
+            out[fractions[-1][0]].append(i)
+    return dict(out)
+
+
+def kineto_summary(trace_path: str, top: int = 20) -> list:
+    """[{name, calls, total_us, share}] of GPU kernels in a chrome trace (torch.profiler export)."""
+    data = json.load(open(trace_path))
+    events = data["traceEvents"] if isinstance(data, dict) else data
+    agg = defaultdict(lambda: [0, 0.0])
+    for ev in events:
+        if ev.get("ph") == "X" and ev.get("cat") in ("kernel", "gpu_memcpy", "gpu_memset"):
+            a = agg[ev["name"]]
+            a[0] += 1
+            a[1] += float(ev.get("dur", 0.0))
+    tot = sum(v[1] for v in agg.values()) or 1.0
+    rows = [dict(name=k, calls=v[0], total_us=round(v[1], 2), share=round(v[1] / tot, 4)) for k, v in agg.items()]
+    rows.sort(key=lambda r: -r["total_us"])
+    return rows[:top]

@@ -22,7 +22,7 @@ from .runtime import WanEngine, WanSpec
 
 class WanBackend(Backend):
     operations = Backend.operations + ("snapshot", "restore", "block_export", "block_import", "encode_start",
-                                       "encode_poll", "distributed", "inventory")
+                                       "encode_poll", "distributed", "inventory", "decode_start", "decode_poll")
 
     def __init__(self, config):
         super().__init__(config)
@@ -37,6 +37,43 @@ class WanBackend(Backend):
         self.tickets: dict = {}
         self.transfer_dir = Path(config.get("transfer_dir", "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"))
         self.layout = None
+        self._decoder = None
+        self.decodes: dict = {}
+
+    def _async_decoder(self):
+        if self._decoder is None:
+            from .async_decode import AsyncDecoder
+            from .vae import WanVAEDecoder
+            dtype = torch.bfloat16 if self.device.type == "cuda" else torch.float32
+            vae = WanVAEDecoder.random_init(device=self.device, dtype=dtype, seed=int(self.config.get("seed", 0)))
+            self._decoder = AsyncDecoder(vae, self.device)
+        return self._decoder
+
+    def decode_start(self, request):
+        """Decode a finished request's latent on the side stream (VAE, Wan2.1 layout)."""
+        st = self.state(request)
+        if not st.done:
+            raise ValueError("decode requires a completed state")
+        if self.engine.cfg.in_channels != 16:
+            raise ValueError("this backend's VAE decodes 16-channel (Wan2.1) latents")
+        dec = self._async_decoder()
+        ticket = dec.start(st.latents, chunked=bool(request.get("chunked", False)))
+        self.decodes[ticket] = request["state_id"]
+        return dict(ticket=ticket, ready=False, state_id=request["state_id"])
+
+    def decode_poll(self, request):
+        ticket = request["ticket"]
+        if ticket not in self.decodes:
+            raise ValueError("unknown decode ticket")
+        dec = self._async_decoder()
+        if "chunked" in dec.jobs.get(ticket, {}) and "out" not in dec.jobs[ticket]:
+            dec.advance(ticket, int(request.get("frames", 1)))
+        if not dec.poll(ticket) and not request.get("wait"):
+            return dict(ticket=ticket, ready=False)
+        video = dec.result(ticket)
+        sid = self.decodes.pop(ticket)
+        art = self.persist(video.float(), dict(request, state_id=sid))
+        return dict(ticket=ticket, ready=True, state_id=sid, artifact=art, shape=list(video.shape))
 
     def capabilities(self):
         return dict(quanta=["step", "blocks"], blocks_per_step=self.engine.cfg.layers, migration=True,

@@ -440,6 +440,24 @@ void strided_put(const at::Tensor& src, int64_t peer, int64_t dst_off, int64_t r
                          at::cuda::getCurrentCUDAStream());
 }
 
+void group_flag(int64_t rank, const std::vector<int64_t>& bases, int64_t timeout_ns, int64_t channel, int64_t epoch,
+                int64_t flag, const at::Tensor& out, const at::Tensor& status) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kInt && out.numel() >= 1, "group_flag: int32 CUDA output");
+  const c10::cuda::CUDAGuard guard(out.device());
+  ds::launch_group_flag(make_group(rank, bases, timeout_ns), static_cast<int>(channel), static_cast<uint64_t>(epoch),
+                        static_cast<int>(flag), out.data_ptr<int>(), status_ptr(status),
+                        at::cuda::getCurrentCUDAStream());
+}
+
+void put_peers(const at::Tensor& src, int64_t mask, int64_t dst_off, int64_t rank, const std::vector<int64_t>& bases,
+               int64_t timeout_ns) {
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous(), "put_peers: contiguous CUDA source");
+  const c10::cuda::CUDAGuard guard(src.device());
+  ds::launch_put_peers(make_group(rank, bases, timeout_ns), static_cast<unsigned>(mask), src.data_ptr(),
+                       static_cast<int64_t>(src.numel() * src.element_size()), dst_off,
+                       at::cuda::getCurrentCUDAStream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -459,6 +477,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_scatter", &attention_scatter, "attention with the head->sequence all-to-all in its epilogue");
   m.def("allgather_rows", &allgather_rows, "sequence all-gather by peer stores");
   m.def("strided_put", &strided_put, "strided slice -> contiguous buffer of a group member (halo exchange)");
+  m.def("group_flag", &group_flag, "doorbell flag MAX over a peer group (one launch, bounded waits)");
+  m.def("put_peers", &put_peers, "copy a buffer into several group members' heaps");
   m.attr("FLAG_BYTES") = ds::kFlagBytes;
   m.attr("MAX_PEERS") = ds::kMaxPeers;
   m.attr("CHANNELS") = ds::kChannels;

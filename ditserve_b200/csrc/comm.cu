@@ -23,6 +23,12 @@
 //                        stores every head group directly into the owning rank's receive
 //                        buffer (reference: usp.py:207-270 + transformer_wan.py:158-191).
 //  * allgather_rows      sequence all-gather by peer stores (SP output gather, usp K12).
+//  * group_flag          doorbell stop flag MAX over an SP group in one launch: the flag
+//                        rides in the low bit of the barrier epoch (reference: all_reduce MAX
+//                        of an int, workers/ditserve/models/xdit/wan.py:257-271).
+//  * put_peers           16-byte vector copy of one buffer into several members' heaps
+//                        (regroup state broadcast; reference: host-staged packet file +
+//                        block_import, study.cpp:1395-1411, parallel.py:903-1050).
 // The inverse (head->sequence) all-to-all is fused into the attention epilogue
 // (attention.cu, peer-store mode).
 #include "sm100.cuh"
@@ -274,7 +280,61 @@ __global__ void __launch_bounds__(256) strided_put_kernel(PeerGroup g, int peer,
   }
 }
 
+// Lane p signals peer p with 2*epoch + flag and waits for 2*epoch from every peer; the
+// OR of the low bits is the group's MAX of a 0/1 flag.  Callers alternate between two
+// channels by epoch parity: a peer can reach epoch+2 on this channel only after this
+// rank signalled epoch+1 on the other one, i.e. after it has read this epoch's value.
+__global__ void group_flag_kernel(PeerGroup g, int channel, uint64_t epoch, int flag, int* out, int* status) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t mine_v = 2 * epoch + (flag ? 1u : 0u);
+  __threadfence_system();
+  if (lane < g.size && lane != g.rank) st_release_sys(g.flags[lane] + channel * kMaxPeers + g.rank, mine_v);
+  __syncwarp();
+  bool ok = true;
+  int f = (lane == g.rank) ? (flag ? 1 : 0) : 0;
+  if (lane < g.size && lane != g.rank) {
+    const uint64_t* slot = g.flags[g.rank] + channel * kMaxPeers + lane;
+    ok = wait_flag(slot, 2 * epoch, g.timeout_ns, status, 340 + channel);
+    if (ok) f = static_cast<int>(ld_acquire_sys(slot) & 1u);
+  }
+  const bool all_ok = __all_sync(0xffffffffu, ok);
+  const int any = __any_sync(0xffffffffu, f != 0);
+  if (lane == 0) *out = all_ok ? any : -1;
+}
+
+__global__ void __launch_bounds__(256) put_peers_kernel(PeerGroup g, unsigned mask, const uint4* src, int64_t n16,
+                                                        int64_t dst_off) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n16;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint4 v = src[i];
+#pragma unroll 1
+    for (int p = 0; p < g.size; ++p) {
+      if (!((mask >> p) & 1u)) continue;
+      reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(g.base[p]) + dst_off)[i] = v;
+    }
+  }
+}
+
 }  // namespace
+
+void launch_group_flag(const PeerGroup& g, int channel, uint64_t epoch, int flag, int* out, int* status,
+                       cudaStream_t s) {
+  if (g.size < 1 || g.size > kMaxPeers || channel < 0 || channel >= kChannels) throw std::runtime_error("bad group");
+  group_flag_kernel<<<1, 32, 0, s>>>(g, channel, epoch, flag, out, status);
+}
+
+void launch_put_peers(const PeerGroup& g, unsigned mask, const void* src, int64_t bytes, int64_t dst_off,
+                      cudaStream_t s) {
+  if (bytes % 16 != 0 || dst_off % 16 != 0 || reinterpret_cast<uintptr_t>(src) % 16 != 0)
+    throw std::runtime_error("put_peers: 16-byte aligned source, size and offset required");
+  if (mask >> g.size) throw std::runtime_error("put_peers: mask names ranks outside the group");
+  const int64_t n16 = bytes / 16;
+  if (n16 == 0 || mask == 0) return;
+  int64_t blocks = (n16 + 255) / 256;
+  if (blocks > 148 * 4) blocks = 148 * 4;
+  put_peers_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(g, mask, reinterpret_cast<const uint4*>(src), n16,
+                                                            dst_off);
+}
 
 void launch_strided_put(const PeerGroup& g, int peer, const void* src, const StridedSlice& sl, int64_t dst_off,
                         cudaStream_t s) {

@@ -183,5 +183,11 @@ struct StridedSlice {
 };
 void launch_strided_put(const PeerGroup& g, int peer, const void* src, const StridedSlice& sl, int64_t dst_off,
                         cudaStream_t s);
+// MAX of a 0/1 flag over the group (out: 0/1, or -1 after a peer timeout).
+void launch_group_flag(const PeerGroup& g, int channel, uint64_t epoch, int flag, int* out, int* status,
+                       cudaStream_t s);
+// Copy `bytes` (16-byte multiple) from src to offset dst_off of every member in `mask`.
+void launch_put_peers(const PeerGroup& g, unsigned mask, const void* src, int64_t bytes, int64_t dst_off,
+                      cudaStream_t s);
 
 }  // namespace ds

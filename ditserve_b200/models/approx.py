@@ -10,7 +10,9 @@
   the first ``front`` and last ``back`` blocks; if the front residual moved less than
   ``threshold`` (relative L1) since it was last computed, skip the middle blocks and add
   the cached middle residual, extrapolated to first order (Taylor) from its last two values.
-  Works for the Wan block stack and (``sd35_step``) the SD3.5 joint blocks.
+  Works for the Wan block stack (``run_wan``) and the SD3.5 joint blocks
+  (``SD35Transformer.forward_packed(..., cache=...)`` through ``run_blocks``; the cache is
+  reset whenever the packed batch's composition changes).
 * ``int8 ring codec`` — per-token, per-head symmetric INT8 with an fp16 scale for KV
   packets exchanged between ring ranks (128 bf16 = 256 B -> 128 B + 2 B).
 Reference: workers/ditserve/models/wan/cfg_reuse.py:19-411, taylor_cache.py:27-179,
@@ -87,6 +89,27 @@ class BlockResidualCache:
             self.reused = 0
         else:
             self.reused += 1
+
+    def run_blocks(self, block_fn, x: torch.Tensor, key=None) -> torch.Tensor:
+        """Generic block stack: ``block_fn(i, x) -> x`` for i < layers, with middle reuse."""
+        if key is not None and key != getattr(self, "_key", None):
+            self.front_res, self.mid_res, self.reused, self._key = None, [], 0, key
+        x_in = x.clone()  # block_fn may update x in place
+        for i in range(self.front):
+            x = block_fn(i, x)
+        front_residual = x.float() - x_in.float()
+        if self.should_skip(front_residual):
+            x.copy_((x.float() + self.predicted_middle()).to(x.dtype))
+            self.skipped_blocks += len(self.middle())
+            self.record(front_residual, None)
+        else:
+            x_mid = x.clone()
+            for i in self.middle():
+                x = block_fn(i, x)
+            self.record(front_residual, x.float() - x_mid.float())
+        for i in range(self.layers - self.back, self.layers):
+            x = block_fn(i, x)
+        return x
 
     def run_wan(self, model, pk, pctx=None):
         """One Wan forward over the block stack with middle-block reuse (packet updated)."""

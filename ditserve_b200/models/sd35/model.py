@@ -215,11 +215,12 @@ class SD35Transformer(nn.Module):
 
     # ------------------------------------------------------------------ packed forward
     @torch.inference_mode()
-    def forward_packed(self, latents: list, timesteps: list, contexts: list, pooled: list) -> list:
+    def forward_packed(self, latents: list, timesteps: list, contexts: list, pooled: list, cache=None) -> list:
         """One denoising forward of R segments of possibly different resolutions.
 
         latents[i] [C, H_i, W_i], timesteps[i] float, contexts[i] [L_i, joint_dim], pooled[i] [pooled_dim].
-        Returns the velocity predictions [C, H_i, W_i] (model dtype).
+        Returns the velocity predictions [C, H_i, W_i] (model dtype).  ``cache`` (an
+        approximate-mode ``BlockResidualCache``) reuses the middle blocks' residual.
         """
         cfg = self.cfg
         dev = self.proj_out.weight.device
@@ -259,8 +260,13 @@ class SD35Transformer(nn.Module):
         cond = temb.float() + te.text_embedder.linear_2(torch.nn.functional.silu(h.float()).to(dtype)).float()
         cond_act = torch.nn.functional.silu(cond).to(dtype)  # [R, d]
         row_img, row_txt = row_seg[:Ti], row_seg[Ti:]
-        for blk in self.transformer_blocks:
-            x = self._block(blk, x, cond_act, Ti, Tt, row_img, row_txt, joint_tbl, img_tbl)
+        blocks = self.transformer_blocks
+        if cache is None:
+            for blk in blocks:
+                x = self._block(blk, x, cond_act, Ti, Tt, row_img, row_txt, joint_tbl, img_tbl)
+        else:
+            x = cache.run_blocks(lambda i, h: self._block(blocks[i], h, cond_act, Ti, Tt, row_img, row_txt, joint_tbl,
+                                                          img_tbl), x, key=(tuple(img_len), tuple(txt_len)))
         # final adaLN-continuous (scale first, then shift) + projection, image rows only
         emb = self.norm_out.linear(cond_act).float()
         scale, shift = emb[:, :d], emb[:, d:]

@@ -3,8 +3,10 @@
 ops: hello, prepare, advance (steps | blocks | quantum="step", doorbell, check_blocks),
 finish, release, snapshot (hot: pinned host copy), restore, block_export / block_import
 (continuation packets through a transfer directory, SHA-256 checked), encode_start /
-encode_poll (encoder tickets; synthetic UMT5 embeddings offline), distributed (init an
-NCCL world and adopt a CFG x SP layout at a step boundary).
+encode_poll (encoder tickets; synthetic UMT5 embeddings offline), decode_start / decode_poll
+(VAE decode on a side stream, optionally chunked), advance_pair (lockstep pair quantum),
+distributed (init an NCCL world; adopt a CFG x SP layout at a step boundary; group
+consensus; regroup state broadcast over peer memory or NCCL; shutdown).
 Reference: workers/ditserve/models/wan/backend.py:12-652.
 """
 from __future__ import annotations
@@ -22,7 +24,8 @@ from .runtime import WanEngine, WanSpec
 
 class WanBackend(Backend):
     operations = Backend.operations + ("snapshot", "restore", "block_export", "block_import", "encode_start",
-                                       "encode_poll", "distributed", "inventory", "decode_start", "decode_poll")
+                                       "encode_poll", "distributed", "inventory", "decode_start", "decode_poll",
+                                       "advance_pair")
 
     def __init__(self, config):
         super().__init__(config)
@@ -39,6 +42,17 @@ class WanBackend(Backend):
         self.layout = None
         self._decoder = None
         self.decodes: dict = {}
+        self._comm: dict = {}
+        self.group_flag = None
+
+    def _group(self, request):
+        """Process group over request['ranks'] (created collectively once per rank set)."""
+        import torch.distributed as dist
+        ranks = tuple(int(r) for r in request.get("ranks", range(dist.get_world_size())))
+        key = ("group", ranks)
+        if key not in self._comm:
+            self._comm[key] = None if len(ranks) == dist.get_world_size() else dist.new_group(list(ranks))
+        return self._comm[key]
 
     def _async_decoder(self):
         if self._decoder is None:
@@ -102,12 +116,14 @@ class WanBackend(Backend):
         t0 = time.perf_counter()
         if request.get("quantum") == "step" or "blocks" in request:
             res = self.engine.advance(st, None if request.get("quantum") == "step" else int(request["blocks"]),
-                                      bell=bell, check_every=int(request.get("check_blocks", 1)), timing=True)
+                                      bell=bell, check_every=int(request.get("check_blocks", 1)), timing=True,
+                                      group_flag=self.group_flag)
         else:
             n = int(request.get("steps", 1))
             res = {}
             for _ in range(min(n, st.spec.steps - st.step)):
-                res = self.engine.advance(st, bell=bell, check_every=int(request.get("check_blocks", 1)))
+                res = self.engine.advance(st, bell=bell, check_every=int(request.get("check_blocks", 1)),
+                                          group_flag=self.group_flag)
                 if res.get("doorbell_stop"):
                     break
         if st.latents.is_cuda:
@@ -115,6 +131,24 @@ class WanBackend(Backend):
         res["model_ms"] = (time.perf_counter() - t0) * 1000
         res["progress"] = self._progress(st)
         res["state_id"] = request["state_id"]
+        return res
+
+    def advance_pair(self, request):
+        """Lockstep pair quantum: ``state_ids`` [a, b], up to ``blocks`` block pairs."""
+        from ...runtime.doorbell import rung
+        ida, idb = request["state_ids"]
+        if ida == idb:
+            raise ValueError("a pair needs two distinct states")
+        a, b = self.state(dict(state_id=ida)), self.state(dict(state_id=idb))
+        t0 = time.perf_counter()
+        blocks = request.get("blocks")
+        res = self.engine.advance_pair(a, b, None if blocks is None else int(blocks), bell=rung(request),
+                                       check_every=int(request.get("check_blocks", 1)), group_flag=self.group_flag)
+        if a.latents.is_cuda:
+            torch.cuda.synchronize(a.latents.device)
+        res["model_ms"] = (time.perf_counter() - t0) * 1000
+        res["a"].update(state_id=ida, progress=self._progress(a))
+        res["b"].update(state_id=idb, progress=self._progress(b))
         return res
 
     def finish(self, request):
@@ -198,7 +232,53 @@ class WanBackend(Backend):
                                         pred_numel=lat[0] * lat[1] * lat[2] * lat[3])
             self.engine.pctx, self.engine.cfg_plan = pctx, plan
             self.layout = layout
+            self.group_flag = None
+            if form.sp > 1:  # doorbell stop agreed over the SP group (MAX of the ranks' flags)
+                from ...parallel.elastic import GroupFlagNCCL, GroupFlagPeer
+                sp_ranks = layout.sp_ranks(dist.get_rank())
+                g = dist.new_group(list(sp_ranks), use_local_synchronization=True)
+                if request.get("path", "fused") == "fused" and self.device.type == "cuda":
+                    from ...parallel.symm import SymmetricHeap
+                    heap = SymmetricHeap(1 << 20, self.device, group=g)
+                    self.group_flag = GroupFlagPeer(heap, tuple(range(len(sp_ranks))))
+                else:
+                    self.group_flag = GroupFlagNCCL(g, self.device)
             return dict(form=form.name, ranks=list(layout.ranks), epoch=layout.epoch)
+        if action == "consensus":
+            from ...parallel.elastic import RequestGroupGate, state_digest
+            group = self._group(request)
+            sid = request["state_id"]
+            st = self.states[sid]
+            agreed = RequestGroupGate(group).consensus(state_digest(sid, st, int(request.get("epoch", 0))))
+            return dict(state_id=sid, agreed=agreed, step=st.step, block=st.block)
+        if action == "migrate_group":
+            # regroup: the source rank's state reaches every rank of the new group, bit-exact
+            from ...parallel.elastic import PeerStateBroadcast, broadcast_state_nccl
+            ranks = tuple(int(r) for r in request["ranks"])
+            src = int(request["src"])
+            sid = request["state_id"]
+            me = dist.get_rank()
+            tree = None
+            if me == src:
+                st = self.states[sid]
+                if st.block != 0:
+                    raise ValueError("regroup only at a solver-step boundary")
+                tree = self.engine.snapshot(st, device=self.device)
+            group = self._group(request)
+            if request.get("path", "fused") == "fused" and self.device.type == "cuda":
+                key = ("bcast", ranks)
+                if key not in self._comm:
+                    from ...parallel.symm import SymmetricHeap
+                    cap = int(request.get("capacity_mb", 256)) << 20
+                    heap = SymmetricHeap(cap + (1 << 20), self.device, group=group)
+                    self._comm[key] = PeerStateBroadcast(heap, tuple(range(len(ranks))), cap, group=group)
+                tree = self._comm[key](tree, ranks.index(src), src)
+            else:
+                tree = broadcast_state_nccl(tree, src, group=group, device=self.device)
+            if me != src:
+                self.states[sid] = self.engine.restore(tree)
+            st = self.states[sid]
+            return dict(state_id=sid, step=st.step, ranks=list(ranks))
         if action == "shutdown":
             if dist.is_initialized():
                 dist.destroy_process_group()

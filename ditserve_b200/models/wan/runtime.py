@@ -261,6 +261,46 @@ class WanEngine:
             out["block_cuda_ms"] = t0.elapsed_time(t1)
         return out
 
+    @torch.inference_mode()
+    def advance_pair(self, a: WanRequestState, b: WanRequestState, blocks: int | None = None, *, bell=None,
+                     check_every: int = 1, group_flag=None) -> dict:
+        """Lockstep interleave of two requests on one group: block i of ``a``, then block i of
+        ``b``, for up to ``blocks`` block pairs, stopping at either request's step boundary or
+        at the doorbell (checked every ``check_every`` pairs, group-agreed via ``group_flag``).
+        One quantum advances both requests, which is what the planner prices as a pair.
+        Reference: advance_pair, workers/ditserve/models/wan/block.py:695-810.
+        """
+        for st in (a, b):
+            if st.done:
+                raise RuntimeError("request already finished")
+            if not st.packets:
+                self._begin(st)
+        L = self.cfg.layers
+        want = min(L - a.block, L - b.block) if blocks is None else min(int(blocks), L - a.block, L - b.block)
+        done, stopped = 0, False
+        while done < want:
+            for _ in range(min(max(1, check_every), want - done)):
+                for st in (a, b):
+                    self.model.forward_block(st.block, st.packets["pk"], self.pctx)
+                    st.block += 1
+                done += 1
+            if bell is None or done >= want:
+                continue
+            flag = 1 if bell() else 0
+            if group_flag is not None:
+                flag = group_flag(flag)
+            if flag:
+                stopped = True
+                break
+        out = {}
+        for key, st in (("a", a), ("b", b)):
+            completed = st.block >= L
+            if completed:
+                self._finish_step(st)
+            out[key] = dict(next_block=st.block, step_completed=completed, step=st.step, steps=st.spec.steps)
+        out.update(blocks=done, doorbell_stop=stopped)
+        return out
+
     def step(self, st: WanRequestState) -> WanRequestState:
         if st.done:
             raise RuntimeError("request already finished")

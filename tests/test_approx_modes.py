@@ -61,3 +61,26 @@ def test_int8_ring_codec():
     y = dequantize_int8(q, s, 128)
     assert _cos(x.float(), y.float()) > 0.999
     assert packet_bytes(1, 1, 128, True) == 130 and packet_bytes(1, 1, 128, False) == 256
+
+
+def test_sd35_block_cache_reuse():
+    import torch
+    from ditserve_b200.models.approx import BlockResidualCache
+    from ditserve_b200.models.sd35.model import SD35_TINY, SD35Transformer
+    m = SD35Transformer.random_init(SD35_TINY, device="cpu", dtype=torch.float32, seed=0)
+    m.prepare()
+    g = torch.Generator().manual_seed(0)
+    lat = [torch.randn(SD35_TINY.in_channels, 32, 32, generator=g)]
+    ctx = [torch.randn(8, SD35_TINY.joint_dim, generator=g)]
+    pooled = [torch.randn(SD35_TINY.pooled_dim, generator=g)]
+    layers = SD35_TINY.layers
+    if layers < 3:
+        import pytest
+        pytest.skip("tiny config has too few blocks for a middle range")
+    cache = BlockResidualCache(layers, front=1, back=1, threshold=1.0, max_reuse=2)
+    exact = m.forward_packed(lat, [500.0], ctx, pooled)[0]
+    first = m.forward_packed(lat, [500.0], ctx, pooled, cache=cache)[0]
+    assert torch.allclose(first, exact, atol=1e-5)  # nothing cached yet: exact
+    again = m.forward_packed(lat, [499.0], ctx, pooled, cache=cache)[0]
+    assert cache.skipped_blocks == layers - 2
+    assert torch.isfinite(again).all()

@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdio>
 #include <fstream>
+#include <functional>
 #include <future>
 #include <map>
 #include <memory>
@@ -97,8 +98,13 @@ std::unique_ptr<Worker> spawn_worker(const Json& def, const StudyOptions& opt, c
                                    (def.get("config").is_null() ? Json::object() : def.at("config")).dump()};
   std::map<std::string, std::string> env;
   if (!opt.package_root.empty()) env["PYTHONPATH"] = opt.package_root;
-  if (!gpu.empty()) env["CUDA_VISIBLE_DEVICES"] = gpu;
-  else if (!gpu_backend) env["CUDA_VISIBLE_DEVICES"] = "";
+  if (gpu == "all") {
+    // every GPU visible (world members address their peers' memory); device chosen in config
+  } else if (!gpu.empty()) {
+    env["CUDA_VISIBLE_DEVICES"] = gpu;
+  } else if (!gpu_backend) {
+    env["CUDA_VISIBLE_DEVICES"] = "";
+  }
   auto w = std::make_unique<Worker>();
   w->name = backend;
   w->proc = std::make_unique<WorkerProcess>(argv, env, log);
@@ -200,43 +206,125 @@ Json run_online(const Json& phase, Worker& w) {
 }
 
 // ---------------------------------------------------------------------------------------
-// multi-GPU executor: one worker per GPU slot; cluster_plan at every event
+// Multi-GPU cluster executor.  Each GPU slot has a video worker and (optionally) an image
+// worker.  With `distributed: true` the video workers form one torch.distributed world
+// (NCCL on GPUs) and every member of a request's group runs the quantum under the
+// assigned CFG x SP layout; otherwise the group's leader runs it alone.  A request's state
+// is tracked per worker: `fresh` copies are current, `stale` ones are outdated and get
+// released.  When a group gains members the state reaches them by `sp_transport`:
+// "collective" (a regroup broadcast over the new group: peer-memory put kernels or NCCL)
+// or "export" (host-staged continuation packets).  A request inside a solver step keeps
+// its group and form until the step ends.  Reference: study.cpp:781-2206 (cluster()).
 struct Live {
   std::string id, kind, klass, status = "future";
   Json row;
   int steps_total = 1, steps_done = 0, blocks_done = 0;
   std::vector<int> group, last_group;
-  std::string form;
-  int owner = -1;  // GPU whose worker holds the state
+  std::string form, last_form;
+  std::set<int> fresh, stale;
   bool prepared = false;
   double quantum_started = 0;
   bool rung = false;
 };
+
+Json ints_json(const std::vector<int>& v) {
+  Json a = Json::array();
+  for (int x : v) a.push_back(x);
+  return a;
+}
+
+// run fn(g) for every g in gs concurrently (one thread per extra member); rethrows the first error
+std::vector<Json> fan_out(const std::vector<int>& gs, const std::function<Json(int)>& fn) {
+  std::vector<std::future<Json>> fs;
+  for (size_t i = 1; i < gs.size(); ++i) fs.push_back(std::async(std::launch::async, fn, gs[i]));
+  std::vector<Json> out;
+  std::exception_ptr err;
+  try {
+    out.push_back(fn(gs[0]));
+  } catch (...) {
+    err = std::current_exception();
+  }
+  for (auto& f : fs) {
+    try {
+      out.push_back(f.get());
+    } catch (...) {
+      if (!err) err = std::current_exception();
+    }
+  }
+  if (err) std::rethrow_exception(err);
+  return out;
+}
 
 Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& run_dir, const Json& workers_def) {
   const int gpus = static_cast<int>(phase.integer("gpus", 8));
   const std::string policy = phase.str("policy", "ditserve");
   const Json options = phase.get("options").is_null() ? Json::object() : phase.at("options");
   const ClusterCost cost(phase.get("profile").is_null() ? synthetic_profile() : phase.at("profile"));
-  const Json& wdef = workers_def.at(phase.str("worker", "model"));
-  const bool gpu_backend = wdef.at("backend").as_string() != "mock";
-  std::vector<std::unique_ptr<Worker>> workers;
-  for (int gidx = 0; gidx < gpus; ++gidx)
-    workers.push_back(spawn_worker(wdef, opt, run_dir + "/worker" + std::to_string(gidx) + ".log",
-                                   gpu_backend ? std::to_string(gidx) : ""));
+  std::string vname = phase.str("worker", "model"), iname = vname;
+  if (phase.contains("workers")) {
+    vname = phase.at("workers").str("video", vname);
+    iname = phase.at("workers").str("image", vname);
+  }
+  const Json& vdef = workers_def.at(vname);
+  const Json& idef = workers_def.at(iname);
+  const bool distributed = phase.flag("distributed", false);
+  const std::string transport = phase.str("sp_transport", distributed ? "collective" : "export");
+  if (transport != "collective" && transport != "export")
+    throw std::invalid_argument("sp_transport must be collective or export");
+  if (transport == "collective" && !distributed)
+    throw std::invalid_argument("sp_transport collective needs distributed: true");
+  const std::string path = phase.str("collectives", "fused");
+  const int batch_quantum = static_cast<int>(phase.integer("batch_quantum_steps", 4));
+  const size_t trace_limit = static_cast<size_t>(phase.integer("trace_limit", 2000));
+  auto is_gpu = [](const Json& d) { return d.at("backend").as_string() != "mock"; };
+
+  auto spawn = [&](const Json& def, const std::string& tag, int gidx, bool world_member) {
+    Json d = def;
+    const bool gpu = is_gpu(def);
+    std::string visible = gpu ? std::to_string(gidx) : "";
+    Json c = d.get("config").is_null() ? Json::object() : d.at("config");
+    if (world_member && gpu && !c.contains("device")) {  // peers' memory must be visible (IPC / NVLink)
+      c["device"] = "cuda:" + std::to_string(gidx);
+      d["config"] = c;
+      visible = "all";
+    }
+    return spawn_worker(d, opt, run_dir + "/" + tag + std::to_string(gidx) + ".log", visible);
+  };
+  std::vector<std::unique_ptr<Worker>> vworkers, iworkers;
+  for (int g = 0; g < gpus; ++g) {
+    vworkers.push_back(spawn(vdef, "video", g, distributed));
+    if (iname != vname) iworkers.push_back(spawn(idef, "image", g, false));
+  }
+  auto W = [&](int g, bool image) -> Worker* {
+    return (image && !iworkers.empty()) ? iworkers[g].get() : vworkers[g].get();
+  };
+  if (distributed) {
+    const std::string init = "tcp://127.0.0.1:" + std::to_string(phase.integer("dist_port", 29700));
+    std::vector<int> all;
+    for (int g = 0; g < gpus; ++g) all.push_back(g);
+    fan_out(all, [&](int g) {
+      Json r = Json::object();
+      r["action"] = "init";
+      r["init_method"] = init;
+      r["rank"] = g;
+      r["world_size"] = gpus;
+      r["timeout_s"] = phase.num("dist_timeout_s", 120.0);
+      return vworkers[g]->call("distributed", r, 300);
+    });
+  }
   // doorbells: one 8-byte epoch file per GPU
   std::vector<std::string> bells;
   std::vector<long long> bell_epoch(gpus, 0);
-  for (int gidx = 0; gidx < gpus; ++gidx) {
-    bells.push_back(run_dir + "/doorbell" + std::to_string(gidx));
+  for (int g = 0; g < gpus; ++g) {
+    bells.push_back(run_dir + "/doorbell" + std::to_string(g));
     std::ofstream(bells.back(), std::ios::binary).write("\0\0\0\0\0\0\0\0", 8);
   }
-  auto ring = [&](int gidx) {
-    ++bell_epoch[gidx];
-    FILE* f = std::fopen(bells[gidx].c_str(), "r+b");
+  auto ring = [&](int g) {
+    ++bell_epoch[g];
+    FILE* f = std::fopen(bells[g].c_str(), "r+b");
     if (!f) return;
     unsigned char b[8];
-    unsigned long long v = static_cast<unsigned long long>(bell_epoch[gidx]);
+    unsigned long long v = static_cast<unsigned long long>(bell_epoch[g]);
     for (int i = 0; i < 8; ++i) b[i] = static_cast<unsigned char>((v >> (8 * i)) & 0xff);
     std::fwrite(b, 1, 8, f);
     std::fclose(f);
@@ -256,54 +344,173 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     live.push_back(l);
   }
   struct Task {
-    std::string id;
+    std::vector<std::string> ids;
     std::future<Json> fut;
     std::vector<int> group;
   };
   std::vector<Task> tasks;
   std::vector<bool> busy(gpus, false);
+  std::vector<std::vector<std::pair<std::string, bool>>> pending_release(gpus);
   const double t0 = monotonic_seconds();
-  long long plans = 0, quanta = 0, preemptions = 0, transfers = 0;
+  long long plans = 0, quanta = 0, preemptions = 0, transfers = 0, pairs = 0, batches = 0, held_mid_step = 0;
+  double plan_ms_total = 0, plan_ms_max = 0;
   size_t finished = 0;
   const double horizon = phase.num("horizon_ms", 1e12);
   Json failures = Json::array();
+  Json trace = Json::array();
+
+  // -- state placement (runs inside a task; members of `exec` are reserved for it) ----------
+  struct Placement {
+    std::string id;
+    Json spec;
+    bool image = false, prepared = false;
+    std::vector<int> exec;
+    std::set<int> fresh, stale;
+  };
+  auto ensure_state = [&, transport, path](const Placement& p) -> bool {
+    if (!p.prepared) {
+      fan_out(p.exec, [&](int g) {
+        Json pr = Json::object();
+        pr["state_id"] = p.id;
+        pr["spec"] = p.spec;
+        return W(g, p.image)->call("prepare", pr);
+      });
+      return false;
+    }
+    std::vector<int> need;
+    for (int g : p.exec)
+      if (!p.fresh.count(g)) need.push_back(g);
+    if (need.empty()) return false;
+    for (int g : need)
+      if (p.stale.count(g)) {
+        Json rel = Json::object();
+        rel["state_id"] = p.id;
+        W(g, p.image)->call("release", rel);
+      }
+    int src = -1;
+    for (int g : p.exec)
+      if (p.fresh.count(g)) {
+        src = g;
+        break;
+      }
+    auto hop = [&](int from, int to) {  // host-staged continuation packet
+      Json ex = Json::object();
+      ex["state_id"] = p.id;
+      Json pk = W(from, p.image)->call("block_export", ex);
+      Json im = pk;
+      im["state_id"] = p.id;
+      W(to, p.image)->call("block_import", im);
+    };
+    if (transport == "collective" && !p.image && p.exec.size() > 1) {
+      if (src < 0) {
+        hop(*p.fresh.begin(), p.exec.front());
+        src = p.exec.front();
+      }
+      fan_out(p.exec, [&](int g) {
+        Json r = Json::object();
+        r["action"] = "migrate_group";
+        r["ranks"] = ints_json(p.exec);
+        r["src"] = src;
+        r["state_id"] = p.id;
+        r["path"] = path;
+        return W(g, false)->call("distributed", r);
+      });
+    } else {
+      const int from = src >= 0 ? src : *p.fresh.begin();
+      for (int g : need) hop(from, g);
+    }
+    return true;
+  };
+  auto finish_release = [&](const std::string& id, const std::vector<int>& exec, bool image) {
+    Json f = Json::object();
+    f["state_id"] = id;
+    f["output_mode"] = "digest";
+    Json art = W(exec.front(), image)->call("finish", f);
+    Json rel = Json::object();
+    rel["state_id"] = id;
+    fan_out(exec, [&](int g) { return W(g, image)->call("release", rel); });
+    return art.get("value");
+  };
+  auto member = [](const std::string& id, const Json& progress, bool done, const Json& digest) {
+    Json m = Json::object();
+    m["id"] = id;
+    m["progress"] = progress;
+    m["finished"] = done;
+    if (done) m["digest"] = digest;
+    return m;
+  };
+
   while (finished < live.size()) {
     const double now = now_ms_since(t0);
     if (now > horizon) break;
-    // harvest
+    // harvest finished quanta
     for (auto it = tasks.begin(); it != tasks.end();) {
       if (it->fut.wait_for(std::chrono::milliseconds(0)) != std::future_status::ready) {
         ++it;
         continue;
       }
-      Live& l = live[idx[it->id]];
-      for (int gi : it->group) busy[gi] = false;
+      for (int g : it->group) busy[g] = false;
+      Json res;
+      std::string err;
       try {
-        Json res = it->fut.get();
-        const Json& prog = res.get("progress");
-        if (prog.is_object()) {
-          l.steps_done = static_cast<int>(prog.at("step").as_int());
-          l.blocks_done = static_cast<int>(prog.integer("block", 0));
-        }
-        if (res.flag("finished", false)) {
-          l.status = "done";
-          l.row["status"] = "done";
-          l.row["finish_ms"] = now_ms_since(t0);
+        res = it->fut.get();
+      } catch (const std::exception& e) {
+        err = e.what();
+      }
+      for (const auto& id : it->ids) {
+        Live& l = live[idx[id]];
+        const Json* m = nullptr;
+        if (err.empty())
+          for (const auto& x : res.at("members").as_array())
+            if (x.at("id").as_string() == id) m = &x;
+        if (!err.empty() || m == nullptr) {
+          l.status = "failed";
+          l.row["status"] = "failed";
+          l.row["error"] = err.empty() ? "no result for member" : err;
+          failures.push_back(l.id);
           ++finished;
         } else {
-          l.status = "suspended";
+          const Json& prog = m->get("progress");
+          if (prog.is_object()) {
+            l.steps_done = static_cast<int>(prog.integer("step", l.steps_done));
+            l.blocks_done = static_cast<int>(prog.integer("block", 0));
+          }
+          if (m->flag("finished", false)) {
+            l.status = "done";
+            l.row["status"] = "done";
+            l.row["finish_ms"] = now_ms_since(t0);
+            if (m->contains("digest")) l.row["digest"] = m->at("digest");
+            ++finished;
+          } else {
+            l.status = "suspended";
+          }
         }
-      } catch (const std::exception& e) {
-        l.status = "failed";
-        l.row["status"] = "failed";
-        l.row["error"] = e.what();
-        failures.push_back(l.id);
-        ++finished;
+        if (l.status == "done" || l.status == "failed") {
+          for (int g : l.stale) pending_release[g].push_back({l.id, l.kind == "image"});
+          if (l.status == "failed")
+            for (int g : l.fresh) pending_release[g].push_back({l.id, l.kind == "image"});
+          l.stale.clear();
+          l.fresh.clear();
+        }
+        l.last_group = l.group;
+        l.last_form = l.form;
+        l.group.clear();
+        l.rung = false;
       }
-      l.last_group = l.group;
-      l.group.clear();
-      l.rung = false;
       it = tasks.erase(it);
+    }
+    // outdated copies on idle workers
+    for (int g = 0; g < gpus; ++g) {
+      if (busy[g] || pending_release[g].empty()) continue;
+      for (const auto& pr : pending_release[g]) {
+        Json rel = Json::object();
+        rel["state_id"] = pr.first;
+        try {
+          W(g, pr.second)->call("release", rel, 60);
+        } catch (const std::exception&) {
+        }
+      }
+      pending_release[g].clear();
     }
     for (auto& l : live)
       if (l.status == "future" && l.row.at("arrival_ms").as_double() <= now) l.status = "waiting";
@@ -329,9 +536,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
       q["steps_total"] = l.steps_total;
       q["steps_done"] = l.steps_done;
       q["blocks_done"] = l.blocks_done;
-      Json grp = Json::array();
-      for (int gi : (l.status == "running" ? l.group : l.last_group)) grp.push_back(gi);
-      q["group"] = grp;
+      q["group"] = ints_json(l.status == "running" ? l.group : l.last_group);
       if (!l.form.empty()) q["form"] = l.form;
       if (l.status == "running") {
         q["quantum_started_ms"] = l.quantum_started;
@@ -341,92 +546,196 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     }
     state["requests"] = reqs;
     if (waiting) {
+      const double tp = monotonic_seconds();
       Json plan = cluster_plan(state, policy, cost, options);
+      const double pms = (monotonic_seconds() - tp) * 1000.0;
+      plan_ms_total += pms;
+      plan_ms_max = std::max(plan_ms_max, pms);
       ++plans;
       for (const auto& pid : plan.at("preempt").as_array()) {
         Live& l = live[idx[pid.as_string()]];
         if (l.status == "running" && !l.rung) {
-          for (int gi : l.group) ring(gi);
+          for (int g : l.group) ring(g);
           l.rung = true;
           ++preemptions;
         }
       }
+      std::map<std::string, Json> by_id;
+      for (const auto& a : plan.at("assignments").as_array()) by_id[a.at("request_id").as_string()] = a;
+      std::set<std::string> handled;
       for (const auto& a : plan.at("assignments").as_array()) {
-        Live& l = live[idx[a.at("request_id").as_string()]];
+        const std::string rid = a.at("request_id").as_string();
+        if (handled.count(rid)) continue;
+        handled.insert(rid);
+        Live& l = live[idx[rid]];
         if (l.status != "waiting" && l.status != "suspended") continue;
         std::vector<int> grp;
         for (const auto& gi : a.at("group").as_array()) grp.push_back(static_cast<int>(gi.as_int()));
-        bool free = true;
-        for (int gi : grp) free = free && !busy[gi];
-        if (!free) continue;
-        const int leader = grp.front();
-        // exact state transfer when the request moves to another worker
-        const bool move = l.prepared && l.owner >= 0 && l.owner != leader;
-        const int from = l.owner;
-        l.status = "running";
-        l.group = grp;
-        l.form = a.at("form").as_string();
-        l.quantum_started = now;
-        if (!l.row.contains("start_ms")) l.row["start_ms"] = now;
-        for (int gi : grp) busy[gi] = true;
-        if (move) ++transfers;
-        const Json quantum = a.at("quantum");
-        const Json spec = l.row.at("spec");
-        const std::string id = l.id;
-        const bool prepared = l.prepared;
-        const long long epoch = bell_epoch[leader];
-        const std::string bell = bells[leader];
-        const int degree = static_cast<int>(grp.size());
+        std::string form = a.at("form").as_string();
         const bool image = l.kind == "image";
-        Worker* dst = workers[leader].get();
-        Worker* src = move ? workers[from].get() : nullptr;
-        l.prepared = true;
-        l.owner = leader;
+        // a request inside a solver step keeps its group and form until the step ends
+        if (!image && l.blocks_done > 0 && !l.last_group.empty() && (grp != l.last_group || form != l.last_form)) {
+          grp = l.last_group;
+          form = l.last_form;
+          ++held_mid_step;
+        }
+        bool free = true;
+        for (int g : grp) free = free && !busy[g];
+        if (!free) continue;
+        // members of this quantum: a lockstep partner, or a continuous image batch
+        std::vector<Live*> members{&l};
+        const Json quantum = a.at("quantum");
+        const std::string qs = quantum.is_string() ? quantum.as_string() : "";
+        if (a.contains("pair") && !image) {
+          const std::string pid = a.at("pair").as_string();
+          Live& o = live[idx[pid]];
+          if ((o.status == "waiting" || o.status == "suspended") && o.blocks_done == 0 && l.blocks_done == 0) {
+            members.push_back(&o);
+            handled.insert(pid);
+          }
+        }
+        if (a.contains("batch"))
+          for (const auto& x : a.at("batch").as_array()) {
+            const std::string mid = x.as_string();
+            if (mid == rid) continue;
+            Live& o = live[idx[mid]];
+            if (o.status != "waiting" && o.status != "suspended") continue;
+            members.push_back(&o);
+            handled.insert(mid);
+          }
+        const int leader = grp.front();
+        const std::vector<int> exec = (distributed && !image) ? grp : std::vector<int>{leader};
+        std::vector<Placement> places;
+        for (Live* m : members) {
+          Placement p;
+          p.id = m->id;
+          p.spec = m->row.at("spec");
+          p.image = image;
+          p.prepared = m->prepared;
+          p.exec = exec;
+          p.fresh = m->fresh;
+          p.stale = m->stale;
+          places.push_back(p);
+          bool moves = m->prepared;
+          if (moves) {
+            bool all = true;
+            for (int g : exec) all = all && m->fresh.count(g);
+            moves = !all;
+          }
+          if (moves) ++transfers;
+          for (int g : m->fresh)
+            if (std::find(exec.begin(), exec.end(), g) == exec.end()) m->stale.insert(g);
+          for (int g : exec) m->stale.erase(g);
+          m->fresh = std::set<int>(exec.begin(), exec.end());
+          m->prepared = true;
+          m->status = "running";
+          m->group = grp;
+          m->form = form;
+          m->quantum_started = now;
+          if (!m->row.contains("start_ms")) m->row["start_ms"] = now;
+        }
+        for (int g : grp) busy[g] = true;
         ++quanta;
-        tasks.push_back({id, std::async(std::launch::async, [=]() -> Json {
-                           if (src != nullptr) {
-                             Json ex = Json::object();
-                             ex["state_id"] = id;
-                             Json pk = src->call("block_export", ex);
-                             src->call("migration_release", ex);
-                             Json im = Json::object();
-                             im["state_id"] = id;
-                             im["packet"] = pk.at("packet");
-                             im["manifest"] = pk.at("manifest");
-                             dst->call("block_import", im);
-                           } else if (!prepared) {
-                             Json pr = Json::object();
-                             pr["state_id"] = id;
-                             pr["spec"] = spec;
-                             dst->call("prepare", pr);
-                           }
-                           Json adv = Json::object();
-                           adv["state_id"] = id;
-                           adv["sp_degree"] = degree;
-                           if (quantum.is_string() && quantum.as_string() == "step") adv["quantum"] = "step";
-                           else if (quantum.is_number()) adv["blocks"] = quantum;
-                           else adv["steps"] = 1000000;  // atomic image / finish: run to the end
-                           Json bellj = Json::object();
-                           bellj["path"] = bell;
-                           bellj["epoch"] = epoch;
-                           adv["doorbell"] = bellj;
-                           Json res;
-                           const bool finish_only = quantum.is_string() && quantum.as_string() == "finish";
-                           if (!finish_only) res = dst->call("advance", adv);
-                           const bool done = finish_only || image || (res.get("progress").is_object() &&
-                                                                     res.at("progress").flag("done", false));
-                           if (done) {
-                             Json f = Json::object();
-                             f["state_id"] = id;
-                             f["output_mode"] = "digest";
-                             Json art = dst->call("finish", f);
-                             dst->call("release", f);
-                             Json out = Json::object();
-                             out["finished"] = true;
-                             out["digest"] = art.get("value");
+        if (members.size() > 1) (image ? batches : pairs) += 1;
+        if (trace.size() < trace_limit) {
+          Json tr = Json::object();
+          tr["t_ms"] = now;
+          tr["request_id"] = rid;
+          tr["group"] = ints_json(grp);
+          tr["form"] = form;
+          tr["quantum"] = quantum;
+          if (members.size() > 1) {
+            Json ms = Json::array();
+            for (Live* m : members) ms.push_back(m->id);
+            tr["members"] = ms;
+          }
+          trace.push_back(tr);
+        }
+        std::vector<long long> epochs;
+        for (int g = 0; g < gpus; ++g) epochs.push_back(bell_epoch[g]);
+        std::vector<std::string> ids;
+        for (Live* m : members) ids.push_back(m->id);
+        const int degree = static_cast<int>(grp.size());
+        const bool batch = a.contains("batch") || qs == "continuous_batch";
+        tasks.push_back({ids, std::async(std::launch::async, [=, &ensure_state, &finish_release, &member, &W,
+                                                               &bells]() -> Json {
+                           for (const auto& p : places) ensure_state(p);
+                           Json out = Json::object();
+                           Json ms = Json::array();
+                           if (image) {
+                             Worker* w = W(leader, true);
+                             if (batch) {
+                               Json ab = Json::object();
+                               Json sids = Json::array();
+                               for (const auto& id : ids) sids.push_back(id);
+                               ab["state_ids"] = sids;
+                               std::map<std::string, Json> prog;
+                               for (int k = 0; k < batch_quantum; ++k) {
+                                 Json r = w->call("advance_batch", ab);
+                                 bool any = false;
+                                 for (const auto& m : r.at("members").as_array()) {
+                                   prog[m.at("state_id").as_string()] = m.at("progress");
+                                   any = any || m.at("progress").flag("done", false);
+                                 }
+                                 if (any) break;
+                               }
+                               for (const auto& id : ids) {
+                                 const bool done = prog[id].is_object() && prog[id].flag("done", false);
+                                 ms.push_back(member(id, prog[id], done, done ? finish_release(id, exec, true) : Json()));
+                               }
+                             } else {
+                               if (qs != "finish") {
+                                 Json adv = Json::object();
+                                 adv["state_id"] = ids[0];
+                                 adv["steps"] = 1000000;
+                                 w->call("advance", adv);
+                               }
+                               ms.push_back(member(ids[0], Json(), true, finish_release(ids[0], exec, true)));
+                             }
+                             out["members"] = ms;
                              return out;
                            }
-                           return res;
+                           if (qs == "finish") {
+                             ms.push_back(member(ids[0], Json(), true, finish_release(ids[0], exec, false)));
+                             out["members"] = ms;
+                             return out;
+                           }
+                           std::vector<Json> res = fan_out(exec, [&](int g) {
+                             Json adv = Json::object();
+                             adv["state_id"] = ids[0];
+                             if (ids.size() > 1) adv["pair_state_id"] = ids[1];
+                             adv["sp_degree"] = degree;
+                             adv["group"] = ints_json(grp);
+                             if (qs == "step") adv["quantum"] = "step";
+                             else if (quantum.is_number()) adv["blocks"] = quantum;
+                             else adv["quantum"] = "step";
+                             Json bell = Json::object();
+                             bell["path"] = bells[g];
+                             bell["epoch"] = epochs[g];
+                             adv["doorbell"] = bell;
+                             if (distributed) {
+                               Json lay = Json::object();
+                               lay["ranks"] = ints_json(grp);
+                               lay["form"] = form;
+                               lay["path"] = path;
+                               adv["layout"] = lay;
+                             }
+                             return W(g, false)->call("advance", adv);
+                           });
+                           for (size_t k = 1; k < res.size(); ++k) {
+                             const Json& p0 = res[0].at("progress");
+                             const Json& pk = res[k].at("progress");
+                             if (p0.integer("step", -1) != pk.integer("step", -1) ||
+                                 p0.integer("block", 0) != pk.integer("block", 0))
+                               throw std::runtime_error("SP group members diverged in progress");
+                           }
+                           for (size_t k = 0; k < ids.size(); ++k) {
+                             const Json& prog = k == 0 ? res[0].at("progress") : res[0].at("pair_progress");
+                             const bool done = prog.flag("done", false);
+                             ms.push_back(member(ids[k], prog, done, done ? finish_release(ids[k], exec, false) : Json()));
+                           }
+                           out["members"] = ms;
+                           return out;
                          }),
                          grp});
       }
@@ -440,13 +749,17 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     out_rows.push_back(l.row);
   }
   bool clean = true;
-  for (auto& w : workers) {
-    try {
-      w->proc->call("shutdown", Json::object(), 30);
-    } catch (const std::exception&) {
+  auto stop_all = [&](std::vector<std::unique_ptr<Worker>>& ws) {
+    for (auto& w : ws) {
+      try {
+        w->proc->call("shutdown", Json::object(), 30);
+      } catch (const std::exception&) {
+      }
+      clean = w->proc->stop(5.0) && clean;
     }
-    clean = w->proc->stop(2.0) && clean;
-  }
+  };
+  stop_all(iworkers);
+  stop_all(vworkers);
   Json out = Json::object();
   out["rows"] = out_rows;
   out["summary"] = request_summary(out_rows);
@@ -455,9 +768,23 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
   c["quanta"] = quanta;
   c["preemptions"] = preemptions;
   c["transfers"] = transfers;
+  c["pairs"] = pairs;
+  c["batches"] = batches;
+  c["held_mid_step"] = held_mid_step;
   c["cleanup_verified"] = clean;
   out["counters"] = c;
+  Json timing = Json::object();
+  timing["plan_ms_total"] = plan_ms_total;
+  timing["plan_ms_max"] = plan_ms_max;
+  timing["wall_ms"] = now_ms_since(t0);
+  out["controller_timing"] = timing;
+  out["trace"] = trace;
   out["failures"] = failures;
+  Json cfg = Json::object();
+  cfg["distributed"] = distributed;
+  cfg["sp_transport"] = transport;
+  cfg["collectives"] = path;
+  out["executor"] = cfg;
   return out;
 }
 

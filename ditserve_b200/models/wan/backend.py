@@ -11,6 +11,7 @@ Reference: workers/ditserve/models/wan/backend.py:12-652.
 """
 from __future__ import annotations
 
+import math
 import os
 import time
 from pathlib import Path
@@ -43,16 +44,66 @@ class WanBackend(Backend):
         self._decoder = None
         self.decodes: dict = {}
         self._comm: dict = {}
+        self._layouts: dict = {}
         self.group_flag = None
 
     def _group(self, request):
-        """Process group over request['ranks'] (created collectively once per rank set)."""
+        """Process group over request['ranks'] (member-local creation, cached per rank set)."""
         import torch.distributed as dist
-        ranks = tuple(int(r) for r in request.get("ranks", range(dist.get_world_size())))
-        key = ("group", ranks)
-        if key not in self._comm:
-            self._comm[key] = None if len(ranks) == dist.get_world_size() else dist.new_group(list(ranks))
-        return self._comm[key]
+        from ...parallel.runtime import group_for
+        return group_for(request.get("ranks", range(dist.get_world_size())))
+
+    def _adopt(self, request, st=None):
+        """Make ``request``'s layout {ranks, form, epoch, spec, path} current.
+
+        Built plans are cached per (ranks, form, latent shape, path): switching between
+        requests of different layouts is a lookup.  A request inside a solver step keeps the
+        layout its step started with.
+        """
+        import torch.distributed as dist
+        from ...parallel.layout import FixedLayout, Form
+        form = Form.parse(request["form"])
+        ranks = tuple(int(r) for r in request["ranks"])
+        if st is not None:
+            shape = tuple(st.latents.shape[1:])
+        else:
+            spec = WanSpec(model=self.model_name, **{k: v for k, v in request.get("spec", {}).items()
+                                                     if k in ("height", "width", "frames")})
+            shape = tuple(spec.latent_shape())
+        path = request.get("path", "fused")
+        key = (ranks, form.name, shape, path)
+        if st is not None and st.block != 0 and st.layout_key not in (None, key):
+            raise ValueError("the SP group may change only at a solver-step boundary")
+        if key not in self._layouts:
+            layout = FixedLayout(ranks, form, int(request.get("epoch", 0)))
+            if form.gpus == 1:
+                from .model import LocalAttention
+                from .runtime import CFGLocal
+                self._layouts[key] = (layout, LocalAttention(), CFGLocal(), None)
+            else:
+                from ...parallel.elastic import GroupFlagNCCL, GroupFlagPeer
+                from ...parallel.runtime import build_parallel, group_for
+                rank = dist.get_rank()
+                pctx, plan = build_parallel(layout, rank, self.device, attention=path,
+                                            seq_local=self.engine.cfg.tokens(shape) // form.sp, cfg=self.engine.cfg,
+                                            pred_numel=math.prod(shape))
+                flag = None
+                if form.sp > 1:  # doorbell stop agreed over the SP group (MAX of the ranks' flags)
+                    sp = layout.sp_ranks(rank)
+                    g = group_for(sp)
+                    if path == "fused" and self.device.type == "cuda":
+                        from ...parallel.symm import SymmetricHeap
+                        heap = SymmetricHeap(1 << 20, self.device, group=g)
+                        flag = GroupFlagPeer(heap, tuple(range(len(sp))))
+                    else:
+                        flag = GroupFlagNCCL(g, self.device)
+                self._layouts[key] = (layout, pctx, plan, flag)
+        layout, pctx, plan, flag = self._layouts[key]
+        self.engine.pctx, self.engine.cfg_plan, self.group_flag = pctx, plan, flag
+        self.layout = layout
+        if st is not None:
+            st.layout_key = key
+        return key
 
     def _async_decoder(self):
         if self._decoder is None:
@@ -110,7 +161,11 @@ class WanBackend(Backend):
         return dict(state_id=key, progress=self._progress(st))
 
     def advance(self, request):
+        if request.get("pair_state_id") is not None:
+            return self.advance_pair(dict(request, state_ids=[request["state_id"], request["pair_state_id"]]))
         st = self.state(request)
+        if request.get("layout") is not None:
+            self._adopt(request["layout"], st)
         from ...runtime.doorbell import rung
         bell = rung(request)
         t0 = time.perf_counter()
@@ -140,6 +195,9 @@ class WanBackend(Backend):
         if ida == idb:
             raise ValueError("a pair needs two distinct states")
         a, b = self.state(dict(state_id=ida)), self.state(dict(state_id=idb))
+        if request.get("layout") is not None:
+            self._adopt(request["layout"], a)
+            self._adopt(request["layout"], b)
         t0 = time.perf_counter()
         blocks = request.get("blocks")
         res = self.engine.advance_pair(a, b, None if blocks is None else int(blocks), bell=rung(request),
@@ -149,6 +207,8 @@ class WanBackend(Backend):
         res["model_ms"] = (time.perf_counter() - t0) * 1000
         res["a"].update(state_id=ida, progress=self._progress(a))
         res["b"].update(state_id=idb, progress=self._progress(b))
+        res["state_id"], res["progress"] = ida, res["a"]["progress"]
+        res["pair_state_id"], res["pair_progress"] = idb, res["b"]["progress"]
         return res
 
     def finish(self, request):
@@ -217,33 +277,11 @@ class WanBackend(Backend):
                                         timeout=timedelta(seconds=float(request.get("timeout_s", 120))))
             return dict(initialised=True, rank=dist.get_rank(), world_size=dist.get_world_size())
         if action == "layout":
-            from ...parallel.layout import FixedLayout, Form
-            from ...parallel.runtime import build_parallel
             for st in self.states.values():
                 if st.block != 0:
                     raise ValueError("the layout may change only at a solver-step boundary")
-            form = Form.parse(request["form"])
-            layout = FixedLayout(tuple(request["ranks"]), form, int(request.get("epoch", 0)))
-            spec = WanSpec(model=self.model_name, **{k: v for k, v in request.get("spec", {}).items()
-                                                     if k in ("height", "width", "frames")})
-            lat = spec.latent_shape()
-            pctx, plan = build_parallel(layout, dist.get_rank(), self.device, attention=request.get("path", "fused"),
-                                        seq_local=self.engine.cfg.tokens(lat) // form.sp, cfg=self.engine.cfg,
-                                        pred_numel=lat[0] * lat[1] * lat[2] * lat[3])
-            self.engine.pctx, self.engine.cfg_plan = pctx, plan
-            self.layout = layout
-            self.group_flag = None
-            if form.sp > 1:  # doorbell stop agreed over the SP group (MAX of the ranks' flags)
-                from ...parallel.elastic import GroupFlagNCCL, GroupFlagPeer
-                sp_ranks = layout.sp_ranks(dist.get_rank())
-                g = dist.new_group(list(sp_ranks), use_local_synchronization=True)
-                if request.get("path", "fused") == "fused" and self.device.type == "cuda":
-                    from ...parallel.symm import SymmetricHeap
-                    heap = SymmetricHeap(1 << 20, self.device, group=g)
-                    self.group_flag = GroupFlagPeer(heap, tuple(range(len(sp_ranks))))
-                else:
-                    self.group_flag = GroupFlagNCCL(g, self.device)
-            return dict(form=form.name, ranks=list(layout.ranks), epoch=layout.epoch)
+            key = self._adopt(request)
+            return dict(form=key[1], ranks=list(key[0]), epoch=self.layout.epoch)
         if action == "consensus":
             from ...parallel.elastic import RequestGroupGate, state_digest
             group = self._group(request)

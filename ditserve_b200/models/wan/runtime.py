@@ -83,6 +83,7 @@ class WanRequestState:
     block: int = 0                   # next block inside the current step (block executor)
     packets: dict = field(default_factory=dict)
     metrics: dict = field(default_factory=dict)
+    layout_key: tuple | None = None  # layout the current (partial) step runs under
 
     @property
     def done(self) -> bool:

@@ -173,17 +173,23 @@ def upgrade(layout, rank, device, pctx, cfg_plan, sp_groups, cfg_groups, seq_loc
         need += P * batch * seq_local * cfg.out_channels * 4 * 2
     pred_numel = pred_numel or 8 * 1024 * 1024
     need += 2 * pred_numel * 2  # double-buffered bf16 prediction slots
-    heap = SymmetricHeap(heap_bytes or int(need * 1.2) + (64 << 20), device)
+    from .runtime import group_for
+    # one heap over the layout's ranks; heap index = position in the sorted rank list
+    heap = SymmetricHeap(heap_bytes or int(need * 1.2) + (64 << 20), device, group=group_for(layout.ranks))
+    hidx = {g: i for i, g in enumerate(sorted(layout.ranks))}
+
+    def h(ranks):
+        return tuple(hidx[r] for r in ranks)
     if P > 1 and form.ring > 1:
-        pctx = FusedUSP(heap, layout.sp_ranks(rank), form.ring, seq_local, cfg.heads, cfg.head_dim, batch,
+        pctx = FusedUSP(heap, h(layout.sp_ranks(rank)), form.ring, seq_local, cfg.heads, cfg.head_dim, batch,
                         gather_cols=cfg.out_channels * math.prod(cfg.patch))
     elif P > 1:
-        pctx = FusedUlysses(heap, layout.sp_ranks(rank), seq_local, cfg.heads, cfg.head_dim, batch,
+        pctx = FusedUlysses(heap, h(layout.sp_ranks(rank)), seq_local, cfg.heads, cfg.head_dim, batch,
                             gather_cols=cfg.out_channels * math.prod(cfg.patch))
     if form.cfg == 2:
         partner = layout.cfg_partner(rank)
         members = (rank, partner) if layout.cfg_role(rank) == 0 else (partner, rank)
-        cfg_plan = FusedCFG(heap, members, numel=pred_numel)
+        cfg_plan = FusedCFG(heap, h(members), numel=pred_numel)
     return pctx, cfg_plan
 
 

@@ -1,8 +1,9 @@
 """Process-group construction for a FixedLayout and selection of the collective path.
 
-Every rank calls ``build_parallel`` with the same layout: it creates the SP
-sub-groups and CFG pairs in one fixed order (``new_group`` is collective) and
-returns ``(pctx, cfg_plan)`` for the Wan engine.  ``attention="nccl"`` is the
+The ranks of a layout call ``build_parallel`` with the same layout; only they take part
+(groups are created member-locally and cached by rank set, so other ranks of the world
+can be busy with other requests meanwhile).  Returns ``(pctx, cfg_plan)`` for the Wan
+engine.  ``attention="nccl"`` is the
 NCCL baseline; ``attention="fused"`` uses the peer-memory kernels of
 ``parallel.fused`` when they are available for the layout.
 """
@@ -17,33 +18,42 @@ from .layout import FixedLayout
 from .nccl import CFGExchangeNCCL, UlyssesNCCL, UlyssesRingNCCL
 
 
+_GROUPS: dict = {}
+
+
+def group_for(ranks):
+    """Process group over ``ranks`` (None = the default group when it spans the world).
+
+    Created member-locally (``use_local_synchronization``): only the member ranks call it,
+    each rank set once per process (torch names such groups by a hash of the ranks).
+    """
+    key = tuple(sorted(int(r) for r in ranks))
+    if len(key) == dist.get_world_size() and key == tuple(range(len(key))):
+        return None
+    if key not in _GROUPS:
+        _GROUPS[key] = dist.new_group(list(key), use_local_synchronization=True)
+    return _GROUPS[key]
+
+
 def build_parallel(layout: FixedLayout, rank: int, device: torch.device, attention: str = "fused",
                    seq_local: int | None = None, cfg=None, pred_numel: int | None = None):
     form = layout.form
     sp_groups, cfg_groups = {}, {}
-    n_sp = len(layout.ranks) // form.sp
-    for i in range(n_sp):
-        ranks = layout.ranks[i * form.sp:(i + 1) * form.sp]
-        g = dist.new_group(list(ranks)) if form.sp > 1 else None
-        sp_groups[ranks] = g
+    my_sp = layout.sp_ranks(rank)
+    if form.sp > 1:
+        sp_groups[my_sp] = group_for(my_sp)
+    else:
+        sp_groups[my_sp] = None
     if form.cfg == 2:
-        for j in range(form.sp):
-            pair = (layout.ranks[j], layout.ranks[j + form.sp])
-            cfg_groups[pair] = dist.new_group(list(pair))
+        pair = tuple(sorted((rank, layout.cfg_partner(rank))))
+        cfg_groups[pair] = group_for(pair)
     u_groups, ring_groups = {}, {}
     if form.ring > 1:
-        U, R = form.ulysses, form.ring
-        for i in range(n_sp):
-            sp = layout.ranks[i * form.sp:(i + 1) * form.sp]
-            for r in range(R):
-                g = tuple(sp[r * U:(r + 1) * U])
-                u_groups[g] = dist.new_group(list(g)) if U > 1 else None
-            for u in range(U):
-                g = tuple(sp[rr * U + u] for rr in range(R))
-                ring_groups[g] = dist.new_group(list(g))
+        ug, rg = layout.ulysses_ranks(rank), layout.ring_ranks(rank)
+        u_groups[ug] = group_for(ug) if len(ug) > 1 else None
+        ring_groups[rg] = group_for(rg)
     pctx = LocalAttention()
     cfg_plan = CFGLocal()
-    my_sp = layout.sp_ranks(rank)
     if form.sp > 1 and form.ring > 1:
         pctx = UlyssesRingNCCL(sp_groups[my_sp], u_groups[layout.ulysses_ranks(rank)],
                                ring_groups[layout.ring_ranks(rank)], form.sp, layout.sp_rank(rank), form.ulysses,

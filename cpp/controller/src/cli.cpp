@@ -54,6 +54,26 @@ std::string read_path(const std::string& p) {
   return slurp(in, 64u << 20);
 }
 
+// phases may name a cost profile file ("profile_path", relative to the config file); it is
+// inlined as "profile" so the study identity covers the profile's content
+Json resolve_profiles(Json config, const std::string& config_path) {
+  if (!config.contains("phases")) return config;
+  std::string base = config_path;
+  const size_t slash = base.find_last_of('/');
+  base = slash == std::string::npos ? "." : base.substr(0, slash);
+  Json phases = Json::array();
+  for (const auto& ph : config.at("phases").as_array()) {
+    Json p = ph;
+    if (p.contains("profile_path") && !p.contains("profile")) {
+      const std::string pp = p.at("profile_path").as_string();
+      p["profile"] = Json::parse(read_path(!pp.empty() && pp[0] == '/' ? pp : base + "/" + pp));
+    }
+    phases.push_back(p);
+  }
+  config["phases"] = phases;
+  return config;
+}
+
 Json pure_rpc(const std::string& cmd, const Json& req) {
   if (cmd == "policies") return policy_catalog();
   if (cmd == "generate") return study_workload(req);
@@ -202,7 +222,7 @@ int command_main(int argc, char** argv) {
         else throw UsageError("unknown run option " + a);
       }
       if (config.empty()) throw UsageError("run requires --config");
-      out = run_study(Json::parse(read_path(config)), opt);
+      out = run_study(resolve_profiles(Json::parse(read_path(config)), config), opt);
     } else if (cmd == "report") {
       if (rest.size() != 2) throw UsageError("report needs exactly one RUN_DIR");
       out = Json::object();

@@ -117,6 +117,11 @@ std::vector<Form> forms_for(const Settings& s, const ClusterCost& cost, const st
     }
     if (!kept.empty()) forms = kept;
   }
+  // classes whose weights or activations do not fit one GPU name a minimum degree
+  const int class_min = cost.has_class(klass) ? static_cast<int>(cost.klass(klass).integer("min_degree", 1)) : 1;
+  if (class_min > 1)
+    forms.erase(std::remove_if(forms.begin(), forms.end(), [&](const Form& f) { return f.degree() < class_min; }),
+                forms.end());
   if (t.min_video_degree > 1) {
     std::vector<Form> wide;
     for (const auto& f : forms)
@@ -518,6 +523,13 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     }
     const auto forms = forms_for(s, cost, r.klass, video_capacity);
     if (forms.empty()) continue;
+    // inside a solver step the request's partial activations live on its group, sharded
+    // for its form: it resumes there (or waits), never on other GPUs
+    if (r.status == "suspended" && r.blocks_done > 0 && !r.group.empty()) {
+      auto grp = pick_group(g, static_cast<int>(r.group.size()), r.group, true);
+      if (grp == r.group) emit_video(r, r.form.empty() ? forms.front() : parse_form(r.form), grp, "mid-step");
+      continue;
+    }
     if (t.hold_diffuse && r.status == "suspended" && !r.group.empty()) {
       // run-to-completion baselines resume on exactly their GPUs
       auto grp = pick_group(g, static_cast<int>(r.group.size()), r.group, true);

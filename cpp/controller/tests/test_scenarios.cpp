@@ -1,0 +1,367 @@
+// Planner, cost-model and simulator scenarios beyond the basic planner checks: solver-step
+// ownership, class memory minimums, pairs, atomic image batches, chunked decode quanta,
+// contention and overhead terms, pruning on slow links, widening, aliases and simulation
+// accounting.  One behaviour per check.
+#include <algorithm>
+#include <set>
+
+#include "check.hpp"
+#include "ds/planner.hpp"
+#include "ds/policy.hpp"
+#include "ds/sim.hpp"
+#include "ds/study.hpp"
+#include "ds/workload.hpp"
+
+using namespace ds;
+
+namespace {
+
+Json profile(double gbps = 700) {
+  Json p = Json::parse(R"({"links":{"default_latency_ms":0.02},
+   "sp_efficiency":{"2":0.97,"4":0.94,"8":0.88},"quantum_overhead_ms":0,"resize_ms":0,
+   "classes":{
+    "vid":{"kind":"video","steps":10,"blocks_per_step":30,"heads":12,"step_compute_ms":800,
+           "comm_mb_per_step":20000,"collectives_per_step":240,"cfg_exchange_mb":4,"decode_ms":100,"decode_chunks":1},
+    "long":{"kind":"video","steps":10,"blocks_per_step":30,"heads":24,"step_compute_ms":800,
+           "comm_mb_per_step":20000,"collectives_per_step":240,"cfg_exchange_mb":4,"decode_ms":400,"decode_chunks":4},
+    "img":{"kind":"image","steps":28,"tokens":1024,"step_ms":12,"service_ms":400,"decode_ms":50,
+           "batch_ms":{"1":400,"2":520,"4":800},
+           "batch_step_ms":{"1":12,"2":16,"4":26,"8":46}}}})");
+  p["links"]["default_gbps"] = gbps;
+  return p;
+}
+
+Json req(const std::string& id, const std::string& kind, const std::string& klass, double arrival, double deadline,
+         int steps_done = 0) {
+  Json r = Json::object();
+  r["request_id"] = id;
+  r["kind"] = kind;
+  r["class"] = klass;
+  r["arrival_ms"] = arrival;
+  r["deadline_ms"] = deadline;
+  r["status"] = "waiting";
+  if (kind == "video") r["steps_done"] = steps_done;
+  return r;
+}
+
+Json state(int gpus, std::vector<Json> reqs, std::vector<int> busy = {}, double now = 0) {
+  Json s = Json::object();
+  s["now_ms"] = now;
+  s["gpus"] = gpus;
+  Json b = Json::array();
+  for (int i = 0; i < gpus; ++i) b.push_back(std::count(busy.begin(), busy.end(), i) > 0);
+  s["busy"] = b;
+  Json r = Json::array();
+  for (auto& x : reqs) r.push_back(x);
+  s["requests"] = r;
+  return s;
+}
+
+const Json* find(const Json& plan, const std::string& id) {
+  for (const auto& a : plan.at("assignments").as_array())
+    if (a.at("request_id").as_string() == id) return &a;
+  return nullptr;
+}
+
+Json suspended(const std::string& id, const char* group, const char* form, int steps_done, int blocks_done) {
+  Json v = req(id, "video", "vid", 0, 1e9, steps_done);
+  v["status"] = "suspended";
+  v["group"] = Json::parse(group);
+  v["form"] = form;
+  v["blocks_done"] = blocks_done;
+  return v;
+}
+
+}  // namespace
+
+TEST("a request inside a solver step resumes on its own group and form") {
+  ClusterCost c(profile());
+  auto v = suspended("v", "[2,3]", "cfg2", 3, 12);
+  auto p = cluster_plan(state(8, {v}), "ditserve", c);
+  const Json* a = find(p, "v");
+  CHECK(a != nullptr);
+  CHECK(a->at("group")[0].as_int() == 2 && a->at("group")[1].as_int() == 3);
+  CHECK(a->at("form").as_string() == "cfg2");
+  CHECK(a->at("reason").as_string() == "mid-step");
+}
+
+TEST("the plan never moves a mid-step request onto other GPUs") {
+  ClusterCost c(profile());
+  auto v = suspended("v", "[2,3]", "cfg2", 3, 12);
+  auto p = cluster_plan(state(8, {v}, {3}), "ditserve", c);  // GPU 3 busy: wait, do not move
+  CHECK(find(p, "v") == nullptr);
+  auto b = suspended("b", "[2,3]", "cfg2", 3, 0);            // at a step boundary: free to move
+  auto q = cluster_plan(state(8, {b}, {3}), "ditserve", c);
+  CHECK(find(q, "b") != nullptr);
+}
+
+TEST("classes that do not fit one GPU get their minimum degree") {
+  Json pr = profile();
+  pr["classes"]["vid"]["min_degree"] = 4;
+  ClusterCost c(pr);
+  for (const char* pol : {"abl-step-elastic", "edf-bestfit", "ditserve"}) {
+    auto forms = candidate_forms(policy_traits(pol), c, "vid", 8, Json::object());
+    CHECK(!forms.empty());
+    for (const auto& f : forms) CHECK(f.degree() >= 4);
+  }
+  auto p = cluster_plan(state(8, {req("a", "video", "vid", 0, 1e9)}, {0, 1, 2, 3, 4}), "abl-step-elastic", c);
+  CHECK(find(p, "a") == nullptr);  // three free GPUs are not enough
+}
+
+TEST("heads divisibility removes Ulysses forms that do not split the heads") {
+  ClusterCost c(profile());
+  auto forms = candidate_forms(policy_traits("abl-step-elastic"), c, "vid", 8, Json::object());
+  for (const auto& f : forms) CHECK(12 % f.ulysses() == 0);
+  auto wide = candidate_forms(policy_traits("abl-step-elastic"), c, "long", 8, Json::object());
+  bool has8 = false;
+  for (const auto& f : wide) has8 = has8 || f.degree() == 8;
+  CHECK(has8);
+}
+
+TEST("lockstep pairing joins a second video onto a placed group") {
+  Json pr = profile();
+  pr["pair_overlap"] = 0.5;
+  ClusterCost c(pr);
+  Json o = Json::object();
+  o["pairing"] = true;
+  o["forms"] = Json::parse(R"(["sp2"])");  // an SP form: one request's all-to-all hides under the other's compute
+  auto a = req("a", "video", "vid", 0, 1e9);
+  auto b = req("b", "video", "vid", 1, 1e9);
+  auto p = cluster_plan(state(2, {a, b}), "ditserve", c, o);
+  const Json* pa = find(p, "a");
+  const Json* pb = find(p, "b");
+  CHECK(pa && pb);
+  CHECK(pa->at("pair").as_string() == "b" && pb->at("pair").as_string() == "a");
+  CHECK(pa->at("group") == pb->at("group"));
+  o["pairing"] = false;
+  auto q = cluster_plan(state(2, {a, b}), "ditserve", c, o);
+  CHECK(find(q, "b") == nullptr);
+  CHECK(c.pair_ms("vid", "vid", parse_form("cfg2")) >= 2 * c.step_ms("vid", parse_form("cfg2")) - 1e-9);
+}
+
+TEST("atomic image batches for batching baselines") {
+  ClusterCost c(profile());
+  std::vector<Json> rs;
+  for (int k = 0; k < 3; ++k) rs.push_back(req("i" + std::to_string(k), "image", "img", 0, 1e9));
+  auto p = cluster_plan(state(1, rs), "sbp-esp", c);
+  CHECK(p.at("assignments").size() == 1);
+  const Json& a = p.at("assignments")[0];
+  CHECK(a.at("quantum").as_string() == "atomic");
+  CHECK(a.at("batch").size() == 3);
+  CHECK(a.at("reason").as_string() == "image-batch");
+}
+
+TEST("chunked decode is preemptible between latent frames") {
+  ClusterCost c(profile());
+  Json v = req("v", "video", "long", 0, 1e9, 10);
+  v["status"] = "suspended";
+  v["group"] = Json::parse("[0,1]");
+  v["form"] = "cfg2";
+  v["decode_done"] = 1;
+  auto p = cluster_plan(state(8, {v}), "ditserve", c);
+  CHECK(find(p, "v")->at("quantum").as_string() == "finish");
+  CHECK(find(p, "v")->at("decode_frames").as_int() == 1);  // block policies: one chunk per quantum
+  auto q = cluster_plan(state(8, {v}), "abl-step-elastic", c);
+  CHECK(find(q, "v")->at("decode_frames").as_int() == 3);  // the rest in one go
+  CHECK_NEAR(c.chunk_ms("long"), 100.0, 1e-9);
+}
+
+TEST("per-block overhead is charged once per block") {
+  Json pr = profile();
+  pr["block_overhead_ms"] = 0.5;
+  ClusterCost c(pr);
+  ClusterCost z(profile());
+  const Form f = parse_form("sp2");
+  CHECK_NEAR(c.block_ms("vid", f) - z.block_ms("vid", f), 0.5, 1e-9);
+  CHECK_NEAR(c.block_ms("vid", parse_form("cfg2")) - z.block_ms("vid", parse_form("cfg2")), 0.25, 1e-9);
+}
+
+TEST("concurrent SP groups see the contention table") {
+  Json pr = profile();
+  pr["links"]["2"] = Json::parse(R"({"gbps":700,"concurrent_gbps":{"1":700,"4":350}})");
+  ClusterCost c(pr);
+  const Form f = parse_form("sp2");
+  CHECK(c.step_ms("vid", f, 4) > c.step_ms("vid", f, 1));
+  CHECK_NEAR(c.step_ms("vid", f, 1), ClusterCost(profile()).step_ms("vid", f, 1), 1e-9);
+}
+
+TEST("measured form entries override the formula and stay per class") {
+  Json pr = profile();
+  pr["classes"]["vid"]["forms"] = Json::parse(R"({"cfg2":{"step_ms":123.0}})");
+  ClusterCost c(pr);
+  CHECK_NEAR(c.step_ms("vid", parse_form("cfg2")), 123.0, 1e-12);
+  CHECK(c.terms("vid", parse_form("cfg2")).measured);
+  CHECK(!c.terms("long", parse_form("cfg2")).measured);
+}
+
+TEST("slow links make wide Ulysses forms dominated and pruned") {
+  ClusterCost slow(profile(2.0));  // 2 GB/s: the all-to-all dominates
+  auto forms = candidate_forms(policy_traits("ditserve"), slow, "vid", 8, Json::object());
+  for (const auto& f : forms) CHECK(f.sp == 1);  // only CFG forms survive
+  ClusterCost fast(profile(700));
+  auto wide = candidate_forms(policy_traits("ditserve"), fast, "vid", 8, Json::object());
+  bool has_sp = false;
+  for (const auto& f : wide) has_sp = has_sp || f.sp > 1;
+  CHECK(has_sp);
+}
+
+TEST("CFG-pair admission waits instead of starting narrow") {
+  ClusterCost c(profile());
+  auto p = cluster_plan(state(4, {req("a", "video", "vid", 0, 1e9)}, {0, 1, 2}), "ditserve", c);
+  CHECK(find(p, "a") == nullptr);  // one free GPU: ditserve does not start at sp1
+  auto q = cluster_plan(state(4, {req("a", "video", "vid", 0, 1e9)}, {0, 1, 2}), "stair-base", c);
+  CHECK(find(q, "a") != nullptr && find(q, "a")->at("degree").as_int() == 1);
+}
+
+TEST("a lone video is widened while scaling stays efficient") {
+  ClusterCost c(profile());
+  auto p = cluster_plan(state(8, {req("a", "video", "vid", 0, 1e9)}), "ditserve", c);
+  CHECK(find(p, "a")->at("degree").as_int() == 8);
+  CHECK(find(p, "a")->at("reason").as_string() == "widened");
+  Json o = Json::object();
+  o["widen_efficiency"] = 0.999;  // no form is that efficient: stay at the minimal one
+  auto q = cluster_plan(state(8, {req("a", "video", "vid", 0, 1e9)}), "ditserve", c, o);
+  CHECK(find(q, "a")->at("degree").as_int() == 2);
+}
+
+TEST("widening stops while an image waits unplaced") {
+  ClusterCost c(profile());
+  std::vector<Json> rs = {req("a", "video", "vid", 0, 1e9)};
+  for (int k = 0; k < 8; ++k) rs.push_back(req("i" + std::to_string(k), "image", "img", 0, 1e9));
+  Json o = Json::object();
+  o["continuous_batch"] = 1;  // one image per GPU: images saturate the node
+  auto p = cluster_plan(state(8, rs), "ditserve", c, o);
+  const Json* a = find(p, "a");
+  CHECK(a == nullptr || a->at("degree").as_int() <= 2);
+}
+
+TEST("doorbell option off disables sub-step preemption") {
+  ClusterCost c(profile());
+  auto v = req("v", "video", "vid", 0, 1e9, 2);
+  v["status"] = "running";
+  v["group"] = Json::parse("[0]");
+  v["form"] = "sp1";
+  v["quantum_started_ms"] = 0.0;
+  auto i = req("i", "image", "img", 0, 800);
+  Json o = Json::object();
+  o["doorbell"] = false;
+  CHECK(cluster_plan(state(1, {v, i}, {0}), "ditserve", c).at("preempt").size() == 1);
+  CHECK(cluster_plan(state(1, {v, i}, {0}), "ditserve", c, o).at("preempt").size() == 0);
+}
+
+TEST("block quanta are emitted only by block policies") {
+  ClusterCost c(profile());
+  Json o = Json::object();
+  o["quantum_blocks"] = 6;
+  auto p = cluster_plan(state(8, {req("a", "video", "vid", 0, 1e9)}), "ditserve", c, o);
+  CHECK(find(p, "a")->at("quantum").as_int() == 6);
+  auto q = cluster_plan(state(8, {req("a", "video", "vid", 0, 1e9)}), "abl-step-elastic", c, o);
+  CHECK(find(q, "a")->at("quantum").as_string() == "step");
+}
+
+TEST("a started image keeps its GPU affinity") {
+  ClusterCost c(profile());
+  auto i = req("i", "image", "img", 0, 1e9);
+  i["affinity"] = 5;
+  auto p = cluster_plan(state(8, {i}), "ditserve", c);
+  CHECK(find(p, "i")->at("group")[0].as_int() == 5);
+  auto q = cluster_plan(state(8, {i}, {5}), "ditserve", c);
+  CHECK(find(q, "i") == nullptr);
+}
+
+TEST("invalid planner input is rejected") {
+  ClusterCost c(profile());
+  CHECK_THROWS(cluster_plan(state(2, {req("a", "video", "vid", 0, 1), req("a", "image", "img", 0, 1)}), "ditserve", c));
+  CHECK_THROWS(cluster_plan(state(2, {req("a", "audio", "img", 0, 1)}), "ditserve", c));
+  Json s = state(2, {});
+  s["busy"] = Json::parse("[false]");
+  CHECK_THROWS(cluster_plan(s, "ditserve", c));
+  Json o = Json::object();
+  o["order"] = "lifo";
+  CHECK_THROWS(cluster_plan(state(2, {}), "ditserve", c, o));
+  o = Json::object();
+  o["continuous_batch"] = 9;
+  CHECK_THROWS(cluster_plan(state(2, {}), "ditserve", c, o));
+}
+
+TEST("legacy aliases plan as their canonical policy and retired names are refused") {
+  ClusterCost c(profile());
+  CHECK(canonical_policy("knapsack_dp") == "ditserve-v1");
+  CHECK(canonical_policy("static_cfg2sp2") == "static-cfg2sp2");
+  auto a = cluster_plan(state(8, {req("a", "video", "vid", 0, 1e9)}), "knapsack_dp", c);
+  auto b = cluster_plan(state(8, {req("a", "video", "vid", 0, 1e9)}), "ditserve-v1", c);
+  CHECK(a == b);
+  CHECK_THROWS(policy_traits("vllm_omni"));
+  CHECK_THROWS(policy_traits("no-such-policy"));
+}
+
+TEST("simulation accounting: every request is counted once and finishes after it starts") {
+  ClusterCost c(profile());
+  Json ph = Json::parse(R"({"generator":{"count":30,"seed":3,"pattern":"poisson","rate_rpm":40,
+     "classes":[{"weight":1,"kind":"video","class":"vid","service_ms":8000,"slo_scale":2},
+                {"weight":2,"kind":"image","class":"img","service_ms":400,"slo_scale":2}]}})");
+  Json rows = study_workload(ph);
+  auto r = simulate_cluster(rows, 4, "ditserve", c);
+  CHECK(r.rows.size() == 30);
+  int on_time = 0;
+  for (const auto& row : r.rows.as_array()) {
+    CHECK(row.at("status").as_string() == "done");
+    CHECK(row.at("finish_ms").as_double() >= row.at("start_ms").as_double());
+    CHECK(row.at("start_ms").as_double() >= row.at("arrival_ms").as_double());
+    on_time += row.at("finish_ms").as_double() <= row.at("deadline_ms").as_double();
+  }
+  CHECK(r.summary.at("on_time").as_int() == on_time);
+  CHECK(r.counters.at("quanta").as_int() >= 30);
+}
+
+TEST("a horizon censors unfinished requests") {
+  ClusterCost c(profile());
+  Json ph = Json::parse(R"({"generator":{"count":10,"seed":1,"pattern":"offline_all",
+     "classes":[{"kind":"video","class":"vid","service_ms":8000,"slo_scale":2}]}})");
+  auto r = simulate_cluster(study_workload(ph), 2, "ditserve", c, Json::object(), nullptr, 5000);
+  CHECK(r.summary.at("completed").as_int() < 10);
+  CHECK(r.summary.at("censored").as_int() + r.summary.at("completed").as_int() +
+            r.summary.at("not_executed").as_int() == 10);
+}
+
+TEST("block preemption shortens image latency behind a long video on one GPU") {
+  ClusterCost c(profile());
+  Json rows = Json::parse(R"([
+    {"request_id":"v","kind":"video","class":"vid","arrival_ms":0,"deadline_ms":1e9,"spec":{"steps":10}},
+    {"request_id":"i","kind":"image","class":"img","arrival_ms":100,"deadline_ms":1100,"spec":{"steps":28}}])");
+  auto with = simulate_cluster(rows, 1, "ditserve", c);
+  auto without = simulate_cluster(rows, 1, "abl-no-block", c);
+  auto fin = [](const SimResult& r, const std::string& id) {
+    for (const auto& row : r.rows.as_array())
+      if (row.at("request_id").as_string() == id) return row.at("finish_ms").as_double();
+    return -1.0;
+  };
+  CHECK(fin(with, "i") < fin(without, "i"));
+  CHECK(fin(with, "i") <= 1100);
+}
+
+TEST("elastic SP finishes a lone video sooner than a fixed single GPU") {
+  ClusterCost c(profile());
+  Json rows = Json::parse(R"([
+    {"request_id":"v","kind":"video","class":"vid","arrival_ms":0,"deadline_ms":1e9,"spec":{"steps":10}}])");
+  auto el = simulate_cluster(rows, 8, "ditserve", c);
+  auto one = simulate_cluster(rows, 8, "xdit-sp1", c);
+  CHECK(el.rows[0].at("finish_ms").as_double() < 0.25 * one.rows[0].at("finish_ms").as_double());
+}
+
+TEST("ring forms are offered only when enabled and price the ring term") {
+  ClusterCost c(profile());
+  Json o = Json::object();
+  auto plain = candidate_forms(policy_traits("abl-step-elastic"), c, "long", 8, o);
+  for (const auto& f : plain) CHECK(f.ring == 1);
+  auto all = enumerate_forms({1, 2, 4, 8}, true, true, 8);
+  bool u2r2 = false;
+  for (const auto& f : all) u2r2 = u2r2 || form_name(f) == "u2r2";
+  CHECK(u2r2);
+  Json pr = profile();
+  pr["classes"]["long"]["ring_mb_per_step"] = 8000;
+  ClusterCost r(pr);
+  CHECK(r.terms("long", parse_form("u2r2")).ring > 0);
+}
+
+int main() { return dstest::run_all(); }

@@ -35,6 +35,8 @@ class WanBackend(Backend):
             raise ValueError(f"unknown Wan model {self.model_name}")
         dev = config.get("device") or ("cuda:0" if torch.cuda.is_available() else "cpu")
         self.device = torch.device(dev)
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)  # NCCL and the object collectives use the current device
         dtype = torch.bfloat16 if self.device.type == "cuda" else torch.float32
         self.engine = WanEngine(self.model_name, device=self.device, dtype=dtype, seed=int(config.get("seed", 0)))
         self.snapshots: dict = {}
@@ -270,6 +272,8 @@ class WanBackend(Backend):
         action = request.get("action", "init")
         if action == "init":
             if not dist.is_initialized():
+                # lazy communicator init (no device_id): sub-groups are then created by their
+                # members alone instead of by a split that every world rank must join
                 from datetime import timedelta
                 backend = "nccl" if self.device.type == "cuda" else "gloo"
                 dist.init_process_group(backend, init_method=request["init_method"], rank=int(request["rank"]),

@@ -73,6 +73,9 @@ class WanBackend(Backend):
                                                      if k in ("height", "width", "frames")})
             shape = tuple(spec.latent_shape())
         path = request.get("path", "fused")
+        if path == "auto":  # measured choice per (form, tokens per rank)
+            from ...parallel.autotune import choose
+            path = choose(form.name, self.engine.cfg.tokens(shape) // form.sp)
         key = (ranks, form.name, shape, path)
         if st is not None and st.block != 0 and st.layout_key not in (None, key):
             raise ValueError("the SP group may change only at a solver-step boundary")

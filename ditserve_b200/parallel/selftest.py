@@ -24,6 +24,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--tiny", action="store_true", help="small 2-block model at 240p (fast)")
     ap.add_argument("--form", default=None, help="parallel form (default: cfg2 x Ulysses over the world)")
+    ap.add_argument("--record", default=None, help="append the timing to this collective-path table (autotune)")
     args = ap.parse_args()
     from ..models.wan.config import WAN21_T2V_1_3B, WanConfig
     from ..models.wan import config as wcfg
@@ -78,6 +79,10 @@ def main():
         print(json.dumps({"selftest": "fused_vs_nccl", "world": world, "form": form.name, "bitwise_equal_all_ranks":
                           bool(flags.item()), "rel_l2": rel, "nccl_ms_per_step": round(out["nccl"]["ms"], 3),
                           "fused_ms_per_step": round(out["fused"]["ms"], 3), "model": cfg.name}))
+        if args.record:
+            from .autotune import record
+            record(args.record, form.name, cfg.tokens(lat) // form.sp, out["nccl"]["ms"], out["fused"]["ms"],
+                   bool(flags.item()), model=cfg.name, world=world)
     dist.destroy_process_group()
 
 

@@ -95,3 +95,16 @@ def test_regroup_consensus_flag_gloo(tmp_path):
     assert res[0][1] and res[1][1]          # agreed after the regroup
     assert res[0][2] == 1 and res[1][2] == 1  # MAX flag
     assert not res[0][3] and not res[1][3]    # divergence detected
+
+
+def test_collective_autotune_table(tmp_path):
+    from ditserve_b200.parallel.autotune import choose, load, record
+    t = tmp_path / "c.json"
+    record(t, "cfg2sp4", 9408, nccl_ms=2.19, fused_ms=1.70, bitwise=True)
+    record(t, "cfg2u2r2", 9408, nccl_ms=2.38, fused_ms=2.48, bitwise=False)
+    record(t, "cfg2u2r2", 1 << 20, nccl_ms=90.0, fused_ms=80.0, bitwise=False)
+    e = load(t)
+    assert len(e) == 3
+    assert choose("cfg2sp4", 10000, e) == "fused"
+    assert choose("cfg2u2r2", 9000, e) == "nccl" and choose("cfg2u2r2", 900000, e) == "fused"
+    assert choose("sp2", 100, e) == "fused"  # never measured: default

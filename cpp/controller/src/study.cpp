@@ -885,8 +885,21 @@ Json validate_study(const Json& config) {
     const std::string kind = p.at("kind").as_string();
     if (kind != "operations" && kind != "online" && kind != "cluster" && kind != "simulate")
       throw std::invalid_argument("phase " + id + ": unknown kind " + kind);
-    if (kind != "simulate" && !config.at("workers").contains(p.str("worker", "model")))
-      throw std::invalid_argument("phase " + id + ": unknown worker");
+    if (kind != "simulate") {
+      std::vector<std::string> names;
+      if (p.contains("workers")) {  // cluster phases: {"video": def, "image": def}
+        if (kind != "cluster") throw std::invalid_argument("phase " + id + ": only cluster phases map workers by kind");
+        for (const auto& kv : p.at("workers").as_object()) {
+          if (kv.first != "video" && kv.first != "image")
+            throw std::invalid_argument("phase " + id + ": workers keys are video and image");
+          names.push_back(kv.second.as_string());
+        }
+      } else {
+        names.push_back(p.str("worker", "model"));
+      }
+      for (const auto& n : names)
+        if (!config.at("workers").contains(n)) throw std::invalid_argument("phase " + id + ": unknown worker " + n);
+    }
     expand_matrix(p);  // validates axes and size
   }
   Json out = Json::object();

@@ -13,8 +13,10 @@
   all_reduce baseline, ``GroupFlagPeer`` one bounded-wait kernel over peer memory.
 * Regroup state transfer (a request's latents and solver history reach the ranks that join
   its new group): ``broadcast_state_nccl`` is the per-tensor NCCL broadcast baseline,
-  ``PeerStateBroadcast`` stores every tensor straight into the joining ranks' heaps with one
-  multi-peer put kernel and a barrier, bit-exact (reference: CacheOffGroupMigration,
+  ``PeerStateBroadcast`` stores every tensor straight into the joining ranks' heaps with
+  multi-peer put kernels: small tensors go to every receiver directly, large ones as a
+  scatter (slice j to receiver j) followed by an all-gather among the receivers, so the
+  source's NVLink egress carries each byte once; bounded barriers between phases; bit-exact (reference: CacheOffGroupMigration,
   parallel.py:903-1050; host-staged packet files, study.cpp:1395-1411).
 """
 from __future__ import annotations
@@ -193,6 +195,7 @@ class PeerStateBroadcast:
         self.heap = heap
         self.capacity = int(capacity_bytes)
         self.off = heap.alloc(self.capacity, align=4096)
+        self.scatter_min_bytes = 1 << 20  # larger tensors go scatter + all-gather (bandwidth-optimal)
 
     def __call__(self, tree, src_member: int, src_global: int | None = None):
         """``src_member`` indexes the group; ``src_global`` is its rank in the default group
@@ -215,25 +218,57 @@ class PeerStateBroadcast:
         if cur > self.capacity:
             raise MemoryError(f"state of {cur} bytes exceeds the broadcast staging area ({self.capacity})")
         r, bases, tmo = g.args()
+        receivers = [m for m in range(g.size) if m != src_member]
+        k = len(receivers)
+        sizes = [math.prod(shape) * torch.empty((), dtype=dt).element_size() for shape, dt in specs]
+
+        def split(nb):
+            """16-byte-aligned slice bounds of the scattered body (one slice per receiver)."""
+            body = nb // 16 * 16
+            if k < 2 or body < self.scatter_min_bytes:
+                return body, None
+            per = -(-body // 16 // k) * 16
+            return body, [(j * per, min(body, (j + 1) * per)) for j in range(k)]
+
         if g.rank == src_member:
-            mask = ((1 << g.size) - 1) & ~(1 << src_member)
-            for t, o in zip(tensors, offs):
+            everyone = ((1 << g.size) - 1) & ~(1 << src_member)
+            for t, o, nb in zip(tensors, offs, sizes):
                 flat = t.contiguous().view(-1).view(torch.uint8)
-                nb = flat.numel()
-                body = nb // 16 * 16
-                if body:
-                    self.ext.put_peers(flat[:body], mask, self.off + o, r, bases, tmo)
+                body, parts = split(nb)
+                if parts is None:  # small: store the whole body into every receiver
+                    if body:
+                        self.ext.put_peers(flat[:body], everyone, self.off + o, r, bases, tmo)
+                else:  # large: slice j to receiver j only (the source's NVLink egress carries it once)
+                    for (lo, hi), m in zip(parts, receivers):
+                        if hi > lo:
+                            self.ext.put_peers(flat[lo:hi], 1 << m, self.off + o + lo, r, bases, tmo)
                 if nb - body:  # ragged tail: pad to one 16-byte vector
                     tail = torch.zeros(16, dtype=torch.uint8, device=flat.device)
                     tail[:nb - body] = flat[body:]
-                    self.ext.put_peers(tail, mask, self.off + o + body, r, bases, tmo)
+                    self.ext.put_peers(tail, everyone, self.off + o + body, r, bases, tmo)
         g.barrier(status)
+        if g.rank != src_member and k >= 2:
+            # all-gather among the receivers: each forwards its slice to the others
+            j = receivers.index(g.rank)
+            others = 0
+            for m in receivers:
+                if m != g.rank:
+                    others |= 1 << m
+            for o, nb in zip(offs, sizes):
+                _, parts = split(nb)
+                if parts is None:
+                    continue
+                lo, hi = parts[j]
+                if hi > lo:
+                    mine = self.heap.tensor[self.off + o + lo:self.off + o + hi]
+                    self.ext.put_peers(mine, others, self.off + o + lo, r, bases, tmo)
+        if k >= 2 and any(split(nb)[1] is not None for nb in sizes):
+            g.barrier(status)
         if g.rank == src_member:
             out = tensors
         else:
             out = []
-            for (shape, dt), o in zip(specs, offs):
-                nb = math.prod(shape) * torch.empty((), dtype=dt).element_size()
+            for (shape, dt), o, nb in zip(specs, offs, sizes):
                 out.append(self.heap.tensor[self.off + o:self.off + o + nb].view(dt).view(shape).clone())
         g.barrier(status)  # the staging area may be reused after every receiver copied out
         check_status(self.heap.device)

@@ -48,9 +48,11 @@ BUDGET = {"limit_gpu_seconds": 3600, "watchdog_seconds": 900, "repair_reserve_gp
 
 def test_mock_cluster_pairs_batches_regroups(controller, tmp_path):
     cfg = {"schema": "ditserve-b200.study.v1", "experiment": "exec-mock",
-           "workers": {"model": {"backend": "mock", "config": {"options": {"costs": {"step_ms": 15}}}}},
+           "workers": {"vid": {"backend": "mock", "config": {"options": {"costs": {"step_ms": 15}}}},
+                       "img": {"backend": "mock", "config": {"options": {"costs": {"step_ms": 5}}}}},
            "budget": BUDGET,
            "phases": [{"id": "cluster", "kind": "cluster", "gpus": 4, "policy": "ditserve", "distributed": True,
+                       "workers": {"video": "vid", "image": "img"},
                        "sp_transport": "export",
                        "options": {"pairing": True, "continuous_batch": 4},
                        "generator": {"count": 12, "seed": 2, "pattern": "poisson", "rate_rps": 40, "classes": [

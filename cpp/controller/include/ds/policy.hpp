@@ -25,6 +25,9 @@ struct PolicyTraits {
   bool best_fit = false;          // EDF best fit + surplus redistribution
   bool approx = false, v3 = false, v5 = false, fission = false;
   double widen = 0.0;             // widen a video when per-GPU efficiency stays >= widen
+  bool widen_past_images = false;  // widening continues while images wait (they preempt by doorbell)
+  double feasible_margin = 0.0;    // slack kept by the feasible-minimal form choice (fraction of remaining)
+  double wide_efficiency = 0.0;    // >0: videos start on their widest form whose per-GPU efficiency stays above it
   std::string image_placement = "first";  // first | pair_fit
   bool hold_diffuse = false;      // a started video keeps its GPUs (no decode shrink)
   bool demote_late = true;        // late requests ranked behind feasible ones

@@ -42,6 +42,9 @@ struct Settings {
   bool ring_forms = false;
   int partition_image_gpus = -1;
   int check_blocks = 1;
+  bool widen_past_images = false;  // widen even while images wait (they preempt by doorbell)
+  double feasible_margin = 0.0;     // feasible-min keeps this fraction of the remaining time as slack
+  double wide_efficiency = 0.0;     // >0: videos start on their widest form at least this efficient
 };
 
 Settings resolve(const PolicyTraits& t, const Json& o) {
@@ -79,6 +82,10 @@ Settings resolve(const PolicyTraits& t, const Json& o) {
   s.ring_forms = o.flag("ring_forms", t.id == "diag-2d-usp");
   s.partition_image_gpus = static_cast<int>(o.integer("partition_image_gpus", -1));
   s.check_blocks = static_cast<int>(o.integer("check_blocks", 1));
+  s.widen_past_images = o.flag("widen_past_images", t.widen_past_images);
+  s.feasible_margin = o.num("feasible_margin", t.feasible_margin);
+  s.wide_efficiency = o.num("wide_efficiency", t.wide_efficiency);
+  if (s.feasible_margin < 0 || s.feasible_margin > 10) throw std::invalid_argument("feasible_margin must be in [0, 10]");
   return s;
 }
 
@@ -122,6 +129,21 @@ std::vector<Form> forms_for(const Settings& s, const ClusterCost& cost, const st
   if (class_min > 1)
     forms.erase(std::remove_if(forms.begin(), forms.end(), [&](const Form& f) { return f.degree() < class_min; }),
                 forms.end());
+  // on hardware where SP scales near-linearly (NVLink/NVSwitch), a video runs fastest and
+  // costs no more GPU time on its widest efficient form: start it there (serialising
+  // videos) instead of sharing the node between narrow groups
+  if (s.wide_efficiency > 0 && forms.size() > 1) {
+    const Form* base = &forms.front();
+    for (const auto& f : forms)
+      if (f.degree() < base->degree()) base = &f;
+    const double base_work = cost.step_ms(klass, *base) * base->degree();
+    int widest = 0;
+    for (const auto& f : forms)
+      if (base_work / (cost.step_ms(klass, f) * f.degree()) >= s.wide_efficiency) widest = std::max(widest, f.degree());
+    if (widest > 1)
+      forms.erase(std::remove_if(forms.begin(), forms.end(), [&](const Form& f) { return f.degree() < widest; }),
+                  forms.end());
+  }
   if (t.min_video_degree > 1) {
     std::vector<Form> wide;
     for (const auto& f : forms)
@@ -557,7 +579,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     std::vector<int> grp;
     std::string reason;
     for (const auto& f : forms) {
-      if (now + cost.remaining_ms(*r.j, f) > r.deadline) continue;
+      if (now + cost.remaining_ms(*r.j, f) * (1.0 + s.feasible_margin) > r.deadline) continue;
       auto cand = pick_group(g, f.degree(), r.group, true);
       if (cand.empty()) continue;
       chosen = f;
@@ -590,7 +612,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
         const double base_work = cost.step_ms(r.klass, chosen) * chosen.degree();
         const double wide_work = cost.step_ms(r.klass, f) * f.degree();
         if (base_work / wide_work < t.widen) break;
-        if (any_waiting_image_unplaced()) break;
+        if (!s.widen_past_images && any_waiting_image_unplaced()) break;
         give(grp);
         auto cand = pick_group(g, f.degree(), r.group, true);
         take(grp);

@@ -45,6 +45,13 @@ std::map<std::string, PolicyTraits> build_table() {
   auto put = [&](PolicyTraits t) { m.emplace(t.id, std::move(t)); };
   put(full("ditserve", "DitServe", "ours", "block preemption, pruned CFG x SP forms, CFG-pair admission, continuous image batching"));
   {
+    auto t = full("ditserve-wide", "DitServe (NVSwitch)", "ours",
+                  "ditserve whose videos start on their widest form while per-GPU efficiency stays >= 0.85 "
+                  "(near-linear SP scaling over NVSwitch makes the wide form fastest at no extra GPU time)");
+    t.wide_efficiency = 0.85;
+    put(t);
+  }
+  {
     auto t = full("ditserve-approx", "DitServe-Approx", "ours", "ditserve plus late-step CFG folding (approximate)");
     t.v5 = t.fission = true;
     put(t);
@@ -300,6 +307,7 @@ Json describe_policy(const PolicyTraits& t) {
   j["partition_divisor"] = t.partition_divisor;
   j["demote_late"] = t.demote_late;
   j["widen"] = t.widen;
+  j["wide_efficiency"] = t.wide_efficiency;
   j["image_placement"] = t.image_placement;
   j["image_batching"] = t.image_batching;
   j["round_steps"] = t.round_steps;

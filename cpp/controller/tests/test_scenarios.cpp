@@ -364,4 +364,27 @@ TEST("ring forms are offered only when enabled and price the ring term") {
   CHECK(r.terms("long", parse_form("u2r2")).ring > 0);
 }
 
+TEST("near-linear scaling starts videos on their widest efficient form") {
+  Json pr = profile();
+  // measured NVSwitch-like forms: per-GPU work within 5% from cfg2 to cfg2sp4
+  pr["classes"]["vid"]["forms"] = Json::parse(R"({"cfg2":{"step_ms":400},"cfg2sp2":{"step_ms":205},
+                                                  "cfg2sp4":{"step_ms":105}})");
+  ClusterCost c(pr);
+  auto forms = candidate_forms(policy_traits("ditserve-wide"), c, "vid", 8, Json::object());
+  CHECK(!forms.empty());
+  for (const auto& f : forms) CHECK(f.degree() == 8);
+  auto p = cluster_plan(state(8, {req("a", "video", "vid", 0, 1e9), req("b", "video", "vid", 0, 1e9)}),
+                        "ditserve-wide", c);
+  CHECK(find(p, "a")->at("degree").as_int() == 8);
+  CHECK(find(p, "b") == nullptr);  // serialised behind a, not squeezed onto a narrow group
+  auto q = cluster_plan(state(8, {req("a", "video", "vid", 0, 1e9), req("b", "video", "vid", 0, 1e9)}),
+                        "ditserve", c);
+  CHECK(find(q, "b") != nullptr || find(q, "a")->at("degree").as_int() == 8);
+  // poor scaling (PCIe-like): the floor stays at the narrowest form
+  Json slow = profile(2.0);
+  ClusterCost s(slow);
+  auto narrow = candidate_forms(policy_traits("ditserve-wide"), s, "vid", 8, Json::object());
+  CHECK(narrow.front().degree() == 2);
+}
+
 int main() { return dstest::run_all(); }

@@ -312,6 +312,28 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
       return vworkers[g]->call("distributed", r, 300);
     });
   }
+  // untimed warm-up: every aligned group of each listed form adopts its layout once, so
+  // communicators, symmetric heaps and fused plans exist before the trace starts
+  double warmup_ms = 0;
+  if (distributed && phase.contains("warmup_forms")) {
+    const double tw = monotonic_seconds();
+    Json spec = phase.get("warmup_spec").is_null() ? Json::object() : phase.at("warmup_spec");
+    for (const auto& fj : phase.at("warmup_forms").as_array()) {
+      const Form f = parse_form(fj.as_string());
+      for (const auto& grp : cluster_groups(gpus, f.degree())) {
+        fan_out(grp, [&](int g) {
+          Json r = Json::object();
+          r["action"] = "layout";
+          r["ranks"] = ints_json(grp);
+          r["form"] = form_name(f);
+          r["spec"] = spec;
+          r["path"] = path;
+          return vworkers[g]->call("distributed", r, 600);
+        });
+      }
+    }
+    warmup_ms = (monotonic_seconds() - tw) * 1000.0;
+  }
   // doorbells: one 8-byte epoch file per GPU
   std::vector<std::string> bells;
   std::vector<long long> bell_epoch(gpus, 0);
@@ -538,6 +560,8 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
       q["blocks_done"] = l.blocks_done;
       q["group"] = ints_json(l.status == "running" ? l.group : l.last_group);
       if (!l.form.empty()) q["form"] = l.form;
+      // a started image keeps its GPU: its state lives in that GPU's image worker
+      if (l.kind == "image" && l.status == "suspended" && !l.fresh.empty()) q["affinity"] = *l.fresh.begin();
       if (l.status == "running") {
         q["quantum_started_ms"] = l.quantum_started;
         q["rung"] = l.rung;
@@ -777,6 +801,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
   timing["plan_ms_total"] = plan_ms_total;
   timing["plan_ms_max"] = plan_ms_max;
   timing["wall_ms"] = now_ms_since(t0);
+  timing["warmup_ms"] = warmup_ms;
   out["controller_timing"] = timing;
   out["trace"] = trace;
   out["failures"] = failures;

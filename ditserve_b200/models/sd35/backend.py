@@ -18,7 +18,8 @@ CONFIGS = {c.name: c for c in (SD35_MEDIUM, SD35_TINY)}
 
 
 class SD35Backend(Backend):
-    operations = Backend.operations + ("advance_batch", "generate_batch", "snapshot", "restore", "inventory")
+    operations = Backend.operations + ("advance_batch", "generate_batch", "snapshot", "restore", "inventory",
+                                       "block_export", "block_import")
 
     def __init__(self, config):
         super().__init__(config)
@@ -100,3 +101,33 @@ class SD35Backend(Backend):
 
     def inventory(self, request):
         return dict(states={k: dict(step=v.step, steps=v.spec.steps) for k, v in self.states.items()})
+
+    def block_export(self, request):
+        """Step-boundary packet of an image request (host-staged move to another GPU's worker)."""
+        import hashlib
+        import io
+        import os
+        from pathlib import Path
+        st = self.state(request)
+        buf = io.BytesIO()
+        torch.save(self.engine.snapshot(st), buf)
+        blob = buf.getvalue()
+        d = Path(self.config.get("transfer_dir", "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"))
+        path = d / f"sd35-packet-{request['state_id']}-{os.getpid()}-{request.get('id', 0)}.pt"
+        path.write_bytes(blob)
+        return dict(path=str(path), manifest=hashlib.sha256(blob).hexdigest(), bytes=len(blob))
+
+    def block_import(self, request):
+        import hashlib
+        import io
+        import os
+        blob = open(request["path"], "rb").read()
+        if hashlib.sha256(blob).hexdigest() != request["manifest"]:
+            raise ValueError("packet manifest mismatch (tampered or truncated transfer)")
+        key = request["state_id"]
+        if key in self.states:
+            raise ValueError("duplicate live state_id")
+        self.states[key] = self.engine.restore(torch.load(io.BytesIO(blob), weights_only=False))
+        os.unlink(request["path"])
+        st = self.states[key]
+        return dict(state_id=key, progress=progress(st.step, st.spec.steps))

@@ -79,6 +79,7 @@ def test_wan_tiny_gloo_world_cluster(controller, tmp_path):
            "budget": BUDGET,
            "phases": [{"id": "cluster", "kind": "cluster", "gpus": 2, "policy": "ditserve", "worker": "wan",
                        "distributed": True, "sp_transport": "collective", "collectives": "nccl",
+                       "warmup_forms": ["cfg2", "sp2"], "warmup_spec": {"height": 64, "width": 64, "frames": 5},
                        "dist_port": 29000 + os.getpid() % 1000,
                        "generator": {"count": 3, "seed": 4, "pattern": "poisson", "rate_rps": 50, "classes": [
                            {"weight": 1, "kind": "video", "class": "wan21_480p", "service_ms": 20000,
@@ -89,5 +90,6 @@ def test_wan_tiny_gloo_world_cluster(controller, tmp_path):
     assert rep["phases"]["cluster"]["gates"]["pass"], rep["phases"]["cluster"]
     last = _last(rep)
     assert not last["failures"], last["failures"]
+    assert last["controller_timing"]["warmup_ms"] > 0
     forms = {t["form"] for t in last["trace"]}
     assert forms & {"cfg2", "sp2"}, forms  # at least one quantum ran on both ranks

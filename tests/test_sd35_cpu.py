@@ -47,3 +47,17 @@ def test_snapshot_restore_is_bitwise():
     r = e.restore(e.snapshot(s))
     e.run(r)
     assert torch.equal(r.latents, full.latents)
+
+
+def test_sd35_block_export_import(tmp_path):
+    from ditserve_b200.models.sd35.backend import SD35Backend
+    a = SD35Backend({"model": "sd3.5-tiny", "device": "cpu", "transfer_dir": str(tmp_path)})
+    b = SD35Backend({"model": "sd3.5-tiny", "device": "cpu", "transfer_dir": str(tmp_path)})
+    a.prepare(dict(id=1, state_id="i", spec=dict(height=64, width=64, steps=3, seed=2)))
+    a.advance(dict(id=2, state_id="i", steps=1))
+    pk = a.block_export(dict(id=3, state_id="i"))
+    b.block_import(dict(id=4, state_id="i", path=pk["path"], manifest=pk["manifest"]))
+    a.advance(dict(id=5, state_id="i", steps=2))
+    b.advance(dict(id=6, state_id="i", steps=2))
+    import torch
+    assert torch.equal(a.states["i"].latents, b.states["i"].latents)

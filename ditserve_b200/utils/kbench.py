@@ -52,6 +52,7 @@ def main():
     ap.add_argument("--json", default=None)
     ap.add_argument("--tokens", type=int, default=32760)
     ap.add_argument("--batch", type=int, default=2)
+    ap.add_argument("--only", default=None, help="'fused': only the peer-memory kernels on a one-member group")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     tflops_peak, hbm_peak, src = peaks()
@@ -73,6 +74,11 @@ def main():
         print(json.dumps(r))
 
     torch.manual_seed(0)
+    if args.only == "fused":
+        fused_rows(row, timeit, dev, S, B, D, H, flush)
+        if args.json:
+            json.dump(res, open(args.json, "w"), indent=1)
+        return
     x = torch.randn(M, D, device=dev).bfloat16()
     for name, N, K, kw in [("qkv_proj", 3 * D, D, {}), ("out_proj_gated", D, D, {"gate": True}),
                            ("ffn_up_gelu", F, D, {"act": "gelu"}), ("ffn_down_gated", D, F, {"gate": True})]:
@@ -131,8 +137,47 @@ def main():
     cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
     ms = timeit(lambda: ops.rmsnorm_rope_(q, w, cos=cos, sin=sin, rows_per_batch=S), flush=flush)
     row("rmsnorm_rope_q", ms, bytes_=2 * M * D * 2, impl="ours")
+    fused_rows(row, timeit, dev, S, B, D, H, flush)
     if args.json:
         json.dump(res, open(args.json, "w"), indent=1)
+
+
+def fused_rows(row, timeit, dev, S, B, D, H, flush):
+    """Peer-memory kernels on a one-member group (this GPU's own heap): the stores stay local,
+    so these rows measure each kernel's compute and HBM side; NVLink timing comes from the
+    multi-GPU selftests."""
+    from ..ops._ext import ext, status_word
+    M, hd = S * B, 128
+    heap, _ = ext().symm_alloc(int(ext().FLAG_BYTES) + 4 * M * 3 * D * 2 + (64 << 20), 0)
+    base = [heap.data_ptr()]
+    recv_off = 1 << 20
+    o_off = recv_off + ((M * 3 * D * 2 + 4095) // 4096) * 4096
+    st = status_word(dev)
+    tmo = int(5e9)
+    qkv = torch.randn(M, 3 * D, device=dev).bfloat16()
+    wq = torch.ones(D, device=dev).bfloat16()
+    wk = torch.ones(D, device=dev).bfloat16()
+    ang = torch.rand(S, hd // 2, device=dev)
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    ms = timeit(lambda: ext().qkv_scatter(qkv, wq, wk, 1e-6, cos, sin, S, H, hd, 0, base, tmo, recv_off, 0),
+                flush=flush)
+    row("qkv_scatter_norm_rope_a2a", ms, bytes_=2 * M * 3 * D * 2, impl="ours (group of 1)")
+    recv = heap[recv_off:recv_off + M * 3 * D * 2].view(torch.bfloat16).view(M, 3 * D)
+    q, k, v = recv[:, :D], recv[:, D:2 * D], recv[:, 2 * D:]
+    fl = 4.0 * B * H * S * S * hd
+    ms = timeit(lambda: ext().attention_scatter(q, k, v, B, S, H, hd, 1.0 / math.sqrt(hd), 0, base, tmo, o_off, S, 0,
+                                                D, st, [], []), iters=5)
+    row("attention_peer_store_epilogue", ms, flops=fl, impl="ours (group of 1)")
+    y = torch.randn(M, 64, device=dev).bfloat16()
+    ms = timeit(lambda: ext().allgather_rows(y, o_off, 0, base, tmo), flush=flush)
+    row("allgather_rows", ms, bytes_=2 * M * 64 * 2, impl="ours (group of 1)")
+    big = torch.randn(32 << 20, device=dev)  # 128 MB
+    ms = timeit(lambda: ext().put_peers(big, 1, recv_off, 0, base, tmo), flush=flush)
+    row("put_peers_128MB", ms, bytes_=2 * big.numel() * 4, impl="ours (group of 1)")
+    out = torch.zeros(1, dtype=torch.int32, device=dev)
+    ms = timeit(lambda: ext().group_flag(0, base, tmo, 5, 0, 0, out, st), iters=20)
+    row("group_flag_launch", ms, impl="ours (group of 1: launch + signal cost only)")
+    del heap
 
 
 if __name__ == "__main__":

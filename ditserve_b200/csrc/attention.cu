@@ -28,7 +28,6 @@ namespace {
 
 constexpr int kQT = 128;  // query rows per CTA
 constexpr int kKT = 128;  // key rows per tile
-constexpr int kAttnThreads = 192;
 
 // K/V descriptors of up to kMaxKvSources key/value sources (ring attention: the local
 // chunk plus the chunks held by the ring peers, read in place over NVLink).
@@ -67,9 +66,10 @@ struct AttnParams {
 //   WG1  softmax of tile A (thread = row),  WG2 softmax of tile B.
 // While WG1 turns S_A(j) into P_A(j) the tensor core runs S_B(j) / PV_B(j-1), and the
 // other way round, so MUFU work and MMA overlap.  TMEM: S_A [0,128), S_B [128,256),
-// O_A [256, 256+D), O_B [384, 384+D).  The row max takes a first pass over S in
-// 64-column halves and the exponentials a second, which keeps each softmax thread
-// under the 168-register budget of a 384-thread CTA.
+// O_A [256, 256+D), O_B [384, 384+D).  Each softmax thread loads its whole 128-column
+// S row from TMEM once, takes the row max, writes bf16 P and only then rescales O (when
+// needed), so the S row and the O chunks are never live together and the 168-register
+// budget of a 384-thread CTA holds without spills.
 constexpr int kAttn2Threads = 384;
 
 template <int D>
@@ -98,6 +98,38 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t r;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
   return r;
+}
+
+// (x0, x1) -> (2^x0, 2^x1) on the FMA pipe, for x <= 0: Cody-Waite split x = j + f with
+// j = rint(x) (magic-number rounding, |f| <= 1/2), 2^f by a cubic whose coefficients were
+// fitted here for minimum relative error on [-1/2, 1/2] (Lawson's iteratively reweighted
+// least squares; max relative error 7.5e-5, below bf16's half ulp of 2^-9), and 2^j added
+// to the exponent field.  x is clamped at -125 so the result stays a normal float (the
+// clamped terms, < 2^-125, vanish next to the row maximum's 1).
+constexpr float kExpC0 = 0.9999280571937561f;
+constexpr float kExpC1 = 0.6932609677314758f;
+constexpr float kExpC2 = 0.24261100590229034f;
+constexpr float kExpC3 = 0.055171530693769455f;
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+__device__ __forceinline__ uint64_t f2_const(float v) { return f2_pack(v, v); }
+#define kOne2 f2_const(1.0f)
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  const uint64_t xc = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t t = f2_fma(xc, kOne2, f2_const(kRoundMagic));     // rint(x) in the low mantissa bits
+  const uint64_t jr = f2_fma(t, kOne2, f2_const(-kRoundMagic));    // rint(x) as a float
+  const uint64_t fr = f2_fma(jr, f2_const(-1.0f), xc);              // f = x - rint(x)
+  uint64_t pp = f2_fma(f2_const(kExpC3), fr, f2_const(kExpC2));
+  pp = f2_fma(pp, fr, f2_const(kExpC1));
+  pp = f2_fma(pp, fr, f2_const(kExpC0));
+  float p0, p1, t0, t1;
+  f2_unpack(pp, p0, p1);
+  f2_unpack(t, t0, t1);
+  // (bits(t) << 23) == rint(x) << 23: the magic number's low nine bits are zero
+  const float e0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  const float e1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+  return f2_pack(e0, e1);
 }
 
 template <int D>
@@ -314,22 +346,25 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       tc_fence_after();
       const int valid = ktile_valid(j);  // columns >= valid are outside the segment
       const bool masked = valid < kKT;
-      // pass 1: row max
+      // one pass over TMEM: the thread's whole 128-column S row into registers
+      uint32_t s[kKT];
+#pragma unroll
+      for (int c = 0; c < kKT / 32; ++c)
+        tmem_ld32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+      tmem_wait_ld();
       float mx = -INFINITY;
+      if (masked) {
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t s[64];
-        tmem_ld32(s_col + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-        tmem_ld32(s_col + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
-        tmem_wait_ld();
-        if (masked) {
+        for (int c = 0; c < kKT; ++c)
+          if (c < valid) mx = fmaxf(mx, __uint_as_float(s[c]));
+      } else {
+        float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (half * 64 + c < valid) mx = fmaxf(mx, __uint_as_float(s[c]));
-        } else {
-#pragma unroll
-          for (int c = 0; c < 64; c += 2) mx = fmaxf(mx, fmaxf(__uint_as_float(s[c]), __uint_as_float(s[c + 1])));
+        for (int c = 0; c < kKT; c += 2) {
+          m0 = fmaxf(m0, __uint_as_float(s[c]));
+          m1 = fmaxf(m1, __uint_as_float(s[c + 1]));
         }
+        mx = fmaxf(m0, m1);
       }
       const float m_new = fmaxf(m_run, mx);
       const bool need = (m_new - m_run) * sl2 > 8.0f;  // always true on the first tile
@@ -340,64 +375,68 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       }
       if (j > 0) {
         // PV(j-1) has completed (the commit behind S(j) covers it); wait formally so the
-        // O rescale and the P overwrite below are ordered after it
+        // P overwrite and the O rescale below are ordered after it
         if (!mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status, 232 + t)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(o_col + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(o_col + c * 32, o);
-          }
-          tmem_wait_st();
-        }
       }
       l_run *= alpha;
       const float neg = -m_run * sl2;
       const uint64_t negx2 = f2_pack(neg, neg);
-      float lsum0 = 0.f, lsum1 = 0.f;
-      // pass 2: exponentials, row sum, bf16 P into shared memory (128-byte swizzle)
+      uint64_t lsum2 = 0;  // (0.f, 0.f)
+      // exponentials, row sum, bf16 P into shared memory (128-byte swizzle).  In unmasked
+      // tiles two of every eight exponentials run on the FMA pipe (exp2_poly2) so the
+      // MUFU unit is not the only one doing softmax work.
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t s[64];
-        tmem_ld32(s_col + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-        tmem_ld32(s_col + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
-        tmem_wait_ld();
+      for (int ch = 0; ch < kKT / 8; ++ch) {
+        float e8[8];
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          float e8[8];
-#pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            const int c = ch * 8 + e;
-            uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2x2, negx2);
+        for (int e = 0; e < 8; e += 2) {
+          const int c = ch * 8 + e;
+          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2x2, negx2);
+          uint64_t e2;
+          if (e == 6 && !masked) {
+            e2 = exp2_poly2(x2);
+          } else {
             float x0, x1;
             f2_unpack(x2, x0, x1);
             if (masked) {
-              if (half * 64 + c >= valid) x0 = -INFINITY;
-              if (half * 64 + c + 1 >= valid) x1 = -INFINITY;
+              if (c >= valid) x0 = -INFINITY;
+              if (c + 1 >= valid) x1 = -INFINITY;
             }
-            e8[e] = ex2_approx(x0);
-            e8[e + 1] = ex2_approx(x1);
-            lsum0 += e8[e];
-            lsum1 += e8[e + 1];
+            e2 = f2_pack(ex2_approx(x0), ex2_approx(x1));
           }
-          uint4 pk;
-          pk.x = pack_bf16x2(e8[0], e8[1]);
-          pk.y = pack_bf16x2(e8[2], e8[3]);
-          pk.z = pack_bf16x2(e8[4], e8[5]);
-          pk.w = pack_bf16x2(e8[6], e8[7]);
-          const int phys = ch ^ (row & 7);
-          *reinterpret_cast<uint4*>(prow + half * (kQT * 128) + phys * 16) = pk;
+          lsum2 = f2_fma(e2, kOne2, lsum2);
+          f2_unpack(e2, e8[e], e8[e + 1]);
         }
+        uint4 pk;
+        pk.x = pack_bf16x2(e8[0], e8[1]);
+        pk.y = pack_bf16x2(e8[2], e8[3]);
+        pk.z = pack_bf16x2(e8[4], e8[5]);
+        pk.w = pack_bf16x2(e8[6], e8[7]);
+        const int half = ch >> 3;
+        const int phys = (ch & 7) ^ (row & 7);
+        *reinterpret_cast<uint4*>(prow + half * (kQT * 128) + phys * 16) = pk;
       }
-      l_run += lsum0 + lsum1;
+      float ls0, ls1;
+      f2_unpack(lsum2, ls0, ls1);
+      l_run += ls0 + ls1;
+      // O rescale after the exponentials: the S row is dead by now, so the O chunks do not
+      // add to the peak register use; PV(j) only starts after p_full below
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_col + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(o_col + c * 32, o);
+        }
+        tmem_wait_st();
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[t]);

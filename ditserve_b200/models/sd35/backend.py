@@ -78,10 +78,26 @@ class SD35Backend(Backend):
             self.release(dict(state_id=s))
         return dict(results=out)
 
+    def _vae(self):
+        if getattr(self, "_decoder", None) is None:
+            from .vae import SD35VAEDecoder
+            dtype = torch.bfloat16 if self.device.type == "cuda" else torch.float32
+            chans = tuple(self.config.get("vae_channels", (128, 256, 512, 512)))
+            self._decoder = SD35VAEDecoder.random_init(device=self.device, dtype=dtype,
+                                                       seed=int(self.config.get("seed", 0)), channels=chans)
+        return self._decoder
+
     def finish(self, request):
         st = self.state(request)
         if not st.done:
             raise ValueError("request is not complete")
+        if request.get("decode", self.config.get("decode_images", False)):
+            lat = st.latents if st.latents.dim() == 4 else st.latents[None]
+            image = self._vae().decode(lat)
+            self._sync()
+            art = self.persist(image.float(), request)
+            return dict(state_id=request["state_id"], artifact=art, value=art.get("array_sha256"),
+                        shape=list(image.shape))
         art = self.persist(st.latents.float(), request)
         return dict(state_id=request["state_id"], artifact=art, value=art.get("array_sha256"))
 

@@ -4,7 +4,8 @@
     torchrun --nproc-per-node N -m ditserve_b200.utils.calibrate --merge profile.json --out profile.json
 
 Single-GPU run: device-timed step of every video class at SP1 (both CFG branches), the
-SD3.5 classes alone and as continuous batches (batch_step_ms), and the Wan VAE decode.
+SD3.5 classes alone and as continuous batches (batch_step_ms) with their 2-D VAE decode,
+and the Wan VAE decode.
 Multi-GPU run: the step of each video class on the default CFG x Ulysses form of N GPUs
 (fused path), merged into the class's measured ``forms`` table.  Forms that were not
 measured are priced by the analytical model from step_compute_ms.  Random weights of the
@@ -107,7 +108,11 @@ def main():
                 for b in (1, 2, 4, 8):
                     sts = [eng.prepare(dict(height=res, width=res, steps=1000, seed=i)) for i in range(b)]
                     table[str(b)] = round(_time(lambda: eng.advance_batch(sts), iters=3, warmup=1), 2)
-                decode = 60.0 if res == 512 else 200.0  # SD3.5 2-D VAE decode estimate
+                from ..models.sd35.vae import SD35VAEDecoder
+                if "vae" not in locals():
+                    vae = SD35VAEDecoder.random_init(device=dev, dtype=torch.bfloat16, seed=1)
+                zl = torch.randn(1, 16, res // 8, res // 8, device=dev, dtype=torch.bfloat16)
+                decode = round(_time(lambda: vae.decode(zl), iters=3, warmup=1), 1)  # measured 2-D VAE decode
                 classes[name] = dict(kind="image", steps=28, tokens=(res // 16) ** 2, step_ms=table["1"],
                                      service_ms=round(28 * table["1"] + decode, 1), decode_ms=decode,
                                      batch_step_ms=table)

@@ -61,3 +61,26 @@ def test_sd35_block_export_import(tmp_path):
     b.advance(dict(id=6, state_id="i", steps=2))
     import torch
     assert torch.equal(a.states["i"].latents, b.states["i"].latents)
+
+
+def test_sd35_vae_decoder_layout_and_finish(tmp_path):
+    import torch
+    from ditserve_b200.models.sd35.backend import SD35Backend
+    from ditserve_b200.models.sd35.vae import SD35VAEDecoder
+    full = SD35VAEDecoder()
+    keys = set(full.state_dict())
+    for k in ("decoder.conv_in.weight", "decoder.mid_block.attentions.0.to_q.weight",
+              "decoder.mid_block.attentions.0.to_out.0.bias", "decoder.mid_block.resnets.1.conv2.weight",
+              "decoder.up_blocks.0.upsamplers.0.conv.weight", "decoder.up_blocks.2.resnets.0.conv_shortcut.weight",
+              "decoder.up_blocks.3.resnets.2.norm2.weight", "decoder.conv_norm_out.weight", "decoder.conv_out.bias"):
+        assert k in keys, k
+    assert "decoder.up_blocks.3.upsamplers.0.conv.weight" not in keys
+    vae = SD35VAEDecoder.random_init(dtype=torch.float32, channels=(32, 32, 64, 64))
+    img = vae.decode(torch.randn(1, 16, 8, 8))
+    assert img.shape == (1, 3, 64, 64) and img.abs().max() <= 1
+    b = SD35Backend({"model": "sd3.5-tiny", "device": "cpu", "transfer_dir": str(tmp_path),
+                     "vae_channels": [32, 32, 64, 64], "decode_images": True})
+    b.prepare(dict(id=1, state_id="i", spec=dict(height=64, width=64, steps=1, seed=2)))
+    b.advance(dict(id=2, state_id="i", steps=1))
+    out = b.finish(dict(id=3, state_id="i", output_mode="digest"))
+    assert out["shape"] == [1, 3, 64, 64]

@@ -36,6 +36,8 @@ class WanSpec:
     text_len: int | None = None
     prompt: str = ""
     negative_prompt: str = ""
+    # approximate mode (opt-in): late-step CFG folding {"warm_frac", "threshold", "fold_span"}
+    cfg_fold: dict | None = None
 
     @classmethod
     def normalize(cls, raw: dict) -> "WanSpec":
@@ -84,6 +86,7 @@ class WanRequestState:
     packets: dict = field(default_factory=dict)
     metrics: dict = field(default_factory=dict)
     layout_key: tuple | None = None  # layout the current (partial) step runs under
+    fold: object | None = None       # CFGFolding state in approximate mode (not snapshotted)
 
     @property
     def done(self) -> bool:
@@ -142,9 +145,13 @@ class WanEngine:
         if negative is None and spec.guidance > 1.0:
             negative = synthetic_text(spec.seed, L, self.cfg.text_dim, 1)
         sched = UniPCFlowScheduler(spec.steps, spec.flow_shift or self.cfg.flow_shift)
-        return WanRequestState(spec=spec, latents=latents, scheduler=sched,
-                               context=context.to(self.device, self.dtype),
-                               negative=None if negative is None else negative.to(self.device, self.dtype))
+        st = WanRequestState(spec=spec, latents=latents, scheduler=sched,
+                             context=context.to(self.device, self.dtype),
+                             negative=None if negative is None else negative.to(self.device, self.dtype))
+        if spec.cfg_fold is not None and st.negative is not None:
+            from ..approx import CFGFolding
+            st.fold = CFGFolding(spec.steps, **spec.cfg_fold)
+        return st
 
     def branches(self, st: WanRequestState) -> list[int]:
         """CFG branches this rank computes: [0, 1] locally, [cfg_rank] under CFG parallelism."""
@@ -152,6 +159,8 @@ class WanEngine:
             return [0]
         if self.cfg_plan.cfg_size == 2:
             return [self.cfg_plan.cfg_rank]
+        if st.fold is not None and st.fold.fold_now(st.step):
+            return [0]  # folded step: the conditional branch only
         return [0, 1]
 
     def _inputs(self, st: WanRequestState):
@@ -171,6 +180,13 @@ class WanEngine:
     def _split(self, st, br, pred):
         if st.negative is None:
             return pred[0], None
+        if st.fold is not None and self.cfg_plan.cfg_size != 2:
+            g = st.spec.guidance
+            if br == [0]:
+                # v = cond + (g-1) d with the last measured d: pass uncond' = cond - d
+                st.fold.combine(st.step, g, pred[0], None)
+                return pred[0], (pred[0].float() - st.fold.delta.view_as(pred[0])).to(pred[0].dtype)
+            st.fold.combine(st.step, g, pred[0], pred[1])
         if len(br) == 2:
             return pred[0], pred[1]
         theirs = self.cfg_plan.exchange(pred[0])

@@ -84,3 +84,23 @@ def test_sd35_block_cache_reuse():
     again = m.forward_packed(lat, [499.0], ctx, pooled, cache=cache)[0]
     assert cache.skipped_blocks == layers - 2
     assert torch.isfinite(again).all()
+
+
+def test_wan_engine_cfg_folding_skips_uncond_branch():
+    import torch
+    from ditserve_b200.models.wan.runtime import WanEngine
+    e = WanEngine("wan-tiny", device="cpu", dtype=torch.float32)
+    base = dict(model="wan-tiny", height=64, width=64, frames=5, steps=6, seed=3, guidance=5.0)
+    exact = e.run(e.prepare(base))
+    st = e.prepare(dict(base, cfg_fold={"warm_frac": 0.0, "threshold": 10.0, "fold_span": 1}))
+    calls = []
+    orig = e.model.begin
+
+    def spy(lat, t, ctx, pctx=None):
+        calls.append(lat.shape[0])
+        return orig(lat, t, ctx, pctx)
+    e.model.begin = spy
+    e.run(st)
+    assert st.fold.folded_steps >= 2 and 1 in calls       # some steps ran the conditional branch only
+    rel = ((st.latents - exact.latents).norm() / exact.latents.norm()).item()
+    assert torch.isfinite(st.latents).all() and rel < 1.0

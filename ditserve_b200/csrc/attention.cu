@@ -100,38 +100,6 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   return r;
 }
 
-// (x0, x1) -> (2^x0, 2^x1) on the FMA pipe, for x <= 0: Cody-Waite split x = j + f with
-// j = rint(x) (magic-number rounding, |f| <= 1/2), 2^f by a cubic whose coefficients were
-// fitted here for minimum relative error on [-1/2, 1/2] (Lawson's iteratively reweighted
-// least squares; max relative error 7.5e-5, below bf16's half ulp of 2^-9), and 2^j added
-// to the exponent field.  x is clamped at -125 so the result stays a normal float (the
-// clamped terms, < 2^-125, vanish next to the row maximum's 1).
-constexpr float kExpC0 = 0.9999280571937561f;
-constexpr float kExpC1 = 0.6932609677314758f;
-constexpr float kExpC2 = 0.24261100590229034f;
-constexpr float kExpC3 = 0.055171530693769455f;
-constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
-__device__ __forceinline__ uint64_t f2_const(float v) { return f2_pack(v, v); }
-#define kOne2 f2_const(1.0f)
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
-  float x0, x1;
-  f2_unpack(x2, x0, x1);
-  const uint64_t xc = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
-  const uint64_t t = f2_fma(xc, kOne2, f2_const(kRoundMagic));     // rint(x) in the low mantissa bits
-  const uint64_t jr = f2_fma(t, kOne2, f2_const(-kRoundMagic));    // rint(x) as a float
-  const uint64_t fr = f2_fma(jr, f2_const(-1.0f), xc);              // f = x - rint(x)
-  uint64_t pp = f2_fma(f2_const(kExpC3), fr, f2_const(kExpC2));
-  pp = f2_fma(pp, fr, f2_const(kExpC1));
-  pp = f2_fma(pp, fr, f2_const(kExpC0));
-  float p0, p1, t0, t1;
-  f2_unpack(pp, p0, p1);
-  f2_unpack(t, t0, t1);
-  // (bits(t) << 23) == rint(x) << 23: the magic number's low nine bits are zero
-  const float e0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  const float e1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-  return f2_pack(e0, e1);
-}
-
 template <int D>
 __global__ void __launch_bounds__(kAttn2Threads, 1)
     attention2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ KvMaps kv,
@@ -358,13 +326,15 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         for (int c = 0; c < kKT; ++c)
           if (c < valid) mx = fmaxf(mx, __uint_as_float(s[c]));
       } else {
-        float m0 = -INFINITY, m1 = -INFINITY;
+        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < kKT; c += 2) {
+        for (int c = 0; c < kKT; c += 4) {  // four independent chains
           m0 = fmaxf(m0, __uint_as_float(s[c]));
           m1 = fmaxf(m1, __uint_as_float(s[c + 1]));
+          m2 = fmaxf(m2, __uint_as_float(s[c + 2]));
+          m3 = fmaxf(m3, __uint_as_float(s[c + 3]));
         }
-        mx = fmaxf(m0, m1);
+        mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
       }
       const float m_new = fmaxf(m_run, mx);
       const bool need = (m_new - m_run) * sl2 > 8.0f;  // always true on the first tile
@@ -385,32 +355,12 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       l_run *= alpha;
       const float neg = -m_run * sl2;
       const uint64_t negx2 = f2_pack(neg, neg);
-      uint64_t lsum2 = 0;  // (0.f, 0.f)
-      // exponentials, row sum, bf16 P into shared memory (128-byte swizzle).  In unmasked
-      // tiles two of every eight exponentials run on the FMA pipe (exp2_poly2) so the
-      // MUFU unit is not the only one doing softmax work.
-#pragma unroll
-      for (int ch = 0; ch < kKT / 8; ++ch) {
-        float e8[8];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const int c = ch * 8 + e;
-          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2x2, negx2);
-          uint64_t e2;
-          if (e == 6 && !masked) {
-            e2 = exp2_poly2(x2);
-          } else {
-            float x0, x1;
-            f2_unpack(x2, x0, x1);
-            if (masked) {
-              if (c >= valid) x0 = -INFINITY;
-              if (c + 1 >= valid) x1 = -INFINITY;
-            }
-            e2 = f2_pack(ex2_approx(x0), ex2_approx(x1));
-          }
-          lsum2 = f2_fma(e2, kOne2, lsum2);
-          f2_unpack(e2, e8[e], e8[e + 1]);
-        }
+      float lsum0 = 0.f, lsum1 = 0.f;
+      // exponentials, row sum, bf16 P into shared memory (128-byte swizzle); masked tiles
+      // (a segment's last) take their own loop so the common tile carries no column tests.
+      // (Moving a quarter or half of the exponentials to an FMA-pipe polynomial measured
+      // 6-13 % slower than all-MUFU here, so every exponential uses ex2.approx.)
+      auto p_chunk = [&](int ch, float (&e8)[8]) {
         uint4 pk;
         pk.x = pack_bf16x2(e8[0], e8[1]);
         pk.y = pack_bf16x2(e8[2], e8[3]);
@@ -419,10 +369,45 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         const int half = ch >> 3;
         const int phys = (ch & 7) ^ (row & 7);
         *reinterpret_cast<uint4*>(prow + half * (kQT * 128) + phys * 16) = pk;
+      };
+      if (masked) {
+#pragma unroll
+        for (int ch = 0; ch < kKT / 8; ++ch) {
+          float e8[8];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            const int c = ch * 8 + e;
+            const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2x2, negx2);
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            if (c >= valid) x0 = -INFINITY;
+            if (c + 1 >= valid) x1 = -INFINITY;
+            e8[e] = ex2_approx(x0);
+            e8[e + 1] = ex2_approx(x1);
+            lsum0 += e8[e];
+            lsum1 += e8[e + 1];
+          }
+          p_chunk(ch, e8);
+        }
+      } else {
+#pragma unroll
+        for (int ch = 0; ch < kKT / 8; ++ch) {
+          float e8[8];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            const int c = ch * 8 + e;
+            const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2x2, negx2);
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            e8[e] = ex2_approx(x0);
+            e8[e + 1] = ex2_approx(x1);
+            lsum0 += e8[e];
+            lsum1 += e8[e + 1];
+          }
+          p_chunk(ch, e8);
+        }
       }
-      float ls0, ls1;
-      f2_unpack(lsum2, ls0, ls1);
-      l_run += ls0 + ls1;
+      l_run += lsum0 + lsum1;
       // O rescale after the exponentials: the S row is dead by now, so the O chunks do not
       // add to the peak register use; PV(j) only starts after p_full below
       if (j > 0 && __any_sync(0xffffffffu, need)) {

@@ -52,7 +52,7 @@ def main():
     ap.add_argument("--json", default=None)
     ap.add_argument("--tokens", type=int, default=32760)
     ap.add_argument("--batch", type=int, default=2)
-    ap.add_argument("--only", default=None, help="'fused': only the peer-memory kernels on a one-member group")
+    ap.add_argument("--only", default=None, help="'fused': only the peer-memory kernels on a one-member group; 'attention': self-attention only")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     tflops_peak, hbm_peak, src = peaks()
@@ -74,6 +74,15 @@ def main():
         print(json.dumps(r))
 
     torch.manual_seed(0)
+    if args.only == "attention":
+        qkv = torch.randn(M, 3 * D, device=dev).bfloat16()
+        q, k, v = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
+        o = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
+        ms = timeit(lambda: ops.attention(q.view(B, S, D), k.view(B, S, D), v.view(B, S, D), H, out=o), iters=5)
+        row("self_attention", ms, flops=4.0 * B * H * S * S * 128, impl="ours")
+        if args.json:
+            json.dump(res, open(args.json, "w"), indent=1)
+        return
     if args.only == "fused":
         fused_rows(row, timeit, dev, S, B, D, H, flush)
         if args.json:

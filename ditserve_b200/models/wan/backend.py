@@ -115,17 +115,19 @@ class WanBackend(Backend):
             from .async_decode import AsyncDecoder
             from .vae import WanVAEDecoder
             dtype = torch.bfloat16 if self.device.type == "cuda" else torch.float32
-            vae = WanVAEDecoder.random_init(device=self.device, dtype=dtype, seed=int(self.config.get("seed", 0)))
+            variant = "wan2.2" if self.engine.cfg.in_channels == 48 else "wan2.1"
+            vae = WanVAEDecoder.random_init(device=self.device, dtype=dtype, seed=int(self.config.get("seed", 0)),
+                                            variant=variant)
             self._decoder = AsyncDecoder(vae, self.device)
         return self._decoder
 
     def decode_start(self, request):
-        """Decode a finished request's latent on the side stream (VAE, Wan2.1 layout)."""
+        """Decode a finished request's latent on the side stream (Wan2.1 or Wan2.2 VAE)."""
         st = self.state(request)
         if not st.done:
             raise ValueError("decode requires a completed state")
-        if self.engine.cfg.in_channels != 16:
-            raise ValueError("this backend's VAE decodes 16-channel (Wan2.1) latents")
+        if self.engine.cfg.in_channels not in (16, 48):
+            raise ValueError("no VAE for this latent width")
         dec = self._async_decoder()
         ticket = dec.start(st.latents, chunked=bool(request.get("chunked", False)))
         self.decodes[ticket] = request["state_id"]

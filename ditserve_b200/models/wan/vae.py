@@ -1,4 +1,6 @@
-"""Wan causal 3-D VAE decoder (Wan2.1 layout: base 96, z 16, mults 1/2/4/4, 2 res blocks).
+"""Wan causal 3-D VAE decoders: Wan2.1 (base 96, z 16, mults 1/2/4/4, 2 res blocks, 8x
+spatial) and Wan2.2-TI2V (residual up blocks with duplicate-upsampling shortcuts, decoder
+base 256, z 48, 12 output channels un-patchified 2x2 into RGB: 16x spatial).
 
 Parameter names follow diffusers ``AutoencoderKLWan`` (``post_quant_conv``, ``decoder.conv_in``,
 ``decoder.mid_block.{resnets,attentions}``, ``decoder.up_blocks.i.{resnets,upsamplers}``,
@@ -141,13 +143,14 @@ class AttentionBlock(nn.Module):
 
 
 class Resample(nn.Module):
-    """Nearest x2 spatial upsampling + 3x3 conv (to dim/2); ``upsample3d`` also doubles time."""
+    """Nearest x2 spatial upsampling + 3x3 conv (to dim/2, or ``out_dim``); ``upsample3d``
+    also doubles time."""
 
-    def __init__(self, dim, mode):
+    def __init__(self, dim, mode, out_dim=None):
         super().__init__()
         self.mode = mode
         self.resample = nn.Sequential(nn.Upsample(scale_factor=(2.0, 2.0), mode="nearest-exact"),
-                                      nn.Conv2d(dim, dim // 2, 3, padding=1))
+                                      nn.Conv2d(dim, out_dim or dim // 2, 3, padding=1))
         if mode == "upsample3d":
             self.time_conv = CausalConv3d(dim, dim * 2, (3, 1, 1), padding=(1, 0, 0))
 
@@ -213,32 +216,85 @@ class UpBlock(nn.Module):
         return x
 
 
+class DupUp3D(nn.Module):
+    """Parameter-free shortcut of a Wan2.2 up block: channels repeated, then moved into
+    time (factor_t) and space (factor_s x factor_s); the first chunk drops the leading
+    duplicated frames (as the causal time upsampler does)."""
+
+    def __init__(self, cin, cout, factor_t, factor_s=1):
+        super().__init__()
+        self.cout, self.ft, self.fs = cout, factor_t, factor_s
+        factor = factor_t * factor_s * factor_s
+        if (cout * factor) % cin:
+            raise ValueError("DupUp3D: cout * factor must be a multiple of cin")
+        self.repeats = cout * factor // cin
+
+    def forward(self, x, first_chunk=False):
+        b, _, t, h, w = x.shape
+        x = x.repeat_interleave(self.repeats, dim=1)
+        x = x.view(b, self.cout, self.ft, self.fs, self.fs, t, h, w)
+        x = x.permute(0, 1, 5, 2, 6, 3, 7, 4).reshape(b, self.cout, t * self.ft, h * self.fs, w * self.fs)
+        return x[:, :, self.ft - 1:] if first_chunk else x
+
+
+class ResidualUpBlock(nn.Module):
+    """Wan2.2 up block: resnets, optional up-sampler to the same width, plus a DupUp3D
+    shortcut of the block input."""
+
+    def __init__(self, cin, cout, blocks, temporal_up, up):
+        super().__init__()
+        self.avg_shortcut = DupUp3D(cin, cout, 2 if temporal_up else 1, 2) if up else None
+        res = []
+        c = cin
+        for _ in range(blocks + 1):
+            res.append(ResidualBlock(c, cout))
+            c = cout
+        self.resnets = nn.ModuleList(res)
+        self.upsampler = Resample(cout, "upsample3d" if temporal_up else "upsample2d", out_dim=cout) if up else None
+
+    def forward(self, x, cache, idx, halo, first_chunk=False):
+        x_in = x
+        for r in self.resnets:
+            x = r(x, cache, idx, halo)
+        if self.upsampler is not None:
+            x = self.upsampler(x, cache, idx, halo)
+        if self.avg_shortcut is not None:
+            x = x + self.avg_shortcut(x_in, first_chunk=first_chunk)
+        return x
+
+
 class Decoder3d(nn.Module):
-    def __init__(self, dim=96, z_dim=16, mult=(1, 2, 4, 4), blocks=2, temporal_up=(True, True, False)):
+    def __init__(self, dim=96, z_dim=16, mult=(1, 2, 4, 4), blocks=2, temporal_up=(True, True, False),
+                 out_channels=3, residual=False):
         super().__init__()
         dims = [dim * m for m in [mult[-1]] + list(mult[::-1])]
+        self.residual = residual
         self.conv_in = CausalConv3d(z_dim, dims[0], 3, padding=1)
         self.mid_block = MidBlock(dims[0])
         ups = []
         for i, (cin, cout) in enumerate(zip(dims[:-1], dims[1:])):
+            up = i != len(mult) - 1
+            if residual:
+                ups.append(ResidualUpBlock(cin, cout, blocks, temporal_up[i] if up else False, up))
+                continue
             if i > 0:
                 cin //= 2
             mode = None
-            if i != len(mult) - 1:
+            if up:
                 mode = "upsample3d" if temporal_up[i] else "upsample2d"
             ups.append(UpBlock(cin, cout, blocks, mode))
         self.up_blocks = nn.ModuleList(ups)
         self.norm_out = RMSNormC(dims[-1], images=False)
-        self.conv_out = CausalConv3d(dims[-1], 3, 3, padding=1)
+        self.conv_out = CausalConv3d(dims[-1], out_channels, 3, padding=1)
 
-    def forward(self, x, cache, idx, halo):
+    def forward(self, x, cache, idx, halo, first_chunk=False):
         new = x[:, :, -CACHE_T:].clone()
         x = self.conv_in(x, cache[idx[0]], halo)
         cache[idx[0]] = new
         idx[0] += 1
         x = self.mid_block(x, cache, idx, halo)
         for up in self.up_blocks:
-            x = up(x, cache, idx, halo)
+            x = up(x, cache, idx, halo, first_chunk) if self.residual else up(x, cache, idx, halo)
         x = F.silu(self.norm_out(x))
         new = x[:, :, -CACHE_T:].clone()
         old = cache[idx[0]]
@@ -251,37 +307,62 @@ class Decoder3d(nn.Module):
 
 
 class WanVAEDecoder(nn.Module):
-    def __init__(self, z_dim=16, base=96):
+    """``variant``: "wan2.1" (z 16, base 96, 8x spatial) or "wan2.2" (z 48, decoder base 256,
+    residual up blocks, 12 channels un-patchified 2x2: 16x spatial).  Latent statistics
+    default to the Wan2.1 values, or zero mean / unit std for Wan2.2 until a checkpoint's
+    config provides them (``set_latent_stats``)."""
+
+    VARIANTS = {"wan2.1": dict(z_dim=16, base=96, residual=False, patch=1),
+                "wan2.2": dict(z_dim=48, base=256, residual=True, patch=2)}
+
+    def __init__(self, z_dim=16, base=96, residual=False, patch=1):
         super().__init__()
-        self.z_dim = z_dim
+        self.z_dim, self.patch = z_dim, patch
         self.post_quant_conv = CausalConv3d(z_dim, z_dim, 1)
-        self.decoder = Decoder3d(base, z_dim)
-        self.register_buffer("latents_mean", torch.tensor(WAN21_LATENTS_MEAN).view(1, z_dim, 1, 1, 1))
-        self.register_buffer("latents_std", torch.tensor(WAN21_LATENTS_STD).view(1, z_dim, 1, 1, 1))
+        self.decoder = Decoder3d(base, z_dim, out_channels=3 * patch * patch, residual=residual)
+        mean = WAN21_LATENTS_MEAN if z_dim == 16 else [0.0] * z_dim
+        std = WAN21_LATENTS_STD if z_dim == 16 else [1.0] * z_dim
+        self.register_buffer("latents_mean", torch.tensor(mean).view(1, z_dim, 1, 1, 1))
+        self.register_buffer("latents_std", torch.tensor(std).view(1, z_dim, 1, 1, 1))
 
     @classmethod
-    def random_init(cls, device="cpu", dtype=torch.bfloat16, seed: int = 0) -> "WanVAEDecoder":
+    def random_init(cls, device="cpu", dtype=torch.bfloat16, seed: int = 0, variant: str = "wan2.1") -> "WanVAEDecoder":
         torch.manual_seed(seed)
-        m = cls().to(device)
+        m = cls(**cls.VARIANTS[variant]).to(device)
         return m.to(dtype).eval()
+
+    def set_latent_stats(self, mean, std):
+        self.latents_mean.copy_(torch.tensor(mean).view_as(self.latents_mean))
+        self.latents_std.copy_(torch.tensor(std).view_as(self.latents_std))
 
     def cache_size(self) -> int:
         return sum(isinstance(m, CausalConv3d) for m in self.decoder.modules())
 
     @torch.inference_mode()
-    def decode_frame(self, z_frame: torch.Tensor, cache: list, halo: Halo | None = None) -> torch.Tensor:
+    def decode_frame(self, z_frame: torch.Tensor, cache: list, halo: Halo | None = None,
+                     first_chunk: bool = False) -> torch.Tensor:
         """Decode one latent frame [B, C, 1, h, w] (already de-normalised), updating ``cache``."""
         halo = halo or Halo()
         x = self.post_quant_conv(z_frame)
         idx = [0]
-        return self.decoder(x, cache, idx, halo)
+        out = self.decoder(x, cache, idx, halo, first_chunk)
+        return self.unpatchify(out)
+
+    def unpatchify(self, x: torch.Tensor) -> torch.Tensor:
+        """[B, 3 p p, T, H, W] -> [B, 3, T, H p, W p] (channel = c p p + r p + q; q along H)."""
+        p = self.patch
+        if p == 1:
+            return x
+        b, cpp, t, h, w = x.shape
+        c = cpp // (p * p)
+        return x.view(b, c, p, p, t, h, w).permute(0, 1, 4, 5, 3, 6, 2).reshape(b, c, t, h * p, w * p)
 
     def denormalize(self, z: torch.Tensor) -> torch.Tensor:
         return z * self.latents_std.to(z) + self.latents_mean.to(z)
 
     @torch.inference_mode()
     def decode(self, z: torch.Tensor, halo: Halo | None = None) -> torch.Tensor:
-        """[B, 16, F, h, w] normalised latents -> [B, 3, 1 + 4(F-1), 8h, 8w] in [-1, 1]."""
+        """[B, z, F, h, w] normalised latents -> [B, 3, 1 + 4(F-1), s h, s w] in [-1, 1]."""
         dec = ChunkedDecode(self, z, halo)
         while not dec.done:
             dec.step()
@@ -308,7 +389,7 @@ class ChunkedDecode:
             if self.done:
                 break
             i = self.next
-            out = self.vae.decode_frame(self.z[:, :, i:i + 1], self.cache, self.halo)
+            out = self.vae.decode_frame(self.z[:, :, i:i + 1], self.cache, self.halo, first_chunk=i == 0)
             self.frames.append(out.clamp(-1, 1))
             self.next += 1
         return self

@@ -125,9 +125,19 @@ def main():
             ms = _time(lambda: vae.decode(z), iters=1, warmup=1)
             classes["wan21_480p"]["decode_ms"] = round(ms, 1)
             classes["wan21_480p"]["decode_chunks"] = 4
-            classes.get("wan22_720p", {}).setdefault("decode_ms", round(ms * 2.2, 1))
-            classes.get("wan22_720p", {}).setdefault("decode_chunks", 4)
             print(json.dumps({"class": "wan_vae_480p", "decode_ms": round(ms, 1)}), flush=True)
+            del vae
+            torch.cuda.empty_cache()
+        if "wan22_720p" in classes:
+            from ..models.wan.vae import WanVAEDecoder
+            vae = WanVAEDecoder.random_init(device=dev, dtype=torch.bfloat16, seed=1, variant="wan2.2")
+            z = torch.randn(1, 48, 31, 44, 80, device=dev, dtype=torch.bfloat16)  # 704x1280, 121 frames
+            ms = _time(lambda: vae.decode(z), iters=1, warmup=1)
+            classes["wan22_720p"]["decode_ms"] = round(ms, 1)
+            classes["wan22_720p"]["decode_chunks"] = 4
+            print(json.dumps({"class": "wan22_vae_720p", "decode_ms": round(ms, 1)}), flush=True)
+            del vae
+            torch.cuda.empty_cache()
     else:
         from ..parallel.layout import FixedLayout, default_form
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)

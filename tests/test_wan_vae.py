@@ -56,3 +56,27 @@ def test_patch_parallel_decode_equals_single_rank():
     mp.spawn(_worker, args=(2, port, out), nprocs=2, join=True)
     ref = _vae().decode(_z())
     torch.testing.assert_close(out["pp"], ref, rtol=1e-4, atol=1e-4)
+
+
+def test_wan22_vae_residual_decoder_chunked_equals_whole():
+    import torch
+    from ditserve_b200.models.wan.vae import ChunkedDecode, DupUp3D, WanVAEDecoder
+    m = WanVAEDecoder.random_init(dtype=torch.float32, variant="wan2.2")
+    keys = set(m.state_dict())
+    for k in ("decoder.up_blocks.0.upsampler.time_conv.weight", "decoder.up_blocks.2.upsampler.resample.1.weight",
+              "decoder.conv_out.weight", "post_quant_conv.weight", "decoder.mid_block.attentions.0.to_qkv.weight"):
+        assert k in keys, k
+    assert "decoder.up_blocks.3.upsampler.resample.1.weight" not in keys
+    assert m.decoder.conv_out.out_channels == 12
+    g = torch.Generator().manual_seed(0)
+    z = torch.randn(1, 48, 3, 2, 3, generator=g)
+    whole = m.decode(z)
+    assert whole.shape == (1, 3, 9, 32, 48)
+    dec = ChunkedDecode(m, z)
+    dec.step(1)
+    dec.step(2)
+    assert torch.equal(dec.result(), whole)
+    # the shortcut's first chunk keeps one frame per latent frame, later chunks double time
+    d = DupUp3D(8, 4, 2, 2)
+    x = torch.randn(1, 8, 1, 2, 2)
+    assert d(x).shape == (1, 4, 2, 4, 4) and d(x, first_chunk=True).shape == (1, 4, 1, 4, 4)

@@ -225,6 +225,9 @@ struct Live {
   bool prepared = false;
   double quantum_started = 0;
   bool rung = false;
+  int decode_done = 0;       // decoded chunks (planner unit)
+  std::string decode_ticket; // worker ticket of a chunked decode in progress
+  int decode_gpu = -1;       // the worker that holds it
 };
 
 Json ints_json(const std::vector<int>& v) {
@@ -275,6 +278,9 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     throw std::invalid_argument("sp_transport collective needs distributed: true");
   const std::string path = phase.str("collectives", "fused");
   const int batch_quantum = static_cast<int>(phase.integer("batch_quantum_steps", 4));
+  // decode: finished videos run the VAE in chunked quanta (decode_start / decode_poll) and
+  // images decode in finish; off: finish persists the final latents only
+  const bool decode = phase.flag("decode", false);
   const size_t trace_limit = static_cast<size_t>(phase.integer("trace_limit", 2000));
   auto is_gpu = [](const Json& d) { return d.at("backend").as_string() != "mock"; };
 
@@ -447,6 +453,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     Json f = Json::object();
     f["state_id"] = id;
     f["output_mode"] = "digest";
+    if (image && decode) f["decode"] = true;
     Json art = W(exec.front(), image)->call("finish", f);
     Json rel = Json::object();
     rel["state_id"] = id;
@@ -496,6 +503,11 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
           if (prog.is_object()) {
             l.steps_done = static_cast<int>(prog.integer("step", l.steps_done));
             l.blocks_done = static_cast<int>(prog.integer("block", 0));
+          }
+          if (m->contains("decode_ticket")) {
+            l.decode_ticket = m->at("decode_ticket").as_string();
+            l.decode_done = static_cast<int>(m->integer("decode_done", l.decode_done));
+            l.decode_gpu = static_cast<int>(m->integer("decode_gpu", -1));
           }
           if (m->flag("finished", false)) {
             l.status = "done";
@@ -558,6 +570,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
       q["steps_total"] = l.steps_total;
       q["steps_done"] = l.steps_done;
       q["blocks_done"] = l.blocks_done;
+      q["decode_done"] = l.decode_done;
       q["group"] = ints_json(l.status == "running" ? l.group : l.last_group);
       if (!l.form.empty()) q["form"] = l.form;
       // a started image keeps its GPU: its state lives in that GPU's image worker
@@ -603,6 +616,9 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
           form = l.last_form;
           ++held_mid_step;
         }
+        // a chunked decode continues on the worker that holds it
+        if (!image && !l.decode_ticket.empty() && l.decode_gpu >= 0 && grp != std::vector<int>{l.decode_gpu})
+          grp = std::vector<int>{l.decode_gpu};
         bool free = true;
         for (int g : grp) free = free && !busy[g];
         if (!free) continue;
@@ -681,6 +697,14 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
         for (Live* m : members) ids.push_back(m->id);
         const int degree = static_cast<int>(grp.size());
         const bool batch = a.contains("batch") || qs == "continuous_batch";
+        const std::string ticket = l.decode_ticket;
+        const int decoded = l.decode_done;
+        const int chunks = std::max(1, cost.decode_chunks(l.klass));
+        const int chunk_quantum = static_cast<int>(a.integer("decode_frames", chunks - decoded));
+        const Json lspec = l.row.at("spec");
+        const int frames = static_cast<int>(lspec.integer("frames", 81));
+        const int latent_frames = (frames - 1) / 4 + 1;
+        const int frames_per_chunk = (latent_frames + chunks - 1) / chunks;
         tasks.push_back({ids, std::async(std::launch::async, [=, &ensure_state, &finish_release, &member, &W,
                                                                &bells]() -> Json {
                            for (const auto& p : places) ensure_state(p);
@@ -720,7 +744,41 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
                              return out;
                            }
                            if (qs == "finish") {
-                             ms.push_back(member(ids[0], Json(), true, finish_release(ids[0], exec, false)));
+                             if (!decode) {
+                               ms.push_back(member(ids[0], Json(), true, finish_release(ids[0], exec, false)));
+                               out["members"] = ms;
+                               return out;
+                             }
+                             Worker* w = W(leader, false);
+                             std::string tk = ticket;
+                             if (tk.empty()) {
+                               Json ds = Json::object();
+                               ds["state_id"] = ids[0];
+                               ds["chunked"] = true;
+                               tk = w->call("decode_start", ds).at("ticket").as_string();
+                             }
+                             Json dp = Json::object();
+                             dp["ticket"] = tk;
+                             dp["frames"] = std::max(1, chunk_quantum) * frames_per_chunk;
+                             dp["output_mode"] = "digest";
+                             if (decoded + chunk_quantum >= chunks) dp["wait"] = true;
+                             Json r = w->call("decode_poll", dp);
+                             if (r.flag("ready", false)) {
+                               Json rel = Json::object();
+                               rel["state_id"] = ids[0];
+                               fan_out(exec, [&](int g) { return W(g, false)->call("release", rel); });
+                               const Json& art = r.get("artifact");
+                               Json digest = art.is_object() && art.contains("array_sha256") ? art.at("array_sha256")
+                                                                                            : r.get("value");
+                               Json m = member(ids[0], Json(), true, digest);
+                               ms.push_back(m);
+                             } else {
+                               Json m = member(ids[0], Json(), false, Json());
+                               m["decode_ticket"] = tk;
+                               m["decode_done"] = std::min(chunks - 1, decoded + std::max(1, chunk_quantum));
+                               m["decode_gpu"] = leader;
+                               ms.push_back(m);
+                             }
                              out["members"] = ms;
                              return out;
                            }

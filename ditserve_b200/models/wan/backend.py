@@ -139,7 +139,9 @@ class WanBackend(Backend):
             raise ValueError("unknown decode ticket")
         dec = self._async_decoder()
         if "chunked" in dec.jobs.get(ticket, {}) and "out" not in dec.jobs[ticket]:
-            dec.advance(ticket, int(request.get("frames", 1)))
+            # a waiting poll finishes the decode whatever frame count it names
+            frames = 1 << 30 if request.get("wait") else int(request.get("frames", 1))
+            dec.advance(ticket, frames)
         if not dec.poll(ticket) and not request.get("wait"):
             return dict(ticket=ticket, ready=False)
         video = dec.result(ticket)

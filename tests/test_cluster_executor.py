@@ -48,11 +48,12 @@ BUDGET = {"limit_gpu_seconds": 3600, "watchdog_seconds": 900, "repair_reserve_gp
 
 def test_mock_cluster_pairs_batches_regroups(controller, tmp_path):
     cfg = {"schema": "ditserve-b200.study.v1", "experiment": "exec-mock",
-           "workers": {"vid": {"backend": "mock", "config": {"options": {"costs": {"step_ms": 15}}}},
+           "workers": {"vid": {"backend": "mock", "config": {"options": {"costs": {"step_ms": 15},
+                                                                          "decode_delay_ms": 20}}},
                        "img": {"backend": "mock", "config": {"options": {"costs": {"step_ms": 5}}}}},
            "budget": BUDGET,
            "phases": [{"id": "cluster", "kind": "cluster", "gpus": 4, "policy": "ditserve", "distributed": True,
-                       "workers": {"video": "vid", "image": "img"},
+                       "workers": {"video": "vid", "image": "img"}, "decode": True,
                        "sp_transport": "export",
                        "options": {"pairing": True, "continuous_batch": 4},
                        "generator": {"count": 12, "seed": 2, "pattern": "poisson", "rate_rps": 40, "classes": [
@@ -80,6 +81,7 @@ def test_wan_tiny_gloo_world_cluster(controller, tmp_path):
            "phases": [{"id": "cluster", "kind": "cluster", "gpus": 2, "policy": "ditserve", "worker": "wan",
                        "distributed": True, "sp_transport": "collective", "collectives": "nccl",
                        "warmup_forms": ["cfg2", "sp2"], "warmup_spec": {"height": 64, "width": 64, "frames": 5},
+                       "decode": True,
                        "dist_port": 29000 + os.getpid() % 1000,
                        "generator": {"count": 3, "seed": 4, "pattern": "poisson", "rate_rps": 50, "classes": [
                            {"weight": 1, "kind": "video", "class": "wan21_480p", "service_ms": 20000,
@@ -93,3 +95,5 @@ def test_wan_tiny_gloo_world_cluster(controller, tmp_path):
     assert last["controller_timing"]["warmup_ms"] > 0
     forms = {t["form"] for t in last["trace"]}
     assert forms & {"cfg2", "sp2"}, forms  # at least one quantum ran on both ranks
+    assert any(t["quantum"] == "finish" for t in last["trace"])  # VAE decode quanta ran
+    assert all(r.get("digest") for r in last["rows"])

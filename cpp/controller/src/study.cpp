@@ -813,7 +813,8 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
                            }
                            for (size_t k = 0; k < ids.size(); ++k) {
                              const Json& prog = k == 0 ? res[0].at("progress") : res[0].at("pair_progress");
-                             const bool done = prog.flag("done", false);
+                             // with decode on, a denoised video waits for its own (chunked) decode quanta
+                             const bool done = prog.flag("done", false) && !decode;
                              ms.push_back(member(ids[k], prog, done, done ? finish_release(ids[k], exec, false) : Json()));
                            }
                            out["members"] = ms;

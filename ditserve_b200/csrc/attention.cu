@@ -326,15 +326,14 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         for (int c = 0; c < kKT; ++c)
           if (c < valid) mx = fmaxf(mx, __uint_as_float(s[c]));
       } else {
-        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+        float mc[8];  // eight independent chains keep the dependent max sequence short
 #pragma unroll
-        for (int c = 0; c < kKT; c += 4) {  // four independent chains
-          m0 = fmaxf(m0, __uint_as_float(s[c]));
-          m1 = fmaxf(m1, __uint_as_float(s[c + 1]));
-          m2 = fmaxf(m2, __uint_as_float(s[c + 2]));
-          m3 = fmaxf(m3, __uint_as_float(s[c + 3]));
-        }
-        mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+        for (int i = 0; i < 8; ++i) mc[i] = __uint_as_float(s[i]);
+#pragma unroll
+        for (int c = 8; c < kKT; c += 8)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mc[i] = fmaxf(mc[i], __uint_as_float(s[c + i]));
+        mx = fmaxf(fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3])), fmaxf(fmaxf(mc[4], mc[5]), fmaxf(mc[6], mc[7])));
       }
       const float m_new = fmaxf(m_run, mx);
       const bool need = (m_new - m_run) * sl2 > 8.0f;  // always true on the first tile
@@ -355,7 +354,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       l_run *= alpha;
       const float neg = -m_run * sl2;
       const uint64_t negx2 = f2_pack(neg, neg);
-      float lsum0 = 0.f, lsum1 = 0.f;
+      float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // per-column-slot partial row sums
       // exponentials, row sum, bf16 P into shared memory (128-byte swizzle); masked tiles
       // (a segment's last) take their own loop so the common tile carries no column tests.
       // (Moving a quarter or half of the exponentials to an FMA-pipe polynomial measured
@@ -384,8 +383,8 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
             if (c + 1 >= valid) x1 = -INFINITY;
             e8[e] = ex2_approx(x0);
             e8[e + 1] = ex2_approx(x1);
-            lsum0 += e8[e];
-            lsum1 += e8[e + 1];
+            ls[e] += e8[e];
+            ls[e + 1] += e8[e + 1];
           }
           p_chunk(ch, e8);
         }
@@ -401,13 +400,13 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
             f2_unpack(x2, x0, x1);
             e8[e] = ex2_approx(x0);
             e8[e + 1] = ex2_approx(x1);
-            lsum0 += e8[e];
-            lsum1 += e8[e + 1];
+            ls[e] += e8[e];
+            ls[e + 1] += e8[e + 1];
           }
           p_chunk(ch, e8);
         }
       }
-      l_run += lsum0 + lsum1;
+      l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
       // O rescale after the exponentials: the S row is dead by now, so the O chunks do not
       // add to the peak register use; PV(j) only starts after p_full below
       if (j > 0 && __any_sync(0xffffffffu, need)) {

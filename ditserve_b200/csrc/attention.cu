@@ -67,9 +67,11 @@ struct AttnParams {
 // While WG1 turns S_A(j) into P_A(j) the tensor core runs S_B(j) / PV_B(j-1), and the
 // other way round, so MUFU work and MMA overlap.  TMEM: S_A [0,128), S_B [128,256),
 // O_A [256, 256+D), O_B [384, 384+D).  Each softmax thread loads its whole 128-column
-// S row from TMEM once, takes the row max, writes bf16 P and only then rescales O (when
-// needed), so the S row and the O chunks are never live together and the 168-register
-// budget of a 384-thread CTA holds without spills.
+// S row from TMEM once, takes the row max, writes bf16 P back into TMEM over the first 64
+// columns of its S (the PV MMA takes P as a tensor-memory A operand, so P never touches
+// shared memory) and only then rescales O (when needed): the S row and the O chunks are
+// never live together and the 168-register budget of a 384-thread CTA holds without
+// spills.  Shared memory holds Q_A, Q_B and two stages each of K and V.
 constexpr int kAttn2Threads = 384;
 
 template <int D>
@@ -78,11 +80,9 @@ struct Attn2Cfg {
   static constexpr int kQBytes = kQT * D * 2;
   static constexpr int kKBytes = kKT * D * 2;
   static constexpr int kVBytes = kKT * D * 2;
-  static constexpr int kPBytes = kQT * kKT * 2;
   static constexpr int KS = 2;
-  static constexpr int VS = D == 64 ? 2 : 1;
-  static constexpr int kSmemBytes =
-      2 * kQBytes + KS * kKBytes + VS * kVBytes + 2 * kPBytes + 1024 /*align*/ + 512 /*barriers*/;
+  static constexpr int VS = 2;
+  static constexpr int kSmemBytes = 2 * kQBytes + KS * kKBytes + VS * kVBytes + 1024 /*align*/ + 512 /*barriers*/;
   static constexpr int kTmemCols = 512;
 };
 
@@ -156,8 +156,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   uint8_t* sQ = smem;                                   // [2][kQBytes]
   uint8_t* sK = sQ + 2 * Cfg::kQBytes;                  // [KS][kKBytes]
   uint8_t* sV = sK + KS * Cfg::kKBytes;                 // [VS][kVBytes]
-  uint8_t* sP = sV + VS * Cfg::kVBytes;                 // [2][kPBytes]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::kPBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + VS * Cfg::kVBytes);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + KS;
@@ -254,13 +253,12 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, 222 + t)) return false;
         tc_fence_after();
         const uint32_t d = tmem_base + 256 + t * 128;
-        const uint32_t p_base = smem_u32(sP + t * Cfg::kPBytes);
+        const uint32_t p_tmem = tmem_base + t * kKT;  // bf16 P packed over the first 64 S columns
         const uint32_t v_base = smem_u32(sV + (j % VS) * Cfg::kVBytes);
 #pragma unroll
         for (int kk = 0; kk < kKT / 16; ++kk) {
-          const uint64_t da = umma_desc_sw128(p_base + (kk >> 2) * (kQT * 128) + (kk & 3) * 32, 16, 1024);
           const uint64_t db = umma_desc_sw128(v_base + kk * (16 * 128), kKT * 128, 1024);
-          umma_bf16_ss(d, da, db, idesc_o, (j | kk) != 0);
+          umma_bf16_ts(d, p_tmem + kk * 8, db, idesc_o, (j | kk) != 0);
         }
         umma_commit(&pv_done[t]);
         return true;
@@ -305,7 +303,6 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = true;
-    uint8_t* prow = sP + t * Cfg::kPBytes + row * 128;
     for (int j = 0; j < n_tiles; ++j) {
       if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.status, 230 + t)) {
         ok = false;
@@ -355,19 +352,20 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       const float neg = -m_run * sl2;
       const uint64_t negx2 = f2_pack(neg, neg);
       float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // per-column-slot partial row sums
-      // exponentials, row sum, bf16 P into shared memory (128-byte swizzle); masked tiles
+      // exponentials, row sum, bf16 P into tensor memory; masked tiles
       // (a segment's last) take their own loop so the common tile carries no column tests.
       // (Moving a quarter or half of the exponentials to an FMA-pipe polynomial measured
       // 6-13 % slower than all-MUFU here, so every exponential uses ex2.approx.)
+      // P goes back into TMEM over the first 64 columns of this tile's S (the S row is in
+      // registers already): 8 packed columns per store, the PV MMA reads it as its A operand
+      uint32_t pk8[8];
       auto p_chunk = [&](int ch, float (&e8)[8]) {
-        uint4 pk;
-        pk.x = pack_bf16x2(e8[0], e8[1]);
-        pk.y = pack_bf16x2(e8[2], e8[3]);
-        pk.z = pack_bf16x2(e8[4], e8[5]);
-        pk.w = pack_bf16x2(e8[6], e8[7]);
-        const int half = ch >> 3;
-        const int phys = (ch & 7) ^ (row & 7);
-        *reinterpret_cast<uint4*>(prow + half * (kQT * 128) + phys * 16) = pk;
+        const int q = (ch & 1) * 4;
+        pk8[q + 0] = pack_bf16x2(e8[0], e8[1]);
+        pk8[q + 1] = pack_bf16x2(e8[2], e8[3]);
+        pk8[q + 2] = pack_bf16x2(e8[4], e8[5]);
+        pk8[q + 3] = pack_bf16x2(e8[6], e8[7]);
+        if (ch & 1) tmem_st8(s_col + (ch >> 1) * 8, pk8);
       };
       if (masked) {
 #pragma unroll
@@ -421,7 +419,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         }
         tmem_wait_st();
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
     }

@@ -545,6 +545,22 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     }
     const auto forms = forms_for(s, cost, r.klass, video_capacity);
     if (forms.empty()) continue;
+    // CFG fission (approximate policies): a video whose next step runs folded (conditional
+    // branch only, the guidance delta reused) continues on the conditional half of its CFG2
+    // group; the unconditional half is free for other work this round
+    if (t.fission && r.j->flag("cfg_fold_eligible", false) && !r.group.empty() && !r.form.empty() &&
+        r.blocks_done == 0) {
+      const Form f = parse_form(r.form);
+      if (f.cfg == 2 && r.group.size() % 2 == 0) {
+        const std::vector<int> half(r.group.begin(), r.group.begin() + r.group.size() / 2);
+        auto grp = pick_group(g, static_cast<int>(half.size()), half, true);
+        if (grp == half) {
+          emit_video(r, Form{1, f.sp, f.ring}, grp, "fission");
+          assignments.at(assignments.size() - 1)["fold"] = true;
+          continue;
+        }
+      }
+    }
     // inside a solver step the request's partial activations live on its group, sharded
     // for its form: it resumes there (or waits), never on other GPUs
     if (r.status == "suspended" && r.blocks_done > 0 && !r.group.empty()) {

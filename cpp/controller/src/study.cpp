@@ -225,6 +225,7 @@ struct Live {
   bool prepared = false;
   double quantum_started = 0;
   bool rung = false;
+  bool fold_eligible = false;  // the worker reports that the next step may run CFG-folded
   int decode_done = 0;       // decoded chunks (planner unit)
   std::string decode_ticket; // worker ticket of a chunked decode in progress
   int decode_gpu = -1;       // the worker that holds it
@@ -503,6 +504,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
           if (prog.is_object()) {
             l.steps_done = static_cast<int>(prog.integer("step", l.steps_done));
             l.blocks_done = static_cast<int>(prog.integer("block", 0));
+            l.fold_eligible = prog.flag("cfg_fold_eligible", false);
           }
           if (m->contains("decode_ticket")) {
             l.decode_ticket = m->at("decode_ticket").as_string();
@@ -571,6 +573,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
       q["steps_done"] = l.steps_done;
       q["blocks_done"] = l.blocks_done;
       q["decode_done"] = l.decode_done;
+      if (l.fold_eligible) q["cfg_fold_eligible"] = true;
       q["group"] = ints_json(l.status == "running" ? l.group : l.last_group);
       if (!l.form.empty()) q["form"] = l.form;
       // a started image keeps its GPU: its state lives in that GPU's image worker

@@ -387,4 +387,21 @@ TEST("near-linear scaling starts videos on their widest efficient form") {
   CHECK(narrow.front().degree() == 2);
 }
 
+TEST("CFG fission runs a fold-eligible video on the conditional half of its group") {
+  ClusterCost c(profile());
+  auto v = suspended("v", "[2,3]", "cfg2", 6, 0);
+  v["cfg_fold_eligible"] = true;
+  auto p = cluster_plan(state(8, {v}), "ditserve-approx", c);
+  const Json* a = find(p, "v");
+  CHECK(a != nullptr);
+  CHECK(a->at("group").size() == 1 && a->at("group")[0].as_int() == 2);
+  CHECK(a->at("form").as_string() == "sp1" && a->at("fold").as_bool());
+  CHECK(a->at("reason").as_string() == "fission");
+  auto q = cluster_plan(state(8, {v}), "ditserve", c);  // exact policy: no fission
+  CHECK(!find(q, "v")->contains("fold"));
+  v["cfg_fold_eligible"] = false;
+  auto r = cluster_plan(state(8, {v}), "ditserve-approx", c);
+  CHECK(!find(r, "v")->contains("fold"));
+}
+
 int main() { return dstest::run_all(); }

@@ -316,7 +316,8 @@ void cfg_step_peer(const at::Tensor& mine, int64_t theirs_off, int64_t role, dou
                    double p_x, double p_x0, double p_v, std::vector<c10::optional<at::Tensor>> p_hist,
                    std::vector<double> p_coef, const c10::optional<at::Tensor>& x0_out,
                    const c10::optional<at::Tensor>& last_out, int64_t rank, const std::vector<int64_t>& bases,
-                   int64_t timeout_ns, int64_t channel, int64_t epoch, const at::Tensor& status) {
+                   int64_t timeout_ns, int64_t channel, int64_t epoch, const at::Tensor& status,
+                   const c10::optional<at::Tensor>& delta_out) {
   TORCH_CHECK(mine.scalar_type() == at::kBFloat16 && mine.is_contiguous() && mine.numel() == sample.numel(),
               "cfg_step_peer: prediction must be contiguous bf16 of the latent size");
   TORCH_CHECK(sample.scalar_type() == at::kFloat && sample.is_contiguous(), "cfg_step_peer: sample fp32");
@@ -343,6 +344,12 @@ void cfg_step_peer(const at::Tensor& mine, int64_t theirs_off, int64_t role, dou
   }
   a.x0_out = x0_out.has_value() ? const_cast<float*>(opt_f32(x0_out)) : nullptr;
   a.last_out = last_out.has_value() ? const_cast<float*>(opt_f32(last_out)) : nullptr;
+  if (delta_out.has_value()) {
+    TORCH_CHECK(delta_out->scalar_type() == at::kFloat && delta_out->is_contiguous() &&
+                    delta_out->numel() == sample.numel(),
+                "cfg_step_peer: delta_out must be contiguous fp32 of the latent size");
+    a.delta_out = delta_out->data_ptr<float>();
+  }
   ds::launch_cfg_step_peer(a, make_group(rank, bases, timeout_ns), static_cast<int>(channel),
                            static_cast<uint64_t>(epoch), mine.data_ptr(), theirs_off, static_cast<int>(role),
                            status_ptr(status), at::cuda::getCurrentCUDAStream());

@@ -148,6 +148,9 @@ __global__ void __launch_bounds__(256) cfg_step_peer_kernel(SchedStepArgs a, Pee
       xcv[e] = xc;
     }
     reinterpret_cast<float4*>(a.sample)[i] = make_float4(out[0], out[1], out[2], out[3]);
+    if (a.delta_out)
+      reinterpret_cast<float4*>(a.delta_out)[i] =
+          make_float4(cv[0] - uv[0], cv[1] - uv[1], cv[2] - uv[2], cv[3] - uv[3]);
     if (a.x0_out) reinterpret_cast<float4*>(a.x0_out)[i] = make_float4(x0v[0], x0v[1], x0v[2], x0v[3]);
     if (a.last_out) reinterpret_cast<float4*>(a.last_out)[i] = make_float4(xcv[0], xcv[1], xcv[2], xcv[3]);
   }

@@ -154,6 +154,7 @@ struct SchedStepArgs {
   float p_hist[3] = {0.f, 0.f, 0.f};
   float* x0_out = nullptr;
   float* last_out = nullptr;
+  float* delta_out = nullptr;  // optional: cond - uncond (fp32), for late-step CFG folding
 };
 void launch_sched_step(const SchedStepArgs& a, cudaStream_t stream);
 

@@ -47,13 +47,22 @@ class CFGFolding:
             self.folded_steps += 1
             return cond.float() + (guidance - 1.0) * self.delta
         d = cond.float() - uncond.float()
-        self.prev_delta, self.delta = self.delta, d
+        self.observe(step, d)
+        return uncond.float() + guidance * d
+
+    def observe(self, step: int, d: torch.Tensor):
+        """Record the guidance delta of a full CFG step (also fed by the fused CFG-parallel
+        kernel, which writes cond - uncond while it applies the step) and run the gate."""
+        self.prev_delta, self.delta = self.delta, d.float().clone()
         self.full_steps += 1
         if self.prev_delta is not None and step >= self.warm:
-            change = ((d - self.prev_delta).norm() / d.norm().clamp_min(1e-12)).item()
+            change = ((self.delta - self.prev_delta).norm() / self.delta.norm().clamp_min(1e-12)).item()
             if change < self.threshold:
                 self.folded_left = self.fold_span
-        return uncond.float() + guidance * d
+
+    def eligible(self, step: int) -> bool:
+        """The next step may run folded (the planner can hand the unconditional half away)."""
+        return self.fold_now(step)
 
 
 class BlockResidualCache:

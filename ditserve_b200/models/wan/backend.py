@@ -157,6 +157,8 @@ class WanBackend(Backend):
         p = progress(st.step, st.spec.steps)
         p["block"] = st.block
         p["transfer_ready"] = st.block == 0
+        if st.fold is not None:
+            p["cfg_fold_eligible"] = bool(st.block == 0 and not st.done and st.fold.eligible(st.step))
         return p
 
     def prepare(self, request):

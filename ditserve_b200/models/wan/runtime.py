@@ -190,7 +190,10 @@ class WanEngine:
         if len(br) == 2:
             return pred[0], pred[1]
         theirs = self.cfg_plan.exchange(pred[0])
-        return (pred[0], theirs) if br[0] == 0 else (theirs, pred[0])
+        cond, uncond = (pred[0], theirs) if br[0] == 0 else (theirs, pred[0])
+        if st.fold is not None:  # CFG parallelism: both predictions are here after the exchange
+            st.fold.observe(st.step, cond.float() - uncond.float())
+        return cond, uncond
 
     @torch.inference_mode()
     def apply(self, st: WanRequestState, cond: torch.Tensor, uncond: torch.Tensor | None):
@@ -212,7 +215,13 @@ class WanEngine:
         pred = self.model.predict(pk, self.pctx)
         if st.negative is not None and hasattr(self.cfg_plan, "fused_step"):
             # CFG parallelism over peer memory: exchange + guidance + update in one kernel
-            self.cfg_plan.fused_step(st.scheduler, st.latents.view(-1), pred[0], st.spec.guidance)
+            delta = None
+            if st.fold is not None:
+                delta = torch.empty(st.latents.numel(), device=st.latents.device, dtype=torch.float32)
+            step = st.step
+            self.cfg_plan.fused_step(st.scheduler, st.latents.view(-1), pred[0], st.spec.guidance, delta_out=delta)
+            if delta is not None:
+                st.fold.observe(step, delta)
             st.step += 1
             st.block = 0
             st.packets.clear()
@@ -351,6 +360,9 @@ class WanEngine:
                              context=snap["context"].to(self.device, copy=True),
                              negative=None if snap["negative"] is None else snap["negative"].to(self.device, copy=True),
                              step=int(snap["step"]))
+        if spec.cfg_fold is not None and st.negative is not None:
+            from ..approx import CFGFolding
+            st.fold = CFGFolding(spec.steps, **spec.cfg_fold)  # the gate restarts: no delta yet
         return st
 
     def export_packet(self, st: WanRequestState) -> tuple[bytes, str]:

@@ -132,7 +132,10 @@ class FusedCFG:
     def exchange(self, mine):  # pragma: no cover - the fused step never exchanges separately
         raise RuntimeError("FusedCFG applies guidance inside the exchange kernel")
 
-    def fused_step(self, scheduler, sample: torch.Tensor, mine: torch.Tensor, guidance: float):
+    def fused_step(self, scheduler, sample: torch.Tensor, mine: torch.Tensor, guidance: float,
+                   delta_out: torch.Tensor | None = None):
+        """Exchange + guidance + solver update in one kernel; ``delta_out`` (fp32, latent size)
+        also receives cond - uncond, which late-step CFG folding reuses."""
         n = mine.numel()
         if n > self.numel:
             raise ValueError(f"prediction of {n} elements exceeds the reserved CFG slot ({self.numel})")
@@ -151,7 +154,7 @@ class FusedCFG:
                 float(c.get("last_coef", 0.0)), float(c.get("x0_coef", 0.0)), list(c.get("hist", [])),
                 [float(v) for v in c.get("hist_coef", [])], float(pred.get("x", 1.0)), float(pred.get("x0", 0.0)),
                 float(pred.get("v", 0.0)), list(pred.get("hist", [])), [float(v) for v in pred.get("hist_coef", [])],
-                x0_out, last_out, r, bases, tmo, self.group.channel, epoch, st)
+                x0_out, last_out, r, bases, tmo, self.group.channel, epoch, st, delta_out)
             return x
 
         return scheduler.step(sample, mine.reshape(-1), None, guidance, kernel=kernel)

@@ -97,3 +97,28 @@ def test_wan_tiny_gloo_world_cluster(controller, tmp_path):
     assert forms & {"cfg2", "sp2"}, forms  # at least one quantum ran on both ranks
     assert any(t["quantum"] == "finish" for t in last["trace"])  # VAE decode quanta ran
     assert all(r.get("digest") for r in last["rows"])
+
+
+def test_cfg_fission_gloo_world(controller, tmp_path):
+    """ditserve-approx hands the unconditional rank away while a video's steps run folded."""
+    cfg = {"schema": "ditserve-b200.study.v1", "experiment": "exec-fission",
+           "workers": {"wan": {"backend": "wan", "config": {"model": "wan-tiny", "device": "cpu",
+                                                            "transfer_dir": str(tmp_path)}}},
+           "budget": BUDGET,
+           "phases": [{"id": "cluster", "kind": "cluster", "gpus": 2, "policy": "ditserve-approx", "worker": "wan",
+                       "distributed": True, "sp_transport": "collective", "collectives": "nccl",
+                       "dist_port": 28000 + os.getpid() % 1000,
+                       "generator": {"count": 1, "seed": 4, "pattern": "offline_all", "classes": [
+                           {"weight": 1, "kind": "video", "class": "wan21_480p", "service_ms": 20000,
+                            "slo_scale": 5, "spec": {"height": 64, "width": 64, "frames": 5, "steps": 6,
+                                                     "guidance": 5.0,
+                                                     "cfg_fold": {"warm_frac": 0.0, "threshold": 10.0,
+                                                                  "fold_span": 1}}}]},
+                       "gates": [{"pointer": "/last/summary/completed", "op": "==", "value": 1}]}]}
+    rep, _ = _run(controller, cfg, tmp_path, allow_gpu=True)
+    assert rep["phases"]["cluster"]["gates"]["pass"], rep["phases"]["cluster"]
+    last = _last(rep)
+    assert not last["failures"], last["failures"]
+    forms = [t["form"] for t in last["trace"]]
+    assert "cfg2" in forms and "sp1" in forms, forms       # full steps on the pair, folded ones alone
+    assert last["counters"]["transfers"] >= 1              # the pair regrouped after a folded step

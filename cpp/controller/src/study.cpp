@@ -21,6 +21,7 @@
 #include "ds/budget.hpp"
 #include "ds/cost.hpp"
 #include "ds/planner.hpp"
+#include "ds/policy.hpp"
 #include "ds/process.hpp"
 #include "ds/sim.hpp"
 #include "ds/workload.hpp"
@@ -322,11 +323,25 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
   // untimed warm-up: every aligned group of each listed form adopts its layout once, so
   // communicators, symmetric heaps and fused plans exist before the trace starts
   double warmup_ms = 0;
+  const double tw = monotonic_seconds();
   if (distributed && phase.contains("warmup_forms")) {
-    const double tw = monotonic_seconds();
     Json spec = phase.get("warmup_spec").is_null() ? Json::object() : phase.at("warmup_spec");
-    for (const auto& fj : phase.at("warmup_forms").as_array()) {
-      const Form f = parse_form(fj.as_string());
+    // "auto": every form the policy may choose for the phase's video classes
+    std::vector<std::string> names;
+    if (phase.at("warmup_forms").is_string() && phase.at("warmup_forms").as_string() == "auto") {
+      std::set<std::string> seen;
+      const Json gen = phase.get("generator");
+      if (gen.is_object() && gen.contains("classes"))
+        for (const auto& c : gen.at("classes").as_array()) {
+          if (c.str("kind", "video") != "video") continue;
+          for (const auto& f : candidate_forms(policy_traits(policy), cost, c.at("class").as_string(), gpus, options))
+            if (f.degree() > 1 && seen.insert(form_name(f)).second) names.push_back(form_name(f));
+        }
+    } else {
+      for (const auto& fj : phase.at("warmup_forms").as_array()) names.push_back(fj.as_string());
+    }
+    for (const auto& name : names) {
+      const Form f = parse_form(name);
       for (const auto& grp : cluster_groups(gpus, f.degree())) {
         fan_out(grp, [&](int g) {
           Json r = Json::object();
@@ -339,8 +354,34 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
         });
       }
     }
-    warmup_ms = (monotonic_seconds() - tw) * 1000.0;
   }
+  // image workers: one short request each, so the first timed image pays no start-up
+  if (phase.contains("warmup_image_spec") && !iworkers.empty()) {
+    std::vector<int> all;
+    for (int g = 0; g < gpus; ++g) all.push_back(g);
+    fan_out(all, [&](int g) {
+      Json pr = Json::object();
+      pr["state_id"] = "__warmup__";
+      pr["spec"] = phase.at("warmup_image_spec");
+      iworkers[g]->call("prepare", pr, 600);
+      Json ab = Json::object();
+      Json ids = Json::array();
+      ids.push_back("__warmup__");
+      ab["state_ids"] = ids;
+      iworkers[g]->call("advance_batch", ab, 600);  // warm-up specs take one step
+      if (decode) {
+        Json f = Json::object();
+        f["state_id"] = "__warmup__";
+        f["output_mode"] = "digest";
+        f["decode"] = true;
+        iworkers[g]->call("finish", f, 600);
+      }
+      Json rel = Json::object();
+      rel["state_id"] = "__warmup__";
+      return iworkers[g]->call("release", rel, 600);
+    });
+  }
+  warmup_ms = (monotonic_seconds() - tw) * 1000.0;
   // doorbells: one 8-byte epoch file per GPU
   std::vector<std::string> bells;
   std::vector<long long> bell_epoch(gpus, 0);

@@ -299,6 +299,9 @@ class MockBackend(Backend):
         if action == "init":
             self.world = dict(rank=request.get("rank", 0), world_size=request.get("world_size", 1))
             return dict(initialised=True, **self.world)
+        if action == "layout":  # the fixture has no collectives: record the layout only
+            self.layout = dict(form=request["form"], ranks=list(request["ranks"]))
+            return dict(self.layout, epoch=int(request.get("epoch", 0)))
         if action == "shutdown":
             self.world = None
             return dict(shutdown=True)

@@ -54,6 +54,7 @@ def test_mock_cluster_pairs_batches_regroups(controller, tmp_path):
            "budget": BUDGET,
            "phases": [{"id": "cluster", "kind": "cluster", "gpus": 4, "policy": "ditserve", "distributed": True,
                        "workers": {"video": "vid", "image": "img"}, "decode": True,
+                       "warmup_forms": "auto", "warmup_image_spec": {"steps": 1},
                        "sp_transport": "export",
                        "options": {"pairing": True, "continuous_batch": 4},
                        "generator": {"count": 12, "seed": 2, "pattern": "poisson", "rate_rps": 40, "classes": [

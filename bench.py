@@ -32,8 +32,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-# published per-step latency of the reference for this request class (BASELINE.md section A,
-# Wan2.1 480p tier, 32 760 tokens): SP1 on 1x A100 and CFG2 on 2x A100.
+# published per-step latency of the reference for this request class (Wan2.1 480p tier,
+# 32 760 tokens; results/5.1_Experimental_Setup/README.md:33-34 of the reference):
+# SP1 on 1x A100 and CFG2 on 2x A100.
 PUBLISHED_MS = {1: 3965.0, 2: 1998.0}
 METRIC = "wan2.1-1.3b 480p (32760 tok) DiT step latency, CFG 5.0"
 

@@ -45,6 +45,7 @@ struct Settings {
   bool widen_past_images = false;  // widen even while images wait (they preempt by doorbell)
   double feasible_margin = 0.0;     // feasible-min keeps this fraction of the remaining time as slack
   double wide_efficiency = 0.0;     // >0: videos start on their widest form at least this efficient
+  double late_short_ms = 0.0;       // late requests this short keep their EDF position
 };
 
 Settings resolve(const PolicyTraits& t, const Json& o) {
@@ -85,6 +86,8 @@ Settings resolve(const PolicyTraits& t, const Json& o) {
   s.widen_past_images = o.flag("widen_past_images", t.widen_past_images);
   s.feasible_margin = o.num("feasible_margin", t.feasible_margin);
   s.wide_efficiency = o.num("wide_efficiency", t.wide_efficiency);
+  s.late_short_ms = o.num("late_short_ms", 0.0);
+  if (s.late_short_ms < 0) throw std::invalid_argument("late_short_ms must be >= 0");
   if (s.feasible_margin < 0 || s.feasible_margin > 10) throw std::invalid_argument("feasible_margin must be in [0, 10]");
   return s;
 }
@@ -319,7 +322,9 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
 
   const bool image_boost = t.feasible_img_priority && t.elastic && !t.deadline_dp && !t.best_fit && !t.knapsack;
   auto key = [&](const Req& r) {
-    const int late = (t.demote_late && !r.feasible) ? 1 : 0;
+    // a late request is demoted behind feasible ones, unless it is short enough that serving
+    // it now costs the others little (late_short_ms)
+    const int late = (t.demote_late && !r.feasible && !(r.best_remaining <= s.late_short_ms)) ? 1 : 0;
     const int boost = (image_boost && !r.video() && r.feasible) ? 0 : 1;
     double primary = r.deadline;
     if (t.order == "srtf") primary = r.best_remaining;

@@ -404,4 +404,16 @@ TEST("CFG fission runs a fold-eligible video on the conditional half of its grou
   CHECK(!find(r, "v")->contains("fold"));
 }
 
+TEST("late short requests keep their EDF position with late_short_ms") {
+  ClusterCost c(profile());
+  auto late_img = req("img", "image", "img", 0, 10);   // already late, 400 ms of work
+  auto vid = req("v", "video", "vid", 0, 20000);
+  auto p = cluster_plan(state(1, {late_img, vid}, {}, 100), "abl-step-elastic", c);
+  CHECK(find(p, "v") != nullptr && find(p, "img") == nullptr);  // demoted behind the feasible video
+  Json o = Json::object();
+  o["late_short_ms"] = 1000;
+  auto q = cluster_plan(state(1, {late_img, vid}, {}, 100), "abl-step-elastic", c, o);
+  CHECK(find(q, "img") != nullptr);                             // short: keeps its EDF slot
+}
+
 int main() { return dstest::run_all(); }

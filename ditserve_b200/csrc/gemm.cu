@@ -8,9 +8,9 @@
 // A/B k-blocks of 64 elements into a STAGES-deep shared-memory ring with TMA
 // (128-byte swizzle, no multicast).  Warp 1 owns TMEM: it allocates two
 // 128 x BN fp32 accumulators and one lane issues tcgen05.mma (M=128, N=BN,
-// K=16 per instruction) into one of them while the four epilogue warps
-// (warps 2..5, one TMEM lane quarter each) drain the other one, so the
-// epilogue of tile i overlaps the main loop of tile i+1.
+// K=16 per instruction) into one of them while the eight epilogue warps
+// (warps 2..9, two per TMEM lane quarter, each taking half the columns) drain the
+// other one, so the epilogue of tile i overlaps the main loop of tile i+1.
 //
 // Epilogues are fused so the hot DiT ops never round-trip through HBM:
 //   kEpiNone      C = acc + bias
@@ -34,7 +34,8 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;  // warp0 TMA, warp1 MMA, warps 2..5 epilogue
+constexpr int kEpiWarps = 8;    // two warps per TMEM lane quarter, each drains half the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp0 TMA, warp1 MMA, warps 2..9 epilogue
 
 template <int BN>
 struct GemmCfg {
@@ -89,7 +90,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
+      mbar_init(&acc_empty[i], 32 * kEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -159,9 +160,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     mma_done:;
     }
   } else {
-    // ---------------- epilogue warps 2..5 ----------------
+    // ---------------- epilogue warps 2..9 ----------------
+    // a warp may only read its TMEM lane quarter (warp % 4); the two warps of a quarter
+    // split the tile's columns, so a tile drains twice as fast as with one warp per quarter
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
+    const int col_half = (warp - 2) / 4;
+    constexpr int kChunks = BN / 32;
+    const int c_begin = col_half * (kChunks / 2), c_end = c_begin + kChunks / 2;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -178,11 +184,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         gate_row = p.gate + static_cast<int64_t>(bidx) * p.gate_stride;
       }
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = c_begin; c < c_end; ++c) {
+        const int n = n0 + c * 32;
+        // the residual row segment is requested before the TMEM load so both latencies overlap
+        uint4 rv[4];
+        if ((EPI == kEpiGatedRes || EPI == kEpiRes) && row_ok) {
+          const uint4* rp = reinterpret_cast<const uint4*>(p.R + static_cast<int64_t>(m) * p.ldr + n);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) rv[q] = rp[q];
+        }
         uint32_t r[32];
         tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + c * 32, r);
         tmem_wait_ld();
-        const int n = n0 + c * 32;
         if (row_ok) {
           float v[32];
 #pragma unroll
@@ -206,11 +219,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
           }
           if (EPI == kEpiGatedRes || EPI == kEpiRes) {
-            const uint4* rp = reinterpret_cast<const uint4*>(p.R + static_cast<int64_t>(m) * p.ldr + n);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              uint4 rv = rp[q];
-              const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+              const uint32_t rw[4] = {rv[q].x, rv[q].y, rv[q].z, rv[q].w};
 #pragma unroll
               for (int t = 0; t < 4; ++t) {
                 float2 f = unpack_bf16x2(rw[t]);

@@ -6,6 +6,7 @@
 //     plan < state.json                        one cluster_plan decision
 //     simulate [--config P] [--count N] [--seed N] [--policy ID]...
 //     run --config P [--run-id ID] [--work-dir P] [--ledger P] [--phase ID] [--resume]
+//     results finalize|verify|inspect PATH | results compact ROOT DEST
 //         [--allow-gpu] [--repair]
 //     report RUN_DIR                           summaries of a finished run
 //     rpc generate|simulate|control|plan|policies|run|simulate-study < request.json
@@ -111,6 +112,7 @@ int usage(std::ostream& os) {
         "  simulate [--config P] [--count N] [--seed N] [--policy ID]...\n"
         "  run --config P [--run-id ID] [--work-dir P] [--ledger P] [--phase ID] [--resume] [--allow-gpu] [--repair]\n"
         "  report RUN_DIR\n"
+        "  results finalize|verify|inspect PATH [--title T] | results compact ROOT DEST [--prune-raw]\n"
         "  rpc generate|simulate|control|plan|policies|run|simulate-study < request.json\n";
   return 2;
 }
@@ -223,6 +225,37 @@ int command_main(int argc, char** argv) {
       }
       if (config.empty()) throw UsageError("run requires --config");
       out = run_study(resolve_profiles(Json::parse(read_path(config)), config), opt);
+    } else if (cmd == "results") {
+      // results finalize|verify|inspect PATH [--title T]; results compact ROOT DEST [--prune-raw]
+      if (rest.size() < 3) throw UsageError("results needs an operation and a path");
+      const std::string op = rest[1];
+      Json req = Json::object();
+      req["path"] = rest[2];
+      size_t i = 3;
+      if (op == "compact") {
+        if (rest.size() < 4) throw UsageError("results compact needs ROOT and DEST");
+        req["destination"] = rest[3];
+        i = 4;
+      } else if (op != "finalize" && op != "verify" && op != "inspect") {
+        throw UsageError("results operation must be finalize, verify, inspect or compact");
+      }
+      for (; i < rest.size(); ++i) {
+        if (rest[i] == "--title" && i + 1 < rest.size()) req["title"] = rest[++i];
+        else if (rest[i] == "--prune-raw") req["prune_raw"] = true;
+        else throw UsageError("unknown results option " + rest[i]);
+      }
+      std::map<std::string, std::string> env;
+      if (!opt.package_root.empty()) env["PYTHONPATH"] = opt.package_root;
+      env["CUDA_VISIBLE_DEVICES"] = "";
+      WorkerProcess w({opt.python, "-m", "ditserve_b200.runtime.worker", "--backend", "results"}, env, "");
+      try {
+        out = w.call(op, req, 600);
+      } catch (...) {
+        w.stop(2.0);
+        throw;
+      }
+      w.call("shutdown", Json::object(), 30);
+      w.stop(2.0);
     } else if (cmd == "report") {
       if (rest.size() != 2) throw UsageError("report needs exactly one RUN_DIR");
       out = Json::object();

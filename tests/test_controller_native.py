@@ -63,3 +63,20 @@ def test_mock_study_end_to_end(controller, tmp_path):
     no = subprocess.run([controller, "run", "--config", cfg, "--run-id", "t1", "--work-dir", str(tmp_path)],
                         capture_output=True, text=True, env=env)
     assert no.returncode == 1
+
+
+def test_results_cli(controller, tmp_path):
+    run = tmp_path / "runs" / "r1"
+    run.mkdir(parents=True)
+    (run / "phase-a.json").write_text(json.dumps({"status": "ok", "last": {"summary": {"slo_attainment": 1.0}},
+                                                  "gates": {"pass": True}}))
+    env = dict(os.environ, DITSERVE_PYTHON=sys.executable, DITSERVE_PACKAGE_ROOT=ROOT)
+    fin = subprocess.run([controller, "--json", "results", "finalize", str(run), "--title", "t"], capture_output=True,
+                         text=True, env=env, timeout=300)
+    assert fin.returncode == 0, fin.stderr
+    assert json.loads(fin.stdout)["phases"]["a"]["summary"]["slo_attainment"] == 1.0
+    ver = subprocess.run([controller, "--json", "results", "verify", str(run)], capture_output=True, text=True,
+                         env=env, timeout=300)
+    assert ver.returncode == 0 and json.loads(ver.stdout)["ok"]
+    bad = subprocess.run([controller, "results", "explode", str(run)], capture_output=True, text=True, env=env)
+    assert bad.returncode == 2

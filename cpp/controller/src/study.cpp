@@ -303,8 +303,61 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     vworkers.push_back(spawn(vdef, "video", g, distributed));
     if (iname != vname) iworkers.push_back(spawn(idef, "image", g, false));
   }
+  // occupancy guard: a CPU-only probe worker lists GPU processes that are not ours; a foreign
+  // process on one of the phase's GPUs aborts the phase, and so do three unknown probes in a row
+  const bool guard = phase.flag("occupancy_guard", false);
+  const double guard_interval_ms = phase.num("occupancy_interval_ms", 5000.0);
+  std::unique_ptr<WorkerProcess> prober;
+  Json own_pids = Json::array();
+  if (guard) {
+    for (auto& w : vworkers) own_pids.push_back(static_cast<long long>(w->proc->pid()));
+    for (auto& w : iworkers) own_pids.push_back(static_cast<long long>(w->proc->pid()));
+    std::map<std::string, std::string> env;
+    if (!opt.package_root.empty()) env["PYTHONPATH"] = opt.package_root;
+    env["CUDA_VISIBLE_DEVICES"] = "";
+    prober = std::make_unique<WorkerProcess>(
+        std::vector<std::string>{opt.python, "-m", "ditserve_b200.runtime.worker", "--backend", "environment"}, env,
+        run_dir + "/occupancy.log");
+    prober->call("hello", Json::object(), 120);
+  }
   auto W = [&](int g, bool image) -> Worker* {
     return (image && !iworkers.empty()) ? iworkers[g].get() : vworkers[g].get();
+  };
+  // ControllerTiming: one bounded span per worker call made for a quantum
+  const size_t span_limit = static_cast<size_t>(phase.integer("span_limit", 4096));
+  std::mutex span_mu;
+  Json spans = Json::array();
+  long long spans_dropped = 0;
+  double t_origin = monotonic_seconds();
+  auto call = [&](int g, bool image, const std::string& op, const Json& req) -> Json {
+    const double a = monotonic_seconds();
+    std::string status = "ok";
+    Json res;
+    try {
+      res = W(g, image)->call(op, req);
+    } catch (const std::exception& e) {
+      status = std::string("error: ") + e.what();
+    }
+    const double b = monotonic_seconds();
+    {
+      std::lock_guard<std::mutex> lock(span_mu);
+      if (spans.size() < span_limit) {
+        Json sp = Json::object();
+        sp["stage"] = op;
+        sp["gpu"] = g;
+        sp["worker"] = image ? "image" : "video";
+        if (req.contains("state_id")) sp["request_id"] = req.at("state_id");
+        sp["start_ms"] = (a - t_origin) * 1000.0;
+        sp["finish_ms"] = (b - t_origin) * 1000.0;
+        sp["status"] = status;
+        if (res.is_object() && res.contains("model_ms")) sp["model_ms"] = res.at("model_ms");
+        spans.push_back(sp);
+      } else {
+        ++spans_dropped;
+      }
+    }
+    if (status != "ok") throw std::runtime_error(status.substr(7));
+    return res;
   };
   if (distributed) {
     const std::string init = "tcp://127.0.0.1:" + std::to_string(phase.integer("dist_port", 29700));
@@ -422,6 +475,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
   std::vector<bool> busy(gpus, false);
   std::vector<std::vector<std::pair<std::string, bool>>> pending_release(gpus);
   const double t0 = monotonic_seconds();
+  t_origin = t0;
   long long plans = 0, quanta = 0, preemptions = 0, transfers = 0, pairs = 0, batches = 0, held_mid_step = 0;
   double plan_ms_total = 0, plan_ms_max = 0;
   size_t finished = 0;
@@ -443,7 +497,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
         Json pr = Json::object();
         pr["state_id"] = p.id;
         pr["spec"] = p.spec;
-        return W(g, p.image)->call("prepare", pr);
+        return call(g, p.image, "prepare", pr);
       });
       return false;
     }
@@ -455,7 +509,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
       if (p.stale.count(g)) {
         Json rel = Json::object();
         rel["state_id"] = p.id;
-        W(g, p.image)->call("release", rel);
+        call(g, p.image, "release", rel);
       }
     int src = -1;
     for (int g : p.exec)
@@ -466,10 +520,10 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     auto hop = [&](int from, int to) {  // host-staged continuation packet
       Json ex = Json::object();
       ex["state_id"] = p.id;
-      Json pk = W(from, p.image)->call("block_export", ex);
+      Json pk = call(from, p.image, "block_export", ex);
       Json im = pk;
       im["state_id"] = p.id;
-      W(to, p.image)->call("block_import", im);
+      call(to, p.image, "block_import", im);
     };
     if (transport == "collective" && !p.image && p.exec.size() > 1) {
       if (src < 0) {
@@ -483,7 +537,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
         r["src"] = src;
         r["state_id"] = p.id;
         r["path"] = path;
-        return W(g, false)->call("distributed", r);
+        return call(g, false, "distributed", r);
       });
     } else {
       const int from = src >= 0 ? src : *p.fresh.begin();
@@ -496,10 +550,10 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     f["state_id"] = id;
     f["output_mode"] = "digest";
     if (image && decode) f["decode"] = true;
-    Json art = W(exec.front(), image)->call("finish", f);
+    Json art = call(exec.front(), image, "finish", f);
     Json rel = Json::object();
     rel["state_id"] = id;
-    fan_out(exec, [&](int g) { return W(g, image)->call("release", rel); });
+    fan_out(exec, [&](int g) { return call(g, image, "release", rel); });
     return art.get("value");
   };
   auto member = [](const std::string& id, const Json& progress, bool done, const Json& digest) {
@@ -511,9 +565,40 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     return m;
   };
 
+  double next_probe = 0;
+  int unknown_probes = 0;
+  std::string abort_reason;
+  Json probes = Json::array();
   while (finished < live.size()) {
     const double now = now_ms_since(t0);
     if (now > horizon) break;
+    if (guard && now >= next_probe) {
+      next_probe = now + guard_interval_ms;
+      Json q = Json::object();
+      Json idx = Json::array();
+      for (int g = 0; g < gpus; ++g) idx.push_back(g);
+      q["gpus"] = idx;
+      q["own_pids"] = own_pids;
+      Json occ;
+      try {
+        occ = prober->call("occupancy", q, 60);
+      } catch (const std::exception& e) {
+        occ = Json::object();
+        occ["state"] = "unknown";
+        occ["source"] = e.what();
+      }
+      const std::string st = occ.str("state", "unknown");
+      if (probes.size() < 256) {
+        Json pr = Json::object();
+        pr["t_ms"] = now;
+        pr["state"] = st;
+        probes.push_back(pr);
+      }
+      unknown_probes = st == "unknown" ? unknown_probes + 1 : 0;
+      if (st == "busy") abort_reason = "foreign GPU process: " + occ.get("foreign").dump();
+      else if (unknown_probes > 2) abort_reason = "occupancy unknown on three probes in a row";
+      if (!abort_reason.empty()) break;
+    }
     // harvest finished quanta
     for (auto it = tasks.begin(); it != tasks.end();) {
       if (it->fut.wait_for(std::chrono::milliseconds(0)) != std::future_status::ready) {
@@ -749,13 +834,12 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
         const int frames = static_cast<int>(lspec.integer("frames", 81));
         const int latent_frames = (frames - 1) / 4 + 1;
         const int frames_per_chunk = (latent_frames + chunks - 1) / chunks;
-        tasks.push_back({ids, std::async(std::launch::async, [=, &ensure_state, &finish_release, &member, &W,
+        tasks.push_back({ids, std::async(std::launch::async, [=, &ensure_state, &finish_release, &member, &call,
                                                                &bells]() -> Json {
                            for (const auto& p : places) ensure_state(p);
                            Json out = Json::object();
                            Json ms = Json::array();
                            if (image) {
-                             Worker* w = W(leader, true);
                              if (batch) {
                                Json ab = Json::object();
                                Json sids = Json::array();
@@ -763,7 +847,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
                                ab["state_ids"] = sids;
                                std::map<std::string, Json> prog;
                                for (int k = 0; k < batch_quantum; ++k) {
-                                 Json r = w->call("advance_batch", ab);
+                                 Json r = call(leader, true, "advance_batch", ab);
                                  bool any = false;
                                  for (const auto& m : r.at("members").as_array()) {
                                    prog[m.at("state_id").as_string()] = m.at("progress");
@@ -780,7 +864,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
                                  Json adv = Json::object();
                                  adv["state_id"] = ids[0];
                                  adv["steps"] = 1000000;
-                                 w->call("advance", adv);
+                                 call(leader, true, "advance", adv);
                                }
                                ms.push_back(member(ids[0], Json(), true, finish_release(ids[0], exec, true)));
                              }
@@ -793,24 +877,23 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
                                out["members"] = ms;
                                return out;
                              }
-                             Worker* w = W(leader, false);
                              std::string tk = ticket;
                              if (tk.empty()) {
                                Json ds = Json::object();
                                ds["state_id"] = ids[0];
                                ds["chunked"] = true;
-                               tk = w->call("decode_start", ds).at("ticket").as_string();
+                               tk = call(leader, false, "decode_start", ds).at("ticket").as_string();
                              }
                              Json dp = Json::object();
                              dp["ticket"] = tk;
                              dp["frames"] = std::max(1, chunk_quantum) * frames_per_chunk;
                              dp["output_mode"] = "digest";
                              if (decoded + chunk_quantum >= chunks) dp["wait"] = true;
-                             Json r = w->call("decode_poll", dp);
+                             Json r = call(leader, false, "decode_poll", dp);
                              if (r.flag("ready", false)) {
                                Json rel = Json::object();
                                rel["state_id"] = ids[0];
-                               fan_out(exec, [&](int g) { return W(g, false)->call("release", rel); });
+                               fan_out(exec, [&](int g) { return call(g, false, "release", rel); });
                                const Json& art = r.get("artifact");
                                Json digest = art.is_object() && art.contains("array_sha256") ? art.at("array_sha256")
                                                                                             : r.get("value");
@@ -846,7 +929,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
                                lay["path"] = path;
                                adv["layout"] = lay;
                              }
-                             return W(g, false)->call("advance", adv);
+                             return call(g, false, "advance", adv);
                            });
                            for (size_t k = 1; k < res.size(); ++k) {
                              const Json& p0 = res[0].at("progress");
@@ -870,6 +953,21 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     std::this_thread::sleep_for(std::chrono::milliseconds(2));
   }
   for (auto& t : tasks) t.fut.wait();
+  if (!abort_reason.empty())
+    for (auto& l : live)
+      if (l.status != "done" && l.status != "failed") {
+        l.status = "failed";
+        l.row["status"] = "failed";
+        l.row["error"] = "aborted: " + abort_reason;
+        failures.push_back(l.id);
+      }
+  if (prober) {
+    try {
+      prober->call("shutdown", Json::object(), 30);
+    } catch (const std::exception&) {
+    }
+    prober->stop(2.0);
+  }
   Json out_rows = Json::array();
   for (auto& l : live) {
     l.row["observation_ms"] = now_ms_since(t0);
@@ -907,6 +1005,12 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
   timing["warmup_ms"] = warmup_ms;
   out["controller_timing"] = timing;
   out["trace"] = trace;
+  out["spans"] = spans;
+  if (guard) {
+    out["occupancy_probes"] = probes;
+    if (!abort_reason.empty()) out["aborted"] = abort_reason;
+  }
+  out["spans_dropped"] = spans_dropped;
   out["failures"] = failures;
   Json cfg = Json::object();
   cfg["distributed"] = distributed;

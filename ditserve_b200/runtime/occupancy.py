@@ -7,6 +7,7 @@ workers/ditserve/runtime/worker.py:312-390, runtime/occupancy_nvml.py:33-193.
 """
 from __future__ import annotations
 
+import json
 import os
 import subprocess
 
@@ -45,9 +46,23 @@ def _smi_probe(indices):
     return out
 
 
+def _file_probe(path):
+    """A recorded process table ({gpu: [{"pid": ...}]}) read from ``path`` — the stand-in for
+    NVML in tests of the controller's occupancy guard (no GPU needed)."""
+    def probe(indices):
+        with open(path) as f:
+            table = json.load(f)
+        if table == "fail":
+            raise RuntimeError("probe failure (recorded)")
+        return {str(i): table.get(str(i), []) for i in indices}
+    return probe
+
+
 def occupancy(indices=None, own_pids=(), probe=None) -> dict:
     """{"state": "idle"|"busy"|"unknown", "foreign": {gpu: [procs]}, "source": ...}"""
     indices = list(indices if indices is not None else range(8))
+    if probe is None and os.environ.get("DITSERVE_OCCUPANCY_TABLE"):
+        probe = _file_probe(os.environ["DITSERVE_OCCUPANCY_TABLE"])
     own = set(own_pids) | {os.getpid()}
     for name, fn in ([("injected", probe)] if probe else [("nvml", _nvml_probe), ("nvidia-smi", _smi_probe)]):
         try:

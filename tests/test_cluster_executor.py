@@ -123,3 +123,36 @@ def test_cfg_fission_gloo_world(controller, tmp_path):
     forms = [t["form"] for t in last["trace"]]
     assert "cfg2" in forms and "sp1" in forms, forms       # full steps on the pair, folded ones alone
     assert last["counters"]["transfers"] >= 1              # the pair regrouped after a folded step
+
+
+def _guard_cfg(tmp):
+    return {"schema": "ditserve-b200.study.v1", "experiment": "exec-guard",
+            "workers": {"model": {"backend": "mock", "config": {"options": {"costs": {"step_ms": 40}}}}},
+            "budget": BUDGET,
+            "phases": [{"id": "cluster", "kind": "cluster", "gpus": 2, "policy": "ditserve",
+                        "occupancy_guard": True, "occupancy_interval_ms": 50,
+                        "generator": {"count": 3, "seed": 1, "pattern": "offline_all", "classes": [
+                            {"kind": "video", "class": "wan21_480p", "service_ms": 5000, "slo_scale": 5,
+                             "spec": {"steps": 6, "blocks_per_step": 2}}]}}]}
+
+
+@pytest.mark.parametrize("table,aborts", [({}, None), ({"1": [{"pid": 999999, "used_mib": "100"}]}, "foreign"),
+                                          ("fail", "unknown")])
+def test_occupancy_guard(controller, tmp_path, table, aborts):
+    path = tmp_path / "occ.json"
+    path.write_text(json.dumps(table))
+    env = dict(os.environ, DITSERVE_PYTHON=sys.executable, DITSERVE_PACKAGE_ROOT=ROOT,
+               DITSERVE_OCCUPANCY_TABLE=str(path))
+    cfgp = tmp_path / "study.json"
+    cfgp.write_text(json.dumps(_guard_cfg(tmp_path)))
+    r = subprocess.run([controller, "--json", "run", "--config", str(cfgp), "--run-id", "g", "--work-dir",
+                        str(tmp_path)], capture_output=True, text=True, env=env, timeout=600)
+    rep = json.loads(r.stdout)
+    last = rep["phases"]["cluster"]["cells"][-1]["result"]
+    assert last["occupancy_probes"]
+    if aborts is None:
+        assert "aborted" not in last and last["summary"]["completed"] == 3
+        assert {"prepare", "advance", "finish"} <= {s["stage"] for s in last["spans"]}
+    else:
+        assert aborts in last["aborted"] and last["failures"]
+        assert all(row["status"] in ("done", "failed") for row in last["rows"])

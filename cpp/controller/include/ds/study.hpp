@@ -5,8 +5,9 @@
 //    watchdog_seconds, repair_reserve_gpu_seconds, carry}, phases: [{id, kind, ...}]}
 // phase kinds:
 //   operations  a list of worker ops sent in order (optionally expecting failures)
-//   online      one worker, requests replayed against the clock; select_action picks
-//               which request advances next (fcfs | edf | srtf), step or block quanta
+//   online      one worker, requests replayed against the clock; select_online picks
+//               which request advances next and for how many steps (benchmark orders,
+//               session policies, EDF arms with fixed quanta, guarded / adaptive arms)
 //   cluster     `gpus` workers (one per GPU), cluster_plan decides every quantum, calls
 //               run concurrently, doorbells preempt block quanta, continuous batches
 //   simulate    the discrete-event simulator over one or more policies
@@ -38,6 +39,7 @@ Json validate_study(const Json& config);
 Json run_study(const Json& config, const StudyOptions& opt);
 Json simulate_study(const Json& config);
 // online single-worker policy: which visible request acts next
+// benchmark orders over rows {request_id, arrival_ms, deadline_ms, remaining_ms}
 Json select_action(const Json& rows, double now_ms, const std::string& policy);
 Json synthetic_profile();
 

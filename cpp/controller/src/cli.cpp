@@ -29,6 +29,7 @@
 #include "ds/policy.hpp"
 #include "ds/process.hpp"
 #include "ds/sim.hpp"
+#include "ds/dispatch.hpp"
 #include "ds/study.hpp"
 #include "ds/workload.hpp"
 
@@ -85,7 +86,10 @@ Json pure_rpc(const std::string& cmd, const Json& req) {
   }
   if (cmd == "control") {
     const std::string op = req.at("op").as_string();
-    if (op == "select") return select_action(req.at("rows"), req.at("now_ms").as_double(), req.str("policy", "edf"));
+    if (op == "select")
+      return select_online(req.at("rows"), req.at("now_ms").as_double(), req.str("policy", "edf"),
+                           req.str("active", ""), req.contains("quantum") ? req.at("quantum") : Json(1),
+                           req.get("costs").is_null() ? Json::object() : req.at("costs"));
     if (op == "workload") return study_workload(req.at("phase"));
     if (op == "matrix") return expand_matrix(req.at("phase"));
     if (op == "summary") return request_summary(req.at("rows"));

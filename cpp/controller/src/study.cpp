@@ -20,6 +20,7 @@
 
 #include "ds/budget.hpp"
 #include "ds/cost.hpp"
+#include "ds/dispatch.hpp"
 #include "ds/planner.hpp"
 #include "ds/policy.hpp"
 #include "ds/process.hpp"
@@ -143,12 +144,17 @@ Json run_operations(const Json& phase, Worker& w) {
 Json run_online(const Json& phase, Worker& w) {
   Json rows = study_workload(phase);
   const std::string policy = phase.str("policy", "edf");
-  const int quantum = static_cast<int>(phase.integer("quantum_steps", 1));
+  if (!is_online_policy(policy)) throw std::invalid_argument("unknown online policy " + policy);
+  const Json default_quantum = phase.contains("quantum_steps") ? phase.at("quantum_steps") : Json(1);
+  const Json costs = phase.get("costs").is_null() ? Json::object() : phase.at("costs");
   std::map<std::string, Json*> by_id;
   for (auto& r : rows.as_array()) by_id[r.at("request_id").as_string()] = &r;
   const double t0 = monotonic_seconds();
   std::set<std::string> prepared, done;
-  std::map<std::string, double> remaining;
+  std::map<std::string, double> remaining, ready_since;
+  std::map<std::string, int> steps_left;
+  std::string active;
+  Json decisions = Json::array();
   while (done.size() < rows.size()) {
     const double now = now_ms_since(t0);
     Json visible = Json::array();
@@ -156,19 +162,55 @@ Json run_online(const Json& phase, Worker& w) {
     for (const auto& r : rows.as_array()) {
       const std::string id = r.at("request_id").as_string();
       if (done.count(id)) continue;
-      if (r.at("arrival_ms").as_double() > now) {
-        next_arrival = std::min(next_arrival, r.at("arrival_ms").as_double());
+      const double arrival = r.at("arrival_ms").as_double();
+      if (arrival > now) {
+        next_arrival = std::min(next_arrival, arrival);
         continue;
       }
-      Json v = r;
-      v["remaining_ms"] = remaining.count(id) ? remaining[id] : r.at("service_ms").as_double();
+      const double service = r.at("service_ms").as_double();
+      const int steps = static_cast<int>(r.at("spec").integer("steps", 1));
+      const int left = steps_left.count(id) ? steps_left[id] : steps;
+      const double per_step = service / std::max(1, steps);
+      Json v = Json::object();
+      v["request_id"] = id;
+      v["kind"] = r.str("kind", "video");
+      v["status"] = "pending";
+      v["arrival_ms"] = arrival;
+      v["deadline_ms"] = r.at("deadline_ms");
+      v["remaining_ms"] = remaining.count(id) ? remaining[id] : service;
+      v["service_ms"] = service;
+      v["ready_since_ms"] = std::min(now, ready_since.count(id) ? ready_since[id] : arrival);
+      v["action"] = v.at("kind").as_string() == "image" ? "image" : "denoise";
+      v["started"] = prepared.count(id) > 0;
+      Json table = Json::object();
+      for (int q : {1, 2, 4, 8}) table[std::to_string(q)] = per_step * std::min(q, left);
+      table["step"] = per_step;
+      v["action_ms_by_quantum"] = table;
+      // session view of the same request (one stage)
+      v["ready"] = true;
+      v["release_ms"] = arrival;
+      v["stage_deadline_ms"] = r.at("deadline_ms");
+      v["remaining_total_ms"] = v.at("remaining_ms");
       visible.push_back(v);
     }
     if (visible.empty()) {
       std::this_thread::sleep_for(std::chrono::duration<double, std::milli>(std::max(0.0, next_arrival - now)));
       continue;
     }
-    const std::string id = select_action(visible, now, policy).at("request_id").as_string();
+    const Json d = select_online(visible, now, policy, active, default_quantum, costs);
+    if (d.at("request_id").is_null()) {
+      std::this_thread::sleep_for(std::chrono::milliseconds(1));
+      continue;
+    }
+    if (decisions.size() < 4096) {
+      Json rec = d;
+      rec["t_ms"] = now;
+      decisions.push_back(rec);
+    }
+    const std::string id = d.at("request_id").as_string();
+    const Json q = d.at("quantum");
+    const int steps_now = q.is_number() ? std::max(1, static_cast<int>(q.as_int())) : 1;
+    active = id;
     Json& row = *by_id[id];
     if (!prepared.count(id)) {
       Json req = Json::object();
@@ -180,11 +222,14 @@ Json run_online(const Json& phase, Worker& w) {
     }
     Json adv = Json::object();
     adv["state_id"] = id;
-    adv["steps"] = quantum;
+    adv["steps"] = steps_now;
     Json res = w.call("advance", adv);
     const Json& prog = res.at("progress");
-    const double frac = prog.at("steps").as_double() > 0 ? prog.at("step").as_double() / prog.at("steps").as_double() : 1;
+    const double total = prog.at("steps").as_double();
+    const double frac = total > 0 ? prog.at("step").as_double() / total : 1;
     remaining[id] = row.at("service_ms").as_double() * (1 - frac);
+    steps_left[id] = static_cast<int>(total - prog.at("step").as_double());
+    ready_since[id] = now_ms_since(t0);
     if (prog.flag("done", false)) {
       Json fin = Json::object();
       fin["state_id"] = id;
@@ -197,12 +242,14 @@ Json run_online(const Json& phase, Worker& w) {
       row["finish_ms"] = now_ms_since(t0);
       if (art.contains("value")) row["digest"] = art.at("value");
       done.insert(id);
+      active.clear();
     }
   }
   for (auto& r : rows.as_array()) r["observation_ms"] = now_ms_since(t0);
   Json out = Json::object();
   out["rows"] = rows;
   out["summary"] = request_summary(rows);
+  out["decisions"] = decisions;
   return out;
 }
 
@@ -1048,25 +1095,11 @@ Json run_simulate(const Json& phase) {
 
 // ---------------------------------------------------------------------------------------
 Json select_action(const Json& rows, double now_ms, const std::string& policy) {
-  if (!rows.is_array() || rows.empty()) throw std::invalid_argument("select_action needs visible requests");
-  if (policy != "fcfs" && policy != "edf" && policy != "srtf") throw std::invalid_argument("online policy must be fcfs, edf or srtf");
-  const Json* best = nullptr;
-  auto key = [&](const Json& r) {
-    const double arrival = r.num("arrival_ms", 0);
-    double primary = arrival;
-    if (policy == "edf") primary = r.num("deadline_ms", 1e300);
-    if (policy == "srtf") primary = r.num("remaining_ms", 0);
-    return std::make_tuple(primary, arrival, r.at("request_id").as_string());
-  };
-  for (const auto& r : rows.as_array()) {
-    if (r.num("arrival_ms", 0) > now_ms) continue;
-    if (best == nullptr || key(r) < key(*best)) best = &r;
-  }
-  if (best == nullptr) throw std::invalid_argument("no request has arrived");
-  Json out = Json::object();
-  out["request_id"] = best->at("request_id");
-  out["policy"] = policy;
-  return out;
+  if (policy != "fcfs" && policy != "edf" && policy != "srtf") throw std::invalid_argument("policy must be fcfs, edf or srtf");
+  Json d = select_online(rows, now_ms, policy);
+  if (d.at("request_id").is_null()) throw std::invalid_argument("no request has arrived");
+  d["policy"] = policy;
+  return d;
 }
 
 Json synthetic_profile() {

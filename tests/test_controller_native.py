@@ -52,7 +52,7 @@ def test_mock_study_end_to_end(controller, tmp_path):
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     rep = json.loads(r.stdout)
     assert rep["status"] == "ok"
-    for pid in ("online", "cluster"):
+    for pid in ("online", "online-arms", "cluster"):
         assert rep["phases"][pid]["gates"]["pass"], rep["phases"][pid]["gates"]
     sims = rep["phases"]["whatif"]["last"]
     assert set(sims) == {"ditserve", "edf-bestfit", "static-cfg2sp4", "xdit-sp1"}

@@ -616,7 +616,30 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
   int unknown_probes = 0;
   std::string abort_reason;
   Json probes = Json::array();
-  while (finished < live.size()) {
+  // admission: with the guard on, the trace starts only once the phase's GPUs are idle
+  double admission_wait_ms = 0;
+  if (guard) {
+    const double limit_s = phase.num("admission_wait_s", 60.0);
+    const double ta = monotonic_seconds();
+    std::string last_state = "unknown";
+    while (true) {
+      Json q = Json::object();
+      Json idx = Json::array();
+      for (int g = 0; g < gpus; ++g) idx.push_back(g);
+      q["gpus"] = idx;
+      q["own_pids"] = own_pids;
+      try {
+        last_state = prober->call("occupancy", q, 60).str("state", "unknown");
+      } catch (const std::exception&) {
+        last_state = "unknown";
+      }
+      if (last_state == "idle" || monotonic_seconds() - ta > limit_s) break;
+      std::this_thread::sleep_for(std::chrono::milliseconds(500));
+    }
+    admission_wait_ms = (monotonic_seconds() - ta) * 1000.0;
+    if (last_state != "idle") abort_reason = "admission: GPUs not idle (" + last_state + ")";
+  }
+  while (finished < live.size() && abort_reason.empty()) {
     const double now = now_ms_since(t0);
     if (now > horizon) break;
     if (guard && now >= next_probe) {
@@ -1055,6 +1078,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
   out["spans"] = spans;
   if (guard) {
     out["occupancy_probes"] = probes;
+    out["admission_wait_ms"] = admission_wait_ms;
     if (!abort_reason.empty()) out["aborted"] = abort_reason;
   }
   out["spans_dropped"] = spans_dropped;

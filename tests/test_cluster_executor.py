@@ -130,7 +130,7 @@ def _guard_cfg(tmp):
             "workers": {"model": {"backend": "mock", "config": {"options": {"costs": {"step_ms": 40}}}}},
             "budget": BUDGET,
             "phases": [{"id": "cluster", "kind": "cluster", "gpus": 2, "policy": "ditserve",
-                        "occupancy_guard": True, "occupancy_interval_ms": 50,
+                        "occupancy_guard": True, "occupancy_interval_ms": 50, "admission_wait_s": 1,
                         "generator": {"count": 3, "seed": 1, "pattern": "offline_all", "classes": [
                             {"kind": "video", "class": "wan21_480p", "service_ms": 5000, "slo_scale": 5,
                              "spec": {"steps": 6, "blocks_per_step": 2}}]}}]}
@@ -149,10 +149,37 @@ def test_occupancy_guard(controller, tmp_path, table, aborts):
                         str(tmp_path)], capture_output=True, text=True, env=env, timeout=600)
     rep = json.loads(r.stdout)
     last = rep["phases"]["cluster"]["cells"][-1]["result"]
-    assert last["occupancy_probes"]
     if aborts is None:
+        assert last["occupancy_probes"]
         assert "aborted" not in last and last["summary"]["completed"] == 3
         assert {"prepare", "advance", "finish"} <= {s["stage"] for s in last["spans"]}
     else:
-        assert aborts in last["aborted"] and last["failures"]
+        assert "admission" in last["aborted"] and last["failures"]   # never admitted: GPUs not idle
         assert all(row["status"] in ("done", "failed") for row in last["rows"])
+
+
+def test_occupancy_guard_aborts_mid_run(controller, tmp_path):
+    """A foreign process appearing on one of the phase's GPUs after admission aborts the phase."""
+    import time
+    path = tmp_path / "occ.json"
+    path.write_text("{}")
+    cfg = _guard_cfg(tmp_path)
+    cfg["phases"][0]["generator"]["count"] = 6
+    cfg["phases"][0]["generator"]["classes"][0]["spec"]["steps"] = 40
+    cfgp = tmp_path / "study.json"
+    cfgp.write_text(json.dumps(cfg))
+    env = dict(os.environ, DITSERVE_PYTHON=sys.executable, DITSERVE_PACKAGE_ROOT=ROOT,
+               DITSERVE_OCCUPANCY_TABLE=str(path))
+    p = subprocess.Popen([controller, "--json", "run", "--config", str(cfgp), "--run-id", "m", "--work-dir",
+                          str(tmp_path)], stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True, env=env)
+    log = tmp_path / "m" / "video0.log"
+    deadline = time.time() + 120
+    while time.time() < deadline and not (log.exists() and log.stat().st_size >= 0 and (tmp_path / "m").exists()):
+        time.sleep(0.1)
+    time.sleep(3.0)  # workers up, trace running
+    path.write_text(json.dumps({"0": [{"pid": 999999, "used_mib": "10"}]}))
+    out, err = p.communicate(timeout=600)
+    rep = json.loads(out)
+    last = rep["phases"]["cluster"]["cells"][-1]["result"]
+    assert "foreign GPU process" in last.get("aborted", ""), (last.get("aborted"), last["summary"])
+    assert last["failures"] and any(pr["state"] == "busy" for pr in last["occupancy_probes"])

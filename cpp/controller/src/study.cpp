@@ -612,6 +612,8 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     return m;
   };
 
+  const size_t decision_plans = static_cast<size_t>(phase.integer("decision_plans", 64));
+  Json decisions = Json::array();
   double next_probe = 0;
   int unknown_probes = 0;
   std::string abort_reason;
@@ -783,7 +785,20 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     state["requests"] = reqs;
     if (waiting) {
       const double tp = monotonic_seconds();
-      Json plan = cluster_plan(state, policy, cost, options);
+      // ControllerDecisions: the planner's ranking rows (laxity, feasibility) of the first
+      // `decision_plans` plans; recording them cannot change a decision
+      PlanTrace ptrace;
+      const bool record = decisions.size() < decision_plans;
+      Json plan = cluster_plan(state, policy, cost, options, record ? &ptrace : nullptr);
+      if (record) {
+        Json dj = Json::object();
+        dj["t_ms"] = now;
+        dj["ranking"] = ptrace.rows;
+        dj["dropped"] = static_cast<long long>(ptrace.dropped);
+        dj["assignments"] = static_cast<long long>(plan.at("assignments").size());
+        dj["preempt"] = plan.at("preempt");
+        decisions.push_back(dj);
+      }
       const double pms = (monotonic_seconds() - tp) * 1000.0;
       plan_ms_total += pms;
       plan_ms_max = std::max(plan_ms_max, pms);
@@ -1082,6 +1097,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     if (!abort_reason.empty()) out["aborted"] = abort_reason;
   }
   out["spans_dropped"] = spans_dropped;
+  out["decisions"] = decisions;
   out["failures"] = failures;
   Json cfg = Json::object();
   cfg["distributed"] = distributed;

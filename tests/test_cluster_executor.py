@@ -69,6 +69,8 @@ def test_mock_cluster_pairs_batches_regroups(controller, tmp_path):
     last = _last(rep)
     assert last is not None and not last["failures"]
     assert last["counters"]["quanta"] >= 12 and last["trace"]
+    assert last["decisions"] and all(len(d["ranking"]) <= 64 for d in last["decisions"])
+    assert {"request_id", "laxity_ms", "feasible"} <= set(last["decisions"][0]["ranking"][0])
     # every video's digest equals the 4-step chain of its own seed: copies stayed consistent
     digests = {r["request_id"]: r.get("digest") for r in last["rows"]}
     assert all(digests.values())

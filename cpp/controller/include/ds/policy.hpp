@@ -28,6 +28,7 @@ struct PolicyTraits {
   bool widen_past_images = false;  // widening continues while images wait (they preempt by doorbell)
   double feasible_margin = 0.0;    // slack kept by the feasible-minimal form choice (fraction of remaining)
   double wide_efficiency = 0.0;    // >0: videos start on their widest form whose per-GPU efficiency stays above it
+  bool load_adaptive = false;      // many videos: the most GPU-efficient form; few: the usual choice
   std::string image_placement = "first";  // first | pair_fit
   bool hold_diffuse = false;      // a started video keeps its GPUs (no decode shrink)
   bool demote_late = true;        // late requests ranked behind feasible ones

@@ -46,6 +46,7 @@ struct Settings {
   double feasible_margin = 0.0;     // feasible-min keeps this fraction of the remaining time as slack
   double wide_efficiency = 0.0;     // >0: videos start on their widest form at least this efficient
   double late_short_ms = 0.0;       // late requests this short keep their EDF position
+  bool load_adaptive = false;       // many videos: most GPU-efficient form; few: normal choice
 };
 
 Settings resolve(const PolicyTraits& t, const Json& o) {
@@ -87,6 +88,7 @@ Settings resolve(const PolicyTraits& t, const Json& o) {
   s.feasible_margin = o.num("feasible_margin", t.feasible_margin);
   s.wide_efficiency = o.num("wide_efficiency", t.wide_efficiency);
   s.late_short_ms = o.num("late_short_ms", 0.0);
+  s.load_adaptive = o.flag("load_adaptive", t.load_adaptive);
   if (s.late_short_ms < 0) throw std::invalid_argument("late_short_ms must be >= 0");
   if (s.feasible_margin < 0 || s.feasible_margin > 10) throw std::invalid_argument("feasible_margin must be in [0, 10]");
   return s;
@@ -282,6 +284,22 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
   std::vector<Req> reqs;
   std::vector<Req> running;
   std::set<std::string> seen;
+  // videos that still denoise (waiting, suspended or running): the load-adaptive choice
+  // switches to the most GPU-efficient form once they could fill every CFG pair
+  int video_load = 0;
+  for (const auto& rj : state.at("requests").as_array()) {
+    const std::string st = rj.str("status", "waiting");
+    if (rj.str("kind", "") != "video" || (st != "waiting" && st != "suspended" && st != "running")) continue;
+    video_load += rj.integer("steps_done", 0) < rj.integer("steps_total", cost.steps(rj.at("class").as_string()));
+  }
+  const bool throughput_mode = s.load_adaptive && video_load * 2 >= video_capacity;
+  auto efficient_only = [&](std::vector<Form> forms, const std::string& klass) {
+    if (!throughput_mode || forms.size() < 2) return forms;
+    const Form* eff = &forms.front();
+    for (const auto& f : forms)
+      if (cost.step_ms(klass, f) * f.degree() < cost.step_ms(klass, *eff) * eff->degree()) eff = &f;
+    return std::vector<Form>{*eff};
+  };
   for (const auto& rj : state.at("requests").as_array()) {
     Req r;
     r.j = &rj;
@@ -306,10 +324,12 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
       continue;
     }
     if (r.status != "waiting" && r.status != "suspended") continue;
-    // best-case finish on the whole cluster decides feasibility
+    // best-case finish on the whole cluster decides feasibility (on the form the video would
+    // actually get when the load-adaptive choice is in throughput mode)
     if (r.video()) {
       double best = kInf;
-      for (const auto& f : forms_for(s, cost, r.klass, video_capacity)) best = std::min(best, cost.remaining_ms(rj, f));
+      for (const auto& f : efficient_only(forms_for(s, cost, r.klass, video_capacity), r.klass))
+        best = std::min(best, cost.remaining_ms(rj, f));
       if (!std::isfinite(best)) best = cost.remaining_ms(rj, Form{});
       r.best_remaining = best;
     } else {
@@ -415,6 +435,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
   std::vector<const Req*> videos, images;
   for (const auto& r : reqs) (r.video() ? videos : images).push_back(&r);
 
+
   // ---- deadline knapsack (TetriServe / SBP-ESP / v1) over movable videos --------------
   std::map<std::string, Form> dp_choice;
   if (t.deadline_dp || t.knapsack) {
@@ -459,8 +480,8 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     for (int k : pick[bw]) dp_choice[items[k].r->id] = items[k].f;
   }
 
-  auto fastest_fit = [&](const Req& r, std::vector<int>& grp_out) -> Form {
-    auto forms = forms_for(s, cost, r.klass, video_capacity);
+  auto fastest_fit = [&](const Req& r, std::vector<int>& grp_out, const std::vector<Form>* only = nullptr) -> Form {
+    auto forms = only ? *only : forms_for(s, cost, r.klass, video_capacity);
     Form best{0, 0, 0};
     double best_ms = kInf;
     for (const auto& f : forms) {
@@ -548,7 +569,10 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
       place_finish(r);
       continue;
     }
-    const auto forms = forms_for(s, cost, r.klass, video_capacity);
+    // load-adaptive form choice: when the videos in the system could fill every CFG pair,
+    // throughput decides and each video takes the form with the least GPU time per step;
+    // otherwise the usual feasible-minimal choice (and widening) keeps latency low
+    const std::vector<Form> forms = efficient_only(forms_for(s, cost, r.klass, video_capacity), r.klass);
     if (forms.empty()) continue;
     // CFG fission (approximate policies): a video whose next step runs folded (conditional
     // branch only, the guidance delta reused) continues on the conditional half of its CFG2
@@ -621,7 +645,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
           }
         }
       } else {
-        chosen = fastest_fit(r, grp);
+        chosen = fastest_fit(r, grp, &forms);
         reason = r.feasible ? "fastest-fit" : "late-fastest";
       }
     }

@@ -45,7 +45,17 @@ std::map<std::string, PolicyTraits> build_table() {
   auto put = [&](PolicyTraits t) { m.emplace(t.id, std::move(t)); };
   put(full("ditserve", "DitServe", "ours", "block preemption, pruned CFG x SP forms, CFG-pair admission, continuous image batching"));
   {
-    auto t = full("ditserve-wide", "DitServe (NVSwitch)", "ours",
+    auto t = full("ditserve-b200", "DitServe (B200)", "ours",
+                  "ditserve tuned on the measured B200 profile: load-adaptive forms (when the denoising videos "
+                  "could fill every CFG pair, each video takes its most GPU-efficient form and feasibility is "
+                  "judged on it; otherwise feasible-minimal forms with widening) and atomic images instead of "
+                  "continuous image batches");
+    t.load_adaptive = true;
+    t.continuous_batch = false;
+    put(t);
+  }
+  {
+    auto t = full("ditserve-wide", "DitServe (widest form)", "diagnostic",
                   "ditserve whose videos start on their widest form while per-GPU efficiency stays >= 0.85 "
                   "(near-linear SP scaling over NVSwitch makes the wide form fastest at no extra GPU time)");
     t.wide_efficiency = 0.85;
@@ -308,6 +318,7 @@ Json describe_policy(const PolicyTraits& t) {
   j["demote_late"] = t.demote_late;
   j["widen"] = t.widen;
   j["wide_efficiency"] = t.wide_efficiency;
+  j["load_adaptive"] = t.load_adaptive;
   j["image_placement"] = t.image_placement;
   j["image_batching"] = t.image_batching;
   j["round_steps"] = t.round_steps;

@@ -416,4 +416,22 @@ TEST("late short requests keep their EDF position with late_short_ms") {
   CHECK(find(q, "img") != nullptr);                             // short: keeps its EDF slot
 }
 
+TEST("load-adaptive forms: efficient CFG pairs under load, the usual choice when few videos run") {
+  Json pr = profile();
+  pr["classes"]["vid"]["forms"] = Json::parse(R"({"cfg2":{"step_ms":400},"cfg2sp2":{"step_ms":210},
+                                                  "cfg2sp4":{"step_ms":110}})");
+  ClusterCost c(pr);
+  std::vector<Json> many;
+  for (int k = 0; k < 6; ++k) many.push_back(req("v" + std::to_string(k), "video", "vid", 0, 1e9));
+  auto p = cluster_plan(state(8, many), "ditserve-b200", c);
+  CHECK(p.at("assignments").size() == 4);
+  for (const auto& a : p.at("assignments").as_array()) CHECK(a.at("form").as_string() == "cfg2");
+  auto q = cluster_plan(state(8, {req("a", "video", "vid", 0, 1e9)}), "ditserve-b200", c);
+  CHECK(find(q, "a")->at("degree").as_int() == 8);  // alone: widened as usual
+  // under load, feasibility is judged on the efficient form: 10 steps x 400 ms misses 3 s
+  many.push_back(req("tight", "video", "vid", 0, 3000));
+  auto r = cluster_plan(state(8, many), "ditserve-b200", c);
+  CHECK(find(r, "tight") == nullptr);               // demoted behind the feasible ones
+}
+
 int main() { return dstest::run_all(); }

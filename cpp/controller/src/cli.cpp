@@ -29,6 +29,7 @@
 #include "ds/policy.hpp"
 #include "ds/process.hpp"
 #include "ds/sim.hpp"
+#include "ds/cost.hpp"
 #include "ds/dispatch.hpp"
 #include "ds/study.hpp"
 #include "ds/workload.hpp"
@@ -90,6 +91,24 @@ Json pure_rpc(const std::string& cmd, const Json& req) {
       return select_online(req.at("rows"), req.at("now_ms").as_double(), req.str("policy", "edf"),
                            req.str("active", ""), req.contains("quantum") ? req.at("quantum") : Json(1),
                            req.get("costs").is_null() ? Json::object() : req.at("costs"));
+    if (op == "price") {  // the cost model's price of each named form of one class
+      const ClusterCost cost(req.get("profile").is_null() ? synthetic_profile() : req.at("profile"));
+      const std::string klass = req.at("class").as_string();
+      Json out = Json::object();
+      for (const auto& f : req.at("forms").as_array()) {
+        const auto t = cost.terms(klass, parse_form(f.as_string()));
+        Json row = Json::object();
+        row["step_ms"] = t.total();
+        row["measured"] = t.measured;
+        row["compute"] = t.compute;
+        row["comm"] = t.comm;
+        row["latency"] = t.latency;
+        row["exchange"] = t.exchange;
+        row["overlap"] = t.overlap;
+        out[f.as_string()] = row;
+      }
+      return out;
+    }
     if (op == "workload") return study_workload(req.at("phase"));
     if (op == "matrix") return expand_matrix(req.at("phase"));
     if (op == "summary") return request_summary(req.at("rows"));

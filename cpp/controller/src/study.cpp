@@ -1,5 +1,6 @@
 #include "ds/study.hpp"
 
+#include <dirent.h>
 #include <sys/stat.h>
 #include <unistd.h>
 
@@ -78,6 +79,75 @@ std::string fnv1a(const std::string& s) {
 }
 
 double now_ms_since(double t0) { return (monotonic_seconds() - t0) * 1000.0; }
+
+// FNV-1a over a file's bytes, folded into `h`
+uint64_t hash_file(const std::string& path, uint64_t h) {
+  std::ifstream in(path, std::ios::binary);
+  char buf[1 << 16];
+  while (in) {
+    in.read(buf, sizeof buf);
+    for (std::streamsize i = 0; i < in.gcount(); ++i) {
+      h ^= static_cast<unsigned char>(buf[i]);
+      h *= 1099511628211ull;
+    }
+  }
+  return h;
+}
+
+void list_code(const std::string& dir, std::vector<std::string>& out) {
+  DIR* d = opendir(dir.c_str());
+  if (!d) return;
+  while (dirent* e = readdir(d)) {
+    const std::string n = e->d_name;
+    if (n == "." || n == ".." || n == "__pycache__") continue;
+    const std::string p = dir + "/" + n;
+    struct stat st;
+    if (stat(p.c_str(), &st) != 0) continue;
+    if (S_ISDIR(st.st_mode)) {
+      list_code(p, out);
+      continue;
+    }
+    for (const char* ext : {".py", ".cu", ".cuh", ".cpp", ".h", ".so"}) {
+      const std::string x(ext);
+      if (n.size() > x.size() && n.compare(n.size() - x.size(), x.size(), x) == 0) {
+        out.push_back(p);
+        break;
+      }
+    }
+  }
+  closedir(d);
+}
+
+// the code a run depends on: this controller binary and the worker package's sources and
+// compiled extension; a resumed run must present the same hashes
+Json code_identity(const StudyOptions& opt) {
+  Json c = Json::object();
+  char exe[4096] = {0};
+  const ssize_t n = readlink("/proc/self/exe", exe, sizeof exe - 1);
+  char hex[20];
+  if (n > 0) {
+    std::snprintf(hex, sizeof hex, "%016llx",
+                  static_cast<unsigned long long>(hash_file(std::string(exe, n), 1469598103934665603ull)));
+    c["controller"] = hex;
+  }
+  if (!opt.package_root.empty()) {
+    std::vector<std::string> files;
+    list_code(opt.package_root + "/ditserve_b200", files);
+    std::sort(files.begin(), files.end());
+    uint64_t h = 1469598103934665603ull;
+    for (const auto& f : files) {
+      for (unsigned char ch : f.substr(opt.package_root.size())) {
+        h ^= ch;
+        h *= 1099511628211ull;
+      }
+      h = hash_file(f, h);
+    }
+    std::snprintf(hex, sizeof hex, "%016llx", static_cast<unsigned long long>(h));
+    c["worker_package"] = hex;
+    c["files"] = static_cast<long long>(files.size());
+  }
+  return c;
+}
 
 // one worker process with serialised calls
 struct Worker {
@@ -1221,16 +1291,21 @@ Json run_study(const Json& config, const StudyOptions& opt) {
   const std::string dir = opt.work_dir + "/" + run_id;
   mkdirs(dir);
   const std::string run_json = dir + "/run.json";
+  const Json code = code_identity(opt);
   if (exists(run_json)) {
     if (!opt.resume) throw std::runtime_error("run " + run_id + " exists; pass --resume to continue it");
     const Json prev = Json::parse(read_file(run_json));
     if (prev.at("identity").as_string() != identity)
       throw std::runtime_error("config changed since run " + run_id + " started; refusing to resume");
+    if (prev.contains("code") && !(prev.at("code") == code))
+      throw std::runtime_error("controller binary or worker sources changed since run " + run_id +
+                               " started; refusing to resume");
   } else {
     Json r = Json::object();
     r["run_id"] = run_id;
     r["identity"] = identity;
     r["config"] = config;
+    r["code"] = code;
     write_atomic(run_json, r.dump(1));
   }
   std::unique_ptr<Budget> budget;
@@ -1253,6 +1328,7 @@ Json run_study(const Json& config, const StudyOptions& opt) {
   Json report = Json::object();
   report["run_id"] = run_id;
   report["identity"] = identity;
+  report["code"] = code;
   Json phases_out = Json::object();
   for (const auto& phase : config.at("phases").as_array()) {
     const std::string pid = phase.at("id").as_string();

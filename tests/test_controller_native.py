@@ -80,3 +80,28 @@ def test_results_cli(controller, tmp_path):
     assert ver.returncode == 0 and json.loads(ver.stdout)["ok"]
     bad = subprocess.run([controller, "results", "explode", str(run)], capture_output=True, text=True, env=env)
     assert bad.returncode == 2
+
+
+def test_resume_refuses_changed_worker_sources(controller, tmp_path):
+    """run.json freezes the controller binary and worker package hashes; a changed source file
+    makes --resume refuse."""
+    pkg = tmp_path / "pkgroot"
+    shutil.copytree(os.path.join(ROOT, "ditserve_b200"), pkg / "ditserve_b200",
+                    ignore=shutil.ignore_patterns("__pycache__", "*.so"))
+    cfg = {"schema": "ditserve-b200.study.v1", "experiment": "freeze",
+           "workers": {"model": {"backend": "mock"}},
+           "phases": [{"id": "ops", "kind": "operations", "operations": [
+               {"op": "prepare", "spec": {"request_id": "a", "steps": 1, "seed": 1}}]}]}
+    cfgp = tmp_path / "s.json"
+    cfgp.write_text(json.dumps(cfg))
+    env = dict(os.environ, DITSERVE_PYTHON=sys.executable, DITSERVE_PACKAGE_ROOT=str(pkg))
+    cmd = [controller, "--json", "run", "--config", str(cfgp), "--run-id", "f", "--work-dir", str(tmp_path / "w")]
+    first = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=300)
+    assert first.returncode == 0, first.stderr
+    assert json.loads(first.stdout)["code"]["files"] > 10
+    same = subprocess.run(cmd + ["--resume"], capture_output=True, text=True, env=env, timeout=300)
+    assert same.returncode == 0, same.stderr
+    with open(pkg / "ditserve_b200" / "models" / "mock.py", "a") as f:
+        f.write("\n# edited\n")
+    changed = subprocess.run(cmd + ["--resume"], capture_output=True, text=True, env=env, timeout=300)
+    assert changed.returncode != 0 and "refusing to resume" in (changed.stdout + changed.stderr)

@@ -355,25 +355,50 @@ Json ints_json(const std::vector<int>& v) {
   return a;
 }
 
-// run fn(g) for every g in gs concurrently (one thread per extra member); rethrows the first error
+// a failure that is a consequence of another member's failure (its peer stopped answering, a
+// collective timed out waiting for it, or the pipe to a dead worker broke)
+bool secondary_failure(const std::string& m) {
+  for (const char* k : {"deadline", "closed its output", "write to worker", "already stopped", "timed out",
+                        "Timeout", "Connection reset", "Broken pipe", "peer flag wait"})
+    if (m.find(k) != std::string::npos) return true;
+  return false;
+}
+
+// run fn(g) for every g in gs concurrently (one thread per extra member); when members fail,
+// the primary failure is rethrown in preference to the secondary ones it caused
 std::vector<Json> fan_out(const std::vector<int>& gs, const std::function<Json(int)>& fn) {
   std::vector<std::future<Json>> fs;
   for (size_t i = 1; i < gs.size(); ++i) fs.push_back(std::async(std::launch::async, fn, gs[i]));
   std::vector<Json> out;
-  std::exception_ptr err;
+  std::vector<std::pair<std::exception_ptr, std::string>> errs;
+  auto note = [&](std::exception_ptr e) {
+    std::string m;
+    try {
+      std::rethrow_exception(e);
+    } catch (const std::exception& x) {
+      m = x.what();
+    } catch (...) {
+      m = "unknown error";
+    }
+    errs.push_back({e, m});
+  };
   try {
     out.push_back(fn(gs[0]));
   } catch (...) {
-    err = std::current_exception();
+    note(std::current_exception());
   }
   for (auto& f : fs) {
     try {
       out.push_back(f.get());
     } catch (...) {
-      if (!err) err = std::current_exception();
+      note(std::current_exception());
     }
   }
-  if (err) std::rethrow_exception(err);
+  if (!errs.empty()) {
+    for (const auto& e : errs)
+      if (!secondary_failure(e.second)) std::rethrow_exception(e.first);
+    std::rethrow_exception(errs.front().first);
+  }
   return out;
 }
 

@@ -760,8 +760,13 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     }
     if (!demand.empty()) {
       std::vector<RunningGroup> groups;
+      std::set<int> claimed;  // the two requests of a lockstep pair share one group: list it once
       for (const auto& r : running) {
         if (!r.video() || r.group.empty()) continue;
+        bool shared = false;
+        for (int gpu : r.group) shared = shared || claimed.count(gpu) > 0;
+        if (shared) continue;
+        claimed.insert(r.group.begin(), r.group.end());
         Form f = r.form.empty() ? Form{1, static_cast<int>(r.group.size()), 1} : parse_form(r.form);
         const double bms = cost.block_ms(r.klass, f);
         const double elapsed = std::max(0.0, now - r.j->num("quantum_started_ms", now));

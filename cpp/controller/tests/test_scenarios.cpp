@@ -434,4 +434,19 @@ TEST("load-adaptive forms: efficient CFG pairs under load, the usual choice when
   CHECK(find(r, "tight") == nullptr);               // demoted behind the feasible ones
 }
 
+TEST("a running lockstep pair is one preemption candidate") {
+  ClusterCost c(profile());
+  auto a = req("a", "video", "vid", 0, 1e9, 2);
+  auto b = req("b", "video", "vid", 0, 1e9, 2);
+  for (Json* r : {&a, &b}) {
+    (*r)["status"] = "running";
+    (*r)["group"] = Json::parse("[0]");
+    (*r)["form"] = "sp1";
+    (*r)["quantum_started_ms"] = 0.0;
+  }
+  auto i = req("i", "image", "img", 0, 800);
+  auto p = cluster_plan(state(1, {a, b, i}, {0}), "ditserve", c);  // must not throw on the shared group
+  CHECK(p.at("preempt").size() == 1);
+}
+
 int main() { return dstest::run_all(); }

@@ -23,7 +23,7 @@ import torch
 from torch import nn
 
 from ... import ops
-from ..wan.model import LNAffine, Linear, RMSWeight, timestep_sinusoid
+from ..wan.model import Linear, RMSWeight, timestep_sinusoid
 
 
 @dataclass(frozen=True)

@@ -6,7 +6,7 @@ plus the tiny 2-block model used for the CPU/Gloo contract gates.
 """
 from __future__ import annotations
 
-from dataclasses import asdict, dataclass, field
+from dataclasses import asdict, dataclass
 
 
 @dataclass(frozen=True)

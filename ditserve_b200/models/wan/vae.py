@@ -19,7 +19,6 @@ the mid-block attention all-gathers the (small) latent-resolution feature map.
 """
 from __future__ import annotations
 
-import math
 
 import torch
 import torch.nn.functional as F

@@ -10,7 +10,6 @@ Reference: workers/ditserve/models/profiling.py:25-136, wan/profile.py:142-358.
 """
 from __future__ import annotations
 
-import json
 import time
 from collections import defaultdict
 

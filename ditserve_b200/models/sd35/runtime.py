@@ -1,7 +1,8 @@
 """SD3.5 request states and the step-level continuous-batching engine.
 
-Each request owns a seeded latent and a flow-matching Euler scheduler (static
-shift 3.0, or the resolution-dependent mu shift).  ``advance_batch(states)``
+Each request owns a seeded latent and a flow-matching solver (Euler by default;
+DPM-Solver++ or UniPC on request) over the shifted sigma grid (static shift 3.0,
+or the resolution-dependent mu shift).  ``advance_batch(states)``
 runs ONE denoising step for every member in a single packed forward (the CFG
 branches are two segments of the same request), so requests with different
 resolutions and progress join and leave the batch between steps.  Reference:
@@ -14,7 +15,7 @@ from dataclasses import asdict, dataclass, field
 
 import torch
 
-from ...schedulers import FlowMatchEulerScheduler, mu_for_seq_len
+from ...schedulers import SOLVERS, flow_shift_sigmas, make_scheduler, mu_for_seq_len, scheduler_from_state
 from .model import SD35_MEDIUM, SD35Config, SD35Transformer
 
 
@@ -29,6 +30,8 @@ class SD35Spec:
     dynamic_shift: bool = False
     prompt: str = ""
     negative_prompt: str = ""
+    # "euler" (the SD3.5 default), "dpm++" or "unipc", all on the shifted flow-matching grid
+    solver: str = "euler"
 
     @classmethod
     def normalize(cls, raw: dict) -> "SD35Spec":
@@ -40,6 +43,8 @@ class SD35Spec:
             raise ValueError("height and width must be multiples of 16")
         if s.steps < 1:
             raise ValueError("steps must be positive")
+        if s.solver not in SOLVERS:
+            raise ValueError(f"unknown solver {s.solver!r}; expected one of {SOLVERS}")
         return s
 
     def to_dict(self):
@@ -50,7 +55,7 @@ class SD35Spec:
 class SD35State:
     spec: SD35Spec
     latents: torch.Tensor          # fp32 [C, H/8, W/8]
-    scheduler: FlowMatchEulerScheduler
+    scheduler: object               # Euler / DPM-Solver++ / UniPC (schedulers package)
     context: torch.Tensor          # [L, joint_dim]
     pooled: torch.Tensor           # [pooled_dim]
     neg_context: torch.Tensor | None
@@ -87,7 +92,8 @@ class SD35Engine:
         g = torch.Generator(device="cpu").manual_seed(int(spec.seed))
         lat = torch.randn(self.cfg.in_channels, h, w, generator=g, dtype=torch.float32).to(self.device)
         mu = mu_for_seq_len((h // self.cfg.patch) * (w // self.cfg.patch)) if spec.dynamic_shift else None
-        sched = FlowMatchEulerScheduler(spec.steps, shift=self.cfg.shift, mu=mu)
+        grid = flow_shift_sigmas(spec.steps, self.cfg.shift, mu)
+        sched = make_scheduler(spec.solver, spec.steps, sigmas=grid, flow_shift=self.cfg.shift)
         ctx, pool = synthetic_embeddings(spec.seed, spec.text_len, self.cfg.joint_dim, self.cfg.pooled_dim, 0)
         nctx = npool = None
         if spec.guidance > 1.0:
@@ -146,6 +152,6 @@ class SD35Engine:
             raise ValueError("not an SD3.5 request snapshot")
         mv = lambda t: None if t is None else t.to(self.device)
         return SD35State(spec=SD35Spec.normalize(snap["spec"]), latents=mv(snap["latents"]),
-                         scheduler=FlowMatchEulerScheduler.from_state_dict(snap["scheduler"]),
+                         scheduler=scheduler_from_state(snap["scheduler"], self.device),
                          context=mv(snap["context"]), pooled=mv(snap["pooled"]), neg_context=mv(snap["neg_context"]),
                          neg_pooled=mv(snap["neg_pooled"]), step=int(snap["step"]))

@@ -18,7 +18,7 @@ from dataclasses import asdict, dataclass, field
 
 import torch
 
-from ...schedulers import UniPCFlowScheduler
+from ...schedulers import SOLVERS, make_scheduler, scheduler_from_state, unipc_flow_sigmas
 from .config import CONFIGS, WanConfig
 from .model import LocalAttention, WanTransformer
 
@@ -38,6 +38,8 @@ class WanSpec:
     negative_prompt: str = ""
     # approximate mode (opt-in): late-step CFG folding {"warm_frac", "threshold", "fold_span"}
     cfg_fold: dict | None = None
+    # "unipc" (the Wan default), "dpm++" (DPM-Solver++ 2M) or "euler", all on the flow-shift grid
+    solver: str = "unipc"
 
     @classmethod
     def normalize(cls, raw: dict) -> "WanSpec":
@@ -54,6 +56,8 @@ class WanSpec:
             raise ValueError("frames must be 4k+1")
         if spec.steps < 1:
             raise ValueError("steps must be positive")
+        if spec.solver not in SOLVERS:
+            raise ValueError(f"unknown solver {spec.solver!r}; expected one of {SOLVERS}")
         return spec
 
     def config(self) -> WanConfig:
@@ -78,7 +82,7 @@ def synthetic_text(seed: int, length: int, dim: int, which: int) -> torch.Tensor
 class WanRequestState:
     spec: WanSpec
     latents: torch.Tensor            # fp32 [1, C, F, H, W], device
-    scheduler: UniPCFlowScheduler
+    scheduler: object               # UniPC / DPM-Solver++ / Euler (schedulers package)
     context: torch.Tensor            # [1, L, text_dim] model dtype, device
     negative: torch.Tensor | None    # [1, L, text_dim] or None (guidance <= 1)
     step: int = 0
@@ -144,7 +148,9 @@ class WanEngine:
             context = synthetic_text(spec.seed, L, self.cfg.text_dim, 0)
         if negative is None and spec.guidance > 1.0:
             negative = synthetic_text(spec.seed, L, self.cfg.text_dim, 1)
-        sched = UniPCFlowScheduler(spec.steps, spec.flow_shift or self.cfg.flow_shift)
+        shift = spec.flow_shift or self.cfg.flow_shift
+        grid = unipc_flow_sigmas(spec.steps, shift) if spec.solver == "euler" else None  # UniPC's grid
+        sched = make_scheduler(spec.solver, spec.steps, sigmas=grid, flow_shift=shift)
         st = WanRequestState(spec=spec, latents=latents, scheduler=sched,
                              context=context.to(self.device, self.dtype),
                              negative=None if negative is None else negative.to(self.device, self.dtype))
@@ -356,7 +362,7 @@ class WanEngine:
             raise ValueError("not a Wan request snapshot")
         spec = WanSpec.normalize(snap["spec"])
         st = WanRequestState(spec=spec, latents=snap["latents"].to(self.device, copy=True),
-                             scheduler=UniPCFlowScheduler.from_state_dict(snap["scheduler"], self.device),
+                             scheduler=scheduler_from_state(snap["scheduler"], self.device),
                              context=snap["context"].to(self.device, copy=True),
                              negative=None if snap["negative"] is None else snap["negative"].to(self.device, copy=True),
                              step=int(snap["step"]))

@@ -41,12 +41,21 @@ def flow_shift_sigmas(steps: int, shift: float = 3.0, mu: float | None = None, t
 
 
 class FlowMatchEulerScheduler:
-    def __init__(self, steps: int, shift: float = 3.0, mu: float | None = None, train_steps: int = 1000):
+    def __init__(self, steps: int, shift: float = 3.0, mu: float | None = None, train_steps: int = 1000,
+                 sigmas: list[float] | None = None):
         self.steps = int(steps)
         self.shift = float(shift)
         self.mu = None if mu is None else float(mu)
         self.train_steps = int(train_steps)
-        self.sigmas = flow_shift_sigmas(self.steps, self.shift, self.mu, self.train_steps)
+        # an explicit grid (steps + 1 values) replaces the shifted linspace, e.g. the UniPC grid
+        # so that an Euler run of a Wan request walks the same sigmas as its UniPC run
+        self.custom_sigmas = None if sigmas is None else [float(v) for v in sigmas]
+        if self.custom_sigmas is not None:
+            if len(self.custom_sigmas) != self.steps + 1:
+                raise ValueError("sigmas must hold steps + 1 values (the last one the terminal sigma)")
+            self.sigmas = list(self.custom_sigmas)
+        else:
+            self.sigmas = flow_shift_sigmas(self.steps, self.shift, self.mu, self.train_steps)
         self.timesteps = [s * self.train_steps for s in self.sigmas[:-1]]
         self.step_index = 0
 
@@ -68,12 +77,12 @@ class FlowMatchEulerScheduler:
 
     def state_dict(self, device=None) -> dict:
         return dict(kind="flowmatch_euler.v1", steps=self.steps, shift=self.shift, mu=self.mu,
-                    train_steps=self.train_steps, step_index=self.step_index)
+                    train_steps=self.train_steps, sigmas=self.custom_sigmas, step_index=self.step_index)
 
     @classmethod
     def from_state_dict(cls, sd: dict, device=None) -> "FlowMatchEulerScheduler":
         if sd.get("kind") != "flowmatch_euler.v1":
             raise ValueError("not a flow-matching Euler scheduler state")
-        s = cls(sd["steps"], sd["shift"], sd["mu"], sd["train_steps"])
+        s = cls(sd["steps"], sd["shift"], sd["mu"], sd["train_steps"], sd.get("sigmas"))
         s.step_index = int(sd["step_index"])
         return s

@@ -38,8 +38,12 @@ def unipc_flow_sigmas(steps: int, flow_shift: float = 3.0, train_steps: int = 10
 
 
 def _lam(s: float) -> float:
+    # the grid's ends (pure data, pure noise) have infinite log-SNR; the update coefficients
+    # take their finite limits there
     if s <= 0.0:
         return math.inf
+    if s >= 1.0:
+        return -math.inf
     return math.log(1.0 - s) - math.log(s)
 
 
@@ -69,7 +73,7 @@ class UniPCFlowScheduler:
     """Stateful UniPC solver; device buffers hold the data-estimate history."""
 
     def __init__(self, steps: int, flow_shift: float = 3.0, order: int = 2, lower_order_final: bool = True,
-                 train_steps: int = 1000):
+                 train_steps: int = 1000, sigmas: list[float] | None = None):
         if order not in (1, 2, 3):
             raise ValueError("UniPC order must be 1, 2 or 3")
         self.steps = int(steps)
@@ -77,7 +81,13 @@ class UniPCFlowScheduler:
         self.order = int(order)
         self.lower_order_final = bool(lower_order_final)
         self.train_steps = int(train_steps)
-        self.sigmas = unipc_flow_sigmas(self.steps, self.flow_shift, self.train_steps)
+        self.custom_sigmas = None if sigmas is None else [float(v) for v in sigmas]
+        if self.custom_sigmas is not None:
+            if len(self.custom_sigmas) != self.steps + 1:
+                raise ValueError("sigmas must hold steps + 1 values (the last one the terminal sigma)")
+            self.sigmas = list(self.custom_sigmas)
+        else:
+            self.sigmas = unipc_flow_sigmas(self.steps, self.flow_shift, self.train_steps)
         self.timesteps = [s * self.train_steps for s in self.sigmas[:-1]]
         self.step_index = 0
         self.lower_order_nums = 0
@@ -188,7 +198,7 @@ class UniPCFlowScheduler:
         mv = (lambda t: t.detach().to(device, copy=True)) if device is not None else (lambda t: t)
         return dict(kind="unipc_flow.v1", steps=self.steps, flow_shift=self.flow_shift, order=self.order,
                     lower_order_final=self.lower_order_final, train_steps=self.train_steps,
-                    step_index=self.step_index, lower_order_nums=self.lower_order_nums,
+                    sigmas=self.custom_sigmas, step_index=self.step_index, lower_order_nums=self.lower_order_nums,
                     this_order=self.this_order, hist_sigmas=list(self.hist_sigmas),
                     hist=[mv(t) for t in self.hist], last=None if self.last is None else mv(self.last))
 
@@ -196,7 +206,8 @@ class UniPCFlowScheduler:
     def from_state_dict(cls, sd: dict, device: str | torch.device | None = None) -> "UniPCFlowScheduler":
         if sd.get("kind") != "unipc_flow.v1":
             raise ValueError("not a UniPC flow scheduler state")
-        s = cls(sd["steps"], sd["flow_shift"], sd["order"], sd["lower_order_final"], sd["train_steps"])
+        s = cls(sd["steps"], sd["flow_shift"], sd["order"], sd["lower_order_final"], sd["train_steps"],
+                sd.get("sigmas"))
         mv = (lambda t: t.to(device, copy=True)) if device is not None else (lambda t: t.clone())
         s.step_index = int(sd["step_index"])
         s.lower_order_nums = int(sd["lower_order_nums"])

@@ -180,6 +180,24 @@ def test_sched_step_matches_reference():
     torch.testing.assert_close(lo.cpu(), lr, rtol=1e-5, atol=1e-4)
 
 
+@pytest.mark.parametrize("solver", ["unipc", "dpm++", "euler"])
+def test_solver_trajectory_through_kernel(solver):
+    """A whole solver run with the CUDA step (CFG combine + update) equals the fp32 reference."""
+    from ditserve_b200.schedulers import make_scheduler
+    torch.manual_seed(11)
+    d = _dev()
+    n = 16 * 21 * 8 * 8
+    x = torch.randn(n, device=d)
+    xr = x.cpu().clone()
+    a, b = make_scheduler(solver, 6, flow_shift=5.0), make_scheduler(solver, 6, flow_shift=5.0)
+    while not a.done:
+        cond = torch.randn(n, device=d).bfloat16()
+        unc = torch.randn(n, device=d).bfloat16()
+        a.step(x, cond, unc, 5.0)
+        b.step(xr, cond.cpu(), unc.cpu(), 5.0, kernel=ops.sched_step_reference)
+    torch.testing.assert_close(x.cpu(), xr, rtol=1e-4, atol=1e-3)
+
+
 @pytest.mark.parametrize("D", [64, 128])
 def test_attention_dual_range_segments(D):
     """MMDiT joint attention: each segment = an image block range + a text block range."""

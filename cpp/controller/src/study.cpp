@@ -165,12 +165,23 @@ std::unique_ptr<Worker> spawn_worker(const Json& def, const StudyOptions& opt, c
   const std::string backend = def.at("backend").as_string();
   const bool gpu_backend = backend == "wan" || backend == "sd35";
   if (gpu_backend && !opt.allow_gpu) throw std::runtime_error("backend " + backend + " needs --allow-gpu");
+  const std::string config = (def.get("config").is_null() ? Json::object() : def.at("config")).dump();
   std::vector<std::string> argv = {def.str("python", opt.python), "-m", "ditserve_b200.runtime.worker",
-                                   "--backend", backend, "--config",
-                                   (def.get("config").is_null() ? Json::object() : def.at("config")).dump()};
+                                   "--backend", backend, "--config", config};
   std::map<std::string, std::string> env;
   if (!opt.package_root.empty()) env["PYTHONPATH"] = opt.package_root;
-  if (gpu == "all") {
+  if (def.contains("remote")) {
+    // a worker on another node: the local process is the bridge proxy (worker protocol on
+    // stdin/stdout, relayed to the node's daemon); the remote worker gets remote_env
+    argv = {def.str("python", opt.python), "-m", "ditserve_b200.runtime.remote_bridge", "proxy", "--connect",
+            def.at("remote").as_string(), "--backend", backend, "--config", config};
+    if (def.contains("remote_env"))
+      for (const auto& [k, v] : def.at("remote_env").as_object()) {
+        argv.push_back("--env");
+        argv.push_back(k + "=" + (v.is_string() ? v.as_string() : v.dump()));
+      }
+    env["CUDA_VISIBLE_DEVICES"] = "";
+  } else if (gpu == "all") {
     // every GPU visible (world members address their peers' memory); device chosen in config
   } else if (!gpu.empty()) {
     env["CUDA_VISIBLE_DEVICES"] = gpu;
@@ -420,6 +431,20 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     throw std::invalid_argument("sp_transport must be collective or export");
   if (transport == "collective" && !distributed)
     throw std::invalid_argument("sp_transport collective needs distributed: true");
+  // remote_slots: {"<slot>": {"address": "host:port", "device": "<GPU index on that node>"}}
+  // puts a slot's workers on another node behind the bridge; state reaches them by host-staged
+  // continuation packets, so the peer-memory world (one node) is not available with them
+  const Json remote_slots = phase.get("remote_slots").is_null() ? Json::object() : phase.at("remote_slots");
+  if (!remote_slots.is_object()) throw std::invalid_argument("remote_slots must be an object");
+  std::set<int> remote;
+  for (const auto& [k, v] : remote_slots.as_object()) {
+    const int g = std::stoi(k);
+    if (g < 0 || g >= gpus) throw std::invalid_argument("remote slot " + k + " outside the phase's GPUs");
+    if (!v.is_object() || !v.contains("address")) throw std::invalid_argument("remote slot " + k + " needs an address");
+    remote.insert(g);
+  }
+  if (!remote.empty() && distributed)
+    throw std::invalid_argument("remote_slots need distributed: false (the export transport crosses nodes)");
   const std::string path = phase.str("collectives", "fused");
   const int batch_quantum = static_cast<int>(phase.integer("batch_quantum_steps", 4));
   // decode: finished videos run the VAE in chunked quanta (decode_start / decode_poll) and
@@ -432,6 +457,15 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     Json d = def;
     const bool gpu = is_gpu(def);
     std::string visible = gpu ? std::to_string(gidx) : "";
+    if (remote.count(gidx)) {
+      const Json& rs = remote_slots.at(std::to_string(gidx));
+      d["remote"] = rs.at("address");
+      Json env = Json::object();
+      if (gpu) env["CUDA_VISIBLE_DEVICES"] = rs.str("device", std::to_string(gidx));
+      else env["CUDA_VISIBLE_DEVICES"] = "";
+      d["remote_env"] = env;
+      return spawn_worker(d, opt, run_dir + "/" + tag + std::to_string(gidx) + ".log", "");
+    }
     Json c = d.get("config").is_null() ? Json::object() : d.at("config");
     if (world_member && gpu && !c.contains("device")) {  // peers' memory must be visible (IPC / NVLink)
       c["device"] = "cuda:" + std::to_string(gidx);
@@ -722,7 +756,8 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     while (true) {
       Json q = Json::object();
       Json idx = Json::array();
-      for (int g = 0; g < gpus; ++g) idx.push_back(g);
+      for (int g = 0; g < gpus; ++g)
+        if (!remote.count(g)) idx.push_back(g);  // the local probe sees this node's GPUs only
       q["gpus"] = idx;
       q["own_pids"] = own_pids;
       try {
@@ -743,7 +778,8 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
       next_probe = now + guard_interval_ms;
       Json q = Json::object();
       Json idx = Json::array();
-      for (int g = 0; g < gpus; ++g) idx.push_back(g);
+      for (int g = 0; g < gpus; ++g)
+        if (!remote.count(g)) idx.push_back(g);
       q["gpus"] = idx;
       q["own_pids"] = own_pids;
       Json occ;

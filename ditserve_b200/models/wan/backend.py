@@ -259,6 +259,7 @@ class WanBackend(Backend):
         if key in self.states:
             raise ValueError("duplicate live state_id")
         self.states[key] = st
+        Path(request["path"]).unlink(missing_ok=True)  # a packet is single-use (one export per hop)
         return dict(state_id=key, progress=self._progress(st))
 
     def encode_start(self, request):

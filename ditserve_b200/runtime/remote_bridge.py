@@ -6,15 +6,23 @@
     python -m ditserve_b200.runtime.remote_bridge proxy --connect node1:7700 --backend wan --config '{...}'
 
 Framing on the wire: 4-byte big-endian length + one JSON document, TCP_NODELAY.
-The first frame of a connection is {"bridge": "spawn", "backend", "config"}; the
-daemon starts a local worker and relays protocol lines both ways.  Extra frames:
+The first frame of a connection is {"bridge": "spawn", "backend", "config", "env"}; the
+daemon starts a local worker in a private session directory (the worker's
+``transfer_dir`` unless the config names one; ``env`` may set CUDA_VISIBLE_DEVICES and
+NCCL_* / DITSERVE_* variables) and relays protocol lines both ways.  Extra frames:
 * {"bridge": "ring", "slot", "epoch"} — doorbell mirroring: the proxy watches the
   controller's local doorbell files and the daemon writes the epoch into its own
   copy, so a remote block quantum stops at its next check like a local one;
-* {"bridge": "put_file", "path", "data_b64"} / {"bridge": "get_file", "path"} —
-  /dev/shm slabs and artifacts;
+* {"bridge": "put_file", "name", "offset", "data_b64", "last"} /
+  {"bridge": "get_file", "path", "offset", "unlink"} — chunked file staging, confined to
+  the session directory;
 * {"bridge": "occupancy"} — the remote node's GPU occupancy probe.
-Requests naming a doorbell get the path rewritten to the daemon-side mirror.
+Requests naming a doorbell get the path rewritten to the daemon-side mirror.  Continuation
+packets cross the bridge transparently: a ``block_export`` reply's packet file is fetched
+into the proxy's staging directory (and removed remotely) and a ``block_import`` of a
+local packet file is first pushed into the session directory, so the controller moves
+state between a local and a remote worker, or between two nodes, exactly as between two
+local workers.
 Reference: workers/ditserve/runtime/remote_bridge.py:1-1009.
 """
 from __future__ import annotations
@@ -23,6 +31,7 @@ import argparse
 import base64
 import json
 import os
+import shutil
 import socket
 import struct
 import subprocess
@@ -32,6 +41,9 @@ import threading
 import time
 
 from .doorbell import Doorbell
+
+
+CHUNK = 8 << 20   # raw bytes per file-staging frame (base64 keeps a frame well under the 64 MiB cap)
 
 
 def send_frame(sock: socket.socket, obj) -> None:
@@ -68,6 +80,7 @@ class BridgeDaemon:
         self.port = self.server.getsockname()[1]
         self.python = python
         self.workdir = workdir or tempfile.mkdtemp(prefix="ds-bridge-")
+        os.makedirs(self.workdir, exist_ok=True)
         self.threads = []
         self._stop = threading.Event()
 
@@ -78,8 +91,10 @@ class BridgeDaemon:
                 conn, _ = self.server.accept()
             except socket.timeout:
                 continue
+            except OSError:  # the listening socket was closed by stop()
+                break
             conn.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
-            t = threading.Thread(target=self._session, args=(conn,), daemon=True)
+            t = threading.Thread(target=self._guarded_session, args=(conn,), daemon=True)
             t.start()
             self.threads.append(t)
 
@@ -87,24 +102,49 @@ class BridgeDaemon:
         self._stop.set()
         self.server.close()
 
+    def _guarded_session(self, conn: socket.socket):
+        try:
+            self._session(conn)
+        except Exception:  # noqa: BLE001 - a failed session ends its connection, not the daemon
+            conn.close()
+
+    ENV_KEYS = ("CUDA_VISIBLE_DEVICES",)
+    ENV_PREFIXES = ("NCCL_", "DITSERVE_")
+
     def _session(self, conn: socket.socket):
         first = recv_frame(conn)
         if not first or first.get("bridge") != "spawn":
             conn.close()
             return
+        sdir = os.path.realpath(tempfile.mkdtemp(prefix="session-", dir=self.workdir))
         env = dict(os.environ)
+        for k, v in (first.get("env") or {}).items():
+            if k in self.ENV_KEYS or k.startswith(self.ENV_PREFIXES):
+                env[str(k)] = str(v)
         root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
         env["PYTHONPATH"] = root + os.pathsep + env.get("PYTHONPATH", "")
+        config = dict(first.get("config", {}))
+        config.setdefault("transfer_dir", sdir)
+        roots = {sdir, os.path.realpath(str(config["transfer_dir"]))}
         proc = subprocess.Popen([self.python, "-m", "ditserve_b200.runtime.worker", "--backend", first["backend"],
-                                 "--config", json.dumps(first.get("config", {}))], stdin=subprocess.PIPE,
+                                 "--config", json.dumps(config)], stdin=subprocess.PIPE,
                                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True, env=env)
         bells: dict = {}
         send_lock = threading.Lock()
 
+        def reply(obj):
+            with send_lock:
+                send_frame(conn, obj)
+
+        def confined(path: str) -> str:
+            real = os.path.realpath(path)
+            if not any(real == r or real.startswith(r + os.sep) for r in roots):
+                raise PermissionError(f"{path} is outside the session's directories")
+            return real
+
         def pump():
             for line in proc.stdout:
-                with send_lock:
-                    send_frame(conn, {"line": line})
+                reply({"line": line})
         threading.Thread(target=pump, daemon=True).start()
         try:
             while True:
@@ -118,26 +158,42 @@ class BridgeDaemon:
                 elif kind == "ring":
                     slot = str(msg["slot"])
                     if slot not in bells:
-                        bells[slot] = Doorbell(os.path.join(self.workdir, f"bell-{slot}"), create=True)
+                        bells[slot] = Doorbell(os.path.join(sdir, f"bell-{slot}"), create=True)
                     bells[slot].ring(int(msg["epoch"]))
                 elif kind == "bell_path":
                     slot = str(msg["slot"])
                     if slot not in bells:
-                        bells[slot] = Doorbell(os.path.join(self.workdir, f"bell-{slot}"), create=True)
-                    with send_lock:
-                        send_frame(conn, {"bridge": "bell_path", "path": bells[slot].path})
+                        bells[slot] = Doorbell(os.path.join(sdir, f"bell-{slot}"), create=True)
+                    reply({"bridge": "bell_path", "path": bells[slot].path})
                 elif kind == "put_file":
-                    with open(msg["path"], "wb") as f:
-                        f.write(base64.b64decode(msg["data_b64"]))
+                    try:
+                        name = str(msg["name"])
+                        if not name or os.path.basename(name) != name or name in (".", ".."):
+                            raise PermissionError("put_file takes a plain file name")
+                        path = os.path.join(sdir, name)
+                        with open(path, "r+b" if int(msg.get("offset", 0)) else "wb") as f:
+                            f.seek(int(msg.get("offset", 0)))
+                            f.write(base64.b64decode(msg["data_b64"]))
+                        reply({"bridge": "put_file", "path": path})
+                    except (OSError, ValueError, KeyError) as exc:
+                        reply({"bridge": "put_file", "error": str(exc)})
                 elif kind == "get_file":
-                    with open(msg["path"], "rb") as f:
-                        data = base64.b64encode(f.read()).decode()
-                    with send_lock:
-                        send_frame(conn, {"bridge": "file", "path": msg["path"], "data_b64": data})
+                    try:
+                        path = confined(msg["path"])
+                        off = int(msg.get("offset", 0))
+                        with open(path, "rb") as f:
+                            f.seek(off)
+                            data = f.read(CHUNK)
+                            eof = f.tell() >= os.fstat(f.fileno()).st_size
+                        if eof and msg.get("unlink"):
+                            os.unlink(path)
+                        reply({"bridge": "file", "path": msg["path"], "offset": off,
+                               "data_b64": base64.b64encode(data).decode(), "eof": eof})
+                    except (OSError, ValueError, KeyError) as exc:
+                        reply({"bridge": "file", "path": msg.get("path"), "error": str(exc)})
                 elif kind == "occupancy":
                     from .occupancy import occupancy
-                    with send_lock:
-                        send_frame(conn, {"bridge": "occupancy", "result": occupancy(msg.get("gpus"))})
+                    reply({"bridge": "occupancy", "result": occupancy(msg.get("gpus"))})
         finally:
             try:
                 proc.stdin.close()
@@ -150,16 +206,21 @@ class BridgeDaemon:
             for b in bells.values():
                 b.close()
             conn.close()
+            shutil.rmtree(sdir, ignore_errors=True)
 
 
 class BridgeProxy:
     """Stand-in worker: protocol lines on stdin/stdout, relayed to a remote daemon."""
 
-    def __init__(self, address: str, backend: str, config: dict):
+    def __init__(self, address: str, backend: str, config: dict, env: dict | None = None,
+                 stage_dir: str | None = None):
         host, port = address.rsplit(":", 1)
         self.sock = socket.create_connection((host, int(port)))
         self.sock.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
-        send_frame(self.sock, {"bridge": "spawn", "backend": backend, "config": config})
+        send_frame(self.sock, {"bridge": "spawn", "backend": backend, "config": config, "env": env or {}})
+        shm = "/dev/shm" if os.path.isdir("/dev/shm") else None
+        self.stage_dir = stage_dir or tempfile.mkdtemp(prefix="ds-bridge-stage-", dir=shm)
+        self.staged = 0
         self.watch: dict = {}   # local bell path -> (slot, last epoch)
         self.remote_path: dict = {}
         self.lock = threading.Lock()
@@ -224,11 +285,61 @@ class BridgeProxy:
                 self.remote_path[path] = rp["path"]
         return dict(req, doorbell=dict(bell, path=self.remote_path[path]))
 
+    def _call(self, frame: dict, kind: str) -> dict:
+        with self.lock:
+            send_frame(self.sock, frame)
+        msg = self._next(lambda m: m.get("bridge") == kind)
+        if msg is None:
+            raise ConnectionError("bridge daemon closed the connection")
+        if "error" in msg:
+            raise OSError(f"bridge {kind}: {msg['error']}")
+        return msg
+
+    def push_file(self, local: str) -> str:
+        """Copy a local file into the remote session directory; returns the remote path."""
+        self.staged += 1
+        name = f"in-{self.staged}-{os.path.basename(local)}"
+        remote = None
+        with open(local, "rb") as f:
+            off = 0
+            while True:
+                data = f.read(CHUNK)
+                if off and not data:
+                    break
+                remote = self._call({"bridge": "put_file", "name": name, "offset": off,
+                                     "data_b64": base64.b64encode(data).decode()}, "put_file")["path"]
+                off += len(data)
+                if len(data) < CHUNK:
+                    break
+        return remote
+
+    def pull_file(self, remote: str, unlink: bool = True) -> str:
+        """Fetch a remote session file into the staging directory; returns the local path."""
+        self.staged += 1
+        local = os.path.join(self.stage_dir, f"out-{self.staged}-{os.path.basename(remote)}")
+        with open(local, "wb") as f:
+            off = 0
+            while True:
+                msg = self._call({"bridge": "get_file", "path": remote, "offset": off, "unlink": unlink}, "file")
+                data = base64.b64decode(msg["data_b64"])
+                f.write(data)
+                off += len(data)
+                if msg["eof"]:
+                    break
+        return local
+
     def relay(self, line: str) -> str:
+        req = None
+        pushed = None
         try:
             req = json.loads(line)
             if isinstance(req, dict):
-                line = json.dumps(self._mirror(req)) + "\n"
+                req = self._mirror(req)
+                if req.get("op") == "block_import" and isinstance(req.get("path"), str) \
+                        and os.path.isfile(req["path"]):
+                    pushed = req["path"]
+                    req = dict(req, path=self.push_file(pushed))
+                line = json.dumps(req) + "\n"
         except ValueError:
             pass  # the remote worker produces the protocol error reply
         with self.lock:
@@ -236,11 +347,23 @@ class BridgeProxy:
         msg = self._next(lambda m: "line" in m)
         if msg is None:
             raise ConnectionError("bridge daemon closed the connection")
-        return msg["line"]
+        out = msg["line"]
+        if isinstance(req, dict) and req.get("op") in ("block_import", "block_export"):
+            rep = json.loads(out)
+            if rep.get("ok") and pushed is not None:
+                os.unlink(pushed)  # consumed, as a local import consumes its packet
+            res = rep.get("result")
+            if rep.get("ok") and req["op"] == "block_export" and isinstance(res, dict) \
+                    and isinstance(res.get("path"), str):
+                res["path"] = self.pull_file(res["path"])
+                out = json.dumps(rep) + "\n"
+        return out
 
     def close(self):
         self._stop.set()
         self.sock.close()
+        if not os.listdir(self.stage_dir):
+            os.rmdir(self.stage_dir)
 
 
 def main(argv=None):
@@ -252,6 +375,9 @@ def main(argv=None):
     p.add_argument("--connect", required=True)
     p.add_argument("--backend", required=True)
     p.add_argument("--config", default="{}")
+    p.add_argument("--env", action="append", default=[], metavar="KEY=VALUE",
+                   help="environment of the remote worker (CUDA_VISIBLE_DEVICES, NCCL_*, DITSERVE_*)")
+    p.add_argument("--stage-dir", default=None, help="local directory for packets fetched from the node")
     args = ap.parse_args(argv)
     if args.mode == "daemon":
         host, port = args.listen.rsplit(":", 1)
@@ -259,7 +385,8 @@ def main(argv=None):
         print(json.dumps({"listening": daemon.port}), flush=True)
         daemon.serve_forever()
         return 0
-    proxy = BridgeProxy(args.connect, args.backend, json.loads(args.config))
+    env = dict(kv.split("=", 1) for kv in args.env)
+    proxy = BridgeProxy(args.connect, args.backend, json.loads(args.config), env, args.stage_dir)
     out = sys.stdout
     for line in sys.stdin:
         if not line.strip():

@@ -65,6 +65,56 @@ def test_remote_bridge_relays_ops_and_mirrors_doorbells(tmp_path):
         daemon.stop()
 
 
+def test_remote_bridge_moves_packets_between_nodes(tmp_path):
+    """A continuation packet crosses the bridge both ways: a remote export lands in the
+    proxy's staging directory, a local packet is pushed into the remote session for import,
+    and the run ends bit-identical to an unmoved one.  File staging stays inside the session."""
+    from ditserve_b200.models.wan.backend import WanBackend
+    from ditserve_b200.runtime.remote_bridge import BridgeDaemon, BridgeProxy
+    daemon = BridgeDaemon("127.0.0.1", 0, workdir=str(tmp_path / "node1"))
+    threading.Thread(target=daemon.serve_forever, daemon=True).start()
+    stage = tmp_path / "stage"
+    stage.mkdir()
+    proxy = BridgeProxy(f"127.0.0.1:{daemon.port}", "wan", {"model": "wan-tiny", "device": "cpu"},
+                        env={"CUDA_VISIBLE_DEVICES": "", "PATH_NOT_PASSED": "x"}, stage_dir=str(stage))
+    ids = iter(range(1, 1000))
+
+    def call(op, **kw):
+        rep = json.loads(proxy.relay(json.dumps(dict(version=1, id=next(ids), op=op, **kw)) + "\n"))
+        assert rep["ok"], rep
+        return rep["result"]
+
+    spec = dict(request_id="v", height=64, width=64, frames=5, steps=3, seed=5)
+    try:
+        call("hello")
+        call("prepare", spec=spec)
+        call("advance", state_id="v", quantum="step")
+        pk = call("block_export", state_id="v")
+        assert pk["path"].startswith(str(stage)) and os.path.getsize(pk["path"]) == pk["bytes"]
+        call("release", state_id="v")
+        local = WanBackend({"model": "wan-tiny", "device": "cpu", "transfer_dir": str(tmp_path)})
+        local.block_import(dict(id=1, state_id="v", path=pk["path"], manifest=pk["manifest"]))
+        assert not os.path.exists(pk["path"])               # single-use packet consumed
+        local.advance(dict(id=2, state_id="v", quantum="step"))
+        back = local.block_export(dict(id=3, state_id="v"))
+        r = call("block_import", state_id="v", path=back["path"], manifest=back["manifest"])
+        assert r["progress"]["step"] == 2 and not os.path.exists(back["path"])
+        call("advance", state_id="v", quantum="step")
+        moved = call("finish", state_id="v", output_mode="digest")["value"]
+        # the file frames cannot reach outside the session directory
+        with pytest.raises(OSError):
+            proxy.pull_file(str(tmp_path / "stage" / "nothing"))
+        with pytest.raises(OSError):
+            proxy._call({"bridge": "put_file", "name": "../escape", "data_b64": ""}, "put_file")
+    finally:
+        proxy.close()
+        daemon.stop()
+    ref = WanBackend({"model": "wan-tiny", "device": "cpu", "transfer_dir": str(tmp_path)})
+    ref.prepare(dict(id=1, spec=spec))
+    ref.advance(dict(id=2, state_id="v", steps=3))
+    assert ref.finish(dict(id=3, state_id="v", output_mode="digest"))["value"] == moved
+
+
 def test_snapshot_integrity(tmp_path):
     from ditserve_b200.runtime.model_integrity import IntegrityError, build_manifest, verify_snapshot
     (tmp_path / "transformer").mkdir()

@@ -55,6 +55,11 @@ class ClusterCost {
   double batch_ms(const std::string& klass, int size) const;
   double continuous_step_ms(const std::string& klass, double effective_size) const;
   double effective_batch(const std::string& klass, const std::vector<const Json*>& members, bool packing) const;
+  // the member class with the most tokens (ties: the smaller name); a mixed continuous batch is
+  // priced on its table, so the price does not depend on which member anchors the batch
+  std::string batch_anchor(const std::vector<const Json*>& members, const std::string& fallback) const;
+  double continuous_batch_step_ms(const std::vector<const Json*>& members, bool packing,
+                                  const std::string& fallback) const;
   double image_step_ms(const std::string& klass) const;
   double resume_ms(const std::string& klass) const;
   double resize_ms() const { return resize_ms_; }

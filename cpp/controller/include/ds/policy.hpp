@@ -45,6 +45,13 @@ struct PolicyTraits {
   bool continuous_batch = false;
   bool sequence_packing = false;
   bool bubble_free = false;
+  // feasibility guards of the full system: a video does not widen to meet its own deadline
+  // when that leaves two or more feasible videos without GPUs; an in-flight video past half
+  // of its steps with a small overrun keeps its rank (sunk-work deadband); a step-boundary
+  // video does not migrate to another group of the same size when the resize would make it
+  // late; images take GPUs that the highest-laxity suspended video holds
+  bool feasibility_guards = false;
+  bool idle_widening = false;     // widen below the efficiency threshold onto GPUs nobody else needs
 };
 
 const PolicyTraits& policy_traits(const std::string& name);  // throws std::invalid_argument

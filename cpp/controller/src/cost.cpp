@@ -196,4 +196,24 @@ double ClusterCost::effective_batch(const std::string& name, const std::vector<c
   return packing ? sum / base : largest * members.size() / base;
 }
 
+std::string ClusterCost::batch_anchor(const std::vector<const Json*>& members, const std::string& fallback) const {
+  std::string best = fallback;
+  double best_tokens = -1;
+  for (const Json* m : members) {
+    const std::string c = m->str("class", fallback);
+    const double tok = has_class(c) ? klass(c).num("tokens", 1.0) : 1.0;
+    if (tok > best_tokens || (tok == best_tokens && c < best)) {
+      best_tokens = tok;
+      best = c;
+    }
+  }
+  return best;
+}
+
+double ClusterCost::continuous_batch_step_ms(const std::vector<const Json*>& members, bool packing,
+                                             const std::string& fallback) const {
+  const std::string anchor = batch_anchor(members, fallback);
+  return continuous_step_ms(anchor, effective_batch(anchor, members, packing));
+}
+
 }  // namespace ds

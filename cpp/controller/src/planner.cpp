@@ -73,11 +73,16 @@ Settings resolve(const PolicyTraits& t, const Json& o) {
   s.t.feasible_img_priority = o.flag("feasible_img_priority", t.feasible_img_priority);
   s.t.blocks = o.flag("block_preemption", t.blocks);
   s.t.sequence_packing = o.flag("sequence_packing", t.sequence_packing);
+  s.t.bubble_free = t.continuous_batch && o.flag("bubble_free", t.bubble_free);
   s.quantum_blocks = static_cast<int>(o.integer("quantum_blocks", 0));
-  const int cb_default = t.continuous_batch ? 8 : 0;
-  s.continuous_batch = static_cast<int>(o.integer("continuous_batch", cb_default));
-  if (!t.continuous_batch && !o.contains("continuous_batch")) s.continuous_batch = 0;
-  if (s.continuous_batch < 0 || s.continuous_batch > 8) throw std::invalid_argument("continuous_batch must be 0..8");
+  // continuous batching is a capability of the policy: the phase option sizes it for the
+  // policies that own it and the others ignore it, so options shared by every arm of a study
+  // do not hand it to the baselines
+  const int cb_option = static_cast<int>(o.integer("continuous_batch", 8));
+  if (cb_option < 0 || cb_option > 8) throw std::invalid_argument("continuous_batch must be 0..8");
+  s.continuous_batch = t.continuous_batch ? cb_option : 0;
+  s.t.feasibility_guards = o.flag("feasibility_guards", t.feasibility_guards);
+  s.t.idle_widening = o.flag("idle_widening", t.idle_widening);
   s.image_batch = static_cast<int>(o.integer("image_batch", t.image_batching ? 4 : 1));
   s.pairing = o.flag("pairing", false);
   s.preempt = o.flag("doorbell", true);
@@ -175,6 +180,7 @@ struct Req {
   int steps_done = 0, steps_total = 0, blocks_done = 0, decode_done = 0;
   int affinity = -1;
   bool feasible = true;
+  bool sunk = false;  // feasible only through the sunk-work deadband
   double best_remaining = 0;
   bool video() const { return kind == "video"; }
   bool finished_denoise() const { return steps_done >= steps_total; }
@@ -183,6 +189,10 @@ struct Req {
 struct Gpus {
   std::vector<bool> free;
   std::vector<bool> image_only;
+  // GPUs whose partial activations belong to a video suspended inside a solver step: other
+  // videos do not take them (images may: a doorbell stopped the video for them)
+  std::vector<std::string> reserved;
+  std::string current;  // the video being placed
   int count() const {
     int n = 0;
     for (bool f : free) n += f;
@@ -193,7 +203,10 @@ struct Gpus {
 // first fully free aligned group of `size`, preferring `prefer` (no resize), then the most overlap
 std::vector<int> pick_group(const Gpus& g, int size, const std::vector<int>& prefer, bool for_video) {
   const int n = static_cast<int>(g.free.size());
-  auto usable = [&](int i) { return g.free[i] && !(for_video && g.image_only[i]); };
+  auto usable = [&](int i) {
+    return g.free[i] &&
+           !(for_video && (g.image_only[i] || (!g.reserved[i].empty() && g.reserved[i] != g.current)));
+  };
   if (static_cast<int>(prefer.size()) == size) {
     bool ok = true;
     for (int i : prefer) ok = ok && i >= 0 && i < n && usable(i);
@@ -215,29 +228,33 @@ std::vector<int> pick_group(const Gpus& g, int size, const std::vector<int>& pre
   return best;
 }
 
-int pick_image_gpu(const Gpus& g, const std::string& placement, int affinity) {
+// `claim` (optional): per GPU, the smallest laxity of the step-boundary videos that would
+// resume there; within a placement tier the image takes the GPU with the largest claim, so
+// it borrows from the video that can best afford to move (ties: the lowest index)
+int pick_image_gpu(const Gpus& g, const std::string& placement, int affinity,
+                   const std::vector<double>* claim = nullptr) {
   const int n = static_cast<int>(g.free.size());
   if (affinity >= 0) return affinity < n && g.free[affinity] ? affinity : -1;
+  auto better = [&](int i, int cur) { return cur < 0 || (claim && (*claim)[i] > (*claim)[cur]); };
   int first = -1;
   // images prefer their reserved share when the cluster is partitioned
   for (int pass = 0; pass < 2 && first < 0; ++pass)
     for (int i = 0; i < n; ++i)
-      if (g.free[i] && (pass == 1 || g.image_only[i])) {
-        first = i;
-        break;
-      }
+      if (g.free[i] && (pass == 1 || g.image_only[i]) && better(i, first)) first = i;
   if (placement != "pair_fit" || first < 0) return first;
   // pair_fit: take a GPU whose CFG-pair partner is already busy, so whole free pairs stay
   // available for videos; then one whose quad is partly busy
   for (int span : {2, 4}) {
+    int pick = -1;
     for (int i = 0; i < n; ++i) {
       if (!g.free[i]) continue;
       const int base = i - i % span;
       bool partner_busy = false;
       for (int k = base; k < std::min(n, base + span); ++k)
         if (k != i && !g.free[k]) partner_busy = true;
-      if (partner_busy) return i;
+      if (partner_busy && better(i, pick)) pick = i;
     }
+    if (pick >= 0) return pick;
   }
   return first;
 }
@@ -266,6 +283,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
   Gpus g;
   g.free.assign(n, true);
   g.image_only.assign(n, false);
+  g.reserved.assign(n, std::string());
   if (state.contains("busy")) {
     const auto& busy = state.at("busy").as_array();
     if (static_cast<int>(busy.size()) != n) throw std::invalid_argument("busy must list every GPU");
@@ -337,6 +355,15 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
       if (!rj.contains("steps_done") && !(s.continuous_batch > 1)) r.best_remaining = cost.service_ms(r.klass);
     }
     r.feasible = now + r.best_remaining <= r.deadline;
+    // sunk-work deadband: an in-flight video past half of its steps whose overrun is small
+    // (at most 15 % of what remains, and at most 10 s) keeps its rank; demoting it would
+    // discard the work already spent for a marginal miss
+    if (!r.feasible && t.feasibility_guards && r.video() && r.status == "suspended" && r.steps_total > 0 &&
+        2 * r.steps_done >= r.steps_total && std::isfinite(r.deadline) &&
+        now + r.best_remaining - r.deadline <= std::min(10000.0, 0.15 * r.best_remaining)) {
+      r.feasible = true;
+      r.sunk = true;
+    }
     reqs.push_back(r);
   }
 
@@ -361,9 +388,15 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
       row["feasible"] = r.feasible;
       row["laxity_ms"] = std::isfinite(r.deadline) ? r.deadline - now - r.best_remaining : 1e18;
       row["best_remaining_ms"] = r.best_remaining;
+      if (r.sunk) row["sunk_work_deadband"] = true;
       trace->add(row);
     }
   }
+
+  for (const auto& r : reqs)
+    if (r.video() && r.status == "suspended" && r.blocks_done > 0)
+      for (int i : r.group)
+        if (i >= 0 && i < n && g.reserved[i].empty()) g.reserved[i] = r.id;
 
   Json assignments = Json::array();
   std::set<std::string> placed;
@@ -401,6 +434,8 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
   };
 
   auto emit_video = [&](const Req& r, const Form& f, const std::vector<int>& grp, const std::string& reason) {
+    for (auto& holder : g.reserved)
+      if (holder == r.id) holder.clear();
     Json a = Json::object();
     a["request_id"] = r.id;
     a["group"] = ints(grp);
@@ -417,6 +452,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
 
   // ---- decode-only videos: a finished denoise decodes on one GPU (decode shrink) ----
   auto place_finish = [&](const Req& r) -> bool {
+    g.current = r.id;
     std::vector<int> grp;
     Form f{1, 1, 1};
     if (t.hold_diffuse && !r.group.empty()) {
@@ -434,6 +470,82 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
 
   std::vector<const Req*> videos, images;
   for (const auto& r : reqs) (r.video() ? videos : images).push_back(&r);
+
+  // ---- feasibility-guard helpers -----------------------------------------------------
+  std::map<std::string, int> min_degree_cache;
+  auto min_feasible_degree = [&](const Req& o) -> int {  // 0: no form meets its deadline
+    auto it = min_degree_cache.find(o.id);
+    if (it != min_degree_cache.end()) return it->second;
+    int d = 0;
+    for (const auto& f : efficient_only(forms_for(s, cost, o.klass, video_capacity), o.klass))
+      if (now + cost.remaining_ms(*o.j, f) <= o.deadline) {
+        d = f.degree();
+        break;
+      }
+    if (d == 0 && o.sunk) {
+      auto forms = forms_for(s, cost, o.klass, video_capacity);
+      if (!forms.empty()) d = forms.back().degree();
+    }
+    return min_degree_cache[o.id] = d;
+  };
+  auto video_free = [&]() {
+    int c = 0;
+    for (int i = 0; i < n; ++i) c += g.free[i] && !g.image_only[i];
+    return c;
+  };
+  auto movable_after = [&](const Req& self, const Req& o, bool& after) {
+    if (&o == &self) {
+      after = true;
+      return false;
+    }
+    return after && o.video() && !placed.count(o.id) && !o.finished_denoise() &&
+           !(o.status == "suspended" && o.blocks_done > 0);
+  };
+  // feasible videos ranked after `self` that still get GPUs, greedily, out of `free_gpus`
+  auto others_fitting = [&](const Req& self, int free_gpus) {
+    int fit = 0;
+    bool after = false;
+    for (const auto& o : reqs) {
+      if (!movable_after(self, o, after) || !o.feasible) continue;
+      const int d = min_feasible_degree(o);
+      if (d > 0 && d <= free_gpus) {
+        free_gpus -= d;
+        ++fit;
+      }
+    }
+    return fit;
+  };
+  // GPUs the requests ranked after `self` still need: each video its minimal (feasible)
+  // degree, each unplaced image one GPU
+  auto others_need = [&](const Req& self) {
+    int need = 0;
+    bool after = false;
+    for (const auto& o : reqs) {
+      if (!o.video()) {
+        if (&o != &self && !placed.count(o.id)) need += 1;
+        continue;
+      }
+      if (!movable_after(self, o, after)) continue;
+      int d = min_feasible_degree(o);
+      if (d == 0) {
+        auto forms = efficient_only(forms_for(s, cost, o.klass, video_capacity), o.klass);
+        d = forms.empty() ? 0 : forms.front().degree();
+      }
+      need += d;
+    }
+    return need;
+  };
+  // laxity claims of the step-boundary videos on the GPUs they would resume on
+  std::vector<double> claim(n, kInf);
+  if (t.feasibility_guards)
+    for (const auto& r : reqs)
+      if (r.video() && r.status == "suspended" && r.blocks_done == 0 && !r.group.empty() && !r.finished_denoise()) {
+        const double lax = std::isfinite(r.deadline) ? r.deadline - now - r.best_remaining : 1e18;
+        for (int i : r.group)
+          if (i >= 0 && i < n) claim[i] = std::min(claim[i], lax);
+      }
+  const std::vector<double>* claims = t.feasibility_guards ? &claim : nullptr;
+
 
 
   // ---- deadline knapsack (TetriServe / SBP-ESP / v1) over movable videos --------------
@@ -506,7 +618,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
   // ---- images ----------------------------------------------------------------------
   auto place_image = [&](const Req& r) -> bool {
     if (placed.count(r.id)) return true;
-    const int gpu = pick_image_gpu(g, t.image_placement, r.affinity);
+    const int gpu = pick_image_gpu(g, t.image_placement, r.affinity, claims);
     if (gpu < 0) return false;
     Json a = Json::object();
     a["request_id"] = r.id;
@@ -519,20 +631,45 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     const bool ab = !cb && s.image_batch > 1 && cost.klass(r.klass).contains("batch_ms") && g.count() <= 1;
     if (cb || ab) {
       std::vector<const Req*> members{&r};
-      const int cap = cb ? s.continuous_batch : s.image_batch;
+      auto joins = [&](const Req* other) {
+        return other != &r && !placed.count(other->id) && (s.t.sequence_packing || other->klass == r.klass) &&
+               (other->affinity < 0 || other->affinity == gpu);
+      };
+      int cap = cb ? s.continuous_batch : s.image_batch;
+      if (cb) {
+        // work-conserving: while GPUs that no waiting video needs are idle, the waiting images
+        // spread over them (fewer members per GPU, shorter rounds) instead of queueing on one
+        int pending = 1;
+        for (const Req* other : images) pending += joins(other);
+        int video_need = 0;
+        for (const Req* v : videos)
+          if (!placed.count(v->id) && !v->finished_denoise() && v->feasible) video_need += min_feasible_degree(*v);
+        const int spare = std::max(1, g.count() - video_need);
+        cap = std::min(cap, std::max(1, (pending + spare - 1) / spare));
+      }
       for (const Req* other : images) {
         if (static_cast<int>(members.size()) >= cap) break;
-        if (other == &r || placed.count(other->id)) continue;
-        if (!s.t.sequence_packing && other->klass != r.klass) continue;
-        if (other->affinity >= 0 && other->affinity != gpu) continue;
+        if (!joins(other)) continue;
         std::vector<const Json*> js;
         for (auto* m : members) js.push_back(m->j);
         js.push_back(other->j);
+        // every member, the joining one included, keeps its deadline; a mixed batch is priced
+        // on the table of its largest class whichever member anchors it
+        double round_ms = cb ? cost.continuous_batch_step_ms(js, s.t.sequence_packing, r.klass) : 0.0;
+        std::vector<const Req*> all = members;
+        all.push_back(other);
+        // without bubble-free admission a member's prepare and finish stall the whole round;
+        // bubble-free batches overlap them with the other members' denoising
+        if (cb && !s.t.bubble_free)
+          for (auto* m : all) {
+            const Json& kc = cost.klass(m->klass);
+            if (!m->j->flag("prepared", m->steps_done > 0)) round_ms += kc.num("prepare_ms", 0.0);
+            if (m->steps_done + 1 >= m->steps_total) round_ms += kc.num("finish_ms", 0.0);
+          }
         bool ok = true;
-        for (auto* m : members) {
-          const double eff = cost.effective_batch(r.klass, js, s.t.sequence_packing);
+        for (auto* m : all) {
           const int left = m->steps_total - m->steps_done;
-          const double ms = cb ? left * cost.continuous_step_ms(r.klass, eff) + cost.decode_ms(m->klass)
+          const double ms = cb ? left * round_ms + cost.decode_ms(m->klass)
                                : cost.batch_ms(r.klass, static_cast<int>(js.size()));
           if (m->feasible && now + ms > m->deadline) ok = false;
         }
@@ -548,6 +685,10 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
       }
       a["quantum"] = cb ? "continuous_batch" : "atomic";
       a["reason"] = cb ? "continuous-batch" : (members.size() > 1 ? "image-batch" : t.image_placement);
+      if (cb) {
+        a["sequence_packing"] = s.t.sequence_packing;
+        a["bubble_free"] = s.t.bubble_free;
+      }
     } else {
       a["quantum"] = r.finished_denoise() && r.j->contains("steps_done") ? "finish" : "atomic";
       a["reason"] = t.image_placement;
@@ -569,6 +710,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
       place_finish(r);
       continue;
     }
+    g.current = r.id;
     // load-adaptive form choice: when the videos in the system could fill every CFG pair,
     // throughput decides and each video takes the form with the least GPU time per step;
     // otherwise the usual feasible-minimal choice (and widening) keeps latency low
@@ -623,15 +765,42 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     Form chosen{0, 0, 0};
     std::vector<int> grp;
     std::string reason;
+    const int free_now = video_free();
+    const int d_min = forms.front().degree();
+    bool guarded = false, migration_held = false;
     for (const auto& f : forms) {
-      if (now + cost.remaining_ms(*r.j, f) * (1.0 + s.feasible_margin) > r.deadline) continue;
+      const double rem = cost.remaining_ms(*r.j, f);
+      if (now + rem * (1.0 + s.feasible_margin) > r.deadline) continue;
       auto cand = pick_group(g, f.degree(), r.group, true);
       if (cand.empty()) continue;
+      if (t.feasibility_guards) {
+        // multi-video guard: widening to save this deadline may not cost two others theirs
+        if (f.degree() > d_min && others_fitting(r, free_now - d_min) - others_fitting(r, free_now - f.degree()) >= 2) {
+          guarded = true;
+          continue;
+        }
+        // migration guard: a prepared video does not move to another group of its size when
+        // the reshard makes it late; it waits for its own GPUs
+        if (r.status == "suspended" && !r.group.empty() && cand != r.group &&
+            static_cast<int>(r.group.size()) == f.degree() && now + rem + cost.resize_ms() > r.deadline) {
+          migration_held = true;
+          continue;
+        }
+      }
       chosen = f;
       grp = cand;
       reason = t.best_fit ? "best-fit" : "feasible-min";
       break;
     }
+    if (chosen.degree() == 0 && guarded) {
+      auto cand = pick_group(g, d_min, r.group, true);
+      if (!cand.empty()) {
+        chosen = forms.front();
+        grp = cand;
+        reason = "multi-video-guard";
+      }
+    }
+    if (chosen.degree() == 0 && migration_held) continue;
     if (chosen.degree() == 0) {
       if (t.best_fit) {
         // largest group that fits
@@ -651,6 +820,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     }
     if (chosen.degree() == 0) continue;
     // widen while the per-GPU efficiency stays above the threshold and no image is starved
+    // (nor, with the guards, any feasible video); `grp` is not taken until emit_video
     if (t.widen > 0 && !t.best_fit) {
       for (const auto& f : forms) {
         if (f.degree() <= chosen.degree()) continue;
@@ -658,13 +828,29 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
         const double wide_work = cost.step_ms(r.klass, f) * f.degree();
         if (base_work / wide_work < t.widen) break;
         if (!s.widen_past_images && any_waiting_image_unplaced()) break;
-        give(grp);
+        if (t.feasibility_guards &&
+            others_fitting(r, free_now - chosen.degree()) - others_fitting(r, free_now - f.degree()) >= 1)
+          break;
         auto cand = pick_group(g, f.degree(), r.group, true);
-        take(grp);
         if (cand.empty()) continue;
         chosen = f;
         grp = cand;
         reason = "widened";
+      }
+    }
+    // idle widening: below the threshold, a faster wider form still takes GPUs that neither
+    // the requests ranked after this one nor a waiting image would use this round
+    if (t.idle_widening && !t.best_fit && !throughput_mode && !any_waiting_image_unplaced()) {
+      const int need = others_need(r);
+      for (const auto& f : forms) {
+        if (f.degree() <= chosen.degree()) continue;
+        if (f.degree() + need > free_now) break;
+        if (cost.step_ms(r.klass, f) >= cost.step_ms(r.klass, chosen)) continue;
+        auto cand = pick_group(g, f.degree(), r.group, true);
+        if (cand.empty()) continue;
+        chosen = f;
+        grp = cand;
+        reason = "idle-widened";
       }
     }
     emit_video(r, chosen, grp, reason);
@@ -674,6 +860,8 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
   if (t.deadline_dp || t.knapsack) {
     for (const Req* r : videos) {
       if (placed.count(r->id) || r->finished_denoise()) continue;
+      if (r->status == "suspended" && r->blocks_done > 0 && !r->group.empty()) continue;  // mid-step: own group only
+      g.current = r->id;
       std::vector<int> grp;
       auto forms = forms_for(s, cost, r->klass, video_capacity);
       for (auto it = forms.rbegin(); it != forms.rend(); ++it) {
@@ -694,6 +882,10 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
       for (auto& pv : placed_videos) {
         Json& a = assignments.at(pv.index);
         if (a.at("quantum").is_string() && a.at("quantum").as_string() == "finish") continue;
+        // a request inside a solver step (or pinned to its group) keeps its group and form
+        const std::string why = a.at("reason").as_string();
+        if (why == "mid-step" || why == "held" || why == "fixed" || why == "fission") continue;
+        g.current = pv.id;
         auto forms = forms_for(s, cost, pv.klass, video_capacity);
         for (const auto& f : forms) {
           if (f.degree() <= pv.form.degree()) continue;

@@ -28,6 +28,7 @@ PolicyTraits full(const std::string& id, const std::string& display, const std::
   t.widen = 0.90;
   t.image_placement = "pair_fit";
   t.continuous_batch = t.sequence_packing = t.bubble_free = true;
+  t.feasibility_guards = t.idle_widening = true;
   return t;
 }
 
@@ -327,6 +328,8 @@ Json describe_policy(const PolicyTraits& t) {
   j["continuous_batch"] = t.continuous_batch;
   j["sequence_packing"] = t.sequence_packing;
   j["bubble_free"] = t.bubble_free;
+  j["feasibility_guards"] = t.feasibility_guards;
+  j["idle_widening"] = t.idle_widening;
   return j;
 }
 

@@ -214,12 +214,13 @@ SimResult simulate_cluster(const Json& workload, int gpus, const std::string& po
         if (qk == "continuous_batch") {
           std::vector<const Json*> js;
           for (const auto& m : members) js.push_back(&reqs[index[m]].row);
-          const double eff = cost.effective_batch(r.klass, js, options.flag("sequence_packing", true));
-          dur += cost.continuous_step_ms(r.klass, eff);
+          const double round_ms =
+              cost.continuous_batch_step_ms(js, options.flag("sequence_packing", true), r.klass);
+          dur += round_ms;
           for (const auto& m : members) {
             auto& mm = reqs[index[m]];
             mm.step_mode = true;
-            if (mm.steps_done + 1 >= mm.steps_total) dur = std::max(dur, cost.continuous_step_ms(r.klass, eff) + cost.decode_ms(mm.klass));
+            if (mm.steps_done + 1 >= mm.steps_total) dur = std::max(dur, round_ms + cost.decode_ms(mm.klass));
           }
           r.q_kind = "cstep";
         } else {

@@ -220,8 +220,14 @@ TEST("a lone video is widened while scaling stays efficient") {
   CHECK(find(p, "a")->at("reason").as_string() == "widened");
   Json o = Json::object();
   o["widen_efficiency"] = 0.999;  // no form is that efficient: stay at the minimal one
+  o["idle_widening"] = false;
   auto q = cluster_plan(state(8, {req("a", "video", "vid", 0, 1e9)}), "ditserve", c, o);
   CHECK(find(q, "a")->at("degree").as_int() == 2);
+  // with idle widening the GPUs nobody else needs still go to the lone video
+  o["idle_widening"] = true;
+  auto w = cluster_plan(state(8, {req("a", "video", "vid", 0, 1e9)}), "ditserve", c, o);
+  CHECK(find(w, "a")->at("degree").as_int() == 8);
+  CHECK(find(w, "a")->at("reason").as_string() == "idle-widened");
 }
 
 TEST("widening stops while an image waits unplaced") {
@@ -450,3 +456,228 @@ TEST("a running lockstep pair is one preemption candidate") {
 }
 
 int main() { return dstest::run_all(); }
+
+TEST("multi-video guard: one video does not widen to its deadline at the cost of two feasible ones") {
+  ClusterCost c(profile());  // cfg2 4100 ms, cfg2sp2 2222 ms, cfg2sp4 1215 ms to finish
+  std::vector<Json> rs = {req("v0", "video", "vid", 0, 1500)};  // only cfg2sp4 (8 GPUs) meets it
+  for (int k = 1; k <= 3; ++k) rs.push_back(req("v" + std::to_string(k), "video", "vid", 0, 5000));
+  auto p = cluster_plan(state(8, rs), "ditserve", c);
+  CHECK(p.at("assignments").size() == 4);
+  CHECK(find(p, "v0")->at("degree").as_int() == 2);
+  CHECK(find(p, "v0")->at("reason").as_string() == "multi-video-guard");
+  auto lone = cluster_plan(state(8, {rs[0]}), "ditserve", c);
+  CHECK(find(lone, "v0")->at("degree").as_int() == 8);  // nobody to protect: it widens
+  Json off = Json::object();
+  off["feasibility_guards"] = false;
+  auto q = cluster_plan(state(8, rs), "ditserve", c, off);
+  CHECK(find(q, "v0")->at("degree").as_int() == 8 && q.at("assignments").size() == 1);
+}
+
+TEST("threshold widening never costs a feasible video its GPUs") {
+  ClusterCost c(profile());  // cfg2 -> cfg2sp2 keeps 94 % per-GPU efficiency (above 0.90)
+  std::vector<Json> rs;
+  for (int k = 0; k < 4; ++k) rs.push_back(req("v" + std::to_string(k), "video", "vid", 0, 5000 + k));
+  auto p = cluster_plan(state(8, rs), "ditserve", c);
+  CHECK(p.at("assignments").size() == 4);
+  for (const auto& a : p.at("assignments").as_array()) CHECK(a.at("degree").as_int() == 2);
+}
+
+TEST("idle widening takes GPUs nobody else needs, below the efficiency threshold") {
+  Json pr = profile();
+  pr["classes"]["vid"]["forms"] = Json::parse(R"({"cfg2sp2":{"step_ms":300},"sp4":{"step_ms":320}})");  // 67 %
+  ClusterCost c(pr);
+  std::vector<Json> rs = {req("v0", "video", "vid", 0, 1e9), req("v1", "video", "vid", 0, 1e9 + 1)};
+  auto p = cluster_plan(state(8, rs), "ditserve", c);
+  CHECK(find(p, "v0")->at("degree").as_int() == 4 && find(p, "v0")->at("form").as_string() == "cfg2sp2");
+  CHECK(find(p, "v0")->at("reason").as_string() == "idle-widened");
+  CHECK(find(p, "v1")->at("degree").as_int() == 4);
+  // three videos: the first may not take the pair the third needs
+  rs.push_back(req("v2", "video", "vid", 0, 1e9 + 2));
+  auto q = cluster_plan(state(8, rs), "ditserve", c);
+  CHECK(q.at("assignments").size() == 3);
+  CHECK(find(q, "v0")->at("degree").as_int() == 4 && find(q, "v1")->at("degree").as_int() == 2);
+  Json off = Json::object();
+  off["idle_widening"] = false;
+  auto r = cluster_plan(state(8, {rs[0], rs[1]}), "ditserve", c, off);
+  CHECK(find(r, "v0")->at("degree").as_int() == 2);
+}
+
+TEST("sunk-work deadband keeps an in-flight video's rank for a small overrun") {
+  ClusterCost c(profile());
+  Json in = suspended("in", "[0,1]", "cfg2", 6, 0);  // 4 steps + decode left: 1700 ms
+  in["deadline_ms"] = 1500;                          // 200 ms over, under 15 % of 1700
+  Json fresh = req("fresh", "video", "vid", 0, 1e5);
+  auto p = cluster_plan(state(2, {in, fresh}), "ditserve", c);
+  CHECK(find(p, "in") != nullptr && find(p, "fresh") == nullptr);
+  // an unstarted video with a similar overrun is still demoted behind the feasible one
+  Json un = req("un", "video", "vid", 0, 4000);      // needs 4100 ms
+  auto q = cluster_plan(state(2, {un, fresh}), "ditserve", c);
+  CHECK(find(q, "fresh") != nullptr && find(q, "un") == nullptr);
+  // and a large overrun gets no deadband
+  in["deadline_ms"] = 1000;
+  auto r = cluster_plan(state(2, {in, fresh}), "ditserve", c);
+  CHECK(find(r, "fresh") != nullptr && find(r, "in") == nullptr);
+}
+
+TEST("an image borrows the GPUs of the step-boundary video with the most laxity") {
+  ClusterCost c(profile());
+  Json urgent = suspended("urgent", "[0,1]", "cfg2", 2, 0);
+  urgent["deadline_ms"] = 5000;   // 3300 ms left to run
+  Json slack = suspended("slack", "[2,3]", "cfg2", 2, 0);
+  slack["deadline_ms"] = 50000;
+  Json img = req("img", "image", "img", 0, 2000);
+  auto p = cluster_plan(state(4, {urgent, slack, img}), "ditserve", c);
+  CHECK(find(p, "img")->at("group")[0].as_int() == 2);
+  CHECK(find(p, "urgent")->at("group")[0].as_int() == 0 && !find(p, "urgent")->at("resize").as_bool());
+  Json off = Json::object();
+  off["feasibility_guards"] = false;
+  auto q = cluster_plan(state(4, {urgent, slack, img}), "ditserve", c, off);
+  CHECK(find(q, "img")->at("group")[0].as_int() == 0);
+}
+
+TEST("migration guard: a prepared video waits rather than reshard into lateness") {
+  Json pr = profile();
+  pr["resize_ms"] = 50;
+  ClusterCost c(pr);
+  Json v = suspended("v", "[0,1]", "cfg2", 9, 0);  // 400 + 100 ms left
+  v["deadline_ms"] = 520;                          // on time in place, late after a 50 ms reshard
+  auto p = cluster_plan(state(4, {v}, {0}), "ditserve", c);
+  CHECK(find(p, "v") == nullptr);
+  v["deadline_ms"] = 1e9;                          // plenty of slack: it moves
+  auto q = cluster_plan(state(4, {v}, {0}), "ditserve", c);
+  CHECK(find(q, "v") && find(q, "v")->at("group")[0].as_int() == 2 && find(q, "v")->at("resize").as_bool());
+  Json off = Json::object();
+  off["feasibility_guards"] = false;
+  v["deadline_ms"] = 520;
+  auto r = cluster_plan(state(4, {v}, {0}), "ditserve", c, off);
+  CHECK(find(r, "v") != nullptr);
+}
+
+TEST("continuous batching belongs to the policy: baselines ignore the shared option") {
+  ClusterCost c(profile());
+  std::vector<Json> imgs = {req("i0", "image", "img", 0, 5000), req("i1", "image", "img", 0, 5000)};
+  Json o = Json::object();
+  o["continuous_batch"] = 4;
+  auto d = cluster_plan(state(1, imgs), "ditserve", c, o);
+  CHECK(d.at("assignments").size() == 1 && d.at("assignments")[0].at("quantum").as_string() == "continuous_batch");
+  for (const char* base : {"abl-no-cb", "edf-bestfit", "tetriserve", "xdit-sp1", "edf-cfg2"}) {
+    auto p = cluster_plan(state(2, imgs, {0}), base, c, o);
+    CHECK(p.at("assignments").size() == 1);
+    CHECK(p.at("assignments")[0].at("quantum").as_string() == "atomic");
+  }
+}
+
+TEST("work-conserving continuous batching spreads waiting images over idle GPUs") {
+  ClusterCost c(profile());
+  std::vector<Json> two = {req("i0", "image", "img", 0, 5000), req("i1", "image", "img", 0, 5000)};
+  auto p = cluster_plan(state(2, two), "ditserve", c);
+  CHECK(p.at("assignments").size() == 2);
+  for (const auto& a : p.at("assignments").as_array()) CHECK(a.at("batch").size() == 1);
+  std::vector<Json> four = two;
+  four.push_back(req("i2", "image", "img", 0, 5000));
+  four.push_back(req("i3", "image", "img", 0, 5000));
+  auto q = cluster_plan(state(2, four), "ditserve", c);
+  CHECK(q.at("assignments").size() == 2);
+  for (const auto& a : q.at("assignments").as_array()) CHECK(a.at("batch").size() == 2);
+  // GPUs a waiting video needs are not counted as idle: four images share the two GPUs
+  // that the video's CFG pair leaves
+  std::vector<Json> mixed = four;
+  mixed.push_back(req("v", "video", "vid", 0, 1e9));
+  auto r = cluster_plan(state(4, mixed), "ditserve", c);
+  CHECK(find(r, "i0")->at("batch").size() == 2);
+  CHECK(find(r, "v") != nullptr && find(r, "v")->at("degree").as_int() == 2);
+}
+
+TEST("mixed-class continuous batches: order-free pricing and every member's deadline") {
+  Json pr = profile();
+  pr["classes"]["big"] = Json::parse(R"({"kind":"image","steps":28,"tokens":4096,"step_ms":40,"service_ms":1300,
+                                         "decode_ms":180,"batch_step_ms":{"1":40,"2":74,"4":142,"8":280}})");
+  ClusterCost c(pr);
+  Json small = req("s", "image", "img", 0, 28 * 12 + 50 + 20);  // only alone keeps this deadline
+  Json big = req("b", "image", "big", 0, 1e6);
+  CHECK(std::abs(c.continuous_batch_step_ms({&small, &big}, true, "img") -
+                 c.continuous_batch_step_ms({&big, &small}, true, "big")) < 1e-9);
+  CHECK(c.batch_anchor({&small, &big}, "img") == "big");
+  auto p = cluster_plan(state(1, {small, big}), "ditserve", c);
+  CHECK(find(p, "s")->at("batch").size() == 1);  // the big member would make the small one late
+  Json relaxed = small;
+  relaxed["deadline_ms"] = 1e6;
+  auto q = cluster_plan(state(1, {relaxed, big}), "ditserve", c);
+  CHECK(q.at("assignments").size() == 1);  // sequence packing joins the two classes
+  CHECK(q.at("assignments")[0].at("batch").size() == 2);
+}
+
+TEST("bubble-free batches hide member prepare and finish; without it they stall the round") {
+  Json pr = profile();
+  pr["classes"]["img"]["prepare_ms"] = 30;
+  pr["classes"]["img"]["finish_ms"] = 30;
+  ClusterCost c(pr);
+  // one new member joining an almost finished batch: its prepare would stall every round
+  Json a = req("a", "image", "img", 0, 28 * 16 + 50 + 20);   // fits a pair batch only when rounds are not stalled
+  Json b = req("b", "image", "img", 0, 1e6);
+  auto p = cluster_plan(state(1, {a, b}), "ditserve", c);
+  CHECK(p.at("assignments").size() == 1 && p.at("assignments")[0].at("batch").size() == 2);
+  CHECK(p.at("assignments")[0].at("bubble_free").as_bool());
+  CHECK(p.at("assignments")[0].at("sequence_packing").as_bool());
+  Json o = Json::object();
+  o["bubble_free"] = false;
+  auto q = cluster_plan(state(1, {a, b}), "ditserve", c, o);
+  CHECK(q.at("assignments")[0].at("batch").size() == 1);
+  CHECK(!q.at("assignments")[0].at("bubble_free").as_bool());
+}
+
+TEST("every policy resumes a mid-step request only on its own group and form") {
+  ClusterCost c(profile());
+  auto v = suspended("v", "[2,3]", "sp2", 3, 12);
+  for (const char* pol : {"xdit-sp2", "tetriserve", "edf-bestfit", "sbp-esp", "ditserve-v1", "ditserve"}) {
+    auto p = cluster_plan(state(8, {v}), pol, c);
+    const Json* a = find(p, "v");
+    CHECK(a != nullptr);
+    CHECK(a->at("group")[0].as_int() == 2 && a->at("group")[1].as_int() == 3);
+    CHECK(a->at("form").as_string() == "sp2");
+    auto q = cluster_plan(state(8, {v}, {3}), pol, c);
+    CHECK(find(q, "v") == nullptr);  // its GPU 3 is busy: wait, never move mid-step
+  }
+}
+
+TEST("an xDiT partition on two GPUs keeps one GPU for videos and one for images") {
+  ClusterCost c(profile());
+  auto p = cluster_plan(state(2, {req("v", "video", "vid", 0, 1e9), req("w", "video", "vid", 0, 1e9 + 1)}),
+                        "xdit-sp1", c);
+  CHECK(p.at("assignments").size() == 1);
+  CHECK(find(p, "v")->at("group")[0].as_int() == 0);
+  auto q = cluster_plan(state(2, {req("i", "image", "img", 0, 5000), req("v", "video", "vid", 0, 1e9)}),
+                        "xdit", c);
+  CHECK(find(q, "i")->at("group")[0].as_int() == 1 && find(q, "v")->at("group")[0].as_int() == 0);
+}
+
+TEST("a video does not take GPUs another video holds inside a solver step") {
+  ClusterCost c(profile());
+  auto held = suspended("held", "[2,3]", "cfg2", 3, 12);  // mid-step on {2,3}, ranked second
+  held["deadline_ms"] = 2e9;
+  auto b = suspended("b", "[0,1]", "cfg2", 3, 0);         // at a step boundary; GPU 0 is busy
+  for (const char* pol : {"ditserve", "edf-bestfit", "tetriserve"}) {
+    auto p = cluster_plan(state(4, {b, held}, {0}), pol, c);
+    CHECK(find(p, "held") != nullptr && find(p, "held")->at("group")[0].as_int() == 2);
+    if (const Json* a = find(p, "b"))  // {2,3} is free but belongs to the mid-step video
+      for (const auto& i : a->at("group").as_array()) CHECK(i.as_int() < 2);
+  }
+  // an image may still use it: the doorbell stopped the video for images
+  auto q = cluster_plan(state(4, {held, req("i", "image", "img", 0, 5000)}, {0, 1, 3}), "ditserve", c);
+  CHECK(find(q, "i") && find(q, "i")->at("group")[0].as_int() == 2);
+}
+
+TEST("deadline doorbells: a group's own timing, natural boundaries and already-rung capacity") {
+  // {id, GPUs, stop_ms, remaining_ms, resume_ms, rung}
+  const std::vector<RunningGroup> hetero = {{"fast-expensive", {0}, 10, 100, 1000, false},
+                                           {"slow-cheap", {1}, 30, 200, 0, false}};
+  auto sel = select_deadline_preemption(0, {{-1, 60, 40}}, hetero);
+  CHECK(sel.selected == std::vector<std::string>{"fast-expensive"});  // only its stop saves the image
+  CHECK(select_deadline_preemption(0, {{1, 60, 40}}, hetero).selected.empty());  // pinned to the slow one
+  const std::vector<RunningGroup> boundary = {{"natural-boundary", {0}, 5, 5, 0, false},
+                                              {"interrupt", {1}, 10, 100, 0, false}};
+  CHECK(select_deadline_preemption(0, {{-1, 60, 40}}, boundary).selected.empty());  // a step ends in time
+  const std::vector<RunningGroup> pending = {{"already-rung", {0, 1}, 5, 100, 0, true},
+                                             {"extra", {2}, 5, 100, 0, false}};
+  CHECK(select_deadline_preemption(0, {{-1, 50, 40}, {-1, 50, 40}}, pending).selected.empty());
+}

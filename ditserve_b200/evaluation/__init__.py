@@ -6,6 +6,8 @@
   takes a feature network and raises a clear error without one.
 * ``hash_bucket_split`` — deterministic train/val/test assignment by SHA-256 of an item id.
 * ``kineto_summary`` — aggregate GPU kernel time by name from a torch.profiler chrome trace.
+* ``nsys_gpu_metrics`` — per-device busy time, top kernels, copies and NVTX ranges from an Nsight
+  Systems SQLite export.
 Reference: workers/ditserve/evaluation/{quality.py:39-125, artifacts.py:186-345, datasets.py,
 cuda_profile.py}.
 """
@@ -96,3 +98,75 @@ def kineto_summary(trace_path: str, top: int = 20) -> list:
     rows = [dict(name=k, calls=v[0], total_us=round(v[1], 2), share=round(v[1] / tot, 4)) for k, v in agg.items()]
     rows.sort(key=lambda r: -r["total_us"])
     return rows[:top]
+
+
+def _union_ns(intervals) -> int:
+    busy, end = 0, None
+    for s, e in sorted(intervals):
+        if end is None or s > end:
+            busy += e - s
+            end = e
+        elif e > end:
+            busy += e - end
+            end = e
+    return busy
+
+
+def nsys_gpu_metrics(sqlite_path: str, top: int = 20) -> dict:
+    """GPU metrics from an Nsight Systems SQLite export (``nsys export --type sqlite``).
+
+    Reads the documented export tables: ``CUPTI_ACTIVITY_KIND_KERNEL`` (start, end, deviceId,
+    shortName -> ``StringIds``), ``CUPTI_ACTIVITY_KIND_MEMCPY`` (start, end, bytes, copyKind) and,
+    when present, ``NVTX_EVENTS`` ranges (start, end, text).  Returns per-device busy time (the
+    union of kernel intervals, so concurrent streams are not double counted) over the span from
+    the first to the last GPU activity, the top kernels by total time, copy totals per kind and
+    NVTX range totals.  Reference: the Nsight Systems metric parser of the reference's evaluation
+    tooling (workers/ditserve/evaluation/nsys_metrics.py)."""
+    import sqlite3
+    con = sqlite3.connect(f"file:{sqlite_path}?mode=ro", uri=True)
+    try:
+        tables = {r[0] for r in con.execute("SELECT name FROM sqlite_master WHERE type='table'")}
+        names = dict(con.execute("SELECT id, value FROM StringIds")) if "StringIds" in tables else {}
+        kernels = []
+        if "CUPTI_ACTIVITY_KIND_KERNEL" in tables:
+            kernels = list(con.execute("SELECT start, end, deviceId, shortName FROM CUPTI_ACTIVITY_KIND_KERNEL"))
+        copies = []
+        if "CUPTI_ACTIVITY_KIND_MEMCPY" in tables:
+            copies = list(con.execute("SELECT start, end, bytes, copyKind FROM CUPTI_ACTIVITY_KIND_MEMCPY"))
+        ranges = []
+        if "NVTX_EVENTS" in tables:
+            ranges = list(con.execute("SELECT start, end, text FROM NVTX_EVENTS WHERE end IS NOT NULL"))
+    finally:
+        con.close()
+    stamps = [t for k in kernels for t in k[:2]] + [t for c in copies for t in c[:2]]
+    span_ns = (max(stamps) - min(stamps)) if stamps else 0
+    per_dev = defaultdict(list)
+    agg = defaultdict(lambda: [0, 0])
+    for s, e, dev, name in kernels:
+        per_dev[dev].append((s, e))
+        a = agg[names.get(name, str(name))]
+        a[0] += 1
+        a[1] += e - s
+    ktot = sum(v[1] for v in agg.values()) or 1
+    top_rows = sorted(([k, v[0], v[1]] for k, v in agg.items()), key=lambda r: -r[2])[:top]
+    copy_kinds = {1: "HtoD", 2: "DtoH", 8: "DtoD", 10: "PtoP"}
+    cagg = defaultdict(lambda: [0, 0, 0])
+    for s, e, nbytes, kind in copies:
+        c = cagg[copy_kinds.get(kind, str(kind))]
+        c[0] += 1
+        c[1] += nbytes
+        c[2] += e - s
+    ragg = defaultdict(lambda: [0, 0])
+    for s, e, text in ranges:
+        r = ragg[text]
+        r[0] += 1
+        r[1] += e - s
+    return dict(
+        span_ms=span_ns / 1e6,
+        devices={int(d): dict(busy_ms=_union_ns(iv) / 1e6, utilization=(_union_ns(iv) / span_ns) if span_ns else 0.0,
+                               kernels=len(iv)) for d, iv in sorted(per_dev.items())},
+        kernels=[dict(name=n, calls=c, total_ms=t / 1e6, share=round(t / ktot, 4)) for n, c, t in top_rows],
+        copies={k: dict(count=v[0], bytes=v[1], total_ms=v[2] / 1e6,
+                        gbps=(v[1] / v[2]) if v[2] else 0.0) for k, v in cagg.items()},
+        nvtx={k: dict(count=v[0], total_ms=v[1] / 1e6) for k, v in ragg.items()},
+    )

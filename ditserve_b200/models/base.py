@@ -55,6 +55,14 @@ def artifact(value, path=None, mode="file") -> dict:
     return out
 
 
+def transfer_dir(config: dict) -> str:
+    """Directory of host-staged continuation packets: the worker config's ``transfer_dir``,
+    else ``DITSERVE_TRANSFER_DIR``, else /dev/shm (tmpfs) when present, else /tmp."""
+    import os
+    return str(config.get("transfer_dir") or os.environ.get("DITSERVE_TRANSFER_DIR")
+               or ("/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"))
+
+
 def progress(step, steps, *, done=None, next_action=None) -> dict:
     done = step >= steps if done is None else bool(done)
     return dict(step=step, steps=steps, done=done, next_action=next_action or ("finish" if done else "advance"))

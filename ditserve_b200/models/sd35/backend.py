@@ -10,7 +10,7 @@ import time
 
 import torch
 
-from ..base import Backend, progress
+from ..base import Backend, progress, transfer_dir
 from .model import SD35_MEDIUM, SD35_TINY
 from .runtime import SD35Engine, SD35Spec
 
@@ -128,7 +128,7 @@ class SD35Backend(Backend):
         buf = io.BytesIO()
         torch.save(self.engine.snapshot(st), buf)
         blob = buf.getvalue()
-        d = Path(self.config.get("transfer_dir", "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"))
+        d = Path(transfer_dir(self.config))
         path = d / f"sd35-packet-{request['state_id']}-{os.getpid()}-{request.get('id', 0)}.pt"
         path.write_bytes(blob)
         return dict(path=str(path), manifest=hashlib.sha256(blob).hexdigest(), bytes=len(blob))

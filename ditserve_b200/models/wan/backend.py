@@ -18,7 +18,7 @@ from pathlib import Path
 
 import torch
 
-from ..base import Backend, artifact, progress
+from ..base import Backend, artifact, progress, transfer_dir
 from .config import CONFIGS
 from .runtime import WanEngine, WanSpec
 
@@ -41,7 +41,7 @@ class WanBackend(Backend):
         self.engine = WanEngine(self.model_name, device=self.device, dtype=dtype, seed=int(config.get("seed", 0)))
         self.snapshots: dict = {}
         self.tickets: dict = {}
-        self.transfer_dir = Path(config.get("transfer_dir", "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"))
+        self.transfer_dir = Path(transfer_dir(config))
         self.layout = None
         self._decoder = None
         self.decodes: dict = {}

@@ -372,7 +372,8 @@ def main(argv=None):
     d = sub.add_parser("daemon")
     d.add_argument("--listen", default="127.0.0.1:7700")
     p = sub.add_parser("proxy")
-    p.add_argument("--connect", required=True)
+    p.add_argument("--connect", default=os.environ.get("DITSERVE_REMOTE_ENDPOINT"),
+                   help="daemon host:port (default: DITSERVE_REMOTE_ENDPOINT)")
     p.add_argument("--backend", required=True)
     p.add_argument("--config", default="{}")
     p.add_argument("--env", action="append", default=[], metavar="KEY=VALUE",
@@ -385,6 +386,8 @@ def main(argv=None):
         print(json.dumps({"listening": daemon.port}), flush=True)
         daemon.serve_forever()
         return 0
+    if not args.connect:
+        ap.error("proxy needs --connect or DITSERVE_REMOTE_ENDPOINT")
     env = dict(kv.split("=", 1) for kv in args.env)
     proxy = BridgeProxy(args.connect, args.backend, json.loads(args.config), env, args.stage_dir)
     out = sys.stdout

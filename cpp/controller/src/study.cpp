@@ -755,10 +755,10 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     std::string last_state = "unknown";
     while (true) {
       Json q = Json::object();
-      Json idx = Json::array();
+      Json probe_gpus = Json::array();
       for (int g = 0; g < gpus; ++g)
-        if (!remote.count(g)) idx.push_back(g);  // the local probe sees this node's GPUs only
-      q["gpus"] = idx;
+        if (!remote.count(g)) probe_gpus.push_back(g);  // the local probe sees this node's GPUs only
+      q["gpus"] = probe_gpus;
       q["own_pids"] = own_pids;
       try {
         last_state = prober->call("occupancy", q, 60).str("state", "unknown");
@@ -777,10 +777,10 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     if (guard && now >= next_probe) {
       next_probe = now + guard_interval_ms;
       Json q = Json::object();
-      Json idx = Json::array();
+      Json probe_gpus = Json::array();
       for (int g = 0; g < gpus; ++g)
-        if (!remote.count(g)) idx.push_back(g);
-      q["gpus"] = idx;
+        if (!remote.count(g)) probe_gpus.push_back(g);
+      q["gpus"] = probe_gpus;
       q["own_pids"] = own_pids;
       Json occ;
       try {

@@ -18,7 +18,7 @@ from pathlib import Path
 
 import torch
 
-from ..base import Backend, artifact, progress, transfer_dir
+from ..base import Backend, progress, transfer_dir
 from .config import CONFIGS
 from .runtime import WanEngine, WanSpec
 

@@ -18,7 +18,6 @@ import math
 
 import torch
 
-from .. import ops
 from ..ops._ext import ext, status_word
 from .symm import PeerGroup, SymmetricHeap
 

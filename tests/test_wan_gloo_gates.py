@@ -16,7 +16,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from ditserve_b200.models.wan.config import WAN_TINY
-from ditserve_b200.models.wan.runtime import WanEngine, WanSpec
+from ditserve_b200.models.wan.runtime import WanEngine
 
 SPEC = dict(model="wan-tiny", height=64, width=64, frames=13, steps=4, guidance=5.0, seed=7)
 

@@ -10,7 +10,6 @@ call's contents, which must not leak into the next result).  This file is collec
 so a failing run has already exercised every other test.
 """
 import ctypes
-import math
 
 import pytest
 import torch

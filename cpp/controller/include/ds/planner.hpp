@@ -3,7 +3,8 @@
 // cluster_plan(state, policy, cost, options) decides, at one instant, which
 // waiting or suspended requests start a quantum on which GPUs.
 //
-// state:   {now_ms, gpus, busy: [bool], requests: [...], sp_groups_running}
+// state:   {now_ms, gpus, busy: [bool], async_decoding?: [bool], requests: [...], sp_groups_running}
+//          (a GPU with an asynchronous VAE decode in flight takes images but no new video)
 // request: {request_id, kind video|image, class, arrival_ms, deadline_ms,
 //           status waiting|suspended, steps_done, blocks_done, steps_total?,
 //           group [] (last GPUs held), form (last form), decode_done, affinity?}

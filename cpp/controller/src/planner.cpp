@@ -193,6 +193,7 @@ struct Gpus {
   // videos do not take them (images may: a doorbell stopped the video for them)
   std::vector<std::string> reserved;
   std::string current;  // the video being placed
+  std::vector<bool> decoding;  // a VAE decode runs on a side stream: no new video, images may overlap
   int count() const {
     int n = 0;
     for (bool f : free) n += f;
@@ -205,7 +206,7 @@ std::vector<int> pick_group(const Gpus& g, int size, const std::vector<int>& pre
   const int n = static_cast<int>(g.free.size());
   auto usable = [&](int i) {
     return g.free[i] &&
-           !(for_video && (g.image_only[i] || (!g.reserved[i].empty() && g.reserved[i] != g.current)));
+           !(for_video && (g.image_only[i] || g.decoding[i] || (!g.reserved[i].empty() && g.reserved[i] != g.current)));
   };
   if (static_cast<int>(prefer.size()) == size) {
     bool ok = true;
@@ -284,6 +285,12 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
   g.free.assign(n, true);
   g.image_only.assign(n, false);
   g.reserved.assign(n, std::string());
+  g.decoding.assign(n, false);
+  if (state.contains("async_decoding")) {
+    const auto& dec = state.at("async_decoding").as_array();
+    if (static_cast<int>(dec.size()) != n) throw std::invalid_argument("async_decoding must list every GPU");
+    for (int i = 0; i < n; ++i) g.decoding[i] = dec[i].as_bool();
+  }
   if (state.contains("busy")) {
     const auto& busy = state.at("busy").as_array();
     if (static_cast<int>(busy.size()) != n) throw std::invalid_argument("busy must list every GPU");
@@ -490,7 +497,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
   };
   auto video_free = [&]() {
     int c = 0;
-    for (int i = 0; i < n; ++i) c += g.free[i] && !g.image_only[i];
+    for (int i = 0; i < n; ++i) c += g.free[i] && !g.image_only[i] && !g.decoding[i];
     return c;
   };
   auto movable_after = [&](const Req& self, const Req& o, bool& after) {

@@ -681,3 +681,17 @@ TEST("deadline doorbells: a group's own timing, natural boundaries and already-r
                                              {"extra", {2}, 5, 100, 0, false}};
   CHECK(select_deadline_preemption(0, {{-1, 50, 40}, {-1, 50, 40}}, pending).selected.empty());
 }
+
+TEST("an asynchronous decode keeps new videos off its GPU but lets images overlap") {
+  ClusterCost c(profile());
+  Json st = state(2, {req("a", "video", "vid", 0, 1e9), req("b", "video", "vid", 0, 1e9 + 1)});
+  st["async_decoding"] = Json::parse("[true, false]");
+  Json o = Json::object();
+  o["degrees"] = Json::parse("[1]");
+  auto p = cluster_plan(st, "abl-step-elastic", c, o);
+  CHECK(p.at("assignments").size() == 1 && p.at("assignments")[0].at("group")[0].as_int() == 1);
+  Json si = state(2, {req("i", "image", "img", 0, 5000)});
+  si["async_decoding"] = Json::parse("[true, false]");
+  auto q = cluster_plan(si, "static-sp1", c);
+  CHECK(q.at("assignments").size() == 1 && q.at("assignments")[0].at("group")[0].as_int() == 0);
+}

@@ -2,6 +2,7 @@
 #include <signal.h>
 #include <unistd.h>
 
+#include <chrono>
 #include <iostream>
 #include <string>
 #include <thread>
@@ -134,6 +135,8 @@ TEST("a dead worker surfaces as WorkerFailure") {
     failed = true;
   }
   CHECK(failed);
+  // the reply pipe closes just before the process is reaped: allow the exit to land
+  for (int i = 0; i < 500 && w.alive(); ++i) std::this_thread::sleep_for(std::chrono::milliseconds(10));
   CHECK(!w.alive());
   CHECK(w.stop());
 }

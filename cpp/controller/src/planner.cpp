@@ -47,6 +47,9 @@ struct Settings {
   double wide_efficiency = 0.0;     // >0: videos start on their widest form at least this efficient
   double late_short_ms = 0.0;       // late requests this short keep their EDF position
   bool load_adaptive = false;       // many videos: most GPU-efficient form; few: normal choice
+  double quantum_ms = 0.0;          // >0: block quanta sized to this much GPU time
+  bool lazy_preemption = true;      // an image that can wait for a mid-step video's boundary does
+  std::string feasibility_degree;   // "free" | "widest": the degree the lateness test assumes
 };
 
 Settings resolve(const PolicyTraits& t, const Json& o) {
@@ -95,6 +98,15 @@ Settings resolve(const PolicyTraits& t, const Json& o) {
   s.late_short_ms = o.num("late_short_ms", 0.0);
   s.load_adaptive = o.flag("load_adaptive", t.load_adaptive);
   if (s.late_short_ms < 0) throw std::invalid_argument("late_short_ms must be >= 0");
+  s.quantum_ms = o.num("quantum_ms", 0.0);
+  if (!(s.quantum_ms >= 0)) throw std::invalid_argument("quantum_ms must be >= 0");
+  s.lazy_preemption = o.flag("lazy_preemption", true);
+  // elastic policies judge lateness on the widest group free when the plan starts (a request
+  // that only an idle node could save would otherwise keep its rank, run narrow and miss);
+  // static policies on their widest degree
+  s.feasibility_degree = o.str("feasibility_degree", t.elastic ? "free" : "widest");
+  if (s.feasibility_degree != "free" && s.feasibility_degree != "widest")
+    throw std::invalid_argument("feasibility_degree must be free or widest");
   if (s.feasible_margin < 0 || s.feasible_margin > 10) throw std::invalid_argument("feasible_margin must be in [0, 10]");
   return s;
 }
@@ -318,6 +330,19 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     video_load += rj.integer("steps_done", 0) < rj.integer("steps_total", cost.steps(rj.at("class").as_string()));
   }
   const bool throughput_mode = s.load_adaptive && video_load * 2 >= video_capacity;
+  // widest aligned group free (and open to videos) when this plan starts
+  int widest_free = 0;
+  for (int d : {1, 2, 4, 8, 16, 32, 64}) {
+    if (d > n) break;
+    for (const auto& grp : cluster_groups(n, d)) {
+      bool ok = true;
+      for (int i : grp) ok = ok && g.free[i] && !g.image_only[i];
+      if (ok) {
+        widest_free = d;
+        break;
+      }
+    }
+  }
   auto efficient_only = [&](std::vector<Form> forms, const std::string& klass) {
     if (!throughput_mode || forms.size() < 2) return forms;
     const Form* eff = &forms.front();
@@ -353,8 +378,13 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     // actually get when the load-adaptive choice is in throughput mode)
     if (r.video()) {
       double best = kInf;
-      for (const auto& f : efficient_only(forms_for(s, cost, r.klass, video_capacity), r.klass))
-        best = std::min(best, cost.remaining_ms(rj, f));
+      const auto forms = efficient_only(forms_for(s, cost, r.klass, video_capacity), r.klass);
+      int limit = video_capacity;
+      if (s.feasibility_degree == "free" && !forms.empty()) limit = std::max(widest_free, forms.front().degree());
+      for (const auto& f : forms)
+        if (f.degree() <= limit) best = std::min(best, cost.remaining_ms(rj, f));
+      if (!std::isfinite(best))
+        for (const auto& f : forms) best = std::min(best, cost.remaining_ms(rj, f));
       if (!std::isfinite(best)) best = cost.remaining_ms(rj, Form{});
       r.best_remaining = best;
     } else {
@@ -425,14 +455,19 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     for (int i : grp) g.free[i] = true;
   };
 
-  auto video_quantum = [&](const Req& r, Json& a) {
+  auto video_quantum = [&](const Req& r, const Form& f, Json& a) {
     if (r.finished_denoise()) {
       a["quantum"] = "finish";
       const int chunks = cost.decode_chunks(r.klass);
       if (chunks > 1) a["decode_frames"] = t.blocks ? 1 : chunks - r.decode_done;
       return;
     }
-    if (t.blocks && s.quantum_blocks > 0) {
+    if (t.blocks && s.quantum_ms > 0) {
+      // a preemption check about every quantum_ms of GPU work, never past the step boundary
+      const int left = std::max(1, cost.blocks_per_step(r.klass) - r.blocks_done);
+      const double blocks = std::floor(s.quantum_ms / cost.block_ms(r.klass, f));
+      a["quantum"] = static_cast<int>(std::max(1.0, std::min(blocks, static_cast<double>(left))));
+    } else if (t.blocks && s.quantum_blocks > 0) {
       a["quantum"] = s.quantum_blocks;
     } else {
       a["quantum"] = "step";
@@ -450,7 +485,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     a["form"] = form_name(f);
     a["resize"] = !r.group.empty() && r.group != grp;
     a["reason"] = reason;
-    video_quantum(r, a);
+    video_quantum(r, f, a);
     take(grp);
     placed.insert(r.id);
     placed_videos.push_back({r.id, grp, f, assignments.size(), r.klass, r.deadline, r.j});
@@ -623,9 +658,34 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
   };
 
   // ---- images ----------------------------------------------------------------------
+  // time until a mid-step video reaches its step boundary if it resumes now
+  auto time_to_boundary = [&](const std::string& owner) -> double {
+    for (const auto& o : reqs)
+      if (o.id == owner) {
+        const Form f = o.form.empty() ? Form{1, static_cast<int>(o.group.size()), 1} : parse_form(o.form);
+        return std::max(0, cost.blocks_per_step(o.klass) - o.blocks_done) * cost.block_ms(o.klass, f);
+      }
+    return kInf;
+  };
   auto place_image = [&](const Req& r) -> bool {
     if (placed.count(r.id)) return true;
+    // lazy block preemption: a new image does not take a GPU whose mid-step video can resume
+    // now when waiting for that video's step boundary still meets the image's deadline
+    std::vector<int> masked;
+    if (t.blocks && s.lazy_preemption && r.affinity < 0 && !r.j->contains("steps_done") && std::isfinite(r.deadline)) {
+      const double slack = r.deadline - now - r.best_remaining;
+      for (int i = 0; i < n; ++i) {
+        if (!g.free[i] || g.reserved[i].empty()) continue;
+        bool resumable = true;
+        for (const auto& o : reqs)
+          if (o.id == g.reserved[i])
+            for (int k : o.group) resumable = resumable && k >= 0 && k < n && g.free[k];
+        if (resumable && slack > 0 && time_to_boundary(g.reserved[i]) <= slack) masked.push_back(i);
+      }
+    }
+    for (int i : masked) g.free[i] = false;
     const int gpu = pick_image_gpu(g, t.image_placement, r.affinity, claims);
+    for (int i : masked) g.free[i] = true;
     if (gpu < 0) return false;
     Json a = Json::object();
     a["request_id"] = r.id;

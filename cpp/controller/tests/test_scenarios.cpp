@@ -695,3 +695,49 @@ TEST("an asynchronous decode keeps new videos off its GPU but lets images overla
   auto q = cluster_plan(si, "static-sp1", c);
   CHECK(q.at("assignments").size() == 1 && q.at("assignments")[0].at("group")[0].as_int() == 0);
 }
+
+TEST("lazy block preemption: a new image waits for a mid-step video's boundary when it can") {
+  ClusterCost c(profile());
+  auto v = suspended("v", "[0,1]", "cfg2", 3, 15);  // 15 of 30 blocks left: 200 ms to its boundary
+  Json relaxed = req("i", "image", "img", 0, 1000);   // 386 ms of work, 614 ms of slack
+  auto p = cluster_plan(state(2, {v, relaxed}), "ditserve", c);
+  CHECK(find(p, "v") != nullptr && find(p, "i") == nullptr);
+  Json tight = req("i", "image", "img", 0, 500);      // 114 ms of slack: it takes the GPU now
+  auto q = cluster_plan(state(2, {v, tight}), "ditserve", c);
+  CHECK(find(q, "i") != nullptr && find(q, "v") == nullptr);
+  Json o = Json::object();
+  o["lazy_preemption"] = false;
+  auto r = cluster_plan(state(2, {v, relaxed}), "ditserve", c, o);
+  CHECK(find(r, "i") != nullptr);
+}
+
+TEST("lateness is judged on the widest group free when the plan starts (elastic policies)") {
+  ClusterCost c(profile());
+  Json v = req("v", "video", "vid", 0, 3000);  // cfg2sp2 (2222 ms) or wider meets it; cfg2 (4100) does not
+  auto feasible_in = [&](const Json& o) {
+    PlanTrace tr;
+    cluster_plan(state(8, {v}, {0, 1, 2, 3, 4, 5}), "ditserve", c, o, &tr);
+    return tr.rows[0].at("feasible").as_bool();
+  };
+  CHECK(!feasible_in(Json::object()));  // only a pair is free
+  Json widest = Json::object();
+  widest["feasibility_degree"] = "widest";
+  CHECK(feasible_in(widest));
+  PlanTrace tr;
+  cluster_plan(state(8, {v}), "ditserve", c, Json::object(), &tr);
+  CHECK(tr.rows[0].at("feasible").as_bool());  // an idle node
+}
+
+TEST("quantum_ms sizes block quanta by GPU time and never crosses the step boundary") {
+  ClusterCost c(profile());  // cfg2: 400 ms per 30-block step
+  Json o = Json::object();
+  o["quantum_ms"] = 100;
+  auto p = cluster_plan(state(2, {req("v", "video", "vid", 0, 1e9)}), "ditserve", c, o);
+  CHECK(find(p, "v")->at("quantum").as_int() == 7);
+  auto m = suspended("m", "[0,1]", "cfg2", 3, 28);
+  auto q = cluster_plan(state(2, {m}), "ditserve", c, o);
+  CHECK(find(q, "m")->at("quantum").as_int() == 2);
+  o["quantum_ms"] = 1e100;
+  auto r = cluster_plan(state(2, {req("v", "video", "vid", 0, 1e9)}), "ditserve", c, o);
+  CHECK(find(r, "v")->at("quantum").as_int() == 30);
+}

@@ -331,6 +331,8 @@ class WanTransformer(nn.Module):
 
     def forward_block(self, i: int, pk: WanPacket, pctx=None) -> WanPacket:
         pctx = pctx or LocalAttention()
+        if hasattr(pctx, "begin_block"):
+            pctx.begin_block(i)  # plans with per-block settings (FP8 payload layers)
         cfg = self.cfg
         blk = self.blocks[i]
         D, Hh, hd = cfg.dim, cfg.heads, cfg.head_dim

@@ -3,9 +3,10 @@
 The ranks of a layout call ``build_parallel`` with the same layout; only they take part
 (groups are created member-locally and cached by rank set, so other ranks of the world
 can be busy with other requests meanwhile).  Returns ``(pctx, cfg_plan)`` for the Wan
-engine.  ``attention="nccl"`` is the
-NCCL baseline; ``attention="fused"`` uses the peer-memory kernels of
-``parallel.fused`` when they are available for the layout.
+engine.  ``attention="nccl"`` is the NCCL baseline; ``attention="nccl-fp8"`` is the same
+path with FP8 payloads on the Ulysses all-to-alls (``parallel.fp8_comms``; plain Ulysses
+forms, ``fp8_layers`` picks the blocks, None = all); ``attention="fused"`` uses the
+peer-memory kernels of ``parallel.fused`` when they are available for the layout.
 """
 from __future__ import annotations
 
@@ -36,7 +37,9 @@ def group_for(ranks):
 
 
 def build_parallel(layout: FixedLayout, rank: int, device: torch.device, attention: str = "fused",
-                   seq_local: int | None = None, cfg=None, pred_numel: int | None = None):
+                   seq_local: int | None = None, cfg=None, pred_numel: int | None = None, fp8_layers=None):
+    if attention not in ("fused", "nccl", "nccl-fp8"):
+        raise ValueError(f"unknown collective path {attention!r}")
     form = layout.form
     sp_groups, cfg_groups = {}, {}
     my_sp = layout.sp_ranks(rank)
@@ -58,6 +61,9 @@ def build_parallel(layout: FixedLayout, rank: int, device: torch.device, attenti
         pctx = UlyssesRingNCCL(sp_groups[my_sp], u_groups[layout.ulysses_ranks(rank)],
                                ring_groups[layout.ring_ranks(rank)], form.sp, layout.sp_rank(rank), form.ulysses,
                                form.ring)
+    elif form.sp > 1 and attention == "nccl-fp8":
+        from .fp8_comms import FP8UlyssesNCCL
+        pctx = FP8UlyssesNCCL(sp_groups[my_sp], form.sp, layout.sp_rank(rank), layers=fp8_layers)
     elif form.sp > 1:
         pctx = UlyssesNCCL(sp_groups[my_sp], form.sp, layout.sp_rank(rank))
     if form.cfg == 2:

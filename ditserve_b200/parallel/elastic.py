@@ -183,10 +183,16 @@ def broadcast_state_nccl(tree, src: int, group=None, device=None):
 
 
 class PeerStateBroadcast:
-    """Regroup transfer over peer memory: the source puts every tensor into the receivers' heaps."""
+    """Regroup transfer over peer memory: the source puts every tensor into the receivers' heaps.
+
+    ``transport="sm"`` stores with the ``put_peers`` kernel (16-byte NVLink stores from SMs);
+    ``transport="ce"`` issues one ``cudaMemcpyAsync`` per receiver and slice on the current
+    stream, so the copy engines move the bytes and the SMs stay free for compute.  Both are
+    ordered before the group barrier that publishes the data (reference copy-engine path:
+    workers/gfc/kernels/copy_engine.py:21-133)."""
 
     def __init__(self, heap, members: tuple, capacity_bytes: int, channel: int = 7, timeout_s: float = 10.0,
-                 group=None):
+                 group=None, transport: str = "sm"):
         from ..ops._ext import ext
         from .symm import PeerGroup
         self.ext = ext()
@@ -196,6 +202,23 @@ class PeerStateBroadcast:
         self.capacity = int(capacity_bytes)
         self.off = heap.alloc(self.capacity, align=4096)
         self.scatter_min_bytes = 1 << 20  # larger tensors go scatter + all-gather (bandwidth-optimal)
+        if transport not in ("sm", "ce"):
+            raise ValueError("transport must be sm or ce")
+        self.transport = transport
+
+    def _put(self, src: torch.Tensor, mask: int, dst_off: int, r, bases, tmo):
+        if self.transport == "sm":
+            self.ext.put_peers(src, mask, dst_off, r, bases, tmo)
+            return
+        from cuda.bindings import runtime as cudart
+        stream = torch.cuda.current_stream(src.device).cuda_stream
+        nbytes = src.numel() * src.element_size()
+        for m, base in enumerate(bases):
+            if mask >> m & 1:
+                err, = cudart.cudaMemcpyAsync(base + dst_off, src.data_ptr(), nbytes,
+                                              cudart.cudaMemcpyKind.cudaMemcpyDefault, stream)
+                if err != cudart.cudaError_t.cudaSuccess:
+                    raise RuntimeError(f"copy-engine put to member {m} failed: {err}")
 
     def __call__(self, tree, src_member: int, src_global: int | None = None):
         """``src_member`` indexes the group; ``src_global`` is its rank in the default group
@@ -237,15 +260,15 @@ class PeerStateBroadcast:
                 body, parts = split(nb)
                 if parts is None:  # small: store the whole body into every receiver
                     if body:
-                        self.ext.put_peers(flat[:body], everyone, self.off + o, r, bases, tmo)
+                        self._put(flat[:body], everyone, self.off + o, r, bases, tmo)
                 else:  # large: slice j to receiver j only (the source's NVLink egress carries it once)
                     for (lo, hi), m in zip(parts, receivers):
                         if hi > lo:
-                            self.ext.put_peers(flat[lo:hi], 1 << m, self.off + o + lo, r, bases, tmo)
+                            self._put(flat[lo:hi], 1 << m, self.off + o + lo, r, bases, tmo)
                 if nb - body:  # ragged tail: pad to one 16-byte vector
                     tail = torch.zeros(16, dtype=torch.uint8, device=flat.device)
                     tail[:nb - body] = flat[body:]
-                    self.ext.put_peers(tail, everyone, self.off + o + body, r, bases, tmo)
+                    self._put(tail, everyone, self.off + o + body, r, bases, tmo)
         g.barrier(status)
         if g.rank != src_member and k >= 2:
             # all-gather among the receivers: each forwards its slice to the others
@@ -261,7 +284,7 @@ class PeerStateBroadcast:
                 lo, hi = parts[j]
                 if hi > lo:
                     mine = self.heap.tensor[self.off + o + lo:self.off + o + hi]
-                    self.ext.put_peers(mine, others, self.off + o + lo, r, bases, tmo)
+                    self._put(mine, others, self.off + o + lo, r, bases, tmo)
         if k >= 2 and any(split(nb)[1] is not None for nb in sizes):
             g.barrier(status)
         if g.rank == src_member:

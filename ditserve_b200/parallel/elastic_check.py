@@ -4,7 +4,7 @@
 
 * group flag: ``GroupFlagPeer`` (one bounded-wait kernel) and ``GroupFlagNCCL`` (all_reduce
   MAX) agree on 64 random flag patterns; device-timed per-call latency of both;
-* regroup transfer: a Wan-request-like snapshot (fp32 latents + solver history, ``--mb``
+* regroup transfer (SM stores and copy engines): a Wan-request-like snapshot (fp32 latents + solver history, ``--mb``
   MB in total) broadcast from rank 0 by ``PeerStateBroadcast`` and by
   ``broadcast_state_nccl``; both must be bit-identical to the source; device time of each
   (max over ranks).  Rank 0 prints one JSON line.
@@ -79,12 +79,20 @@ def main():
     dg = [torch.zeros_like(digest) for _ in range(world)]
     dist.all_gather(dg, digest)
     ok &= all(torch.equal(d, dg[0]) for d in dg)
+    # the same transfer by copy engines (one cudaMemcpyAsync per receiver and slice)
+    bc.transport = "ce"
+    c = bc(src, 0)
+    ok_ce = all(torch.equal(x, y) for x, y in zip([a["latents"], *a["scheduler"]["hist"], a["scheduler"]["last"]],
+                                                  [c["latents"], *c["scheduler"]["hist"], c["scheduler"]["last"]]))
+    bc_ce_ms = _timed(lambda: bc(src, 0), 5, dev)
+    bc.transport = "sm"
     bc_peer_ms = _timed(lambda: bc(src, 0), 5, dev)
     bc_nccl_ms = _timed(lambda: broadcast_state_nccl(src, 0, device=dev), 5, dev)
     nbytes = 4 * (4 * n + n + 3)
     out = dict(world=world, flags_agree=bool(agree), flag_peer_us=round(flag_peer_us, 1),
                flag_nccl_us=round(flag_nccl_us, 1), state_mb=round(nbytes / 2 ** 20, 1), broadcast_bitwise=bool(ok),
                broadcast_peer_ms=round(bc_peer_ms, 3), broadcast_nccl_ms=round(bc_nccl_ms, 3),
+               broadcast_ce_bitwise=bool(ok_ce), broadcast_ce_ms=round(bc_ce_ms, 3),
                broadcast_peer_gbs=round(nbytes * (world - 1) / bc_peer_ms / 1e6, 1))
     if rank == 0:
         print(json.dumps(out), flush=True)

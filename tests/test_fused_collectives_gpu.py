@@ -91,4 +91,4 @@ def test_elastic_paths_multi_gpu():
                        text=True, env=env, timeout=360)
     assert r.returncode == 0, r.stderr[-3000:]
     res = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
-    assert res["flags_agree"] and res["broadcast_bitwise"], res
+    assert res["flags_agree"] and res["broadcast_bitwise"] and res["broadcast_ce_bitwise"], res

@@ -77,6 +77,8 @@ class WanBackend(Backend):
             from ...parallel.autotune import choose
             path = choose(form.name, self.engine.cfg.tokens(shape) // form.sp)
         key = (ranks, form.name, shape, path)
+        if path == "nccl-fp8" and request.get("fp8_layers") is not None:
+            key += (tuple(sorted(int(i) for i in request["fp8_layers"])),)
         if st is not None and st.block != 0 and st.layout_key not in (None, key):
             raise ValueError("the SP group may change only at a solver-step boundary")
         if key not in self._layouts:
@@ -91,7 +93,7 @@ class WanBackend(Backend):
                 rank = dist.get_rank()
                 pctx, plan = build_parallel(layout, rank, self.device, attention=path,
                                             seq_local=self.engine.cfg.tokens(shape) // form.sp, cfg=self.engine.cfg,
-                                            pred_numel=math.prod(shape))
+                                            pred_numel=math.prod(shape), fp8_layers=request.get("fp8_layers"))
                 flag = None
                 if form.sp > 1:  # doorbell stop agreed over the SP group (MAX of the ranks' flags)
                     sp = layout.sp_ranks(rank)

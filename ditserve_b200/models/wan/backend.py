@@ -169,9 +169,32 @@ class WanBackend(Backend):
         spec.pop("request_id", None)
         spec.setdefault("model", self.model_name)
         spec = {k: v for k, v in spec.items() if k in WanSpec.__dataclass_fields__}
-        st = self.engine.prepare(spec)
+        context = negative = None
+        enc_cfg = self.config.get("text_encoder")
+        if enc_cfg:  # {"config": "tiny" | "xxl", "seed": n}: UMT5 architecture, seeded weights
+            context, negative = self._encode(WanSpec.normalize(spec), enc_cfg)
+        st = self.engine.prepare(spec, context=context, negative=negative)
         self.states[key] = st
         return dict(state_id=key, progress=self._progress(st))
+
+    def _encode(self, spec: WanSpec, enc_cfg: dict):
+        """Prompt and negative prompt through the UMT5 encoder: valid tokens only, zero-padded
+        to the model's text length (the valid-token crop)."""
+        from ..encoder_pool import trim_and_pad
+        from ..text_encoders import TINY_T5, UMT5TextEncoder
+        if getattr(self, "_text_encoder", None) is None:
+            cfg = TINY_T5 if enc_cfg.get("config", "xxl") == "tiny" else None
+            dtype = torch.float32 if self.device.type == "cpu" else torch.bfloat16
+            self._text_encoder = UMT5TextEncoder(cfg, device=self.device, dtype=dtype,
+                                                 seed=int(enc_cfg.get("seed", 0)))
+        L = spec.text_len or self.engine.cfg.text_len
+        if self._text_encoder.dim != self.engine.cfg.text_dim:
+            raise ValueError(f"text encoder width {self._text_encoder.dim} != model text_dim {self.engine.cfg.text_dim}")
+        out = []
+        for text in (spec.prompt, spec.negative_prompt):
+            tokens, valid = self._text_encoder(text, L)
+            out.append(trim_and_pad(tokens, valid, L)[None])
+        return out[0], (out[1] if spec.guidance > 1.0 else None)
 
     def advance(self, request):
         if request.get("pair_state_id") is not None:

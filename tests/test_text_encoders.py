@@ -50,3 +50,18 @@ def test_encoder_pool_with_umt5(tmp_path):
         assert got is not None
     finally:
         pool.close()
+
+
+def test_wan_backend_encodes_prompts_with_umt5(tmp_path):
+    from ditserve_b200.models.wan.backend import WanBackend
+    w = WanBackend({"model": "wan-tiny", "device": "cpu", "transfer_dir": str(tmp_path),
+                    "text_encoder": {"config": "tiny", "seed": 4}})
+    base = dict(height=32, width=32, frames=5, steps=2, seed=3, guidance=4.0, negative_prompt="blurry")
+    outs = {}
+    for sid, prompt in (("a", "a red fox in snow"), ("b", "a red fox in snow"), ("c", "a blue whale")):
+        w.prepare(dict(id=1, spec=dict(base, request_id=sid, prompt=prompt)))
+        st = w.states[sid]
+        assert st.context.shape == (1, 16, 64) and torch.count_nonzero(st.context[0, 6:]) == 0
+        w.advance(dict(id=2, state_id=sid, steps=2))
+        outs[sid] = w.finish(dict(id=3, state_id=sid, output_mode="digest"))["value"]
+    assert outs["a"] == outs["b"] and outs["a"] != outs["c"]

@@ -38,7 +38,11 @@ class SD35Backend(Backend):
     def prepare(self, request):
         key = self.new_id(request)
         spec = {k: v for k, v in request.get("spec", {}).items() if k in SD35Spec.__dataclass_fields__}
-        self.states[key] = self.engine.prepare(spec)
+        text = negative = None
+        enc_cfg = self.config.get("text_encoder")
+        if enc_cfg:  # {"config": "tiny" | "full", "seed": n}: CLIP-L + bigG + T5-XXL, seeded weights
+            text, negative = self._encode(SD35Spec.normalize(spec), enc_cfg)
+        self.states[key] = self.engine.prepare(spec, text=text, negative_text=negative)
         st = self.states[key]
         return dict(state_id=key, progress=progress(st.step, st.spec.steps))
 
@@ -114,6 +118,31 @@ class SD35Backend(Backend):
             raise ValueError("no snapshot for state_id")
         self.states[request["state_id"]] = self.engine.restore(snap)
         return dict(state_id=request["state_id"])
+
+    def _encode(self, spec, enc_cfg: dict):
+        """Prompt and negative prompt through the three encoders; the joint context is cut or
+        zero-padded to the spec's text length (77 CLIP positions, then T5)."""
+        from ..text_encoders import SD3TextEncoders
+        cfg = self.engine.cfg
+        if getattr(self, "_text_encoders", None) is None:
+            tiny = enc_cfg.get("config", "full") == "tiny"
+            dims = None
+            if tiny:  # split the tiny model's pooled width 3:5 between CLIP-L and CLIP-G
+                wl = cfg.pooled_dim * 3 // 8 // 4 * 4
+                dims = (wl, cfg.pooled_dim - wl, cfg.joint_dim)
+            dtype = torch.float32 if self.device.type == "cpu" else torch.bfloat16
+            self._text_encoders = SD3TextEncoders(tiny=tiny, device=self.device, dtype=dtype,
+                                                  seed=int(enc_cfg.get("seed", 0)),
+                                                  t5_len=max(1, spec.text_len - 77), tiny_dims=dims)
+        enc = self._text_encoders
+        if enc.joint_dim != cfg.joint_dim or enc.pooled_dim != cfg.pooled_dim:
+            raise ValueError("text encoder widths do not match the model's joint / pooled widths")
+        out = []
+        for text in (spec.prompt, spec.negative_prompt):
+            ctx, pooled = enc(text)
+            ctx = ctx[:spec.text_len]
+            out.append((ctx.to(self.device, self.engine.dtype), pooled.to(self.device, self.engine.dtype)))
+        return out[0], (out[1] if spec.guidance > 1.0 else None)
 
     def inventory(self, request):
         return dict(states={k: dict(step=v.step, steps=v.spec.steps) for k, v in self.states.items()})

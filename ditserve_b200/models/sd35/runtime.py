@@ -86,7 +86,9 @@ class SD35Engine:
         self.model = model or SD35Transformer.random_init(cfg, device=self.device, dtype=dtype, seed=seed)
         self.max_batch = max_batch
 
-    def prepare(self, spec: SD35Spec | dict) -> SD35State:
+    def prepare(self, spec: SD35Spec | dict, text=None, negative_text=None) -> SD35State:
+        """``text`` / ``negative_text``: optional (context [L, joint_dim], pooled [pooled_dim])
+        from the text encoders; seeded synthetic embeddings otherwise."""
         spec = spec if isinstance(spec, SD35Spec) else SD35Spec.normalize(spec)
         h, w = spec.height // self.cfg.vae_scale, spec.width // self.cfg.vae_scale
         g = torch.Generator(device="cpu").manual_seed(int(spec.seed))
@@ -94,10 +96,11 @@ class SD35Engine:
         mu = mu_for_seq_len((h // self.cfg.patch) * (w // self.cfg.patch)) if spec.dynamic_shift else None
         grid = flow_shift_sigmas(spec.steps, self.cfg.shift, mu)
         sched = make_scheduler(spec.solver, spec.steps, sigmas=grid, flow_shift=self.cfg.shift)
-        ctx, pool = synthetic_embeddings(spec.seed, spec.text_len, self.cfg.joint_dim, self.cfg.pooled_dim, 0)
+        ctx, pool = text or synthetic_embeddings(spec.seed, spec.text_len, self.cfg.joint_dim, self.cfg.pooled_dim, 0)
         nctx = npool = None
         if spec.guidance > 1.0:
-            nctx, npool = synthetic_embeddings(spec.seed, spec.text_len, self.cfg.joint_dim, self.cfg.pooled_dim, 1)
+            nctx, npool = negative_text or synthetic_embeddings(spec.seed, spec.text_len, self.cfg.joint_dim,
+                                                                self.cfg.pooled_dim, 1)
             nctx, npool = nctx.to(self.device, self.dtype), npool.to(self.device, self.dtype)
         return SD35State(spec=spec, latents=lat, scheduler=sched, context=ctx.to(self.device, self.dtype),
                          pooled=pool.to(self.device, self.dtype), neg_context=nctx, neg_pooled=npool)

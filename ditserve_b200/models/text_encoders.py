@@ -94,14 +94,22 @@ class UMT5TextEncoder:
 class SD3TextEncoders:
     """CLIP-L + CLIP-G + T5-XXL: ``encode(prompt) -> (context [77 + t5_len, 4096], pooled [2048])``."""
 
-    def __init__(self, tiny: bool = False, device="cpu", dtype=torch.float32, seed: int = 0, t5_len: int = 256):
+    def __init__(self, tiny: bool = False, device="cpu", dtype=torch.float32, seed: int = 0, t5_len: int = 256,
+                 tiny_dims: tuple[int, int, int] | None = None):
+        """``tiny_dims`` = (CLIP-L width, CLIP-G width, T5 width) of a test-sized set."""
         from transformers import CLIPTextConfig, CLIPTextModelWithProjection
         lcfg, gcfg = (TINY_CLIP_L, TINY_CLIP_G) if tiny else (CLIP_L, CLIP_G)
+        t5cfg = TINY_T5 if tiny else T5_XXL
+        if tiny and tiny_dims is not None:
+            wl, wg, wt = tiny_dims
+            lcfg = dict(lcfg, hidden_size=wl, intermediate_size=2 * wl, projection_dim=wl)
+            gcfg = dict(gcfg, hidden_size=wg, intermediate_size=2 * wg, projection_dim=wg)
+            t5cfg = dict(t5cfg, d_model=wt, d_kv=wt // t5cfg["num_heads"], d_ff=2 * wt)
         self.clip_l = _init(CLIPTextModelWithProjection(CLIPTextConfig(**lcfg, eos_token_id=lcfg["vocab_size"] - 1)),
                             seed, device, dtype)
         self.clip_g = _init(CLIPTextModelWithProjection(CLIPTextConfig(**gcfg, eos_token_id=gcfg["vocab_size"] - 1)),
                             seed + 1, device, dtype)
-        self.t5 = UMT5TextEncoder(TINY_T5 if tiny else T5_XXL, device, dtype, seed + 2, t5=True)
+        self.t5 = UMT5TextEncoder(t5cfg, device, dtype, seed + 2, t5=True)
         self.clip_tok = HashTokenizer(lcfg["vocab_size"], bos=lcfg["vocab_size"] - 2)
         self.t5_len, self.device = t5_len, device
         self.joint_dim = self.t5.dim

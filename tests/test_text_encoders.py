@@ -65,3 +65,18 @@ def test_wan_backend_encodes_prompts_with_umt5(tmp_path):
         w.advance(dict(id=2, state_id=sid, steps=2))
         outs[sid] = w.finish(dict(id=3, state_id=sid, output_mode="digest"))["value"]
     assert outs["a"] == outs["b"] and outs["a"] != outs["c"]
+
+
+def test_sd35_backend_encodes_prompts_with_clip_and_t5():
+    from ditserve_b200.models.sd35.backend import SD35Backend
+    b = SD35Backend({"model": "sd3.5-tiny", "device": "cpu", "text_encoder": {"config": "tiny", "seed": 2}})
+    spec = dict(height=64, width=64, steps=2, seed=1, guidance=3.0, text_len=90, negative_prompt="low quality")
+    outs = {}
+    for sid, prompt in (("a", "a teapot"), ("b", "a teapot"), ("c", "a castle")):
+        b.prepare(dict(id=1, spec=dict(spec, request_id=sid, prompt=prompt)))
+        st = b.states[sid]
+        assert st.context.shape == (90, 256) and st.pooled.shape == (128,)
+        while not st.done:
+            b.engine.advance_batch([st])
+        outs[sid] = st.latents.clone()
+    assert torch.equal(outs["a"], outs["b"]) and not torch.equal(outs["a"], outs["c"])

@@ -52,6 +52,7 @@ struct PolicyTraits {
   // late; images take GPUs that the highest-laxity suspended video holds
   bool feasibility_guards = false;
   bool idle_widening = false;     // widen below the efficiency threshold onto GPUs nobody else needs
+  bool late_image_batching = false;  // late images share continuous batches though on-time ones run alone
 };
 
 const PolicyTraits& policy_traits(const std::string& name);  // throws std::invalid_argument

@@ -50,6 +50,7 @@ struct Settings {
   double quantum_ms = 0.0;          // >0: block quanta sized to this much GPU time
   bool lazy_preemption = true;      // an image that can wait for a mid-step video's boundary does
   std::string feasibility_degree;   // "free" | "widest": the degree the lateness test assumes
+  bool late_image_batching = false; // late images go to continuous batches even without the trait
 };
 
 Settings resolve(const PolicyTraits& t, const Json& o) {
@@ -101,6 +102,7 @@ Settings resolve(const PolicyTraits& t, const Json& o) {
   s.quantum_ms = o.num("quantum_ms", 0.0);
   if (!(s.quantum_ms >= 0)) throw std::invalid_argument("quantum_ms must be >= 0");
   s.lazy_preemption = o.flag("lazy_preemption", true);
+  s.late_image_batching = o.flag("late_image_batching", t.late_image_batching);
   // elastic policies judge lateness on the widest group free when the plan starts (a request
   // that only an idle node could save would otherwise keep its rank, run narrow and miss);
   // static policies on their widest degree
@@ -694,15 +696,19 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     a["form"] = "sp1";
     a["resize"] = false;
     // continuous batching: same-class waiting images join while every member keeps its deadline
-    const bool cb = s.continuous_batch > 1 && cost.klass(r.klass).contains("batch_step_ms");
+    // late_image_batching: an image that can no longer make its deadline is packed into a
+    // continuous batch (fewer GPUs for work that is late anyway) even when the policy runs
+    // on-time images atomically
+    const bool late_cb = s.late_image_batching && !r.feasible && s.continuous_batch <= 1;
+    const bool cb = (s.continuous_batch > 1 || late_cb) && cost.klass(r.klass).contains("batch_step_ms");
     const bool ab = !cb && s.image_batch > 1 && cost.klass(r.klass).contains("batch_ms") && g.count() <= 1;
     if (cb || ab) {
       std::vector<const Req*> members{&r};
       auto joins = [&](const Req* other) {
         return other != &r && !placed.count(other->id) && (s.t.sequence_packing || other->klass == r.klass) &&
-               (other->affinity < 0 || other->affinity == gpu);
+               (other->affinity < 0 || other->affinity == gpu) && (!late_cb || !other->feasible);
       };
-      int cap = cb ? s.continuous_batch : s.image_batch;
+      int cap = cb ? (late_cb ? 8 : s.continuous_batch) : s.image_batch;
       if (cb) {
         // work-conserving: while GPUs that no waiting video needs are idle, the waiting images
         // spread over them (fewer members per GPU, shorter rounds) instead of queueing on one

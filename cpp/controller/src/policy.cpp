@@ -50,9 +50,10 @@ std::map<std::string, PolicyTraits> build_table() {
                   "ditserve tuned on the measured B200 profile: load-adaptive forms (when the denoising videos "
                   "could fill every CFG pair, each video takes its most GPU-efficient form and feasibility is "
                   "judged on it; otherwise feasible-minimal forms with widening) and atomic images instead of "
-                  "continuous image batches");
+                  "continuous image batches (images that are already late share continuous batches)");
     t.load_adaptive = true;
     t.continuous_batch = false;
+    t.late_image_batching = true;
     put(t);
   }
   {
@@ -330,6 +331,7 @@ Json describe_policy(const PolicyTraits& t) {
   j["bubble_free"] = t.bubble_free;
   j["feasibility_guards"] = t.feasibility_guards;
   j["idle_widening"] = t.idle_widening;
+  j["late_image_batching"] = t.late_image_batching;
   return j;
 }
 

@@ -741,3 +741,20 @@ TEST("quantum_ms sizes block quanta by GPU time and never crosses the step bound
   auto r = cluster_plan(state(2, {req("v", "video", "vid", 0, 1e9)}), "ditserve", c, o);
   CHECK(find(r, "v")->at("quantum").as_int() == 30);
 }
+
+TEST("late images share continuous batches under ditserve-b200; on-time images run alone") {
+  ClusterCost c(profile());
+  // img: 28 steps x 12 ms + 50 ms decode = 386 ms alone
+  std::vector<Json> late = {req("l0", "image", "img", 0, 100), req("l1", "image", "img", 0, 100),
+                            req("l2", "image", "img", 0, 100)};
+  auto p = cluster_plan(state(1, late), "ditserve-b200", c);
+  CHECK(p.at("assignments").size() == 1 && p.at("assignments")[0].at("quantum").as_string() == "continuous_batch");
+  CHECK(p.at("assignments")[0].at("batch").size() == 3);
+  std::vector<Json> fine = {req("f0", "image", "img", 0, 5000), req("f1", "image", "img", 0, 5000)};
+  auto q = cluster_plan(state(1, fine), "ditserve-b200", c);
+  CHECK(q.at("assignments").size() == 1 && q.at("assignments")[0].at("quantum").as_string() == "atomic");
+  Json off = Json::object();
+  off["late_image_batching"] = false;
+  auto r = cluster_plan(state(1, late), "ditserve-b200", c, off);
+  CHECK(r.at("assignments")[0].at("quantum").as_string() == "atomic");
+}

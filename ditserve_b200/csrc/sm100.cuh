@@ -2,7 +2,7 @@
 //
 // Everything here is hand-written inline PTX for Blackwell (compute_100a):
 //   * mbarrier init / arrive / expect-tx / bounded parity waits,
-//   * TMA 2D tile loads (cp.async.bulk.tensor, never with .multicast::cluster),
+//   * TMA 2D tile loads (cp.async.bulk.tensor, never with cluster multicast),
 //   * tcgen05 TMEM allocation, MMA issue (kind::f16, cta_group::1), commit,
 //     TMEM loads/stores and the tcgen05 ordering fences,
 //   * UMMA shared-memory and instruction descriptors.

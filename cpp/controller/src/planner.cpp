@@ -352,6 +352,13 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
       if (cost.step_ms(klass, f) * f.degree() < cost.step_ms(klass, *eff) * eff->degree()) eff = &f;
     return std::vector<Form>{*eff};
   };
+  // the candidate forms of a class depend only on the class within one plan
+  std::map<std::string, std::vector<Form>> forms_cache;
+  auto class_forms = [&](const std::string& klass) -> const std::vector<Form>& {
+    auto it = forms_cache.find(klass);
+    if (it == forms_cache.end()) it = forms_cache.emplace(klass, forms_for(s, cost, klass, video_capacity)).first;
+    return it->second;
+  };
   for (const auto& rj : state.at("requests").as_array()) {
     Req r;
     r.j = &rj;
@@ -380,7 +387,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     // actually get when the load-adaptive choice is in throughput mode)
     if (r.video()) {
       double best = kInf;
-      const auto forms = efficient_only(forms_for(s, cost, r.klass, video_capacity), r.klass);
+      const auto forms = efficient_only(class_forms(r.klass), r.klass);
       int limit = video_capacity;
       if (s.feasibility_degree == "free" && !forms.empty()) limit = std::max(widest_free, forms.front().degree());
       for (const auto& f : forms)
@@ -521,13 +528,13 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     auto it = min_degree_cache.find(o.id);
     if (it != min_degree_cache.end()) return it->second;
     int d = 0;
-    for (const auto& f : efficient_only(forms_for(s, cost, o.klass, video_capacity), o.klass))
+    for (const auto& f : efficient_only(class_forms(o.klass), o.klass))
       if (now + cost.remaining_ms(*o.j, f) <= o.deadline) {
         d = f.degree();
         break;
       }
     if (d == 0 && o.sunk) {
-      auto forms = forms_for(s, cost, o.klass, video_capacity);
+      auto forms = class_forms(o.klass);
       if (!forms.empty()) d = forms.back().degree();
     }
     return min_degree_cache[o.id] = d;
@@ -572,7 +579,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
       if (!movable_after(self, o, after)) continue;
       int d = min_feasible_degree(o);
       if (d == 0) {
-        auto forms = efficient_only(forms_for(s, cost, o.klass, video_capacity), o.klass);
+        auto forms = efficient_only(class_forms(o.klass), o.klass);
         d = forms.empty() ? 0 : forms.front().degree();
       }
       need += d;
@@ -606,7 +613,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     std::vector<Item> items;
     for (const Req* r : videos) {
       if (r->finished_denoise()) continue;
-      for (const auto& f : forms_for(s, cost, r->klass, video_capacity)) {
+      for (const auto& f : class_forms(r->klass)) {
         if (now + cost.remaining_ms(*r->j, f) <= r->deadline) {
           // unit value per request kept on track; v1 weighs urgency (small laxity first)
           double value = 1.0;
@@ -637,7 +644,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
   }
 
   auto fastest_fit = [&](const Req& r, std::vector<int>& grp_out, const std::vector<Form>* only = nullptr) -> Form {
-    auto forms = only ? *only : forms_for(s, cost, r.klass, video_capacity);
+    auto forms = only ? *only : class_forms(r.klass);
     Form best{0, 0, 0};
     double best_ms = kInf;
     for (const auto& f : forms) {
@@ -787,7 +794,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     // load-adaptive form choice: when the videos in the system could fill every CFG pair,
     // throughput decides and each video takes the form with the least GPU time per step;
     // otherwise the usual feasible-minimal choice (and widening) keeps latency low
-    const std::vector<Form> forms = efficient_only(forms_for(s, cost, r.klass, video_capacity), r.klass);
+    const std::vector<Form> forms = efficient_only(class_forms(r.klass), r.klass);
     if (forms.empty()) continue;
     // CFG fission (approximate policies): a video whose next step runs folded (conditional
     // branch only, the guidance delta reused) continues on the conditional half of its CFG2
@@ -936,7 +943,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
       if (r->status == "suspended" && r->blocks_done > 0 && !r->group.empty()) continue;  // mid-step: own group only
       g.current = r->id;
       std::vector<int> grp;
-      auto forms = forms_for(s, cost, r->klass, video_capacity);
+      auto forms = class_forms(r->klass);
       for (auto it = forms.rbegin(); it != forms.rend(); ++it) {
         grp = pick_group(g, it->degree(), r->group, true);
         if (!grp.empty()) {
@@ -959,7 +966,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
         const std::string why = a.at("reason").as_string();
         if (why == "mid-step" || why == "held" || why == "fixed" || why == "fission") continue;
         g.current = pv.id;
-        auto forms = forms_for(s, cost, pv.klass, video_capacity);
+        auto forms = class_forms(pv.klass);
         for (const auto& f : forms) {
           if (f.degree() <= pv.form.degree()) continue;
           give(pv.group);

@@ -23,12 +23,17 @@ into the proxy's staging directory (and removed remotely) and a ``block_import``
 local packet file is first pushed into the session directory, so the controller moves
 state between a local and a remote worker, or between two nodes, exactly as between two
 local workers.
+
+The daemon runs whatever worker a client asks for: bind it to a cluster-internal address and
+give it a shared secret (``--token`` or ``DITSERVE_BRIDGE_TOKEN``); a connection whose spawn
+frame carries another token is closed before anything starts.
 Reference: workers/ditserve/runtime/remote_bridge.py:1-1009.
 """
 from __future__ import annotations
 
 import argparse
 import base64
+import hmac
 import json
 import os
 import shutil
@@ -75,7 +80,8 @@ def _recv_exact(sock, n):
 class BridgeDaemon:
     """Accepts connections; each one gets its own local worker subprocess."""
 
-    def __init__(self, host: str = "127.0.0.1", port: int = 0, python: str = sys.executable, workdir: str | None = None):
+    def __init__(self, host: str = "127.0.0.1", port: int = 0, python: str = sys.executable, workdir: str | None = None,
+                 token: str | None = None):
         self.server = socket.create_server((host, port))
         self.port = self.server.getsockname()[1]
         self.python = python
@@ -83,6 +89,7 @@ class BridgeDaemon:
         os.makedirs(self.workdir, exist_ok=True)
         self.threads = []
         self._stop = threading.Event()
+        self.token = token if token is not None else os.environ.get("DITSERVE_BRIDGE_TOKEN")
 
     def serve_forever(self):
         self.server.settimeout(0.2)
@@ -114,6 +121,9 @@ class BridgeDaemon:
     def _session(self, conn: socket.socket):
         first = recv_frame(conn)
         if not first or first.get("bridge") != "spawn":
+            conn.close()
+            return
+        if self.token and not hmac.compare_digest(str(first.get("token", "")), self.token):
             conn.close()
             return
         sdir = os.path.realpath(tempfile.mkdtemp(prefix="session-", dir=self.workdir))
@@ -213,12 +223,15 @@ class BridgeProxy:
     """Stand-in worker: protocol lines on stdin/stdout, relayed to a remote daemon."""
 
     def __init__(self, address: str, backend: str, config: dict, env: dict | None = None,
-                 stage_dir: str | None = None):
+                 stage_dir: str | None = None, token: str | None = None):
         host, port = address.rsplit(":", 1)
         self.sock = socket.create_connection((host, int(port)))
         self.sock.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
-        send_frame(self.sock, {"bridge": "spawn", "backend": backend, "config": config, "env": env or {}})
+        token = token if token is not None else os.environ.get("DITSERVE_BRIDGE_TOKEN", "")
+        send_frame(self.sock, {"bridge": "spawn", "backend": backend, "config": config, "env": env or {},
+                               "token": token})
         shm = "/dev/shm" if os.path.isdir("/dev/shm") else None
+        self._own_stage = stage_dir is None
         self.stage_dir = stage_dir or tempfile.mkdtemp(prefix="ds-bridge-stage-", dir=shm)
         self.staged = 0
         self.watch: dict = {}   # local bell path -> (slot, last epoch)
@@ -362,7 +375,7 @@ class BridgeProxy:
     def close(self):
         self._stop.set()
         self.sock.close()
-        if not os.listdir(self.stage_dir):
+        if self._own_stage and not os.listdir(self.stage_dir):
             os.rmdir(self.stage_dir)
 
 
@@ -371,6 +384,7 @@ def main(argv=None):
     sub = ap.add_subparsers(dest="mode", required=True)
     d = sub.add_parser("daemon")
     d.add_argument("--listen", default="127.0.0.1:7700")
+    d.add_argument("--token", default=None, help="shared secret (default: DITSERVE_BRIDGE_TOKEN)")
     p = sub.add_parser("proxy")
     p.add_argument("--connect", default=os.environ.get("DITSERVE_REMOTE_ENDPOINT"),
                    help="daemon host:port (default: DITSERVE_REMOTE_ENDPOINT)")
@@ -382,7 +396,7 @@ def main(argv=None):
     args = ap.parse_args(argv)
     if args.mode == "daemon":
         host, port = args.listen.rsplit(":", 1)
-        daemon = BridgeDaemon(host, int(port))
+        daemon = BridgeDaemon(host, int(port), token=args.token)
         print(json.dumps({"listening": daemon.port}), flush=True)
         daemon.serve_forever()
         return 0

@@ -142,3 +142,19 @@ def test_diffusers_layout_round_trip(tmp_path):
     assert info["tensors"] == len(a.state_dict())
     for k, v in a.state_dict().items():
         assert torch.equal(v, b.state_dict()[k])
+
+
+def test_remote_bridge_refuses_a_wrong_token(tmp_path):
+    from ditserve_b200.runtime.remote_bridge import BridgeDaemon, BridgeProxy
+    daemon = BridgeDaemon("127.0.0.1", 0, workdir=str(tmp_path), token="s3cret")
+    threading.Thread(target=daemon.serve_forever, daemon=True).start()
+    try:
+        bad = BridgeProxy(f"127.0.0.1:{daemon.port}", "mock", {}, token="wrong", stage_dir=str(tmp_path))
+        with pytest.raises((ConnectionError, OSError)):
+            bad.relay(json.dumps(dict(version=1, id=1, op="hello")) + "\n")
+        bad.close()
+        good = BridgeProxy(f"127.0.0.1:{daemon.port}", "mock", {}, token="s3cret", stage_dir=str(tmp_path))
+        assert json.loads(good.relay(json.dumps(dict(version=1, id=1, op="hello")) + "\n"))["ok"]
+        good.close()
+    finally:
+        daemon.stop()

@@ -592,8 +592,14 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     for (const auto& r : reqs)
       if (r.video() && r.status == "suspended" && r.blocks_done == 0 && !r.group.empty() && !r.finished_denoise()) {
         const double lax = std::isfinite(r.deadline) ? r.deadline - now - r.best_remaining : 1e18;
-        for (int i : r.group)
-          if (i >= 0 && i < n) claim[i] = std::min(claim[i], lax);
+        // a fold-eligible CFG2 video under fission continues on the conditional half of its
+        // group: only that half is claimed, the companion half is the first choice for images
+        size_t held = r.group.size();
+        if (t.fission && r.j->flag("cfg_fold_eligible", false) && !r.form.empty() && parse_form(r.form).cfg == 2 &&
+            held % 2 == 0)
+          held /= 2;
+        for (size_t k = 0; k < held; ++k)
+          if (r.group[k] >= 0 && r.group[k] < n) claim[r.group[k]] = std::min(claim[r.group[k]], lax);
       }
   const std::vector<double>* claims = t.feasibility_guards ? &claim : nullptr;
 

@@ -758,3 +758,14 @@ TEST("late images share continuous batches under ditserve-b200; on-time images r
   auto r = cluster_plan(state(1, late), "ditserve-b200", c, off);
   CHECK(r.at("assignments")[0].at("quantum").as_string() == "atomic");
 }
+
+TEST("fission: an urgent image takes the companion GPU while the folded video keeps its primary") {
+  ClusterCost c(profile());
+  Json v = suspended("v", "[0,1]", "cfg2", 6, 0);
+  v["cfg_fold_eligible"] = true;
+  Json img = req("i", "image", "img", 0, 500);
+  auto p = cluster_plan(state(2, {v, img}), "ditserve-approx", c);
+  CHECK(find(p, "i") && find(p, "i")->at("group")[0].as_int() == 1);
+  CHECK(find(p, "v") && find(p, "v")->at("group")[0].as_int() == 0 && find(p, "v")->at("degree").as_int() == 1);
+  CHECK(find(p, "v")->at("reason").as_string() == "fission");
+}

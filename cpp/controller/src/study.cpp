@@ -747,6 +747,48 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
   int unknown_probes = 0;
   std::string abort_reason;
   Json probes = Json::array();
+  // one occupancy verdict over the phase's GPUs: the local probe for this node's slots, and
+  // each remote slot's bridge daemon for its GPU (the daemon excludes its own workers)
+  auto probe_occupancy = [&]() -> Json {
+    Json q = Json::object();
+    Json probe_gpus = Json::array();
+    for (int g = 0; g < gpus; ++g)
+      if (!remote.count(g)) probe_gpus.push_back(g);
+    q["gpus"] = probe_gpus;
+    q["own_pids"] = own_pids;
+    Json occ;
+    try {
+      occ = probe_gpus.empty() ? Json::object() : prober->call("occupancy", q, 60);
+      if (probe_gpus.empty()) occ["state"] = "idle";
+    } catch (const std::exception& e) {
+      occ = Json::object();
+      occ["state"] = "unknown";
+      occ["source"] = e.what();
+    }
+    for (int g : remote) {
+      const Json& rs = remote_slots.at(std::to_string(g));
+      Json rq = Json::object();
+      Json dev = Json::array();
+      dev.push_back(std::stoi(rs.str("device", std::to_string(g))));
+      rq["gpus"] = dev;
+      std::string st = "unknown";
+      Json r;
+      try {
+        r = vworkers[g]->call("bridge_occupancy", rq, 60);
+        st = r.str("state", "unknown");
+      } catch (const std::exception&) {
+      }
+      const std::string cur = occ.str("state", "unknown");
+      if (st == "busy") {
+        occ["state"] = "busy";
+        if (!occ.contains("foreign") || !occ.at("foreign").is_object()) occ["foreign"] = Json::object();
+        occ["foreign"]["remote-" + std::to_string(g)] = r.get("foreign");
+      } else if (st == "unknown" && cur != "busy") {
+        occ["state"] = "unknown";
+      }
+    }
+    return occ;
+  };
   // admission: with the guard on, the trace starts only once the phase's GPUs are idle
   double admission_wait_ms = 0;
   if (guard) {
@@ -754,17 +796,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     const double ta = monotonic_seconds();
     std::string last_state = "unknown";
     while (true) {
-      Json q = Json::object();
-      Json probe_gpus = Json::array();
-      for (int g = 0; g < gpus; ++g)
-        if (!remote.count(g)) probe_gpus.push_back(g);  // the local probe sees this node's GPUs only
-      q["gpus"] = probe_gpus;
-      q["own_pids"] = own_pids;
-      try {
-        last_state = prober->call("occupancy", q, 60).str("state", "unknown");
-      } catch (const std::exception&) {
-        last_state = "unknown";
-      }
+      last_state = probe_occupancy().str("state", "unknown");
       if (last_state == "idle" || monotonic_seconds() - ta > limit_s) break;
       std::this_thread::sleep_for(std::chrono::milliseconds(500));
     }
@@ -776,20 +808,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     if (now > horizon) break;
     if (guard && now >= next_probe) {
       next_probe = now + guard_interval_ms;
-      Json q = Json::object();
-      Json probe_gpus = Json::array();
-      for (int g = 0; g < gpus; ++g)
-        if (!remote.count(g)) probe_gpus.push_back(g);
-      q["gpus"] = probe_gpus;
-      q["own_pids"] = own_pids;
-      Json occ;
-      try {
-        occ = prober->call("occupancy", q, 60);
-      } catch (const std::exception& e) {
-        occ = Json::object();
-        occ["state"] = "unknown";
-        occ["source"] = e.what();
-      }
+      const Json occ = probe_occupancy();
       const std::string st = occ.str("state", "unknown");
       if (probes.size() < 256) {
         Json pr = Json::object();

@@ -16,7 +16,9 @@ NCCL_* / DITSERVE_* variables) and relays protocol lines both ways.  Extra frame
 * {"bridge": "put_file", "name", "offset", "data_b64", "last"} /
   {"bridge": "get_file", "path", "offset", "unlink"} — chunked file staging, confined to
   the session directory;
-* {"bridge": "occupancy"} — the remote node's GPU occupancy probe.
+* {"bridge": "occupancy", "gpus", "own_pids"} — the remote node's GPU occupancy probe (the
+  session's worker counts as ours); the proxy answers the protocol op ``bridge_occupancy``
+  with it, which is how the cluster executor's occupancy guard covers remote slots.
 Requests naming a doorbell get the path rewritten to the daemon-side mirror.  Continuation
 packets cross the bridge transparently: a ``block_export`` reply's packet file is fetched
 into the proxy's staging directory (and removed remotely) and a ``block_import`` of a
@@ -203,7 +205,8 @@ class BridgeDaemon:
                         reply({"bridge": "file", "path": msg.get("path"), "error": str(exc)})
                 elif kind == "occupancy":
                     from .occupancy import occupancy
-                    reply({"bridge": "occupancy", "result": occupancy(msg.get("gpus"))})
+                    own = [proc.pid] + [int(p) for p in msg.get("own_pids", [])]  # this session's worker is ours
+                    reply({"bridge": "occupancy", "result": occupancy(msg.get("gpus"), own_pids=own)})
         finally:
             try:
                 proc.stdin.close()
@@ -346,6 +349,12 @@ class BridgeProxy:
         pushed = None
         try:
             req = json.loads(line)
+            if isinstance(req, dict) and req.get("op") == "bridge_occupancy":
+                # answered by the daemon's node, not by the remote worker
+                res = self._call({"bridge": "occupancy", "gpus": req.get("gpus"),
+                                  "own_pids": req.get("own_pids", [])}, "occupancy")["result"]
+                return json.dumps({"version": req.get("version", 1), "id": req.get("id"), "ok": True,
+                                   "result": res}) + "\n"
             if isinstance(req, dict):
                 req = self._mirror(req)
                 if req.get("op") == "block_import" and isinstance(req.get("path"), str) \

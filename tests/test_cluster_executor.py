@@ -234,3 +234,38 @@ def test_remote_slot_through_bridge(controller, tmp_path, bridge_daemon):
         ref.advance(dict(id=2, state_id=f"ref{i}", steps=spec["steps"]))
         want = ref.finish(dict(id=3, state_id=f"ref{i}", output_mode="digest"))["value"]
         assert row["digest"] == want, row
+
+
+@pytest.mark.parametrize("foreign", [True, False])
+def test_occupancy_guard_covers_remote_slots(controller, tmp_path, foreign):
+    """A foreign process on a remote slot's GPU (reported by that node's daemon) aborts the phase;
+    an idle remote node lets it run."""
+    table = tmp_path / "occ.json"
+    table.write_text(json.dumps({"0": [{"pid": 999999, "used_mib": "100"}]} if foreign else {}))
+    env = dict(os.environ, PYTHONPATH=ROOT, DITSERVE_OCCUPANCY_TABLE=str(table))
+    d = subprocess.Popen([sys.executable, "-m", "ditserve_b200.runtime.remote_bridge", "daemon", "--listen",
+                          "127.0.0.1:0"], stdout=subprocess.PIPE, text=True, env=env, cwd=str(tmp_path))
+    try:
+        port = json.loads(d.stdout.readline())["listening"]
+        cfg = _guard_cfg(tmp_path)
+        ph = cfg["phases"][0]
+        ph["remote_slots"] = {"1": {"address": f"127.0.0.1:{port}", "device": "0"}}
+        ph["admission_wait_s"] = 1
+        path = tmp_path / "study.json"
+        path.write_text(json.dumps(cfg))
+        run_env = dict(os.environ, DITSERVE_PYTHON=sys.executable, DITSERVE_PACKAGE_ROOT=ROOT)
+        empty = tmp_path / "local.json"
+        empty.write_text("{}")
+        run_env["DITSERVE_OCCUPANCY_TABLE"] = str(empty)  # this node: idle
+        r = subprocess.run([controller, "--json", "run", "--config", str(path), "--run-id", "g", "--work-dir",
+                            str(tmp_path)], capture_output=True, text=True, env=run_env, timeout=600)
+        rep = json.loads(r.stdout)
+        last = rep["phases"]["cluster"]["cells"][-1]["result"]
+        if foreign:
+            assert "admission" in last.get("aborted", ""), {k: last.get(k) for k in ("aborted", "occupancy_probes")}
+            assert last["failures"]
+        else:
+            assert "aborted" not in last and last["summary"]["completed"] == 3
+    finally:
+        d.terminate()
+        d.wait(timeout=10)

@@ -105,3 +105,30 @@ def test_resume_refuses_changed_worker_sources(controller, tmp_path):
         f.write("\n# edited\n")
     changed = subprocess.run(cmd + ["--resume"], capture_output=True, text=True, env=env, timeout=300)
     assert changed.returncode != 0 and "refusing to resume" in (changed.stdout + changed.stderr)
+
+
+def test_operations_phase_on_a_remote_worker(controller, tmp_path):
+    """A worker definition with "remote": "host:port" runs behind the bridge proxy in any phase."""
+    env = dict(os.environ, PYTHONPATH=ROOT, DITSERVE_BRIDGE_TOKEN="t0k")
+    d = subprocess.Popen([sys.executable, "-m", "ditserve_b200.runtime.remote_bridge", "daemon", "--listen",
+                          "127.0.0.1:0"], stdout=subprocess.PIPE, text=True, env=env, cwd=str(tmp_path))
+    try:
+        port = json.loads(d.stdout.readline())["listening"]
+        cfg = {"schema": "ditserve-b200.study.v1", "experiment": "remote-ops",
+               "workers": {"model": {"backend": "mock", "remote": f"127.0.0.1:{port}"}},
+               "phases": [{"id": "ops", "kind": "operations", "operations": [
+                   {"op": "prepare", "spec": {"request_id": "a", "steps": 2, "seed": 1}},
+                   {"op": "advance", "state_id": "a", "steps": 2},
+                   {"op": "finish", "state_id": "a", "output_mode": "digest"}]}]}
+        cfgp = tmp_path / "s.json"
+        cfgp.write_text(json.dumps(cfg))
+        run_env = dict(os.environ, DITSERVE_PYTHON=sys.executable, DITSERVE_PACKAGE_ROOT=ROOT,
+                       DITSERVE_BRIDGE_TOKEN="t0k")
+        r = subprocess.run([controller, "--json", "run", "--config", str(cfgp), "--run-id", "r", "--work-dir",
+                            str(tmp_path / "w")], capture_output=True, text=True, env=run_env, timeout=300)
+        assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+        rows = json.loads(r.stdout)["phases"]["ops"]["cells"][-1]["result"]["operations"]
+        assert all(x["ok"] for x in rows) and rows[-1]["result"]["value"]
+    finally:
+        d.terminate()
+        d.wait(timeout=10)

@@ -359,6 +359,26 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     if (it == forms_cache.end()) it = forms_cache.emplace(klass, forms_for(s, cost, klass, video_capacity)).first;
     return it->second;
   };
+  // remaining time including the dispatch overhead of the quanta still to run: one per solver
+  // step (a step quantum stops early only on a doorbell), one per block quantum when the policy
+  // runs fixed block quanta, one per decode chunk; images one
+  auto remaining_q = [&](const Json& rj, const Form& f) {
+    const double ms = cost.remaining_ms(rj, f);
+    if (cost.overhead_ms() <= 0) return ms;
+    const std::string k = rj.at("class").as_string();
+    if (cost.kind(k) == "image") return ms + cost.overhead_ms();
+    const int total = static_cast<int>(rj.integer("steps_total", cost.steps(k)));
+    const int done = static_cast<int>(rj.integer("steps_done", 0));
+    const int steps_left = std::max(0, total - done);
+    long quanta = steps_left;
+    if (t.blocks && s.quantum_blocks > 0 && steps_left > 0) {
+      const int bps = cost.blocks_per_step(k), qb = s.quantum_blocks;
+      const int first = std::max(0, bps - static_cast<int>(rj.integer("blocks_done", 0)));
+      quanta = (first + qb - 1) / qb + static_cast<long>(steps_left - 1) * ((bps + qb - 1) / qb);
+    }
+    quanta += std::max(0, cost.decode_chunks(k) - static_cast<int>(rj.integer("decode_done", 0)));
+    return ms + cost.overhead_ms() * static_cast<double>(quanta);
+  };
   for (const auto& rj : state.at("requests").as_array()) {
     Req r;
     r.j = &rj;
@@ -391,13 +411,13 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
       int limit = video_capacity;
       if (s.feasibility_degree == "free" && !forms.empty()) limit = std::max(widest_free, forms.front().degree());
       for (const auto& f : forms)
-        if (f.degree() <= limit) best = std::min(best, cost.remaining_ms(rj, f));
+        if (f.degree() <= limit) best = std::min(best, remaining_q(rj, f));
       if (!std::isfinite(best))
-        for (const auto& f : forms) best = std::min(best, cost.remaining_ms(rj, f));
-      if (!std::isfinite(best)) best = cost.remaining_ms(rj, Form{});
+        for (const auto& f : forms) best = std::min(best, remaining_q(rj, f));
+      if (!std::isfinite(best)) best = remaining_q(rj, Form{});
       r.best_remaining = best;
     } else {
-      r.best_remaining = r.finished_denoise() ? cost.decode_ms(r.klass) : cost.remaining_ms(rj, Form{}) + cost.decode_ms(r.klass);
+      r.best_remaining = r.finished_denoise() ? cost.decode_ms(r.klass) : remaining_q(rj, Form{}) + cost.decode_ms(r.klass);
       if (!rj.contains("steps_done") && !(s.continuous_batch > 1)) r.best_remaining = cost.service_ms(r.klass);
     }
     r.feasible = now + r.best_remaining <= r.deadline;
@@ -529,7 +549,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     if (it != min_degree_cache.end()) return it->second;
     int d = 0;
     for (const auto& f : efficient_only(class_forms(o.klass), o.klass))
-      if (now + cost.remaining_ms(*o.j, f) <= o.deadline) {
+      if (now + remaining_q(*o.j, f) <= o.deadline) {
         d = f.degree();
         break;
       }
@@ -620,7 +640,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     for (const Req* r : videos) {
       if (r->finished_denoise()) continue;
       for (const auto& f : class_forms(r->klass)) {
-        if (now + cost.remaining_ms(*r->j, f) <= r->deadline) {
+        if (now + remaining_q(*r->j, f) <= r->deadline) {
           // unit value per request kept on track; v1 weighs urgency (small laxity first)
           double value = 1.0;
           if (t.knapsack) value += 1.0 / (1.0 + std::max(0.0, r->deadline - now) / 1000.0);
@@ -656,7 +676,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     for (const auto& f : forms) {
       auto grp = pick_group(g, f.degree(), r.group, true);
       if (grp.empty()) continue;
-      const double ms = cost.remaining_ms(*r.j, f);
+      const double ms = remaining_q(*r.j, f);
       if (ms < best_ms) {
         best_ms = ms;
         best = f;
@@ -855,7 +875,7 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
     const int d_min = forms.front().degree();
     bool guarded = false, migration_held = false;
     for (const auto& f : forms) {
-      const double rem = cost.remaining_ms(*r.j, f);
+      const double rem = remaining_q(*r.j, f);
       if (now + rem * (1.0 + s.feasible_margin) > r.deadline) continue;
       auto cand = pick_group(g, f.degree(), r.group, true);
       if (cand.empty()) continue;

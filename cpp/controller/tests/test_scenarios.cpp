@@ -769,3 +769,21 @@ TEST("fission: an urgent image takes the companion GPU while the folded video ke
   CHECK(find(p, "v") && find(p, "v")->at("group")[0].as_int() == 0 && find(p, "v")->at("degree").as_int() == 1);
   CHECK(find(p, "v")->at("reason").as_string() == "fission");
 }
+
+TEST("feasibility counts the dispatch overhead of the quanta still to run") {
+  Json pr = profile();
+  pr["quantum_overhead_ms"] = 10;
+  ClusterCost c(pr);  // cfg2: 10 steps x 400 ms + 100 ms decode = 4100 ms, 11 quanta
+  Json v = req("v", "video", "vid", 0, 4150);
+  auto feasible = [&](const Json& o) {
+    PlanTrace tr;
+    cluster_plan(state(2, {v}), "ditserve", c, o, &tr);
+    return tr.rows[0].at("feasible").as_bool();
+  };
+  CHECK(!feasible(Json::object()));          // 4100 + 11 x 10 > 4150
+  v["deadline_ms"] = 4250;
+  CHECK(feasible(Json::object()));           // 4210 <= 4250
+  Json blocks = Json::object();
+  blocks["quantum_blocks"] = 4;              // 8 block quanta per step: 81 quanta, 4910 ms
+  CHECK(!feasible(blocks));
+}

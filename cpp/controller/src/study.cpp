@@ -416,7 +416,7 @@ std::vector<Json> fan_out(const std::vector<int>& gs, const std::function<Json(i
 Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& run_dir, const Json& workers_def) {
   const int gpus = static_cast<int>(phase.integer("gpus", 8));
   const std::string policy = phase.str("policy", "ditserve");
-  const Json options = phase.get("options").is_null() ? Json::object() : phase.at("options");
+  Json options = phase.get("options").is_null() ? Json::object() : phase.at("options");
   const ClusterCost cost(phase.get("profile").is_null() ? synthetic_profile() : phase.at("profile"));
   std::string vname = phase.str("worker", "model"), iname = vname;
   if (phase.contains("workers")) {
@@ -443,8 +443,44 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     if (!v.is_object() || !v.contains("address")) throw std::invalid_argument("remote slot " + k + " needs an address");
     remote.insert(g);
   }
-  if (!remote.empty() && distributed)
-    throw std::invalid_argument("remote_slots need distributed: false (the export transport crosses nodes)");
+  // nodes: this node's slots and each remote address's slots.  With `distributed: true` every
+  // node forms its own torch.distributed world (peer memory and NVLink stay inside a node): the
+  // nodes' slot blocks must be aligned power-of-two blocks, this node's first, and the planner's
+  // degrees are capped at the smallest block so that no group crosses a node
+  std::vector<int> node_base(gpus, 0), node_size(gpus, gpus);
+  std::vector<std::string> node_key(gpus);
+  std::map<std::string, std::vector<int>> nodes;
+  for (int g = 0; g < gpus; ++g) {
+    node_key[g] = remote.count(g) ? remote_slots.at(std::to_string(g)).at("address").as_string() : std::string();
+    nodes[node_key[g]].push_back(g);
+  }
+  if (distributed && nodes.size() > 1) {
+    int smallest = gpus;
+    for (const auto& [key, slots] : nodes) {
+      const int b = slots.front(), k = static_cast<int>(slots.size());
+      const bool contiguous = slots.back() - b + 1 == k;
+      if (!contiguous || (k & (k - 1)) != 0 || b % k != 0)
+        throw std::invalid_argument("with distributed: true each node's slots must form an aligned power-of-two block");
+      if (key.empty() && b != 0) throw std::invalid_argument("this node's slots must come first");
+      for (int g : slots) {
+        node_base[g] = b;
+        node_size[g] = k;
+      }
+      smallest = std::min(smallest, k);
+    }
+    if (transport != "collective" && transport != "export") throw std::invalid_argument("bad sp_transport");
+    if (!options.contains("degrees")) {
+      Json deg = Json::array();
+      for (int d = 1; d <= smallest; d *= 2) deg.push_back(d);
+      options["degrees"] = deg;
+    }
+  }
+  auto lr = [&](int g) { return g - node_base[g]; };  // rank inside its node's world
+  auto lranks = [&](const std::vector<int>& v) {
+    Json a = Json::array();
+    for (int g : v) a.push_back(lr(g));
+    return a;
+  };
   const std::string path = phase.str("collectives", "fused");
   const int batch_quantum = static_cast<int>(phase.integer("batch_quantum_steps", 4));
   // decode: finished videos run the VAE in chunked quanta (decode_start / decode_poll) and
@@ -461,8 +497,17 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
       const Json& rs = remote_slots.at(std::to_string(gidx));
       d["remote"] = rs.at("address");
       Json env = Json::object();
-      if (gpu) env["CUDA_VISIBLE_DEVICES"] = rs.str("device", std::to_string(gidx));
-      else env["CUDA_VISIBLE_DEVICES"] = "";
+      if (gpu && world_member) {  // the node's world: every device of the node visible, ours by index
+        std::string all;
+        for (int h : nodes[node_key[gidx]])
+          all += (all.empty() ? "" : ",") + remote_slots.at(std::to_string(h)).str("device", std::to_string(h));
+        env["CUDA_VISIBLE_DEVICES"] = all;
+        Json c = d.get("config").is_null() ? Json::object() : d.at("config");
+        if (!c.contains("device")) c["device"] = "cuda:" + std::to_string(lr(gidx));
+        d["config"] = c;
+      } else {
+        env["CUDA_VISIBLE_DEVICES"] = gpu ? rs.str("device", std::to_string(gidx)) : "";
+      }
       d["remote_env"] = env;
       return spawn_worker(d, opt, run_dir + "/" + tag + std::to_string(gidx) + ".log", "");
     }
@@ -536,15 +581,18 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
     return res;
   };
   if (distributed) {
-    const std::string init = "tcp://127.0.0.1:" + std::to_string(phase.integer("dist_port", 29700));
+    // one world per node, each rendezvousing on its own node's loopback
+    std::map<std::string, int> node_port;
+    int next_port = static_cast<int>(phase.integer("dist_port", 29700));
+    for (const auto& kv : nodes) node_port[kv.first] = next_port++;
     std::vector<int> all;
     for (int g = 0; g < gpus; ++g) all.push_back(g);
     fan_out(all, [&](int g) {
       Json r = Json::object();
       r["action"] = "init";
-      r["init_method"] = init;
-      r["rank"] = g;
-      r["world_size"] = gpus;
+      r["init_method"] = "tcp://127.0.0.1:" + std::to_string(node_port[node_key[g]]);
+      r["rank"] = lr(g);
+      r["world_size"] = node_size[g];
       r["timeout_s"] = phase.num("dist_timeout_s", 120.0);
       return vworkers[g]->call("distributed", r, 300);
     });
@@ -575,7 +623,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
         fan_out(grp, [&](int g) {
           Json r = Json::object();
           r["action"] = "layout";
-          r["ranks"] = ints_json(grp);
+          r["ranks"] = lranks(grp);
           r["form"] = form_name(f);
           r["spec"] = spec;
           r["path"] = path;
@@ -709,8 +757,8 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
       fan_out(p.exec, [&](int g) {
         Json r = Json::object();
         r["action"] = "migrate_group";
-        r["ranks"] = ints_json(p.exec);
-        r["src"] = src;
+        r["ranks"] = lranks(p.exec);
+        r["src"] = lr(src);
         r["state_id"] = p.id;
         r["path"] = path;
         return call(g, false, "distributed", r);
@@ -1159,7 +1207,7 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
                              adv["doorbell"] = bell;
                              if (distributed) {
                                Json lay = Json::object();
-                               lay["ranks"] = ints_json(grp);
+                               lay["ranks"] = lranks(grp);
                                lay["form"] = form;
                                lay["path"] = path;
                                adv["layout"] = lay;

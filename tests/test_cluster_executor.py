@@ -269,3 +269,31 @@ def test_occupancy_guard_covers_remote_slots(controller, tmp_path, foreign):
     finally:
         d.terminate()
         d.wait(timeout=10)
+
+
+def test_two_node_worlds_through_the_bridge(controller, tmp_path, bridge_daemon):
+    """Slots 0-1 on this node and 2-3 behind a bridge daemon ("another node") each form their own
+    Gloo world of Wan-tiny workers; groups never cross nodes (degrees capped at the node size) and
+    every request completes."""
+    cfg = {"schema": "ditserve-b200.study.v1", "experiment": "exec-two-node",
+           "workers": {"wan": {"backend": "wan", "config": {"model": "wan-tiny", "device": "cpu",
+                                                            "transfer_dir": str(tmp_path)}}},
+           "budget": BUDGET,
+           "phases": [{"id": "cluster", "kind": "cluster", "gpus": 4, "policy": "ditserve", "worker": "wan",
+                       "distributed": True, "sp_transport": "collective", "collectives": "nccl",
+                       "remote_slots": {"2": {"address": bridge_daemon, "device": "0"},
+                                        "3": {"address": bridge_daemon, "device": "1"}},
+                       "dist_port": 27000 + os.getpid() % 1000,
+                       "generator": {"count": 4, "seed": 6, "pattern": "offline_all", "classes": [
+                           {"weight": 1, "kind": "video", "class": "wan21_480p", "service_ms": 20000,
+                            "slo_scale": 5, "spec": {"height": 64, "width": 64, "frames": 5, "steps": 2,
+                                                     "guidance": 5.0}}]},
+                       "gates": [{"pointer": "/last/summary/completed", "op": "==", "value": 4}]}]}
+    rep, _ = _run(controller, cfg, tmp_path, allow_gpu=True)
+    assert rep["phases"]["cluster"]["gates"]["pass"], rep["phases"]["cluster"]
+    last = _last(rep)
+    assert not last["failures"], last["failures"]
+    groups = [tuple(t.get("group") or []) for t in last["trace"]]
+    assert all(set(g) <= {0, 1} or set(g) <= {2, 3} for g in groups), groups
+    assert any(set(g) == {2, 3} for g in groups), groups       # the remote node ran a 2-rank group
+    assert all(r.get("digest") for r in last["rows"])  # CFG2 groups: equal up to the drift gate, not bitwise

@@ -394,6 +394,7 @@ def main(argv=None):
     d = sub.add_parser("daemon")
     d.add_argument("--listen", default="127.0.0.1:7700")
     d.add_argument("--token", default=None, help="shared secret (default: DITSERVE_BRIDGE_TOKEN)")
+    d.add_argument("--workdir", default=None, help="root of the per-session directories (default: a temp dir)")
     p = sub.add_parser("proxy")
     p.add_argument("--connect", default=os.environ.get("DITSERVE_REMOTE_ENDPOINT"),
                    help="daemon host:port (default: DITSERVE_REMOTE_ENDPOINT)")
@@ -402,17 +403,18 @@ def main(argv=None):
     p.add_argument("--env", action="append", default=[], metavar="KEY=VALUE",
                    help="environment of the remote worker (CUDA_VISIBLE_DEVICES, NCCL_*, DITSERVE_*)")
     p.add_argument("--stage-dir", default=None, help="local directory for packets fetched from the node")
+    p.add_argument("--token", default=None, help="shared secret (default: DITSERVE_BRIDGE_TOKEN)")
     args = ap.parse_args(argv)
     if args.mode == "daemon":
         host, port = args.listen.rsplit(":", 1)
-        daemon = BridgeDaemon(host, int(port), token=args.token)
+        daemon = BridgeDaemon(host, int(port), workdir=args.workdir, token=args.token)
         print(json.dumps({"listening": daemon.port}), flush=True)
         daemon.serve_forever()
         return 0
     if not args.connect:
         ap.error("proxy needs --connect or DITSERVE_REMOTE_ENDPOINT")
     env = dict(kv.split("=", 1) for kv in args.env)
-    proxy = BridgeProxy(args.connect, args.backend, json.loads(args.config), env, args.stage_dir)
+    proxy = BridgeProxy(args.connect, args.backend, json.loads(args.config), env, args.stage_dir, args.token)
     out = sys.stdout
     for line in sys.stdin:
         if not line.strip():

@@ -103,24 +103,51 @@ def reference_arm(args):
     """Run the unmodified reference through its own public API, or say why it cannot run.
 
     The reference's Wan entry point is ``ditserve.models.wan.runtime.WanStepWorker``
-    (installed from the reference tree into baseline/_ref).  Its constructor
-    checks pinned package versions and imports diffusers before touching the GPU.
+    (installed from the reference tree into baseline/_ref).  The probe walks the
+    path a user of the reference takes, in order, and reports the first step that
+    fails with the exception text verbatim: the install is present, ``import
+    ditserve`` works, the worker module imports, and the worker constructs on this
+    rank's GPU.  When the constructor fails, the packages it pins are then looked up
+    (installed version or "not installed") and listed after the failure as facts of
+    this box, not as the cause.
     """
+    import importlib
+    import importlib.metadata as md
+
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    def unavailable(reason: str) -> int:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": reason}))
+        return 0
+
     ref = os.path.join(ROOT, "baseline", "_ref")
-    if os.path.isdir(ref):
-        sys.path.insert(0, ref)
+    if not os.path.isdir(os.path.join(ref, "ditserve")):
+        return unavailable(f"the reference is not installed on this box: {ref}/ditserve does not exist")
+    sys.path.insert(0, ref)
     try:
-        from ditserve.models.wan.runtime import WanStepWorker
-        local = int(os.environ.get("LOCAL_RANK", "0"))
-        WanStepWorker(device=f"cuda:{local}", attention="flash")
-        reason = "reference worker constructed but no offline Wan snapshot exists for it to serve"
+        importlib.import_module("ditserve")
     except Exception as exc:
-        reason = (f"reference WanStepWorker refused to start: {type(exc).__name__}: {exc} "
-                  "(it pins torch 2.10.0+cu126, diffusers 0.36.0 and cache-dit 1.5.0; diffusers and "
-                  "cache-dit are not installed and not in the offline wheelhouse)")
-    if int(os.environ.get("RANK", "0")) == 0:
-        print(json.dumps({"impl": "reference", "unavailable": reason}))
-    return 0
+        return unavailable(f"import ditserve (from {ref}) failed: {type(exc).__name__}: {exc}")
+    try:
+        runtime = importlib.import_module("ditserve.models.wan.runtime")
+    except Exception as exc:
+        return unavailable(f"import ditserve.models.wan.runtime failed: {type(exc).__name__}: {exc}")
+    try:
+        runtime.WanStepWorker(device=f"cuda:{local}", attention="flash")
+    except Exception as exc:
+        facts = []
+        for pkg, want in getattr(runtime, "REQUIRED_VERSIONS", {}).items():
+            try:
+                have = md.version(pkg)
+            except md.PackageNotFoundError:
+                have = "not installed"
+            facts.append(f"{pkg}: pinned {want}, here {have}")
+        tail = f" [{'; '.join(facts)}]" if facts else ""
+        return unavailable(f"WanStepWorker(device='cuda:{local}', attention='flash') raised "
+                           f"{type(exc).__name__}: {exc}{tail}")
+    return unavailable("WanStepWorker constructed, but bench.py has no offline Wan snapshot for it to serve")
 
 
 def main():
@@ -146,16 +173,22 @@ def main():
     form = default_form(world)
     pctx, cfg_plan = LocalAttention(), CFGLocal()
     layout = FixedLayout(tuple(range(world)), form)
+    nccl_plans = None
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
         from ditserve_b200.parallel.runtime import build_parallel
-        pctx, cfg_plan = build_parallel(layout, rank, dev, attention=args.attention,
-                                        seq_local=WAN21_T2V_1_3B.tokens((16, 21, 60, 104)) // form.sp,
-                                        cfg=WAN21_T2V_1_3B, pred_numel=16 * 21 * 60 * 104)
+        kw = dict(seq_local=WAN21_T2V_1_3B.tokens((16, 21, 60, 104)) // form.sp, cfg=WAN21_T2V_1_3B,
+                  pred_numel=16 * 21 * 60 * 104)
+        pctx, cfg_plan = build_parallel(layout, rank, dev, attention=args.attention, **kw)
+        if args.attention == "fused":
+            nccl_plans = build_parallel(layout, rank, dev, attention="nccl", **kw)
 
     engine = WanEngine(WAN21_T2V_1_3B, device=dev, pctx=pctx, cfg_plan=cfg_plan, seed=0)
     spec = WanSpec(model=WAN21_T2V_1_3B.name, height=480, width=832, frames=81, steps=50, guidance=5.0, seed=42)
+
+    def set_plans(plans):
+        engine.pctx, engine.cfg_plan = plans
 
     def barrier():
         if world > 1:
@@ -169,6 +202,24 @@ def main():
         return float(t.item())
 
     st = engine.prepare(spec)
+    check = None
+    if nccl_plans is not None:
+        # Untimed check before warm-up: one step of the same state through the NCCL path and
+        # through the fused peer-memory path; the latents must agree bit for bit on every rank.
+        snap = engine.snapshot(st, device=dev)
+        fused_plans = (engine.pctx, engine.cfg_plan)
+        set_plans(nccl_plans)
+        st_n = engine.step(engine.restore(snap))
+        set_plans(fused_plans)
+        st_f = engine.step(engine.restore(snap))
+        torch.cuda.synchronize()
+        a, b = st_n.latents.double().flatten(), st_f.latents.double().flatten()
+        flags = torch.tensor([1.0 if torch.equal(st_n.latents, st_f.latents) else 0.0,
+                              -((a - b).norm() / a.norm()).item()], device=dev, dtype=torch.float64)
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+        check = {"fused_equals_nccl": bool(flags[0].item() == 1.0), "max_rel_l2": float(-flags[1].item()),
+                 "compared": "latents after one step from the same state, all ranks"}
+        del st_n, st_f, snap
     for _ in range(args.warmup):
         engine.step(st)
     torch.cuda.synchronize()
@@ -194,6 +245,32 @@ def main():
     clk = clocks.stop()
     launches = sum(ops.launch_counts(reset=True).values())
     ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+    ops.check_status(dev)
+
+    # per-kernel device time of one more (untimed) step: CUDA events around every launch of
+    # this package's kernels on the launching stream, summed per entry point, max over ranks
+    breakdown = None
+    if not st.done:
+        with ops.KernelTimer() as kt:
+            b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b0.record()
+            engine.step(st)
+            b1.record()
+            totals = kt.totals_ms()
+        names = sorted(set(totals) | {"gemm", "attention", "attention_scatter", "qkv_scatter", "group_barrier",
+                                      "allgather_rows", "cfg_step_peer", "layernorm_modulate", "rmsnorm_rope",
+                                      "sched_step"})
+        vec = torch.tensor([totals.get(n, 0.0) for n in names] + [b0.elapsed_time(b1)], device=dev,
+                           dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(vec, op=dist.ReduceOp.MAX)
+        vals = vec.tolist()
+        step_ms = vals[-1]
+        per_kernel = {n: round(v, 3) for n, v in zip(names, vals[:-1]) if v > 0}
+        breakdown = {"step_ms": round(step_ms, 3), "kernels_ms": per_kernel,
+                     "outside_kernels_ms": round(step_ms - sum(vals[:-1]), 3),
+                     "how": "one untimed step with CUDA events around each launch (adds host work per launch); "
+                            "max over ranks per entry"}
     ops.check_status(dev)
 
     e2e = None
@@ -237,6 +314,10 @@ def main():
                        "l2": "no flush: per-step activations (0.2-1.2 GB) exceed the 126 MB L2"},
             "clocks": clk, "e2e": e2e, "gpu_launches": launches,
         }
+        if check is not None:
+            line.update(check)
+        if breakdown is not None:
+            line["breakdown"] = breakdown
         print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()

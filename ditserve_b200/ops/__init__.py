@@ -1,6 +1,6 @@
 """Hot DiT ops.  CUDA tensors run the hand-written sm_100a kernels of
 ``ditserve_b200._C``; CPU tensors run the fp32 PyTorch statement of the same op."""
-from ._ext import KernelTimeout, available, check_status, ext, kernel, launch_counts, status_word
+from ._ext import KernelTimeout, KernelTimer, available, check_status, ext, kernel, launch_counts, status_word
 from .attention import attention, attention_reference, attention_segments, segment_table, segments_reference
 from .gemm import linear, linear_reference
 from .norm import (layernorm_modulate, layernorm_modulate_reference, rms_norm_reference, rmsnorm_rope_,
@@ -8,7 +8,7 @@ from .norm import (layernorm_modulate, layernorm_modulate_reference, rms_norm_re
 from .sched import sched_step, sched_step_reference
 
 __all__ = [
-    "KernelTimeout", "available", "check_status", "ext", "kernel", "launch_counts", "status_word",
+    "KernelTimeout", "KernelTimer", "available", "check_status", "ext", "kernel", "launch_counts", "status_word",
     "attention", "attention_reference", "attention_segments", "segment_table", "segments_reference", "linear", "linear_reference",
     "layernorm_modulate", "layernorm_modulate_reference", "rms_norm_reference", "rmsnorm_rope_",
     "rope_reference", "sched_step", "sched_step_reference",

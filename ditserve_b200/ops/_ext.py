@@ -37,12 +37,56 @@ def ext():
 
 
 _launches: dict[str, int] = {}
+_timer: "KernelTimer | None" = None
+
+
+class KernelTimer:
+    """Device time per extension entry point, from CUDA events on the launching stream.
+
+    While active (``with KernelTimer() as kt:``) every ``kernel(name)`` call is bracketed by
+    two events on the current stream; ``totals_ms()`` synchronises and sums the elapsed
+    time per entry-point name.  The events add a few microseconds of host work per launch,
+    so the timer is for breakdowns of an untimed step, never for the timed region.
+    """
+
+    def __init__(self):
+        self.records: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+
+    def __enter__(self):
+        global _timer
+        self._prev, _timer = _timer, self
+        return self
+
+    def __exit__(self, *exc):
+        global _timer
+        _timer = self._prev
+        return False
+
+    def wrap(self, name: str, fn):
+        def timed(*args, **kwargs):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            out = fn(*args, **kwargs)
+            e1.record()
+            self.records.append((name, e0, e1))
+            return out
+        return timed
+
+    def totals_ms(self) -> dict[str, float]:
+        torch.cuda.synchronize()
+        out: dict[str, float] = {}
+        for name, e0, e1 in self.records:
+            out[name] = out.get(name, 0.0) + e0.elapsed_time(e1)
+        return out
 
 
 def kernel(name: str):
-    """The bound extension entry point ``name``; counts one launch per call."""
+    """The bound extension entry point ``name``; counts one launch per call (and times it
+    while a ``KernelTimer`` is active)."""
     fn = getattr(ext(), name)
     _launches[name] = _launches.get(name, 0) + 1
+    if _timer is not None:
+        return _timer.wrap(name, fn)
     return fn
 
 

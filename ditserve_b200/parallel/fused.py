@@ -18,7 +18,7 @@ import math
 
 import torch
 
-from ..ops._ext import ext, status_word
+from ..ops._ext import ext, kernel, status_word
 from .symm import PeerGroup, SymmetricHeap
 
 CH_SP, CH_CFG, CH_GATHER, CH_USP_ADDR = 0, 1, 2, 3
@@ -48,13 +48,13 @@ class FusedUlysses:
         assert batch == self.batch and seq_local == self.seq_local and heads == self.heads
         st = status_word(qkv.device)
         r, bases, tmo = self.group.args()
-        ext().qkv_scatter(qkv, wq, wk, float(eps), cos_full, sin_full, seq_local, heads, self.head_dim, r, bases,
+        kernel("qkv_scatter")(qkv, wq, wk, float(eps), cos_full, sin_full, seq_local, heads, self.head_dim, r, bases,
                           tmo, self.recv_off, 0)
         self.group.barrier(st)
         hl = heads // self.sp_size
         w = hl * self.head_dim
         q, k, v = self.recv[:, :w], self.recv[:, w:2 * w], self.recv[:, 2 * w:]
-        ext().attention_scatter(q, k, v, batch, seq_local * self.sp_size, hl, self.head_dim,
+        kernel("attention_scatter")(q, k, v, batch, seq_local * self.sp_size, hl, self.head_dim,
                                 1.0 / math.sqrt(self.head_dim), r, bases, tmo, self.o_off, seq_local,
                                 self.sp_rank * hl, heads * self.head_dim, st, [], [])
         self.group.barrier(st)
@@ -64,7 +64,7 @@ class FusedUlysses:
         if y.shape[1] != self.gather_cols:
             raise ValueError("gather width differs from the reserved buffer")
         r, bases, tmo = self.gather_group.args()
-        ext().allgather_rows(y.contiguous(), self.gather_off, r, bases, tmo)
+        kernel("allgather_rows")(y.contiguous(), self.gather_off, r, bases, tmo)
         self.gather_group.barrier(status_word(y.device))
         P = self.sp_size
         return self.gathered.view(P, batch, seq_local, -1).permute(1, 0, 2, 3).reshape(batch * P * seq_local, -1)
@@ -99,7 +99,7 @@ class FusedUSP(FusedUlysses):
         st = status_word(qkv.device)
         ur, ub, utmo = self.ugroup.args()
         chunk = seq_local * self.U
-        ext().qkv_scatter(qkv, wq, wk, float(eps), cos_full, sin_full, seq_local, heads, self.head_dim, ur, ub,
+        kernel("qkv_scatter")(qkv, wq, wk, float(eps), cos_full, sin_full, seq_local, heads, self.head_dim, ur, ub,
                           utmo, self.recv_off, self.r * chunk)
         self.sp_group.barrier(st)
         hl = heads // self.U
@@ -108,7 +108,7 @@ class FusedUSP(FusedUlysses):
         peers = [m for m in self.ring_members if m != self.heap.rank]
         k_extra = [self.heap.bases[m] + self.recv_off + w * 2 for m in peers]
         v_extra = [self.heap.bases[m] + self.recv_off + 2 * w * 2 for m in peers]
-        ext().attention_scatter(q, k, v, batch, chunk, hl, self.head_dim, 1.0 / math.sqrt(self.head_dim), ur, ub,
+        kernel("attention_scatter")(q, k, v, batch, chunk, hl, self.head_dim, 1.0 / math.sqrt(self.head_dim), ur, ub,
                                 utmo, self.o_off, seq_local, self.u * hl, heads * self.head_dim, st, k_extra,
                                 v_extra)
         self.sp_group.barrier(st)
@@ -148,7 +148,7 @@ class FusedCFG:
 
         def kernel(cond, uncond, g, x, sigma, corr, pred, x0_out=None, last_out=None):
             c = corr or {}
-            ext().cfg_step_peer(
+            kernel("cfg_step_peer")(
                 slot, slot_off, self.cfg_rank, float(g), x, float(sigma), corr is not None, c.get("last"),
                 float(c.get("last_coef", 0.0)), float(c.get("x0_coef", 0.0)), list(c.get("hist", [])),
                 [float(v) for v in c.get("hist_coef", [])], float(pred.get("x", 1.0)), float(pred.get("x0", 0.0)),
@@ -231,9 +231,9 @@ class PeerHalo:
         self.calls += 1
         sq = lambda t: t.squeeze(a)  # 4-D strided view of the slice
         if self.rank > 0:
-            ext().strided_put(sq(first), self.rank - 1, self.right_off[slot], r, bases, tmo)
+            kernel("strided_put")(sq(first), self.rank - 1, self.right_off[slot], r, bases, tmo)
         if self.rank < self.size - 1:
-            ext().strided_put(sq(last), self.rank + 1, self.left_off[slot], r, bases, tmo)
+            kernel("strided_put")(sq(last), self.rank + 1, self.left_off[slot], r, bases, tmo)
         self.group.barrier(status_word(x.device))
         esz = x.element_size()
         view = lambda off: self.heap.tensor[off:off + numel * esz].view(x.dtype).view(shape)

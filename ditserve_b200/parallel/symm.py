@@ -17,7 +17,7 @@ import math
 import torch
 import torch.distributed as dist
 
-from ..ops._ext import ext
+from ..ops._ext import ext, kernel
 
 _DTYPE_SIZE = {torch.bfloat16: 2, torch.float16: 2, torch.float32: 4, torch.int32: 4, torch.uint8: 1}
 
@@ -89,5 +89,5 @@ class PeerGroup:
         return self.rank, self.bases, self.timeout_ns
 
     def barrier(self, status):
-        ext().group_barrier(self.rank, self.bases, self.timeout_ns, self.channel,
+        kernel("group_barrier")(self.rank, self.bases, self.timeout_ns, self.channel,
                             self.heap.next_epoch(self.channel), status)

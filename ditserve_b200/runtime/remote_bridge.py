@@ -1,14 +1,14 @@
 """Multi-node bridge: a worker on another node behind a local stand-in process.
 
     # node 1 (the GPUs): serve workers over TCP
-    python -m ditserve_b200.runtime.remote_bridge daemon --listen 0.0.0.0:7700
+    python -m ditserve_b200.runtime.remote_bridge daemon --listen 0.0.0.0:7700 --token "$SECRET"
     # node 0 (controller): a process that speaks the worker protocol on stdin/stdout
     python -m ditserve_b200.runtime.remote_bridge proxy --connect node1:7700 --backend wan --config '{...}'
 
 Framing on the wire: 4-byte big-endian length + one JSON document, TCP_NODELAY.
 The first frame of a connection is {"bridge": "spawn", "backend", "config", "env"}; the
-daemon starts a local worker in a private session directory (the worker's
-``transfer_dir`` unless the config names one; ``env`` may set CUDA_VISIBLE_DEVICES and
+daemon starts a local worker in a private session directory (always the worker's
+``transfer_dir``; ``env`` may set CUDA_VISIBLE_DEVICES and
 NCCL_* / DITSERVE_* variables) and relays protocol lines both ways.  Extra frames:
 * {"bridge": "ring", "slot", "epoch"} — doorbell mirroring: the proxy watches the
   controller's local doorbell files and the daemon writes the epoch into its own
@@ -28,7 +28,10 @@ local workers.
 
 The daemon runs whatever worker a client asks for: bind it to a cluster-internal address and
 give it a shared secret (``--token`` or ``DITSERVE_BRIDGE_TOKEN``); a connection whose spawn
-frame carries another token is closed before anything starts.
+frame carries another token is closed before anything starts.  Without a token the daemon
+refuses to listen on anything but a loopback address.  The remote worker's ``transfer_dir``
+is always its session directory (a value in the client's config is replaced), so the file
+frames never reach beyond the session.
 Reference: workers/ditserve/runtime/remote_bridge.py:1-1009.
 """
 from __future__ import annotations
@@ -51,6 +54,17 @@ from .doorbell import Doorbell
 
 
 CHUNK = 8 << 20   # raw bytes per file-staging frame (base64 keeps a frame well under the 64 MiB cap)
+
+
+def _is_loopback(host: str) -> bool:
+    """True when every address ``host`` resolves to is a loopback address."""
+    import ipaddress
+    try:
+        infos = socket.getaddrinfo(host, None)
+    except OSError:
+        return False
+    addrs = {info[4][0] for info in infos}
+    return bool(addrs) and all(ipaddress.ip_address(a.split("%")[0]).is_loopback for a in addrs)
 
 
 def send_frame(sock: socket.socket, obj) -> None:
@@ -84,6 +98,12 @@ class BridgeDaemon:
 
     def __init__(self, host: str = "127.0.0.1", port: int = 0, python: str = sys.executable, workdir: str | None = None,
                  token: str | None = None):
+        token = token if token is not None else os.environ.get("DITSERVE_BRIDGE_TOKEN")
+        if not token and not _is_loopback(host):
+            # the daemon starts whatever worker a client asks for: off the loopback interface
+            # only a client holding the shared secret may do that
+            raise ValueError(f"refusing to listen on {host!r} without a token: set --token or "
+                             "DITSERVE_BRIDGE_TOKEN, or bind to a loopback address")
         self.server = socket.create_server((host, port))
         self.port = self.server.getsockname()[1]
         self.python = python
@@ -91,7 +111,7 @@ class BridgeDaemon:
         os.makedirs(self.workdir, exist_ok=True)
         self.threads = []
         self._stop = threading.Event()
-        self.token = token if token is not None else os.environ.get("DITSERVE_BRIDGE_TOKEN")
+        self.token = token
 
     def serve_forever(self):
         self.server.settimeout(0.2)
@@ -136,8 +156,11 @@ class BridgeDaemon:
         root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
         env["PYTHONPATH"] = root + os.pathsep + env.get("PYTHONPATH", "")
         config = dict(first.get("config", {}))
-        config.setdefault("transfer_dir", sdir)
-        roots = {sdir, os.path.realpath(str(config["transfer_dir"]))}
+        # the remote worker always stages packets in its session directory: a client-chosen
+        # transfer_dir would widen the file frames' reach (get_file with unlink) to anything
+        # the daemon can touch, so the client's value is replaced, never trusted
+        config["transfer_dir"] = sdir
+        roots = {sdir}
         proc = subprocess.Popen([self.python, "-m", "ditserve_b200.runtime.worker", "--backend", first["backend"],
                                  "--config", json.dumps(config)], stdin=subprocess.PIPE,
                                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True, env=env)

@@ -158,3 +158,37 @@ def test_remote_bridge_refuses_a_wrong_token(tmp_path):
         good.close()
     finally:
         daemon.stop()
+
+
+def test_remote_bridge_refuses_public_listen_without_token(monkeypatch):
+    """Off the loopback interface the daemon would start workers for anyone: no token, no daemon."""
+    from ditserve_b200.runtime.remote_bridge import BridgeDaemon, _is_loopback
+    monkeypatch.delenv("DITSERVE_BRIDGE_TOKEN", raising=False)
+    assert _is_loopback("127.0.0.1") and _is_loopback("localhost")
+    assert not _is_loopback("0.0.0.0")
+    with pytest.raises(ValueError, match="without a token"):
+        BridgeDaemon("0.0.0.0", 0)
+    d = BridgeDaemon("0.0.0.0", 0, token="s3cret")  # with a shared secret it may listen anywhere
+    d.stop()
+
+
+def test_remote_bridge_file_frames_stay_in_the_session(tmp_path):
+    """A client that names its own transfer_dir still cannot read or delete files outside the
+    session directory: the worker's transfer_dir is replaced and get_file is confined."""
+    from ditserve_b200.runtime.remote_bridge import BridgeDaemon, BridgeProxy
+    outside = tmp_path / "outside"
+    outside.mkdir()
+    secret = outside / "keep.txt"
+    secret.write_text("not yours")
+    daemon = BridgeDaemon("127.0.0.1", 0, workdir=str(tmp_path / "node1"))
+    threading.Thread(target=daemon.serve_forever, daemon=True).start()
+    try:
+        proxy = BridgeProxy(f"127.0.0.1:{daemon.port}", "mock", {"transfer_dir": str(outside)},
+                            stage_dir=str(tmp_path))
+        assert json.loads(proxy.relay(json.dumps(dict(version=1, id=1, op="hello")) + "\n"))["ok"]
+        with pytest.raises(OSError):
+            proxy.pull_file(str(secret), unlink=True)
+        assert secret.read_text() == "not yours"
+        proxy.close()
+    finally:
+        daemon.stop()

@@ -1,10 +1,15 @@
 // Golden decision fixture: the simulator's outcome for every registered policy on a seeded
 // mixed trace, the planner's assignments on a set of fixed cluster states, and the online
-// selector's decisions on fixed queues, compared against tests/fixtures/control-golden.json.
+// selector's decisions on fixed queues, the resolution of every way a policy name can be
+// written, and the block-preemption selectors' decisions on generated cases (ties included),
+// compared against tests/fixtures/control-golden.json.
 // Any change of a decision rule shows up here as a diff; after an intended change, rebuild
 // the fixture with DS_UPDATE_GOLDEN=1 and review the diff.  (The reference keeps such a
 // fixture for its control rules: tests/fixtures/control-baseline.json.)
 #include <cmath>
+#include <cstdint>
+#include <initializer_list>
+#include <vector>
 #include <cstdlib>
 #include <fstream>
 #include <sstream>
@@ -34,6 +39,195 @@ Json profile() {
 }
 
 double round6(double x) { return std::round(x * 1e6) / 1e6; }
+
+// Deterministic case generator for the decision sections below (a 64-bit LCG, so the cases
+// never depend on the standard library's distributions).
+struct CaseGen {
+  uint64_t s;
+  explicit CaseGen(uint64_t seed) : s(seed * 2862933555777941757ull + 3037000493ull) {}
+  uint64_t next() {
+    s = s * 6364136223846793005ull + 1442695040888963407ull;
+    return s >> 17;
+  }
+  int below(int n) { return static_cast<int>(next() % static_cast<uint64_t>(n)); }
+  template <class T>
+  T pick(std::initializer_list<T> v) { return *(v.begin() + below(static_cast<int>(v.size()))); }
+};
+
+Json name_resolution() {
+  // every way a policy name can be written: registered ids, legacy aliases, retired names,
+  // parameterised families in both spellings, malformed forms and unknown names
+  std::vector<std::string> names;
+  const Json catalog = policy_catalog();
+  for (const auto& p : catalog.as_array()) names.push_back(p.at("id").as_string());
+  for (const char* n : {"heterodit_exact", "knapsack_dp", "heterodit_v5", "step_elastic", "block_elastic",
+                        "round_elastic", "heterodit_approx", "heterodit_v3", "ablation_tiered", "ablation_2d_usp",
+                        "static_partition", "vanilla_xdit", "tridentserve_stage", "vllm_omni", "gf_dit",
+                        "genserve_40gb", "xdit", "xdit_sp2", "xdit-sp8", "xdit-cfg2sp4", "static-sp1", "static_sp2",
+                        "static_cfg2sp2", "static-u2r2", "static_u2r4", "block-cfg2", "block_cfg2sp4", "block-sp4",
+                        "fold-cfg2", "fold-sp2", "fold_cfg2", "approx-cfg2sp2", "approx_cfg2sp2", "static-bogus",
+                        "static_bogus", "block-", "static-cfg3", "static-u2r1x", "nope", "", "ditserve_",
+                        "static_cfg2-sp2", "block-sp2_x", "static-sp32", "xdit-u1r2", "STATIC-sp2"})
+    names.push_back(n);
+  Json out = Json::object();
+  for (const auto& n : names) {
+    Json r = Json::object();
+    try {
+      r["legacy_alias"] = legacy_policy_alias(n);
+    } catch (const std::exception& e) {
+      r["legacy_alias_error"] = std::string(e.what());
+    }
+    try {
+      r["canonical"] = canonical_policy(n);
+    } catch (const std::exception& e) {
+      r["canonical_error"] = std::string(e.what());
+    }
+    try {
+      r["traits"] = describe_policy(policy_traits(n));
+    } catch (const std::exception& e) {
+      r["traits_error"] = std::string(e.what());
+    }
+    out[n.empty() ? std::string("<empty>") : n] = r;
+  }
+  return out;
+}
+
+std::vector<RunningGroup> random_running(CaseGen& g, int gpus) {
+  std::vector<RunningGroup> run;
+  int gpu = 0, id = 0;
+  std::vector<int> order(gpus);
+  for (int i = 0; i < gpus; ++i) order[i] = i;
+  for (int i = gpus - 1; i > 0; --i) std::swap(order[i], order[g.below(i + 1)]);
+  while (gpu < gpus) {
+    const int w = std::min(gpus - gpu, g.pick({1, 1, 2, 2, 4, 8}));
+    RunningGroup r;
+    r.request_id = "r" + std::to_string(id++);
+    for (int k = 0; k < w; ++k) r.group.push_back(order[gpu + k]);
+    gpu += w;
+    if (g.below(5) == 0) continue;  // idle GPUs
+    r.stop_ms = g.pick({0.0, 20.0, 50.0, 80.0, 100.0, 120.0, 200.0});
+    r.remaining_ms = g.pick({0.0, 40.0, 100.0, 300.0, 600.0, 1500.0, 4000.0});
+    r.resume_ms = g.pick({0.0, 10.0, 25.0, 60.0});
+    r.rung = g.below(4) == 0;
+    run.push_back(r);
+  }
+  return run;
+}
+
+Json group_json(const std::vector<RunningGroup>& run) {
+  Json a = Json::array();
+  for (const auto& r : run) {
+    Json o = Json::object();
+    o["id"] = r.request_id;
+    Json gg = Json::array();
+    for (int x : r.group) gg.push_back(x);
+    o["group"] = gg;
+    o["stop"] = r.stop_ms;
+    o["remaining"] = r.remaining_ms;
+    o["resume"] = r.resume_ms;
+    o["rung"] = r.rung;
+    a.push_back(o);
+  }
+  return a;
+}
+
+Json preemption_decisions() {
+  Json out = Json::object();
+  Json groups = Json::array();
+  CaseGen g(101);
+  for (int c = 0; c < 300; ++c) {
+    const int gpus = g.pick({2, 4, 4, 8, 8, 8, 16});
+    auto run = random_running(g, gpus);
+    std::vector<int> aff;
+    const int n = 1 + g.below(6);
+    for (int i = 0; i < n; ++i) aff.push_back(g.below(3) == 0 ? g.below(gpus) : -1);
+    Json rec = Json::object();
+    Json aj = Json::array();
+    for (int a : aff) aj.push_back(a);
+    rec["affinities"] = aj;
+    rec["running"] = group_json(run);
+    try {
+      Json sel = Json::array();
+      for (const auto& id : select_preemption_groups(aff, run)) sel.push_back(id);
+      rec["selected"] = sel;
+    } catch (const std::exception& e) {
+      rec["error"] = std::string(e.what());
+    }
+    groups.push_back(rec);
+  }
+  out["groups"] = groups;
+  Json deadline = Json::array();
+  CaseGen h(202);
+  for (int c = 0; c < 400; ++c) {
+    const int gpus = h.pick({2, 4, 8, 8, 16});
+    auto run = random_running(h, gpus);
+    const double now = h.pick({0.0, 100.0, 1000.0});
+    std::vector<ImageDemand> dem;
+    const int n = 1 + h.below(5);
+    for (int i = 0; i < n; ++i) {
+      ImageDemand d;
+      d.affinity = h.below(4) == 0 ? h.below(gpus) : -1;
+      d.service_ms = h.pick({100.0, 300.0, 400.0, 1000.0});
+      d.deadline_ms = now + d.service_ms * h.pick({0.5, 0.85, 0.9, 1.0, 1.2, 1.35, 1.4, 2.0, 4.0}) +
+                      h.pick({0.0, 0.0, 20.0, 120.0});
+      dem.push_back(d);
+    }
+    Json rec = Json::object();
+    rec["now"] = now;
+    Json dj = Json::array();
+    for (const auto& d : dem) {
+      Json o = Json::object();
+      o["affinity"] = d.affinity;
+      o["deadline"] = d.deadline_ms;
+      o["service"] = d.service_ms;
+      dj.push_back(o);
+    }
+    rec["waiting"] = dj;
+    rec["running"] = group_json(run);
+    try {
+      auto r = select_deadline_preemption(now, dem, run);
+      Json sel = Json::array();
+      for (const auto& id : r.selected) sel.push_back(id);
+      rec["selected"] = sel;
+      rec["skips"] = static_cast<long long>(r.deadline_skips);
+    } catch (const std::exception& e) {
+      rec["error"] = std::string(e.what());
+    }
+    deadline.push_back(rec);
+  }
+  out["deadline"] = deadline;
+  Json timing = Json::array();
+  CaseGen t(303);
+  for (int c = 0; c < 60; ++c) {
+    const double block = t.pick({0.0, 5.0, 12.5, 40.0});
+    const int total = t.pick({0, 30, 60});
+    const int done = t.pick({-1, 0, 10, 30, 70});
+    const double elapsed = t.pick({0.0, 3.0, 500.0});
+    const int check = t.pick({0, 1, 2, 4});
+    const int per = t.pick({1, 2});
+    const bool delayed = t.below(2) == 0;
+    Json rec = Json::object();
+    rec["in"] = Json::parse("[" + std::to_string(block) + "," + std::to_string(total) + "," + std::to_string(done) +
+                            "," + std::to_string(elapsed) + "," + std::to_string(check) + "," +
+                            std::to_string(per) + "," + (delayed ? "true" : "false") + "]");
+    try {
+      auto e = estimate_preemption_timing(block, total, done, elapsed, check, per, delayed);
+      rec["stop"] = e.stop_ms;
+      rec["remaining"] = e.remaining_ms;
+    } catch (const std::exception& e) {
+      rec["error"] = std::string(e.what());
+    }
+    try {
+      rec["converts"] = preemption_converts_deadline(elapsed, block * 40 + elapsed, block * 10, block * check,
+                                                     block * total - elapsed);
+    } catch (const std::exception& e) {
+      rec["converts_error"] = std::string(e.what());
+    }
+    timing.push_back(rec);
+  }
+  out["timing"] = timing;
+  return out;
+}
 
 Json snapshot_json() {
   ClusterCost c(profile());
@@ -99,6 +293,9 @@ Json snapshot_json() {
     if (is_online_policy(pol))
       online[pol] = select_online(q, 1200, pol, "v", Json(1), Json::parse(R"({"image_deadline_ms": 2000})"));
   out["online"] = online;
+  // 4. policy-name resolution and 5. block-preemption selection on generated cases
+  out["names"] = name_resolution();
+  out["preemption"] = preemption_decisions();
   return out;
 }
 
@@ -118,7 +315,7 @@ TEST("decisions match the golden fixture") {
   std::stringstream ss;
   ss << f.rdbuf();
   const Json want = Json::parse(ss.str());
-  for (const char* part : {"simulate", "plan", "online"}) {
+  for (const char* part : {"simulate", "plan", "online", "names", "preemption"}) {
     for (const auto& [k, v] : want.at(part).as_object()) {
       const bool same = now.at(part).contains(k) && now.at(part).at(k) == v;
       if (!same) std::cerr << "  golden diff in " << part << "/" << k << "\n    want " << v.dump() << "\n    got  "

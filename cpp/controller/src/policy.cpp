@@ -2,7 +2,6 @@
 
 #include <map>
 #include <mutex>
-#include <set>
 #include <stdexcept>
 
 namespace ds {
@@ -210,91 +209,172 @@ const std::map<std::string, PolicyTraits>& table() {
   return t;
 }
 
-const std::map<std::string, std::string>& aliases() {
-  static const std::map<std::string, std::string> a = {
-      {"heterodit_exact", "ditserve-v1"}, {"knapsack_dp", "ditserve-v1"}, {"heterodit_v5", "ditserve-v1-approx"},
-      {"step_elastic", "abl-step-elastic"}, {"block_elastic", "abl-block-elastic"},
-      {"round_elastic", "abl-round-elastic"}, {"heterodit_approx", "diag-feature-cache"}, {"heterodit_v3", "diag-v3"},
-      {"ablation_tiered", "diag-tiered"}, {"ablation_2d_usp", "diag-2d-usp"},
-      {"static_partition", "diag-elastic-partition"}};
-  return a;
+// ---------------------------------------------------------------------------
+// Name resolution
+//
+// Three kinds of name besides the registered ids:
+//  * exact names from older studies: either an alias (it resolves to another name) or a
+//    retired policy (resolving it is an error that says so);
+//  * "xdit" on its own, the single-GPU xDiT baseline;
+//  * family names "<kind>-<form>" (a fixed parallel form, see form.hpp).  Two families were
+//    also written "<kind>_<form>" in older studies; that spelling is accepted only in a
+//    name without any '-', and it canonicalises to the '-' spelling.
+// A name that claims a family kind but carries a malformed form is an error, never a
+// silent fallback to another policy.
+
+enum class OldName { kAlias, kRetired };
+struct OldNameRule {
+  const char* name;
+  OldName what;
+  const char* target;  // alias target (unused for retired names)
+};
+constexpr OldNameRule kOldNames[] = {
+    {"heterodit_exact", OldName::kAlias, "ditserve-v1"},
+    {"knapsack_dp", OldName::kAlias, "ditserve-v1"},
+    {"heterodit_v5", OldName::kAlias, "ditserve-v1-approx"},
+    {"step_elastic", OldName::kAlias, "abl-step-elastic"},
+    {"block_elastic", OldName::kAlias, "abl-block-elastic"},
+    {"round_elastic", OldName::kAlias, "abl-round-elastic"},
+    {"heterodit_approx", OldName::kAlias, "diag-feature-cache"},
+    {"heterodit_v3", OldName::kAlias, "diag-v3"},
+    {"ablation_tiered", OldName::kAlias, "diag-tiered"},
+    {"ablation_2d_usp", OldName::kAlias, "diag-2d-usp"},
+    {"static_partition", OldName::kAlias, "diag-elastic-partition"},
+    {"vanilla_xdit", OldName::kRetired, ""},
+    {"tridentserve_stage", OldName::kRetired, ""},
+    {"vllm_omni", OldName::kRetired, ""},
+    {"gf_dit", OldName::kRetired, ""},
+    {"genserve_40gb", OldName::kRetired, ""},
+};
+
+const OldNameRule* old_name(const std::string& name) {
+  for (const auto& r : kOldNames)
+    if (name == r.name) return &r;
+  return nullptr;
 }
 
-const std::set<std::string>& retired() {
-  static const std::set<std::string> r = {"vanilla_xdit", "tridentserve_stage", "vllm_omni", "gf_dit", "genserve_40gb"};
-  return r;
+// What a family name implies.  Every family runs one fixed form chosen by the name.
+struct FamilySpec {
+  const char* kind;
+  bool underscore_spelling;  // also accepted as "<kind>_<form>" (older studies)
+  const char* family;
+  const char* display;       // display prefix; the form name follows
+  const char* source;
+  bool blocks, v5, fission;
+  bool xdit_partition;       // the xDiT static partition: FCFS, run to completion, a quarter of the GPUs for images
+  bool cfg_only;             // only meaningful with CFG parallelism (listed with cfg2 forms in the catalog)
+};
+constexpr FamilySpec kFamilies[] = {
+    {"static", true, "control", "Static-", "fixed parallel form, EDF, whole-step quanta", false, false, false, false,
+     false},
+    {"block", true, "control", "Block-", "fixed parallel form with block quanta and sub-step preemption", true, false,
+     false, false, false},
+    {"fold", false, "ablation", "Fold-", "fixed-form CFG folding, unconditional subgroup idle", true, true, false,
+     false, true},
+    {"approx", false, "ablation", "Approx-", "fixed CFG form with folding and fission", true, true, true, false, true},
+    {"xdit", false, "baseline", "xDiT-",
+     "xDiT static partition: fixed form per video, image share gpus/4, FCFS, run to completion", false, false, false,
+     true, false},
+};
+
+const FamilySpec* family_of(const std::string& kind) {
+  for (const auto& f : kFamilies)
+    if (kind == f.kind) return &f;
+  return nullptr;
 }
 
-bool split_parameterised(const std::string& name, std::string& kind, Form& form) {
-  for (const char* prefix : {"static-", "block-", "xdit-", "fold-", "approx-", "static_", "block_"}) {
-    const std::string p(prefix);
-    if (name.compare(0, p.size(), p) != 0) continue;
-    try {
-      form = parse_form(name.substr(p.size()));
-    } catch (const std::invalid_argument&) {
-      throw std::invalid_argument("unknown cluster policy: " + name);
-    }
-    kind = p.substr(0, p.size() - 1);
-    return true;
+struct FamilyName {
+  const FamilySpec* spec = nullptr;
+  char separator = '-';
+  Form form;
+};
+
+// Splits "<kind><sep><form>" at the first separator.  Returns false when the name does not
+// claim a family (no separator, an unknown kind, or '_' for a family without that spelling);
+// throws when it claims one and the form part is malformed.
+bool read_family_name(const std::string& name, FamilyName& out) {
+  const size_t cut = name.find_first_of("-_");
+  if (cut == std::string::npos) return false;
+  const FamilySpec* spec = family_of(name.substr(0, cut));
+  if (spec == nullptr) return false;
+  if (name[cut] == '_' && !spec->underscore_spelling) return false;
+  try {
+    out.form = parse_form(name.substr(cut + 1));
+  } catch (const std::invalid_argument&) {
+    throw std::invalid_argument("unknown cluster policy: " + name);
   }
-  return false;
+  out.spec = spec;
+  out.separator = name[cut];
+  return true;
 }
 
-}  // namespace
-
-std::string legacy_policy_alias(const std::string& name) {
-  auto it = aliases().find(name);
-  if (it != aliases().end()) return it->second;
-  std::string kind;
-  Form form;
-  if (name.find('_') != std::string::npos && name.find('-') == std::string::npos &&
-      split_parameterised(name, kind, form))
-    return kind + "-" + form_name(form);
-  return "";
-}
-
-std::string canonical_policy(const std::string& name) {
-  if (name == "xdit") return "xdit-sp1";
-  std::string legacy = legacy_policy_alias(name);
-  return legacy.empty() ? name : legacy;
-}
-
-const PolicyTraits& policy_traits(const std::string& raw) {
-  if (retired().count(raw)) throw std::invalid_argument("retired cluster policy: " + raw);
-  const std::string name = canonical_policy(raw);
-  auto it = table().find(name);
-  if (it != table().end()) return it->second;
-  std::string kind;
-  Form form;
-  if (!split_parameterised(name, kind, form)) throw std::invalid_argument("unknown cluster policy: " + raw);
-  static std::mutex mu;
-  static std::map<std::string, PolicyTraits> cache;
-  std::lock_guard<std::mutex> lock(mu);
-  auto c = cache.find(name);
-  if (c != cache.end()) return c->second;
-  const std::string fname = form_name(form);
-  PolicyTraits t;
-  if (kind == "static") {
-    t = base(name, "Static-" + fname, "control", "fixed parallel form, EDF, whole-step quanta");
-  } else if (kind == "block") {
-    t = base(name, "Block-" + fname, "control", "fixed parallel form with block quanta and sub-step preemption");
-    t.blocks = true;
-  } else if (kind == "fold" || kind == "approx") {
-    t = base(name, (kind == "fold" ? "Fold-" : "Approx-") + fname, "ablation",
-             kind == "fold" ? "fixed-form CFG folding, unconditional subgroup idle" : "fixed CFG form with folding and fission");
-    t.blocks = t.v5 = true;
-    t.fission = kind == "approx";
-  } else {
-    t = base(name, fname == "sp1" ? "xDiT" : "xDiT-" + fname, "baseline",
-             "xDiT static partition: fixed form per video, image share gpus/4, FCFS, run to completion");
+PolicyTraits family_traits(const std::string& id, const FamilyName& fn) {
+  const FamilySpec& f = *fn.spec;
+  const std::string form = form_name(fn.form);
+  const std::string display =
+      f.xdit_partition && form == "sp1" ? std::string("xDiT") : std::string(f.display) + form;
+  PolicyTraits t = base(id, display, f.family, f.source);
+  t.blocks = f.blocks;
+  t.v5 = f.v5;
+  t.fission = f.fission;
+  if (f.xdit_partition) {
     t.hold_diffuse = true;
     t.order = "fcfs";
     t.demote_late = false;
     t.partition_divisor = 4;
   }
-  t.fixed_form = form;
-  t.fixed_degree = form.degree();
-  return cache.emplace(name, t).first->second;
+  t.fixed_form = fn.form;
+  t.fixed_degree = fn.form.degree();
+  return t;
+}
+
+// Traits of family names are built on first use and kept for the life of the process, so
+// the references handed out stay valid.
+class FamilyRegistry {
+ public:
+  const PolicyTraits& get(const std::string& id, const FamilyName& fn) {
+    std::lock_guard<std::mutex> lock(mu_);
+    auto it = built_.find(id);
+    if (it == built_.end()) it = built_.emplace(id, family_traits(id, fn)).first;
+    return it->second;
+  }
+
+ private:
+  std::mutex mu_;
+  std::map<std::string, PolicyTraits> built_;
+};
+
+FamilyRegistry& families() {
+  static FamilyRegistry r;
+  return r;
+}
+
+}  // namespace
+
+std::string legacy_policy_alias(const std::string& name) {
+  if (const OldNameRule* r = old_name(name)) return r->what == OldName::kAlias ? r->target : "";
+  FamilyName fn;
+  const bool old_spelling = name.find('-') == std::string::npos && name.find('_') != std::string::npos;
+  if (old_spelling && read_family_name(name, fn) && fn.separator == '_')
+    return std::string(fn.spec->kind) + "-" + form_name(fn.form);
+  return "";
+}
+
+std::string canonical_policy(const std::string& name) {
+  if (name == "xdit") return "xdit-sp1";
+  const std::string alias = legacy_policy_alias(name);
+  return alias.empty() ? name : alias;
+}
+
+const PolicyTraits& policy_traits(const std::string& raw) {
+  if (const OldNameRule* r = old_name(raw); r != nullptr && r->what == OldName::kRetired)
+    throw std::invalid_argument("retired cluster policy: " + raw);
+  const std::string id = canonical_policy(raw);
+  const auto& registered = table();
+  if (auto it = registered.find(id); it != registered.end()) return it->second;
+  FamilyName fn;
+  if (!read_family_name(id, fn)) throw std::invalid_argument("unknown cluster policy: " + raw);
+  return families().get(id, fn);
 }
 
 Json describe_policy(const PolicyTraits& t) {
@@ -336,10 +416,16 @@ Json describe_policy(const PolicyTraits& t) {
 }
 
 Json policy_catalog() {
+  // registered ids, then every family on the fixed forms of this framework's default layouts
+  // for 1, 2, 4 and 8 GPUs (sp1, cfg2, cfg2sp2, cfg2sp4); families that need CFG parallelism
+  // are listed on the cfg2 forms only
   Json out = Json::array();
   for (const auto& kv : table()) out.push_back(describe_policy(kv.second));
-  for (const char* n : {"xdit-sp1", "xdit-sp2", "xdit-cfg2", "static-cfg2", "block-cfg2", "fold-cfg2sp3", "approx-cfg2sp3"})
-    out.push_back(describe_policy(policy_traits(n)));
+  for (const auto& f : kFamilies)
+    for (const char* form : {"sp1", "cfg2", "cfg2sp2", "cfg2sp4"}) {
+      if (f.cfg_only && parse_form(form).cfg != 2) continue;
+      out.push_back(describe_policy(policy_traits(std::string(f.kind) + "-" + form)));
+    }
   return out;
 }
 

@@ -67,7 +67,8 @@ Json name_resolution() {
                         "static_cfg2sp2", "static-u2r2", "static_u2r4", "block-cfg2", "block_cfg2sp4", "block-sp4",
                         "fold-cfg2", "fold-sp2", "fold_cfg2", "approx-cfg2sp2", "approx_cfg2sp2", "static-bogus",
                         "static_bogus", "block-", "static-cfg3", "static-u2r1x", "nope", "", "ditserve_",
-                        "static_cfg2-sp2", "block-sp2_x", "static-sp32", "xdit-u1r2", "STATIC-sp2"})
+                        "static_cfg2-sp2", "block-sp2_x", "static-sp32", "xdit-u1r2", "STATIC-sp2", "xdit-sp2",
+                        "fold-cfg2sp3", "approx-cfg2sp3", "xdit-cfg2"})
     names.push_back(n);
   Json out = Json::object();
   for (const auto& n : names) {

@@ -1084,175 +1084,292 @@ Json cluster_plan(const Json& state, const std::string& policy, const ClusterCos
 }
 
 // ---------------------------------------------------------------------------------------
+// Block preemption (sub-step, through doorbells).
+//
+// Decision rules; the golden fixture's "preemption" section pins them on generated cases,
+// ties included.
+//
+// Timing of a running group.  A rung group stops at its next doorbell check, which comes
+//   every check_blocks x blocks_per_iteration blocks, or twice that when the group agrees on
+//   the flag one checkpoint late.  Unrung, it runs to its step boundary: the blocks still to
+//   run less the time already spent, and never less than one block.
+//
+// A stop saves an image when waiting for the group's boundary makes the image late and the
+//   earlier of the stop and the boundary lets it finish on time.
+//
+// Freeing GPUs for waiting images (select_preemption_groups):
+//   1. Groups that already rang, and groups that hold a GPU some image is pinned to, stop
+//      anyway; those that did not ring yet are selected, in input order.
+//   2. Their GPUs that no image is pinned to go to the images that take any GPU.
+//   3. If such images remain without a GPU, more groups are chosen so that they free at
+//      least that many GPUs (or all they have), displacing the least GPU time, where a group
+//      displaces |group| x (min(stop, remaining) + resume).  Candidate sets are ordered by
+//      displaced time (summed in input order), then by GPUs freed, then by the number of
+//      groups, then by the position of their last group in the input, comparing from the
+//      back (the set whose last member comes earlier wins).  The chosen groups follow the
+//      pinned ones, in input order.
+//
+// Matching images to groups by deadline (select_deadline_preemption):
+//   Images are served in deadline order; among equal deadlines an image pinned to a GPU goes
+//   first.  A group can serve an image when it holds a GPU that no earlier image was promised
+//   and that the image may use; the first such GPU of the group is the one promised.  The
+//   image's window is tight when its deadline lies between 0.85x and 1.35x of its service
+//   time from now; a tight image tolerates a rung group overrunning its deadline by
+//   max(1.5 x stop, 120 ms).
+//   a) A group that already rang and responds in time (within that tolerance) takes the
+//      image, the earliest responder first.
+//   b) Otherwise, if waiting for the earliest response among the usable groups is late, a
+//      group is rung: one whose early stop saves the image, or, failing that and only for a
+//      tight image, one that stops before its boundary and within the tolerance.  Among the
+//      candidates the least displaced time wins, then the narrower group, then the earlier.
+//   c) An image served neither way counts as a deadline skip.
+
 PreemptionTiming estimate_preemption_timing(double block_ms, int blocks_total, int blocks_done, double elapsed_ms,
                                             int check_blocks, int blocks_per_iteration, bool delayed_group_check) {
-  if (!(block_ms > 0) || !std::isfinite(block_ms) || blocks_total <= 0 || blocks_done < 0 || !(elapsed_ms >= 0) ||
-      check_blocks <= 0 || blocks_per_iteration <= 0)
-    throw std::invalid_argument("invalid block preemption timing");
-  PreemptionTiming t;
-  t.stop_ms = block_ms * check_blocks * blocks_per_iteration * (delayed_group_check ? 2 : 1);
-  t.remaining_ms = std::max(block_ms, std::max(0, blocks_total - blocks_done) * block_ms - elapsed_ms);
-  return t;
-}
-
-bool preemption_converts_deadline(double now_ms, double deadline_ms, double service_ms, double stop_ms,
-                                  double boundary_ms) {
-  for (double v : {now_ms, deadline_ms, service_ms, stop_ms, boundary_ms})
-    if (!std::isfinite(v)) throw std::invalid_argument("non-finite preemption input");
-  if (now_ms < 0 || service_ms < 0 || stop_ms < 0 || boundary_ms < 0)
-    throw std::invalid_argument("negative preemption input");
-  const bool late_if_patient = now_ms + boundary_ms + service_ms > deadline_ms;
-  const bool on_time_if_stopped = now_ms + std::min(stop_ms, boundary_ms) + service_ms <= deadline_ms;
-  return late_if_patient && on_time_if_stopped;
+  const bool sane = block_ms > 0 && std::isfinite(block_ms) && blocks_total > 0 && blocks_done >= 0 &&
+                    elapsed_ms >= 0 && check_blocks > 0 && blocks_per_iteration > 0;
+  if (!sane) throw std::invalid_argument("invalid block preemption timing");
+  const int blocks_per_check = check_blocks * blocks_per_iteration;
+  const double checks_to_stop = delayed_group_check ? 2 : 1;
+  const int blocks_left = blocks_total > blocks_done ? blocks_total - blocks_done : 0;
+  PreemptionTiming out;
+  out.stop_ms = block_ms * blocks_per_check * checks_to_stop;
+  out.remaining_ms = std::max(block_ms, blocks_left * block_ms - elapsed_ms);
+  return out;
 }
 
 namespace {
-void validate_groups(const std::vector<RunningGroup>& running) {
-  std::set<int> used;
-  std::set<std::string> ids;
-  for (const auto& r : running) {
-    if (r.request_id.empty() || !ids.insert(r.request_id).second || r.group.empty())
-      throw std::invalid_argument("invalid running group");
-    for (double v : {r.stop_ms, r.remaining_ms, r.resume_ms})
+
+void require_preemption_inputs(double now_ms, double deadline_ms, double service_ms, double stop_ms,
+                               double boundary_ms) {
+  const double all[] = {now_ms, deadline_ms, service_ms, stop_ms, boundary_ms};
+  if (!std::all_of(std::begin(all), std::end(all), [](double v) { return std::isfinite(v); }))
+    throw std::invalid_argument("non-finite preemption input");
+  if (std::min({now_ms, service_ms, stop_ms, boundary_ms}) < 0)
+    throw std::invalid_argument("negative preemption input");
+}
+
+}  // namespace
+
+bool preemption_converts_deadline(double now_ms, double deadline_ms, double service_ms, double stop_ms,
+                                  double boundary_ms) {
+  require_preemption_inputs(now_ms, deadline_ms, service_ms, stop_ms, boundary_ms);
+  const double finish_waiting = now_ms + boundary_ms + service_ms;
+  const double finish_stopping = now_ms + std::min(stop_ms, boundary_ms) + service_ms;
+  return finish_waiting > deadline_ms && finish_stopping <= deadline_ms;
+}
+
+namespace {
+
+void require_disjoint_groups(const std::vector<RunningGroup>& running) {
+  std::set<std::string> seen_ids;
+  std::set<int> seen_gpus;
+  for (const auto& g : running) {
+    const bool named = !g.request_id.empty() && seen_ids.insert(g.request_id).second && !g.group.empty();
+    if (!named) throw std::invalid_argument("invalid running group");
+    const double times[] = {g.stop_ms, g.remaining_ms, g.resume_ms};
+    for (double v : times)
       if (!std::isfinite(v) || v < 0) throw std::invalid_argument("invalid running group timing");
-    for (int gpu : r.group)
-      if (gpu < 0 || !used.insert(gpu).second) throw std::invalid_argument("running groups must be disjoint");
+    for (int gpu : g.group)
+      if (gpu < 0 || !seen_gpus.insert(gpu).second) throw std::invalid_argument("running groups must be disjoint");
   }
 }
-double displaced(const RunningGroup& r) {
-  return r.group.size() * (std::min(r.stop_ms, r.remaining_ms) + r.resume_ms);
+
+// GPU time lost when a group stops now and later resumes: every GPU of the group idles for
+// the stop (or the boundary, if sooner) and then pays the resume.
+double displaced_gpu_ms(const RunningGroup& g) {
+  return g.group.size() * (std::min(g.stop_ms, g.remaining_ms) + g.resume_ms);
 }
+
+// Least displaced GPU time that frees at least `need` GPUs out of `pool` (indices into
+// `running`), by the order stated above.  A table over (groups considered, GPUs freed)
+// holds the best set for each exact GPU count; a set that leaves out the newest group wins
+// every tie against one that takes it, which is the "last member earlier" rule.
+std::vector<size_t> cheapest_cover(const std::vector<RunningGroup>& running, const std::vector<size_t>& pool,
+                                   int need) {
+  struct Best {
+    double cost = std::numeric_limits<double>::infinity();
+    int groups = 0;
+    bool took = false;
+  };
+  int total = 0;
+  for (size_t idx : pool) total += static_cast<int>(running[idx].group.size());
+  const size_t n = pool.size();
+  std::vector<std::vector<Best>> best(n + 1, std::vector<Best>(total + 1));
+  best[0][0].cost = 0;
+  for (size_t i = 1; i <= n; ++i) {
+    const RunningGroup& g = running[pool[i - 1]];
+    const int w = static_cast<int>(g.group.size());
+    const double d = displaced_gpu_ms(g);
+    for (int c = 0; c <= total; ++c) {
+      Best keep = best[i - 1][c];
+      keep.took = false;
+      best[i][c] = keep;
+      if (c < w || !std::isfinite(best[i - 1][c - w].cost)) continue;
+      const Best& from = best[i - 1][c - w];
+      const double cost = from.cost + d;
+      const int groups = from.groups + 1;
+      const bool better = cost < keep.cost || (cost == keep.cost && groups < keep.groups);
+      if (better) best[i][c] = Best{cost, groups, true};
+    }
+  }
+  int pick = need;
+  for (int c = need + 1; c <= total; ++c)
+    if (best[n][c].cost < best[n][pick].cost) pick = c;
+  std::vector<size_t> chosen;
+  for (size_t i = n, c = static_cast<size_t>(pick); i > 0; --i) {
+    if (!best[i][c].took) continue;
+    chosen.push_back(pool[i - 1]);
+    c -= running[pool[i - 1]].group.size();
+  }
+  std::reverse(chosen.begin(), chosen.end());
+  return chosen;
+}
+
 }  // namespace
 
 std::vector<std::string> select_preemption_groups(const std::vector<int>& affinities,
                                                   const std::vector<RunningGroup>& running) {
-  validate_groups(running);
-  std::set<int> pinned;
-  size_t flexible = 0;
-  for (int a : affinities) {
-    if (a < -1) throw std::invalid_argument("invalid image affinity");
-    if (a < 0) ++flexible;
-    else pinned.insert(a);
-  }
-  std::vector<std::string> chosen;
-  std::set<int> freed;
-  std::vector<const RunningGroup*> optional;
-  int optional_gpus = 0;
-  for (const auto& r : running) {
-    bool must = r.rung;
-    for (int gpu : r.group) must = must || pinned.count(gpu);
-    if (must) {
-      freed.insert(r.group.begin(), r.group.end());
-      if (!r.rung) chosen.push_back(r.request_id);
-    } else {
-      optional.push_back(&r);
-      optional_gpus += static_cast<int>(r.group.size());
+  require_disjoint_groups(running);
+  if (std::any_of(affinities.begin(), affinities.end(), [](int a) { return a < -1; }))
+    throw std::invalid_argument("invalid image affinity");
+  const std::set<int> pinned_gpus = [&] {
+    std::set<int> s;
+    for (int a : affinities)
+      if (a >= 0) s.insert(a);
+    return s;
+  }();
+  const size_t any_gpu_images = static_cast<size_t>(std::count(affinities.begin(), affinities.end(), -1));
+
+  std::vector<std::string> out;
+  std::set<int> stopping_gpus;
+  std::vector<size_t> pool;  // groups that may keep running
+  for (size_t i = 0; i < running.size(); ++i) {
+    const RunningGroup& g = running[i];
+    const bool holds_pinned =
+        std::any_of(g.group.begin(), g.group.end(), [&](int gpu) { return pinned_gpus.count(gpu) > 0; });
+    if (!g.rung && !holds_pinned) {
+      pool.push_back(i);
+      continue;
     }
+    stopping_gpus.insert(g.group.begin(), g.group.end());
+    if (!g.rung) out.push_back(g.request_id);
   }
-  size_t spare = 0;
-  for (int gpu : freed) spare += !pinned.count(gpu);
-  if (flexible <= spare) return chosen;
-  const int need = static_cast<int>(std::min<size_t>(flexible - spare, optional_gpus));
-  if (need == 0) return chosen;
-  // min displaced GPU-time to free >= need GPUs (fewer interruptions on ties)
-  struct Cell {
-    double cost = kInf;
-    std::vector<std::string> ids;
-  };
-  std::vector<Cell> dp(optional_gpus + 1);
-  dp[0].cost = 0;
-  for (const RunningGroup* r : optional) {
-    const int w = static_cast<int>(r->group.size());
-    for (int c = optional_gpus - w; c >= 0; --c) {
-      if (!std::isfinite(dp[c].cost)) continue;
-      const double v = dp[c].cost + displaced(*r);
-      Cell& dst = dp[c + w];
-      if (v < dst.cost || (v == dst.cost && dp[c].ids.size() + 1 < dst.ids.size())) {
-        dst = dp[c];
-        dst.cost = v;
-        dst.ids.push_back(r->request_id);
-      }
-    }
-  }
-  int best = need;
-  for (int c = need + 1; c <= optional_gpus; ++c)
-    if (dp[c].cost < dp[best].cost) best = c;
-  chosen.insert(chosen.end(), dp[best].ids.begin(), dp[best].ids.end());
-  return chosen;
+  const size_t free_for_any = static_cast<size_t>(
+      std::count_if(stopping_gpus.begin(), stopping_gpus.end(), [&](int gpu) { return !pinned_gpus.count(gpu); }));
+  if (any_gpu_images <= free_for_any) return out;
+  int pool_gpus = 0;
+  for (size_t i : pool) pool_gpus += static_cast<int>(running[i].group.size());
+  const int shortfall = static_cast<int>(std::min<size_t>(any_gpu_images - free_for_any, pool_gpus));
+  if (shortfall == 0) return out;
+  for (size_t i : cheapest_cover(running, pool, shortfall)) out.push_back(running[i].request_id);
+  return out;
 }
+
+namespace {
+
+// The candidate that displaces the least GPU time; the narrower group on equal time; the
+// first offered on a full tie.
+class CheapestStop {
+ public:
+  void offer(int index, double cost, size_t width) {
+    const bool better = index_ < 0 || cost < cost_ || (cost == cost_ && width < width_);
+    if (!better) return;
+    index_ = index;
+    cost_ = cost;
+    width_ = width;
+  }
+  int index() const { return index_; }
+
+ private:
+  int index_ = -1;
+  double cost_ = 0;
+  size_t width_ = 0;
+};
+
+}  // namespace
 
 DeadlinePreemption select_deadline_preemption(double now_ms, const std::vector<ImageDemand>& waiting,
                                               const std::vector<RunningGroup>& running) {
-  validate_groups(running);
-  auto demand = waiting;
-  for (const auto& d : demand) {
-    if (d.affinity < -1) throw std::invalid_argument("invalid image affinity");
-    preemption_converts_deadline(now_ms, d.deadline_ms, d.service_ms, 0, 0);  // validates
+  require_disjoint_groups(running);
+  for (const auto& img : waiting) {
+    if (img.affinity < -1) throw std::invalid_argument("invalid image affinity");
+    require_preemption_inputs(now_ms, img.deadline_ms, img.service_ms, 0, 0);
   }
-  std::stable_sort(demand.begin(), demand.end(), [](const ImageDemand& a, const ImageDemand& b) {
-    if (a.deadline_ms != b.deadline_ms) return a.deadline_ms < b.deadline_ms;
-    return a.affinity >= 0 && b.affinity < 0;
+  std::vector<const ImageDemand*> queue;
+  for (const auto& img : waiting) queue.push_back(&img);
+  std::stable_sort(queue.begin(), queue.end(), [](const ImageDemand* a, const ImageDemand* b) {
+    if (a->deadline_ms != b->deadline_ms) return a->deadline_ms < b->deadline_ms;
+    return a->affinity >= 0 && b->affinity < 0;
   });
-  auto groups = running;
-  std::set<int> reserved;
+
+  std::vector<bool> rung(running.size());
+  for (size_t i = 0; i < running.size(); ++i) rung[i] = running[i].rung;
+  std::set<int> promised;
   DeadlinePreemption out;
-  for (const auto& d : demand) {
-    auto slot = [&](const RunningGroup& r) {
-      for (int gpu : r.group)
-        if (!reserved.count(gpu) && (d.affinity < 0 || gpu == d.affinity)) return gpu;
+  for (const ImageDemand* img : queue) {
+    // the GPU of group i this image would get, or -1
+    auto usable_gpu = [&](size_t i) {
+      for (int gpu : running[i].group) {
+        if (promised.count(gpu)) continue;
+        if (img->affinity < 0 || gpu == img->affinity) return gpu;
+      }
       return -1;
     };
-    // tight SLOs tolerate a doorbell's own latency on an already-rung group
-    const bool tight = d.deadline_ms >= now_ms + 0.85 * d.service_ms && d.deadline_ms - now_ms <= 1.35 * d.service_ms;
-    auto grace = [&](const RunningGroup& r) { return tight ? std::max(1.5 * r.stop_ms, 120.0) : 0.0; };
-    double boundary = kInf;
-    int reuse = -1;
-    double reuse_at = kInf;
-    for (size_t i = 0; i < groups.size(); ++i) {
-      const auto& r = groups[i];
-      if (slot(r) < 0) continue;
-      const double response = r.rung ? std::min(r.stop_ms, r.remaining_ms) : r.remaining_ms;
-      boundary = std::min(boundary, response);
-      if (r.rung && now_ms + response + d.service_ms <= d.deadline_ms + grace(r) && response < reuse_at) {
-        reuse = static_cast<int>(i);
-        reuse_at = response;
+    const bool tight =
+        img->deadline_ms >= now_ms + 0.85 * img->service_ms && img->deadline_ms - now_ms <= 1.35 * img->service_ms;
+    auto tolerance = [&](size_t i) { return tight ? std::max(1.5 * running[i].stop_ms, 120.0) : 0.0; };
+    auto in_time = [&](size_t i, double response) {
+      return now_ms + response + img->service_ms <= img->deadline_ms + tolerance(i);
+    };
+
+    // a) an already-rung group responding in time
+    double earliest = std::numeric_limits<double>::infinity();
+    int responder = -1;
+    double responder_at = std::numeric_limits<double>::infinity();
+    for (size_t i = 0; i < running.size(); ++i) {
+      if (usable_gpu(i) < 0) continue;
+      const RunningGroup& g = running[i];
+      const double response = rung[i] ? std::min(g.stop_ms, g.remaining_ms) : g.remaining_ms;
+      earliest = std::min(earliest, response);
+      if (rung[i] && in_time(i, response) && response < responder_at) {
+        responder = static_cast<int>(i);
+        responder_at = response;
       }
     }
-    if (reuse >= 0) {
-      reserved.insert(slot(groups[reuse]));
+    if (responder >= 0) {
+      promised.insert(usable_gpu(static_cast<size_t>(responder)));
       continue;
     }
-    int best = -1;
-    double best_cost = kInf;
-    auto consider = [&](size_t i) {
-      const double c = displaced(groups[i]);
-      if (c < best_cost || (c == best_cost && best >= 0 && groups[i].group.size() < groups[best].group.size())) {
-        best = static_cast<int>(i);
-        best_cost = c;
+
+    // b) ring a group, only if waiting for the earliest response is late
+    CheapestStop pick;
+    const bool waiting_is_late =
+        std::isfinite(earliest) && now_ms + earliest + img->service_ms > img->deadline_ms;
+    if (waiting_is_late) {
+      for (size_t i = 0; i < running.size(); ++i) {
+        const RunningGroup& g = running[i];
+        if (rung[i] || usable_gpu(i) < 0) continue;
+        if (preemption_converts_deadline(now_ms, img->deadline_ms, img->service_ms, g.stop_ms, g.remaining_ms))
+          pick.offer(static_cast<int>(i), displaced_gpu_ms(g), g.group.size());
       }
-    };
-    if (std::isfinite(boundary) && now_ms + boundary + d.service_ms > d.deadline_ms) {
-      for (size_t i = 0; i < groups.size(); ++i) {
-        const auto& r = groups[i];
-        if (r.rung || slot(r) < 0) continue;
-        if (preemption_converts_deadline(now_ms, d.deadline_ms, d.service_ms, r.stop_ms, r.remaining_ms)) consider(i);
-      }
-      if (best < 0 && tight) {
-        for (size_t i = 0; i < groups.size(); ++i) {
-          const auto& r = groups[i];
-          if (r.rung || slot(r) < 0 || r.stop_ms >= r.remaining_ms) continue;
-          if (now_ms + std::min(r.stop_ms, r.remaining_ms) + d.service_ms > d.deadline_ms + grace(r)) continue;
-          consider(i);
+      if (pick.index() < 0 && tight) {
+        for (size_t i = 0; i < running.size(); ++i) {
+          const RunningGroup& g = running[i];
+          if (rung[i] || usable_gpu(i) < 0 || g.stop_ms >= g.remaining_ms) continue;
+          if (in_time(i, std::min(g.stop_ms, g.remaining_ms)))
+            pick.offer(static_cast<int>(i), displaced_gpu_ms(g), g.group.size());
         }
       }
     }
-    if (best < 0) {
-      ++out.deadline_skips;
+    if (pick.index() < 0) {
+      ++out.deadline_skips;  // c)
       continue;
     }
-    out.selected.push_back(groups[best].request_id);
-    groups[best].rung = true;
-    reserved.insert(slot(groups[best]));
+    const size_t chosen = static_cast<size_t>(pick.index());
+    out.selected.push_back(running[chosen].request_id);
+    rung[chosen] = true;
+    promised.insert(usable_gpu(chosen));
   }
   return out;
 }

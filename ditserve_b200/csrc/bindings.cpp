@@ -75,6 +75,7 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c10::op
     a.row_batch = row_batch->data_ptr<int>();
   }
   ds::launch_gemm(a, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 void attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
@@ -146,6 +147,7 @@ void attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
     a.v_extra[i] = v_extra[i].data_ptr();
   }
   ds::launch_attention(a, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 void layernorm_modulate(const at::Tensor& x, at::Tensor& y, const c10::optional<at::Tensor>& scale,
@@ -180,6 +182,7 @@ void layernorm_modulate(const at::Tensor& x, at::Tensor& y, const c10::optional<
     a.row_batch = row_batch->data_ptr<int>();
   }
   ds::launch_layernorm_modulate(a, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 void rmsnorm_rope(at::Tensor& x, const c10::optional<at::Tensor>& weight, int64_t width, int64_t groups, double eps,
@@ -208,6 +211,7 @@ void rmsnorm_rope(at::Tensor& x, const c10::optional<at::Tensor>& weight, int64_
   a.rows_per_batch = static_cast<int>(rows_per_batch);
   a.head_dim = static_cast<int>(head_dim);
   ds::launch_rmsnorm_rope(a, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 const float* opt_f32(const c10::optional<at::Tensor>& t) {
@@ -260,6 +264,7 @@ void sched_step(const at::Tensor& cond, const c10::optional<at::Tensor>& uncond,
   a.x0_out = x0_out.has_value() ? const_cast<float*>(opt_f32(x0_out)) : nullptr;
   a.last_out = last_out.has_value() ? const_cast<float*>(opt_f32(last_out)) : nullptr;
   ds::launch_sched_step(a, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 // ---------------------------------------------------------------- symmetric heap + fused collectives
@@ -290,6 +295,22 @@ int64_t symm_open(const py::bytes& handle, int64_t device) {
 
 void symm_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
 
+// Lets kernels on `device` read and write `peer`'s memory directly (one process driving
+// several GPUs, e.g. the single-process peer-memory probes); true when access is on.
+bool peer_enable(int64_t device, int64_t peer) {
+  int can = 0;
+  C10_CUDA_CHECK(cudaDeviceCanAccessPeer(&can, static_cast<int>(device), static_cast<int>(peer)));
+  if (!can) return false;
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  const cudaError_t e = cudaDeviceEnablePeerAccess(static_cast<int>(peer), 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    (void)cudaGetLastError();
+    return true;
+  }
+  C10_CUDA_CHECK(e);
+  return true;
+}
+
 ds::PeerGroup make_group(int64_t rank, const std::vector<int64_t>& bases, int64_t timeout_ns) {
   TORCH_CHECK(!bases.empty() && bases.size() <= static_cast<size_t>(ds::kMaxPeers), "group size out of range");
   TORCH_CHECK(rank >= 0 && rank < static_cast<int64_t>(bases.size()), "rank outside the group");
@@ -308,6 +329,7 @@ void group_barrier(int64_t rank, const std::vector<int64_t>& bases, int64_t time
                    int64_t epoch, const at::Tensor& status) {
   ds::launch_group_barrier(make_group(rank, bases, timeout_ns), static_cast<int>(channel),
                            static_cast<uint64_t>(epoch), status_ptr(status), at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 void cfg_step_peer(const at::Tensor& mine, int64_t theirs_off, int64_t role, double guidance, at::Tensor& sample,
@@ -353,6 +375,7 @@ void cfg_step_peer(const at::Tensor& mine, int64_t theirs_off, int64_t role, dou
   ds::launch_cfg_step_peer(a, make_group(rank, bases, timeout_ns), static_cast<int>(channel),
                            static_cast<uint64_t>(epoch), mine.data_ptr(), theirs_off, static_cast<int>(role),
                            status_ptr(status), at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 void qkv_scatter(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk, double eps,
@@ -379,6 +402,7 @@ void qkv_scatter(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& 
   a.recv_off = recv_off;
   a.pos_base = static_cast<int>(pos_base);
   ds::launch_qkv_scatter(a, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 void attention_scatter(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t batch, int64_t seq,
@@ -420,6 +444,7 @@ void attention_scatter(const at::Tensor& q, const at::Tensor& k, const at::Tenso
     a.v_extra[i] = reinterpret_cast<const void*>(v_extra_ptrs[i]);
   }
   ds::launch_attention(a, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 void allgather_rows(const at::Tensor& src, int64_t dst_off, int64_t rank, const std::vector<int64_t>& bases,
@@ -429,6 +454,7 @@ void allgather_rows(const at::Tensor& src, int64_t dst_off, int64_t rank, const 
   ds::launch_allgather_rows(make_group(rank, bases, timeout_ns), src.data_ptr(),
                             static_cast<int64_t>(src.numel() * src.element_size()), dst_off,
                             at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 void strided_put(const at::Tensor& src, int64_t peer, int64_t dst_off, int64_t rank,
@@ -445,6 +471,7 @@ void strided_put(const at::Tensor& src, int64_t peer, int64_t dst_off, int64_t r
   }
   ds::launch_strided_put(make_group(rank, bases, timeout_ns), static_cast<int>(peer), src.data_ptr(), sl, dst_off,
                          at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 void group_flag(int64_t rank, const std::vector<int64_t>& bases, int64_t timeout_ns, int64_t channel, int64_t epoch,
@@ -454,6 +481,42 @@ void group_flag(int64_t rank, const std::vector<int64_t>& bases, int64_t timeout
   ds::launch_group_flag(make_group(rank, bases, timeout_ns), static_cast<int>(channel), static_cast<uint64_t>(epoch),
                         static_cast<int>(flag), out.data_ptr<int>(), status_ptr(status),
                         at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
+}
+
+ds::RingCodecArgs ring_args(int64_t rows, int64_t heads, int64_t head_dim, int64_t src, int64_t slot_off,
+                           int64_t slot_bytes, int64_t rank, const std::vector<int64_t>& bases, int64_t timeout_ns) {
+  ds::RingCodecArgs a;
+  a.rows = static_cast<int>(rows);
+  a.heads = static_cast<int>(heads);
+  a.head_dim = static_cast<int>(head_dim);
+  a.src = static_cast<int>(src);
+  a.slot_off = slot_off;
+  a.slot_bytes = slot_bytes;
+  a.group = make_group(rank, bases, timeout_ns);
+  return a;
+}
+
+void ring_quant_push(const at::Tensor& kv, int64_t heads, int64_t head_dim, int64_t src, int64_t slot_off,
+                     int64_t slot_bytes, int64_t rank, const std::vector<int64_t>& bases, int64_t timeout_ns) {
+  check_cuda_bf16_2d(kv, "kv");
+  TORCH_CHECK(kv.size(1) >= 2 * heads * head_dim, "ring_quant_push: kv narrower than K and V");
+  const c10::cuda::CUDAGuard guard(kv.device());
+  ds::RingCodecArgs a = ring_args(kv.size(0), heads, head_dim, src, slot_off, slot_bytes, rank, bases, timeout_ns);
+  a.kv = kv.data_ptr();
+  a.kv_stride = kv.stride(0);
+  ds::launch_ring_quant_push(a, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
+}
+
+void ring_dequant(at::Tensor& out, int64_t heads, int64_t head_dim, int64_t src, int64_t slot_off, int64_t slot_bytes,
+                  int64_t rank, const std::vector<int64_t>& bases, int64_t timeout_ns) {
+  check_cuda_bf16_2d(out, "out");
+  TORCH_CHECK(out.size(1) >= 3 * heads * head_dim, "ring_dequant: out must be [rows, >= 3*heads*head_dim]");
+  const c10::cuda::CUDAGuard guard(out.device());
+  ds::RingCodecArgs a = ring_args(out.size(0), heads, head_dim, src, slot_off, slot_bytes, rank, bases, timeout_ns);
+  ds::launch_ring_dequant(a, static_cast<int>(src), out.data_ptr(), out.stride(0), at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 void put_peers(const at::Tensor& src, int64_t mask, int64_t dst_off, int64_t rank, const std::vector<int64_t>& bases,
@@ -463,6 +526,7 @@ void put_peers(const at::Tensor& src, int64_t mask, int64_t dst_off, int64_t ran
   ds::launch_put_peers(make_group(rank, bases, timeout_ns), static_cast<unsigned>(mask), src.data_ptr(),
                        static_cast<int64_t>(src.numel() * src.element_size()), dst_off,
                        at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
 }  // namespace
@@ -478,6 +542,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_alloc", &symm_alloc, "allocate a zeroed symmetric heap and its IPC handle");
   m.def("symm_open", &symm_open, "open a peer heap from its IPC handle");
   m.def("symm_close", &symm_close);
+  m.def("peer_enable", &peer_enable, "enable direct access from one device to a peer's memory (same process)");
   m.def("group_barrier", &group_barrier, "bounded flag barrier over peer memory");
   m.def("cfg_step_peer", &cfg_step_peer, "CFG exchange over NVLink fused with guidance + latent update");
   m.def("qkv_scatter", &qkv_scatter, "RMS qk-norm + RoPE + Ulysses all-to-all scatter");
@@ -486,6 +551,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("strided_put", &strided_put, "strided slice -> contiguous buffer of a group member (halo exchange)");
   m.def("group_flag", &group_flag, "doorbell flag MAX over a peer group (one launch, bounded waits)");
   m.def("put_peers", &put_peers, "copy a buffer into several group members' heaps");
+  m.def("ring_quant_push", &ring_quant_push, "INT8-quantize this rank's ring K/V chunk into every ring peer's slot");
+  m.def("ring_dequant", &ring_dequant, "dequantize one peer's INT8 ring slot into a local bf16 [rows, 3w] buffer");
+  m.def("ring_slot_bytes", &ds::ring_slot_bytes, "bytes of one INT8 ring slot");
   m.attr("FLAG_BYTES") = ds::kFlagBytes;
   m.attr("MAX_PEERS") = ds::kMaxPeers;
   m.attr("CHANNELS") = ds::kChannels;

@@ -84,20 +84,17 @@ __global__ void group_barrier_kernel(PeerGroup g, int channel, uint64_t epoch, i
 }
 
 // ---------------------------------------------------------------------------
-// CFG exchange + guidance + latent update.  Block 0 signals the partner; every
-// block waits for the partner's signal before it reads the partner's prediction.
+// CFG exchange + guidance + latent update.  Every block signals the partner (the
+// same epoch, an idempotent release store) and then waits for the partner's
+// signal before it reads the partner's prediction.  No block depends on another
+// block of its own grid, so the exchange completes whatever subset of the grid
+// happens to be resident on either GPU.
 __global__ void __launch_bounds__(256) cfg_step_peer_kernel(SchedStepArgs a, PeerGroup g, int channel,
                                                             uint64_t epoch, const void* mine, int64_t theirs_off,
                                                             int my_role, int* status) {
   __shared__ int ok_s;
   if (threadIdx.x < 32) {
-    bool ok = true;
-    if (blockIdx.x == 0) {
-      ok = warp_barrier(g, channel, epoch, status, 320);
-    } else if ((threadIdx.x & 31) < g.size && (threadIdx.x & 31) != g.rank) {
-      ok = wait_flag(g.flags[g.rank] + channel * kMaxPeers + (threadIdx.x & 31), epoch, g.timeout_ns, status, 321);
-    }
-    ok = __all_sync(0xffffffffu, ok);
+    const bool ok = warp_barrier(g, channel, epoch, status, 320);
     if (threadIdx.x == 0) ok_s = ok ? 1 : 0;
   }
   __syncthreads();

@@ -185,6 +185,19 @@ struct StridedSlice {
 void launch_strided_put(const PeerGroup& g, int peer, const void* src, const StridedSlice& sl, int64_t dst_off,
                         cudaStream_t s);
 // MAX of a 0/1 flag over the group (out: 0/1, or -1 after a peer timeout).
+// ---- INT8 ring K/V transport (ring_codec.cu) ----
+struct RingCodecArgs {
+  const void* kv = nullptr;  // bf16 rows: K at column 0, V at column heads*head_dim (row stride kv_stride)
+  int64_t kv_stride = 0;
+  int rows = 0, heads = 0, head_dim = 128;
+  int src = 0;               // slot index of this rank's packet (its position in the ring group)
+  int64_t slot_off = 0;      // heap offset of slot 0 in every member
+  int64_t slot_bytes = 0;    // >= ring_slot_bytes(rows, heads, head_dim)
+  PeerGroup group;           // the ring group
+};
+int64_t ring_slot_bytes(int rows, int heads, int head_dim);
+void launch_ring_quant_push(const RingCodecArgs& a, cudaStream_t s);
+void launch_ring_dequant(const RingCodecArgs& a, int src, void* out, int64_t out_stride, cudaStream_t s);
 void launch_group_flag(const PeerGroup& g, int channel, uint64_t epoch, int flag, int* out, int* status,
                        cudaStream_t s);
 // Copy `bytes` (16-byte multiple) from src to offset dst_off of every member in `mask`.

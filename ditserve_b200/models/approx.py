@@ -13,8 +13,10 @@
   Works for the Wan block stack (``run_wan``) and the SD3.5 joint blocks
   (``SD35Transformer.forward_packed(..., cache=...)`` through ``run_blocks``; the cache is
   reset whenever the packed batch's composition changes).
-* ``int8 ring codec`` — per-token, per-head symmetric INT8 with an fp16 scale for KV
-  packets exchanged between ring ranks (128 bf16 = 256 B -> 128 B + 2 B).
+* ``int8 ring codec`` — per-token, per-head symmetric INT8 with an fp32 scale for the K/V
+  chunks exchanged between ring ranks (128 bf16 = 256 B -> 128 B + 4 B); the codec itself,
+  its anchor-step schedule and both transports live in ``parallel.ring_codec``; these
+  helpers are its torch statement.
 Reference: workers/ditserve/models/wan/cfg_reuse.py:19-411, taylor_cache.py:27-179,
 ring_quant.py:18-171, models/sd35_cache.py:8-286.
 """
@@ -142,22 +144,18 @@ class BlockResidualCache:
 
 
 def quantize_int8(x: torch.Tensor, head_dim: int):
-    """[..., H*D] -> (int8 [..., H*D], fp16 scale [..., H]) per token and head."""
-    shp = x.shape
-    h = shp[-1] // head_dim
-    xf = x.float().reshape(*shp[:-1], h, head_dim)
-    scale = xf.abs().amax(-1).clamp_min(1e-8) / 127.0
-    q = torch.round(xf / scale[..., None]).clamp(-127, 127).to(torch.int8)
-    return q.reshape(shp), scale.to(torch.float16)
+    """Ring K/V codec, encode side (see ``parallel.ring_codec``)."""
+    from ..parallel.ring_codec import RingInt8Codec
+    return RingInt8Codec.encode(x, head_dim)
 
 
 def dequantize_int8(q: torch.Tensor, scale: torch.Tensor, head_dim: int, dtype=torch.bfloat16):
-    shp = q.shape
-    h = shp[-1] // head_dim
-    x = q.float().reshape(*shp[:-1], h, head_dim) * scale.float()[..., None]
-    return x.reshape(shp).to(dtype)
+    """Ring K/V codec, decode side (see ``parallel.ring_codec``)."""
+    from ..parallel.ring_codec import RingInt8Codec
+    return RingInt8Codec.decode(q, scale, head_dim, dtype)
 
 
 def packet_bytes(tokens: int, heads: int, head_dim: int, int8: bool) -> int:
-    per = heads * (head_dim + 2) if int8 else heads * head_dim * 2
-    return tokens * per
+    """Bytes of ``tokens`` x ``heads`` vectors of one of K or V on the wire."""
+    from ..parallel.ring_codec import RingInt8Codec
+    return RingInt8Codec.wire_bytes(tokens, heads, head_dim, int8) // 2

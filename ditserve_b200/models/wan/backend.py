@@ -11,6 +11,7 @@ Reference: workers/ditserve/models/wan/backend.py:12-652.
 """
 from __future__ import annotations
 
+import json
 import math
 import os
 import time
@@ -79,6 +80,9 @@ class WanBackend(Backend):
         key = (ranks, form.name, shape, path)
         if path == "nccl-fp8" and request.get("fp8_layers") is not None:
             key += (tuple(sorted(int(i) for i in request["fp8_layers"])),)
+        codec = request.get("ring_codec", self.config.get("ring_codec"))
+        if codec is not None and form.ring > 1:
+            key += (("ring_codec", json.dumps(codec, sort_keys=True)),)
         if st is not None and st.block != 0 and st.layout_key not in (None, key):
             raise ValueError("the SP group may change only at a solver-step boundary")
         if key not in self._layouts:
@@ -93,7 +97,8 @@ class WanBackend(Backend):
                 rank = dist.get_rank()
                 pctx, plan = build_parallel(layout, rank, self.device, attention=path,
                                             seq_local=self.engine.cfg.tokens(shape) // form.sp, cfg=self.engine.cfg,
-                                            pred_numel=math.prod(shape), fp8_layers=request.get("fp8_layers"))
+                                            pred_numel=math.prod(shape), fp8_layers=request.get("fp8_layers"),
+                                            ring_codec=codec)
                 flag = None
                 if form.sp > 1:  # doorbell stop agreed over the SP group (MAX of the ranks' flags)
                     sp = layout.sp_ranks(rank)

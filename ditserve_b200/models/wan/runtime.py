@@ -212,6 +212,8 @@ class WanEngine:
 
     # ------------------------------------------------------------------ block executor
     def _begin(self, st: WanRequestState):
+        if hasattr(self.pctx, "set_step"):
+            self.pctx.set_step(st.step, st.spec.steps)  # step-aware collectives (ring codec anchors)
         br, lat, t, ctx = self._inputs(st)
         st.packets["pk"] = self.model.begin(lat, t, ctx, self.pctx)
         st.packets["branches"] = br

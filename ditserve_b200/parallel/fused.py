@@ -21,7 +21,7 @@ import torch
 from ..ops._ext import ext, kernel, status_word
 from .symm import PeerGroup, SymmetricHeap
 
-CH_SP, CH_CFG, CH_GATHER, CH_USP_ADDR = 0, 1, 2, 3
+CH_SP, CH_CFG, CH_GATHER, CH_USP_ADDR, CH_RING = 0, 1, 2, 3, 8
 
 
 class FusedUlysses:
@@ -72,10 +72,13 @@ class FusedUlysses:
 
 class FusedUSP(FusedUlysses):
     """Ulysses x ring (2D USP): heads exchanged inside the U-group, keys/values of the ring
-    peers read in place by the attention mainloop (multi-source TMA over peer memory)."""
+    peers read in place by the attention mainloop (multi-source TMA over peer memory, no
+    multicast).  With an active INT8 ring codec the peers' chunks come instead as int8
+    packets pushed into this rank's heap (``ring_quant_push``) and decoded locally
+    (``ring_dequant``) before the same attention kernel reads them."""
 
     def __init__(self, heap: SymmetricHeap, sp_members: tuple, ring: int, seq_local: int, heads: int, head_dim: int,
-                 batch: int, gather_cols: int = 64):
+                 batch: int, gather_cols: int = 64, codec=None):
         P = len(sp_members)
         U = P // ring
         m = sp_members.index(heap.rank)
@@ -94,20 +97,57 @@ class FusedUSP(FusedUlysses):
         self.gather_off, self.gathered = heap.alloc_view((P * batch * seq_local, gather_cols))
         self.gather_cols = gather_cols
         self.group = self.sp_group
+        self.codec = codec
+        if codec is not None:
+            # INT8 ring transport: one packet slot per ring source in every ring member's heap,
+            # and local bf16 buffers (receive-buffer layout) for the decoded peer chunks
+            rows = batch * chunk
+            self.ring_group = PeerGroup(heap, tuple(self.ring_members), CH_RING)
+            self.slot_bytes = int(ext().ring_slot_bytes(rows, hl, head_dim))
+            self.slot_off = heap.alloc(ring * self.slot_bytes, align=256)
+            self.decoded = torch.empty((ring - 1, rows, 3 * hl * head_dim), device=heap.device, dtype=torch.bfloat16)
+
+    def set_step(self, step: int, total_steps: int):
+        if self.codec is not None:
+            self.codec.set_step(step, total_steps)
+
+    def _int8_ring_sources(self, w, st):
+        """Quantize this rank's K/V chunk into every ring peer's slot, then decode the peers'
+        slots locally; returns the decoded chunks' K and V addresses in ring order."""
+        rg = self.ring_group
+        r, bases, tmo = rg.args()
+        hl = self.heads // self.U
+        kernel("ring_quant_push")(self.recv[:, w:], hl, self.head_dim, r, self.slot_off, self.slot_bytes, r, bases,
+                                  tmo)
+        rg.barrier(st)
+        k_extra, v_extra = [], []
+        others = [i for i in range(self.R) if i != r]
+        for buf, src in zip(self.decoded, others):
+            kernel("ring_dequant")(buf, hl, self.head_dim, src, self.slot_off, self.slot_bytes, r, bases, tmo)
+            k_extra.append(buf.data_ptr() + w * 2)
+            v_extra.append(buf.data_ptr() + 2 * w * 2)
+        self.codec.account(self.recv.shape[0], hl, self.head_dim, True, self.R - 1)
+        return k_extra, v_extra
 
     def fused_qkv_attention(self, qkv, wq, wk, eps, cos_full, sin_full, heads, batch, seq_local):
         st = status_word(qkv.device)
         ur, ub, utmo = self.ugroup.args()
         chunk = seq_local * self.U
         kernel("qkv_scatter")(qkv, wq, wk, float(eps), cos_full, sin_full, seq_local, heads, self.head_dim, ur, ub,
-                          utmo, self.recv_off, self.r * chunk)
+                              utmo, self.recv_off, self.r * chunk)
         self.sp_group.barrier(st)
         hl = heads // self.U
         w = hl * self.head_dim
         q, k, v = self.recv[:, :w], self.recv[:, w:2 * w], self.recv[:, 2 * w:]
-        peers = [m for m in self.ring_members if m != self.heap.rank]
-        k_extra = [self.heap.bases[m] + self.recv_off + w * 2 for m in peers]
-        v_extra = [self.heap.bases[m] + self.recv_off + 2 * w * 2 for m in peers]
+        if self.codec is not None and self.codec.active:
+            k_extra, v_extra = self._int8_ring_sources(w, st)
+        else:
+            # bf16: the attention mainloop reads the ring peers' chunks in place (TMA, no multicast)
+            peers = [m for m in self.ring_members if m != self.heap.rank]
+            k_extra = [self.heap.bases[m] + self.recv_off + w * 2 for m in peers]
+            v_extra = [self.heap.bases[m] + self.recv_off + 2 * w * 2 for m in peers]
+            if self.codec is not None:
+                self.codec.account(self.recv.shape[0], hl, self.head_dim, False, self.R - 1)
         kernel("attention_scatter")(q, k, v, batch, chunk, hl, self.head_dim, 1.0 / math.sqrt(self.head_dim), ur, ub,
                                 utmo, self.o_off, seq_local, self.u * hl, heads * self.head_dim, st, k_extra,
                                 v_extra)
@@ -160,7 +200,7 @@ class FusedCFG:
 
 
 def upgrade(layout, rank, device, pctx, cfg_plan, sp_groups, cfg_groups, seq_local=None, cfg=None,
-            heap_bytes: int | None = None, pred_numel: int | None = None):
+            heap_bytes: int | None = None, pred_numel: int | None = None, codec=None):
     """Replace the NCCL plans of ``build_parallel`` by fused peer-memory ones (same layout)."""
     if device.type != "cuda" or cfg is None or seq_local is None:
         return pctx, cfg_plan
@@ -173,6 +213,8 @@ def upgrade(layout, rank, device, pctx, cfg_plan, sp_groups, cfg_groups, seq_loc
         hl = cfg.heads // form.ulysses
         need += batch * seq_local * form.ulysses * 3 * hl * cfg.head_dim * 2 + batch * seq_local * cfg.dim * 2
         need += P * batch * seq_local * cfg.out_channels * 4 * 2
+        if form.ring > 1 and codec is not None:
+            need += form.ring * int(ext().ring_slot_bytes(batch * seq_local * form.ulysses, hl, cfg.head_dim)) + 4096
     pred_numel = pred_numel or 8 * 1024 * 1024
     need += 2 * pred_numel * 2  # double-buffered bf16 prediction slots
     from .runtime import group_for
@@ -184,7 +226,7 @@ def upgrade(layout, rank, device, pctx, cfg_plan, sp_groups, cfg_groups, seq_loc
         return tuple(hidx[r] for r in ranks)
     if P > 1 and form.ring > 1:
         pctx = FusedUSP(heap, h(layout.sp_ranks(rank)), form.ring, seq_local, cfg.heads, cfg.head_dim, batch,
-                        gather_cols=cfg.out_channels * math.prod(cfg.patch))
+                        gather_cols=cfg.out_channels * math.prod(cfg.patch), codec=codec)
     elif P > 1:
         pctx = FusedUlysses(heap, h(layout.sp_ranks(rank)), seq_local, cfg.heads, cfg.head_dim, batch,
                             gather_cols=cfg.out_channels * math.prod(cfg.patch))

@@ -65,9 +65,10 @@ class CFGExchangeNCCL:
 class UlyssesRingNCCL(UlyssesNCCL):
     """NCCL baseline of Ulysses x ring: all-to-all inside the U-group, then the ring
     group's key/value chunks gathered and attended to in one pass (the exact result of a
-    ring rotation with log-sum-exp merging)."""
+    ring rotation with log-sum-exp merging).  With an INT8 ring codec active for the step,
+    the chunks travel as int8 values plus fp32 scales (``parallel.ring_codec``)."""
 
-    def __init__(self, sp_group, u_group, ring_group, sp_size, sp_rank, ulysses, ring):
+    def __init__(self, sp_group, u_group, ring_group, sp_size, sp_rank, ulysses, ring, codec=None):
         self.group = u_group
         self.u_size = ulysses
         self.sp_group = sp_group
@@ -76,6 +77,30 @@ class UlyssesRingNCCL(UlyssesNCCL):
         self.sp_size = sp_size          # the model shards the sequence over the whole SP group
         self.sp_rank = sp_rank
         self.sp_size_total = sp_size
+        self.ring_rank = sp_rank // ulysses
+        self.codec = codec              # parallel.ring_codec.RingInt8Codec or None
+
+    def set_step(self, step: int, total_steps: int):
+        if self.codec is not None:
+            self.codec.set_step(step, total_steps)
+
+    def _gather_ring_kv(self, kv: torch.Tensor, hd: int) -> torch.Tensor:
+        """All ring members' [B, chunk, 2, w] key/value chunks, stacked on a new leading axis."""
+        parts = torch.empty((self.ring, *kv.shape), device=kv.device, dtype=kv.dtype)
+        if self.codec is None or not self.codec.active:
+            dist.all_gather_into_tensor(parts.view(self.ring * kv.shape[0], *kv.shape[1:]), kv, group=self.ring_group)
+            if self.codec is not None:
+                self.codec.account(kv.shape[0] * kv.shape[1], kv.shape[-1] // hd, hd, False, self.ring - 1)
+            return parts
+        q8, sc = self.codec.encode(kv, hd)
+        q_all = torch.empty((self.ring, *q8.shape), device=kv.device, dtype=q8.dtype)
+        s_all = torch.empty((self.ring, *sc.shape), device=kv.device, dtype=sc.dtype)
+        dist.all_gather_into_tensor(q_all.view(self.ring * q8.shape[0], *q8.shape[1:]), q8, group=self.ring_group)
+        dist.all_gather_into_tensor(s_all.view(self.ring * sc.shape[0], *sc.shape[1:]), sc, group=self.ring_group)
+        parts.copy_(self.codec.decode(q_all, s_all, hd, kv.dtype))
+        parts[self.ring_rank] = kv  # the local chunk stays exact
+        self.codec.account(kv.shape[0] * kv.shape[1], kv.shape[-1] // hd, hd, True, self.ring - 1)
+        return parts
 
     def self_attention_qkv(self, qkv, heads, batch, seq_local):
         U = self.u_size
@@ -89,8 +114,7 @@ class UlyssesRingNCCL(UlyssesNCCL):
         else:
             chunk = qkv.view(batch, seq_local, 3, heads * hd)
         kv = chunk[:, :, 1:].contiguous()
-        parts = torch.empty((self.ring, *kv.shape), device=kv.device, dtype=kv.dtype)
-        dist.all_gather_into_tensor(parts.view(self.ring * kv.shape[0], *kv.shape[1:]), kv, group=self.ring_group)
+        parts = self._gather_ring_kv(kv, hd)
         keys = parts.permute(1, 0, 2, 3, 4).reshape(batch, self.ring * U * seq_local, 2, hl * hd)
         o = ops.attention(chunk[:, :, 0], keys[:, :, 0], keys[:, :, 1], hl)
         if U == 1:

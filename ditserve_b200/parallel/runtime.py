@@ -7,6 +7,8 @@ engine.  ``attention="nccl"`` is the NCCL baseline; ``attention="nccl-fp8"`` is 
 path with FP8 payloads on the Ulysses all-to-alls (``parallel.fp8_comms``; plain Ulysses
 forms, ``fp8_layers`` picks the blocks, None = all); ``attention="fused"`` uses the
 peer-memory kernels of ``parallel.fused`` when they are available for the layout.
+``ring_codec`` ("int8" or a dict of ``RingInt8Codec`` options) sends the ring key/value
+chunks of ring forms as int8 packets outside the bf16 anchor steps, on either path.
 """
 from __future__ import annotations
 
@@ -37,7 +39,8 @@ def group_for(ranks):
 
 
 def build_parallel(layout: FixedLayout, rank: int, device: torch.device, attention: str = "fused",
-                   seq_local: int | None = None, cfg=None, pred_numel: int | None = None, fp8_layers=None):
+                   seq_local: int | None = None, cfg=None, pred_numel: int | None = None, fp8_layers=None,
+                   ring_codec=None):
     if attention not in ("fused", "nccl", "nccl-fp8"):
         raise ValueError(f"unknown collective path {attention!r}")
     form = layout.form
@@ -57,10 +60,14 @@ def build_parallel(layout: FixedLayout, rank: int, device: torch.device, attenti
         ring_groups[rg] = group_for(rg)
     pctx = LocalAttention()
     cfg_plan = CFGLocal()
+    codec = None
+    if form.ring > 1 and ring_codec is not None:
+        from .ring_codec import make_codec
+        codec = make_codec(ring_codec)
     if form.sp > 1 and form.ring > 1:
         pctx = UlyssesRingNCCL(sp_groups[my_sp], u_groups[layout.ulysses_ranks(rank)],
                                ring_groups[layout.ring_ranks(rank)], form.sp, layout.sp_rank(rank), form.ulysses,
-                               form.ring)
+                               form.ring, codec=codec)
     elif form.sp > 1 and attention == "nccl-fp8":
         from .fp8_comms import FP8UlyssesNCCL
         pctx = FP8UlyssesNCCL(sp_groups[my_sp], form.sp, layout.sp_rank(rank), layers=fp8_layers)
@@ -77,5 +84,5 @@ def build_parallel(layout: FixedLayout, rank: int, device: torch.device, attenti
             fused = None
         if fused is not None:
             pctx, cfg_plan = fused.upgrade(layout, rank, device, pctx, cfg_plan, sp_groups, cfg_groups,
-                                           seq_local=seq_local, cfg=cfg, pred_numel=pred_numel)
+                                           seq_local=seq_local, cfg=cfg, pred_numel=pred_numel, codec=codec)
     return pctx, cfg_plan

@@ -60,7 +60,7 @@ def test_int8_ring_codec():
     q, s = quantize_int8(x, 128)
     y = dequantize_int8(q, s, 128)
     assert _cos(x.float(), y.float()) > 0.999
-    assert packet_bytes(1, 1, 128, True) == 130 and packet_bytes(1, 1, 128, False) == 256
+    assert packet_bytes(1, 1, 128, True) == 132 and packet_bytes(1, 1, 128, False) == 256
 
 
 def test_sd35_block_cache_reuse():

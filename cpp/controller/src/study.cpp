@@ -486,6 +486,9 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
   // decode: finished videos run the VAE in chunked quanta (decode_start / decode_poll) and
   // images decode in finish; off: finish persists the final latents only
   const bool decode = phase.flag("decode", false);
+  // decode_parallel: a finished video decodes on the group that ran its last step, patch
+  // parallel (every member decodes its rows, halo rows over peer memory), in one quantum
+  const bool decode_parallel = decode && phase.flag("decode_parallel", false);
   const size_t trace_limit = static_cast<size_t>(phase.integer("trace_limit", 2000));
   auto is_gpu = [](const Json& d) { return d.at("backend").as_string() != "mock"; };
 
@@ -1031,6 +1034,10 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
         // a chunked decode continues on the worker that holds it
         if (!image && !l.decode_ticket.empty() && l.decode_gpu >= 0 && grp != std::vector<int>{l.decode_gpu})
           grp = std::vector<int>{l.decode_gpu};
+        // a patch-parallel decode takes the group of the video's last step
+        if (!image && decode_parallel && l.decode_ticket.empty() && l.steps_done >= l.steps_total &&
+            !l.last_group.empty() && distributed)
+          grp = l.last_group;
         bool free = true;
         for (int g : grp) free = free && !busy[g];
         if (!free) continue;
@@ -1157,6 +1164,29 @@ Json run_cluster(const Json& phase, const StudyOptions& opt, const std::string& 
                            if (qs == "finish") {
                              if (!decode) {
                                ms.push_back(member(ids[0], Json(), true, finish_release(ids[0], exec, false)));
+                               out["members"] = ms;
+                               return out;
+                             }
+                             if (decode_parallel && distributed && exec.size() > 1) {
+                               // every member decodes its rows; the video is gathered on each
+                               std::vector<Json> rs = fan_out(exec, [&](int g) {
+                                 Json ds = Json::object();
+                                 ds["state_id"] = ids[0];
+                                 ds["group"] = lranks(grp);
+                                 const std::string t = call(g, false, "decode_start", ds).at("ticket").as_string();
+                                 Json dp = Json::object();
+                                 dp["ticket"] = t;
+                                 dp["wait"] = true;
+                                 dp["output_mode"] = "digest";
+                                 return call(g, false, "decode_poll", dp);
+                               });
+                               Json rel = Json::object();
+                               rel["state_id"] = ids[0];
+                               fan_out(exec, [&](int g) { return call(g, false, "release", rel); });
+                               const Json& art = rs[0].get("artifact");
+                               Json digest = art.is_object() && art.contains("array_sha256") ? art.at("array_sha256")
+                                                                                            : rs[0].get("value");
+                               ms.push_back(member(ids[0], Json(), true, digest));
                                out["members"] = ms;
                                return out;
                              }

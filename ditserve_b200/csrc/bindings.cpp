@@ -32,7 +32,7 @@ int* status_ptr(const at::Tensor& status) {
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c10::optional<at::Tensor>& bias,
           int64_t epilogue, const c10::optional<at::Tensor>& R, const c10::optional<at::Tensor>& gate,
           int64_t gate_stride, int64_t rows_per_batch, const at::Tensor& status, int64_t bn_override,
-          const c10::optional<at::Tensor>& row_batch) {
+          const c10::optional<at::Tensor>& row_batch, int64_t cta_pair) {
   check_cuda_bf16_2d(A, "A");
   check_cuda_bf16_2d(B, "B");
   check_cuda_bf16_2d(C, "C");
@@ -69,6 +69,7 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const c10::op
   a.rows_per_batch = static_cast<int>(rows_per_batch);
   a.status = status_ptr(status);
   a.bn_override = static_cast<int>(bn_override);
+  a.cta_pair = static_cast<int>(cta_pair);
   if (row_batch.has_value()) {
     TORCH_CHECK(row_batch->scalar_type() == at::kInt && row_batch->numel() >= A.size(0) && row_batch->is_cuda(),
                 "gemm: row_batch must be int32 CUDA with one entry per row");
@@ -484,6 +485,49 @@ void group_flag(int64_t rank, const std::vector<int64_t>& bases, int64_t timeout
   C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
+void conv(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& bias,
+          const c10::optional<at::Tensor>& residual, int64_t kt, int64_t kh, int64_t kw, int64_t pad_h, int64_t pad_w,
+          const at::Tensor& status, int64_t bn_override) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 4 && x.is_contiguous(),
+              "conv: x must be contiguous bf16 [T, H, W, C]");
+  TORCH_CHECK(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.dim() == 4 && y.is_contiguous(),
+              "conv: y must be contiguous bf16 [T, H, W, C_out]");
+  TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kBFloat16 && w.dim() == 2 && w.is_contiguous(),
+              "conv: w must be contiguous bf16 [C_out_pad, KT*KH*KW*C_in]");
+  TORCH_CHECK(w.size(1) == kt * kh * kw * x.size(3), "conv: weight K does not match the kernel and C_in");
+  TORCH_CHECK(y.size(0) == x.size(0) - kt + 1 && y.size(1) == x.size(1) + 2 * pad_h - kh + 1 &&
+                  y.size(2) == x.size(2) + 2 * pad_w - kw + 1 && y.size(3) <= w.size(0),
+              "conv: output shape mismatch");
+  if (bias.has_value())
+    TORCH_CHECK(bias->is_contiguous() && bias->scalar_type() == at::kBFloat16 && bias->numel() == w.size(0),
+                "conv: bias must be contiguous bf16 [C_out_pad]");
+  if (residual.has_value())
+    TORCH_CHECK(residual->is_contiguous() && residual->scalar_type() == at::kBFloat16 && residual->sizes() == y.sizes(),
+                "conv: residual must be contiguous bf16 shaped like y");
+  const c10::cuda::CUDAGuard guard(x.device());
+  ds::ConvArgs a;
+  a.X = x.data_ptr();
+  a.W = w.data_ptr();
+  a.Y = y.data_ptr();
+  a.bias = opt_ptr(bias);
+  a.R = opt_ptr(residual);
+  a.T_in = static_cast<int>(x.size(0));
+  a.H_in = static_cast<int>(x.size(1));
+  a.W_in = static_cast<int>(x.size(2));
+  a.C_in = static_cast<int>(x.size(3));
+  a.C_out = static_cast<int>(y.size(3));
+  a.C_out_pad = static_cast<int>(w.size(0));
+  a.KT = static_cast<int>(kt);
+  a.KH = static_cast<int>(kh);
+  a.KW = static_cast<int>(kw);
+  a.pad_h = static_cast<int>(pad_h);
+  a.pad_w = static_cast<int>(pad_w);
+  a.status = status_ptr(status);
+  a.bn_override = static_cast<int>(bn_override);
+  ds::launch_conv(a, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
+}
+
 ds::RingCodecArgs ring_args(int64_t rows, int64_t heads, int64_t head_dim, int64_t src, int64_t slot_off,
                            int64_t slot_bytes, int64_t rank, const std::vector<int64_t>& bases, int64_t timeout_ns) {
   ds::RingCodecArgs a;
@@ -551,6 +595,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("strided_put", &strided_put, "strided slice -> contiguous buffer of a group member (halo exchange)");
   m.def("group_flag", &group_flag, "doorbell flag MAX over a peer group (one launch, bounded waits)");
   m.def("put_peers", &put_peers, "copy a buffer into several group members' heaps");
+  m.def("conv", &conv, "implicit-GEMM convolution, channels-last (tcgen05/TMEM)");
   m.def("ring_quant_push", &ring_quant_push, "INT8-quantize this rank's ring K/V chunk into every ring peer's slot");
   m.def("ring_dequant", &ring_dequant, "dequantize one peer's INT8 ring slot into a local bf16 [rows, 3w] buffer");
   m.def("ring_slot_bytes", &ds::ring_slot_bytes, "bytes of one INT8 ring slot");

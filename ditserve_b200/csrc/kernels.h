@@ -43,6 +43,7 @@ struct GemmArgs {
   int* status = nullptr;  // device status word pair (code, site)
   int num_sms = 0;        // 0: all SMs of the current device
   int bn_override = 0;    // 0: heuristic
+  int cta_pair = -1;      // CTA-pair (cta_group::2) kernel: 1 on, 0 off, -1 default (DS_GEMM_PAIR, else on)
 };
 void launch_gemm(const GemmArgs& a, cudaStream_t stream);
 int gemm_pick_bn(int M, int N);
@@ -185,6 +186,21 @@ struct StridedSlice {
 void launch_strided_put(const PeerGroup& g, int peer, const void* src, const StridedSlice& sl, int64_t dst_off,
                         cudaStream_t s);
 // MAX of a 0/1 flag over the group (out: 0/1, or -1 after a peer timeout).
+// ---- implicit-GEMM convolution, channels-last (conv.cu) ----
+struct ConvArgs {
+  const void* X = nullptr;   // [T_in, H_in, W_in, C_in] bf16
+  const void* W = nullptr;   // [C_out_pad, KT*KH*KW*C_in] bf16 (tap-major, then C_in)
+  void* Y = nullptr;         // [T_out, H_out, W_out, C_out] bf16
+  const void* bias = nullptr;  // bf16 [C_out_pad] or null
+  const void* R = nullptr;     // residual, Y's layout, or null
+  int T_in = 0, H_in = 0, W_in = 0, C_in = 0, C_out = 0, C_out_pad = 0;
+  int KT = 1, KH = 3, KW = 3, pad_h = 1, pad_w = 1;
+  int* status = nullptr;
+  int bn_override = 0;
+};
+int conv_pick_bn(int c_out_pad);
+void launch_conv(const ConvArgs& a, cudaStream_t stream);
+
 // ---- INT8 ring K/V transport (ring_codec.cu) ----
 struct RingCodecArgs {
   const void* kv = nullptr;  // bf16 rows: K at column 0, V at column heads*head_dim (row stride kv_stride)

@@ -12,9 +12,14 @@ from __future__ import annotations
 import torch
 
 from .vae import ChunkedDecode, WanVAEDecoder
+from .vae_fast import FastChunkedDecode
 
 
 class AsyncDecoder:
+    """On a GPU the decode runs channels-last on the implicit-GEMM tcgen05 convolution
+    (``vae_fast``); on the CPU it runs the module's fp32 NCDHW statement.  ``halo`` (a
+    ``vae_fast.HaloCL`` over the decode group) splits every frame's rows over the group."""
+
     def __init__(self, vae: WanVAEDecoder, device):
         self.vae = vae
         self.device = torch.device(device)
@@ -23,7 +28,12 @@ class AsyncDecoder:
         self.jobs: dict = {}
         self.counter = 0
 
-    def start(self, latents: torch.Tensor, chunked: bool = False) -> str:
+    def _job(self, z, halo):
+        if self.cuda or halo is not None:
+            return FastChunkedDecode(self.vae, z, halo)
+        return ChunkedDecode(self.vae, z)
+
+    def start(self, latents: torch.Tensor, chunked: bool = False, halo=None) -> str:
         self.counter += 1
         ticket = f"decode-{self.counter}"
         if self.cuda:
@@ -31,18 +41,18 @@ class AsyncDecoder:
             ready.record(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self.stream):
                 self.stream.wait_event(ready)
-                z = latents.clone()
+                job = self._job(latents.clone(), halo)
                 if chunked:
-                    job = ChunkedDecode(self.vae, z)
                     self.jobs[ticket] = dict(chunked=job, event=None)
                     return ticket
-                out = self.vae.decode(z)
+                out = job.step(1 << 30).result()
                 done = torch.cuda.Event()
                 done.record(self.stream)
             self.jobs[ticket] = dict(out=out, event=done)
         else:
-            self.jobs[ticket] = dict(out=self.vae.decode(latents), event=None) if not chunked else \
-                dict(chunked=ChunkedDecode(self.vae, latents), event=None)
+            job = self._job(latents, halo)
+            self.jobs[ticket] = dict(chunked=job, event=None) if chunked else \
+                dict(out=job.step(1 << 30).result(), event=None)
         return ticket
 
     def advance(self, ticket: str, frames: int = 1) -> bool:

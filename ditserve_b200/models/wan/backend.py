@@ -45,6 +45,7 @@ class WanBackend(Backend):
         self.transfer_dir = Path(transfer_dir(config))
         self.layout = None
         self._decoder = None
+        self._decode_halos: dict = {}
         self.decodes: dict = {}
         self._comm: dict = {}
         self._layouts: dict = {}
@@ -128,15 +129,41 @@ class WanBackend(Backend):
             self._decoder = AsyncDecoder(vae, self.device)
         return self._decoder
 
+    def _decode_halo(self, group):
+        """Row halo of a patch-parallel decode over ``group`` (global ranks), cached per group:
+        peer-memory stores into the neighbours' halo slots on GPUs, send/recv otherwise."""
+        key = tuple(sorted(int(r) for r in group))
+        if key not in self._decode_halos:
+            from ...parallel.runtime import group_for
+            from .vae_fast import NCCLHaloCL, PeerHaloCL
+            g = group_for(key)
+            if self.device.type == "cuda" and self.config.get("decode_halo", "peer") == "peer":
+                from ...parallel.fused import PeerHalo
+                from ...parallel.symm import SymmetricHeap
+                elems = int(self.config.get("decode_halo_elems", 4 << 20))
+                heap = SymmetricHeap(4 * elems * 4 + (1 << 20), self.device, group=g)
+                halo = PeerHaloCL(PeerHalo(heap, tuple(range(len(key))), max_halo_elems=elems), group=g)
+            else:
+                halo = NCCLHaloCL(g)
+            self._decode_halos[key] = halo
+        return self._decode_halos[key]
+
     def decode_start(self, request):
-        """Decode a finished request's latent on the side stream (Wan2.1 or Wan2.2 VAE)."""
+        """Decode a finished request's latent on the side stream (Wan2.1 or Wan2.2 VAE).
+
+        With ``group`` (global ranks, every member calling with the same request) the decode is
+        patch parallel: each member decodes its rows of every frame, completing each 3-high
+        convolution's input with one halo row from each neighbour, and the finished video is
+        gathered on every member."""
         st = self.state(request)
         if not st.done:
             raise ValueError("decode requires a completed state")
         if self.engine.cfg.in_channels not in (16, 48):
             raise ValueError("no VAE for this latent width")
         dec = self._async_decoder()
-        ticket = dec.start(st.latents, chunked=bool(request.get("chunked", False)))
+        group = request.get("group")
+        halo = self._decode_halo(group) if group is not None and len(group) > 1 else None
+        ticket = dec.start(st.latents, chunked=bool(request.get("chunked", False)), halo=halo)
         self.decodes[ticket] = request["state_id"]
         return dict(ticket=ticket, ready=False, state_id=request["state_id"])
 

@@ -2,6 +2,7 @@
 ``ditserve_b200._C``; CPU tensors run the fp32 PyTorch statement of the same op."""
 from ._ext import KernelTimeout, KernelTimer, available, check_status, ext, kernel, launch_counts, status_word
 from .attention import attention, attention_reference, attention_segments, segment_table, segments_reference
+from .conv import conv_bias, conv_cl, conv_cl_reference, conv_weight_2d
 from .gemm import linear, linear_reference
 from .norm import (layernorm_modulate, layernorm_modulate_reference, rms_norm_reference, rmsnorm_rope_,
                    rope_reference)
@@ -9,7 +10,7 @@ from .sched import sched_step, sched_step_reference
 
 __all__ = [
     "KernelTimeout", "KernelTimer", "available", "check_status", "ext", "kernel", "launch_counts", "status_word",
-    "attention", "attention_reference", "attention_segments", "segment_table", "segments_reference", "linear", "linear_reference",
+    "attention", "attention_reference", "conv_bias", "conv_cl", "conv_cl_reference", "conv_weight_2d", "attention_segments", "segment_table", "segments_reference", "linear", "linear_reference",
     "layernorm_modulate", "layernorm_modulate_reference", "rms_norm_reference", "rmsnorm_rope_",
     "rope_reference", "sched_step", "sched_step_reference",
 ]

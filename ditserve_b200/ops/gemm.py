@@ -58,7 +58,7 @@ def linear_reference(x, w, b=None, act=None, residual=None, gate=None, rows_per_
 def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None, *, act: str | None = None,
            residual: torch.Tensor | None = None, gate: torch.Tensor | None = None,
            rows_per_batch: int | None = None, out: torch.Tensor | None = None,
-           bn: int = 0, row_batch: torch.Tensor | None = None) -> torch.Tensor:
+           bn: int = 0, row_batch: torch.Tensor | None = None, pair: int = -1) -> torch.Tensor:
     if not use_kernels(x, w):
         y = linear_reference(x, w, b, act, residual, gate, rows_per_batch, row_batch)
         if out is not None:
@@ -92,5 +92,5 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None, *, a
             raise ValueError("gate must have unit column stride")
         gate_stride = gate.stride(0) if gate.shape[0] > 1 else 0
     kernel("gemm")(x2, w, out2, b, epi, r2, gate, gate_stride, int(rows_per_batch or M),
-                   status_word(x.device), bn, row_batch)
+                   status_word(x.device), bn, row_batch, int(pair))
     return out2.reshape(*shape[:-1], N)

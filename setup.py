@@ -30,6 +30,7 @@ ext = CUDAExtension(
         os.path.join(CSRC, "comm.cu"),
         os.path.join(CSRC, "noalloc.cu"),
         os.path.join(CSRC, "ring_codec.cu"),
+        os.path.join(CSRC, "conv.cu"),
     ],
     include_dirs=[os.path.join(HERE, CSRC)],
     extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},

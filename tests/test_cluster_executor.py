@@ -297,3 +297,35 @@ def test_two_node_worlds_through_the_bridge(controller, tmp_path, bridge_daemon)
     assert all(set(g) <= {0, 1} or set(g) <= {2, 3} for g in groups), groups
     assert any(set(g) == {2, 3} for g in groups), groups       # the remote node ran a 2-rank group
     assert all(r.get("digest") for r in last["rows"])  # CFG2 groups: equal up to the drift gate, not bitwise
+
+
+def test_patch_parallel_decode_in_a_gloo_world(controller, tmp_path):
+    """decode_parallel: a finished video decodes on the group of its last step, every member
+    decoding its rows with halo exchange (the row-split decode equals the single-rank one to
+    fp32 rounding: tests/test_wan_vae_fast.py), and every member ends with the same video."""
+    def study(parallel, port):
+        return {"schema": "ditserve-b200.study.v1", "experiment": f"exec-ppdecode-{parallel}",
+                "workers": {"wan": {"backend": "wan", "config": {"model": "wan-tiny", "device": "cpu",
+                                                                 "transfer_dir": str(tmp_path)}}},
+                "budget": BUDGET,
+                "phases": [{"id": "cluster", "kind": "cluster", "gpus": 2, "policy": "static-sp2", "worker": "wan",
+                            "distributed": True, "sp_transport": "collective", "collectives": "nccl",
+                            "decode": True, "decode_parallel": parallel, "dist_port": port,
+                            "generator": {"count": 1, "seed": 4, "pattern": "offline_all", "classes": [
+                                {"weight": 1, "kind": "video", "class": "wan21_480p", "service_ms": 20000,
+                                 "slo_scale": 5, "spec": {"height": 64, "width": 64, "frames": 5, "steps": 2,
+                                                          "guidance": 5.0}}]},
+                            "gates": [{"pointer": "/last/summary/completed", "op": "==", "value": 1}]}]}
+    base = 30000 + os.getpid() % 1000
+    for parallel in (False, True):
+        sub = tmp_path / ("pp" if parallel else "single")
+        sub.mkdir()
+        rep, _ = _run(controller, study(parallel, base + (7 if parallel else 0)), sub, allow_gpu=True)
+        assert rep["phases"]["cluster"]["gates"]["pass"], rep["phases"]["cluster"]
+        last = _last(rep)
+        assert not last["failures"], last["failures"]
+        fin = [t for t in last["trace"] if t["quantum"] == "finish"]
+        assert fin, last["trace"]
+        if parallel:
+            assert any(len(t.get("group") or []) == 2 for t in fin), fin
+        assert last["rows"][0]["digest"]

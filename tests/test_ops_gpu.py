@@ -44,6 +44,34 @@ def test_gemm_epilogues(M, N, K, epi):
     torch.testing.assert_close(y.cpu().float(), ref.float(), rtol=3e-2, atol=3e-2)
 
 
+@pytest.mark.parametrize("M,N,K", [(300, 256, 192), (129, 128, 64), (1000, 1536, 1536), (2049, 384, 4104)])
+@pytest.mark.parametrize("epi", ["none", "gelu", "gated", "res"])
+def test_gemm_cta_pair_epilogues(M, N, K, epi):
+    """The CTA-pair (cta_group::2, 256-row tiles) kernel forced on, against the fp32 statement:
+    M tails that leave the second CTA of a pair partly or wholly outside the matrix, both pair
+    tile widths (N % 256 and N % 128), and a K tail."""
+    torch.manual_seed(5)
+    d = _dev()
+    x = torch.randn(M, K, device=d).bfloat16()
+    w = (torch.randn(N, K, device=d) / math.sqrt(K)).bfloat16()
+    b = torch.randn(N, device=d).bfloat16()
+    kw = {}
+    if epi == "gelu":
+        kw["act"] = "gelu"
+    if epi in ("gated", "res"):
+        kw["residual"] = torch.randn(M, N, device=d).bfloat16()
+    if epi == "gated":
+        kw["gate"] = torch.randn(2, N, device=d)
+        kw["rows_per_batch"] = (M + 1) // 2
+    y = ops.linear(x, w, b, pair=1, **kw)
+    ops.check_status(d)
+    ref = ops.linear_reference(x.cpu(), w.cpu(), b.cpu(), **{k: (v.cpu() if torch.is_tensor(v) else v)
+                                                              for k, v in kw.items()})
+    assert _rel(y.cpu(), ref) < 1e-2
+    single = ops.linear(x, w, b, pair=0, **kw)
+    assert _rel(y.cpu(), single.cpu()) < 1e-2
+
+
 @pytest.mark.parametrize("bn", [64, 128, 256])
 def test_gemm_tile_widths(bn):
     torch.manual_seed(1)
@@ -235,3 +263,22 @@ def test_attention_multi_source_kv_equals_concatenated(sources):
     ref = ops.attention_reference(q.cpu(), torch.cat([k.cpu() for k in ks], 1), torch.cat([v.cpu() for v in vs], 1), H)
     ops.check_status(d)
     assert _rel(o.cpu(), ref) < 2e-2
+
+
+@pytest.mark.parametrize("B,Sq,Sk,H", [(2, 300, 300, 2), (1, 129, 1030, 1)])
+def test_attention_split_row_variant(B, Sq, Sk, H):
+    """The split-row softmax (two warps per S row, DS_ATTN_ROWSPLIT=2) in a child process, since
+    the switch is read once per process."""
+    import subprocess
+    import sys
+    code = (
+        "import torch;from ditserve_b200 import ops\n"
+        f"torch.manual_seed(3);d=torch.device('cuda',0);B,Sq,Sk,H={B},{Sq},{Sk},{H}\n"
+        "q=torch.randn(B,Sq,H*128,device=d).bfloat16();k=torch.randn(B,Sk,H*128,device=d).bfloat16()\n"
+        "v=torch.randn(B,Sk,H*128,device=d).bfloat16();o=ops.attention(q,k,v,H);ops.check_status(d)\n"
+        "r=ops.attention_reference(q.cpu(),k.cpu(),v.cpu(),H)\n"
+        "rel=((o.cpu().float()-r.float()).norm()/r.float().norm()).item();print(rel);assert rel<2e-2,rel\n")
+    import os
+    env = dict(os.environ, DS_ATTN_ROWSPLIT="2")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr

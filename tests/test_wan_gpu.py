@@ -148,9 +148,10 @@ def test_fused_ulysses_kernels_as_a_one_member_group(heads, hd, seq):
 SENTINEL = 1024.0  # exactly representable in bf16, far outside what the ops write here
 
 
+@pytest.mark.parametrize("pair", [0, 1])
 @pytest.mark.parametrize("M,N,K,epi", [(300, 192, 200, "none"), (129, 256, 72, "gelu"), (1000, 384, 1536, "res"),
                                        (77, 512, 4104, "gated")])
-def test_gemm_leaves_the_guard_band_untouched(M, N, K, epi):
+def test_gemm_leaves_the_guard_band_untouched(M, N, K, epi, pair):
     dev = torch.device("cuda", 0)
     torch.manual_seed(M)
     x = torch.randn(M, K, device=dev).bfloat16()
@@ -165,7 +166,7 @@ def test_gemm_leaves_the_guard_band_untouched(M, N, K, epi):
         kw["residual"] = torch.randn(M, N, device=dev).bfloat16()
     if epi == "gated":
         kw["gate"] = torch.randn(1, N, device=dev)
-    ops.linear(x, w, b, out=out, **kw)
+    ops.linear(x, w, b, out=out, pair=pair, **kw)
     torch.cuda.synchronize()
     ops.check_status(dev)
     band = buf.clone()

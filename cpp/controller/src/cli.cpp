@@ -6,7 +6,7 @@
 //     plan < state.json                        one cluster_plan decision
 //     simulate [--config P] [--count N] [--seed N] [--policy ID]...
 //     run --config P [--run-id ID] [--work-dir P] [--ledger P] [--phase ID] [--resume]
-//     results finalize|verify|inspect PATH | results compact ROOT DEST
+//     results finalize|verify|inspect|cleanup PATH | results compact ROOT DEST
 //         [--allow-gpu] [--repair]
 //     report RUN_DIR                           summaries of a finished run
 //     rpc generate|simulate|control|plan|policies|run|simulate-study < request.json
@@ -135,7 +135,8 @@ int usage(std::ostream& os) {
         "  simulate [--config P] [--count N] [--seed N] [--policy ID]...\n"
         "  run --config P [--run-id ID] [--work-dir P] [--ledger P] [--phase ID] [--resume] [--allow-gpu] [--repair]\n"
         "  report RUN_DIR\n"
-        "  results finalize|verify|inspect PATH [--title T] | results compact ROOT DEST [--prune-raw]\n"
+        "  results finalize RUN_DIR [--output DEST] [--title T] [--v1] | results verify|inspect PATH\n"
+        "  results cleanup RUN_DIR --whitelist GLOB [...] [--dry-run] | results compact ROOT DEST [--prune-raw]\n"
         "  rpc generate|simulate|control|plan|policies|run|simulate-study < request.json\n";
   return 2;
 }
@@ -259,13 +260,22 @@ int command_main(int argc, char** argv) {
         if (rest.size() < 4) throw UsageError("results compact needs ROOT and DEST");
         req["destination"] = rest[3];
         i = 4;
-      } else if (op != "finalize" && op != "verify" && op != "inspect") {
-        throw UsageError("results operation must be finalize, verify, inspect or compact");
+      } else if (op != "finalize" && op != "verify" && op != "inspect" && op != "cleanup") {
+        throw UsageError("results operation must be finalize, verify, inspect, compact or cleanup");
       }
+      Json whitelist = Json::array();
       for (; i < rest.size(); ++i) {
         if (rest[i] == "--title" && i + 1 < rest.size()) req["title"] = rest[++i];
+        else if (rest[i] == "--output" && i + 1 < rest.size()) req["destination"] = rest[++i];
+        else if (rest[i] == "--v1") req["format"] = "v1";
         else if (rest[i] == "--prune-raw") req["prune_raw"] = true;
+        else if (rest[i] == "--whitelist" && i + 1 < rest.size()) whitelist.push_back(rest[++i]);
+        else if (rest[i] == "--dry-run") req["dry_run"] = true;
         else throw UsageError("unknown results option " + rest[i]);
+      }
+      if (op == "cleanup") {
+        if (whitelist.as_array().empty()) throw UsageError("results cleanup needs at least one --whitelist GLOB");
+        req["whitelist"] = whitelist;
       }
       std::map<std::string, std::string> env;
       if (!opt.package_root.empty()) env["PYTHONPATH"] = opt.package_root;
@@ -299,8 +309,12 @@ int command_main(int argc, char** argv) {
       throw UsageError("unknown command " + cmd);
     }
     std::cout << (as_json ? out.dump() : out.dump(1)) << "\n";
-    if (out.is_object() && out.contains("status") && out.at("status").is_string() && out.at("status").as_string() != "ok")
-      return 1;
+    if (out.is_object() && out.contains("status") && out.at("status").is_string()) {
+      // a run reports "ok"; results operations report what they did (finalized, cleaned, dry-run)
+      // or why they did nothing (protected, deferred): the latter exit 1
+      const std::string st = out.at("status").as_string();
+      if (st != "ok" && st != "finalized" && st != "cleaned" && st != "dry-run") return 1;
+    }
     return 0;
   } catch (const UsageError& e) {
     std::cerr << "usage error: " << e.what() << "\n";

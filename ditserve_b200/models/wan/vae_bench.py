@@ -1,12 +1,17 @@
-"""Wan VAE decode: single GPU vs patch-parallel (NCCL halo baseline vs peer-memory halo).
+"""Wan VAE decode timing: the tcgen05 conv path vs cuDNN, one GPU and row-split over N GPUs.
 
     python -m ditserve_b200.models.wan.vae_bench                      # 1 GPU
-    torchrun --nproc-per-node N -m ditserve_b200.models.wan.vae_bench   # N GPUs, split along W
+    torchrun --nproc-per-node N -m ditserve_b200.models.wan.vae_bench   # N GPUs, rows split
 
 Decodes a Wan2.1 480p latent (16 x 21 x 60 x 104 -> 3 x 81 x 480 x 832, bf16, random
-weights).  Multi-GPU runs check that both transports give the same video as each other
-and report device time (max over ranks).  The reference decodes on rank 0 only
-(6.91 s for this tier on A100).
+weights; ``DS_VAE_FRAMES`` latent frames).  One GPU: the module's NCDHW decode (convolutions
+by cuDNN through torch, the library baseline) against the channels-last decode on this
+package's implicit-GEMM convolution, with their relative L2 difference.  N GPUs: the
+channels-last decode with each rank decoding 60 / N latent rows, halo rows exchanged through
+NCCL send/recv or stored straight into the neighbours' heap slots; both transports must give
+the same video.  Times are CUDA events around the whole decode, after one warm-up decode of
+two latent frames, max over ranks.  The reference decodes on rank 0 only (6.91 s for this
+tier on A100).
 """
 from __future__ import annotations
 
@@ -17,7 +22,25 @@ from datetime import timedelta
 import torch
 import torch.distributed as dist
 
-from .vae import PatchParallel, WanVAEDecoder, split_latent
+from .vae import WanVAEDecoder
+from .vae_fast import FastDecoder, NCCLHaloCL, PeerHaloCL
+
+
+def _timed(fn, dev, world):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    out = fn()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return out, round(ms, 2)
 
 
 def main():
@@ -30,38 +53,28 @@ def main():
     vae = WanVAEDecoder.random_init(device=dev, dtype=torch.bfloat16, seed=1)
     g = torch.Generator().manual_seed(2)
     z = torch.randn(1, 16, frames, 60, 104, generator=g).to(dev, torch.bfloat16)
-    results = {}
-    if world > 1:
+    results, outs = {}, {}
+    if world == 1:
+        for name, fn in (("cudnn_ncdhw", lambda zz: vae.decode(zz)),
+                         ("ours_channels_last", lambda zz: FastDecoder(vae).decode(zz))):
+            fn(z[:, :, :2])  # warm-up (cuDNN autotune, allocator, weight layouts)
+            outs[name], results[name] = _timed(lambda: fn(z), dev, 1)
+        a, b = outs["ours_channels_last"].float(), outs["cudnn_ncdhw"].float()
+        results["rel_l2_ours_vs_cudnn"] = round(((a - b).norm() / b.norm()).item(), 5)
+    else:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-        base = PatchParallel(axis=4)
         from ...parallel.fused import PeerHalo
         from ...parallel.symm import SymmetricHeap
-        heap = SymmetricHeap(64 << 20, dev)
-        peer = PeerHalo(heap, tuple(range(world)), axis=4, baseline=base)
-        halos = {"nccl": base, "peer": peer}
-    else:
-        halos = {"single": None}
-    outs = {}
-    for name, halo in halos.items():
-        zl = split_latent(z, halo) if halo is not None else z
-        vae.decode(zl[:, :, :2], halo)  # warm-up (cuDNN autotune, allocator)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        out = vae.decode(zl, halo)
-        e.record()
-        torch.cuda.synchronize()
-        ms = s.elapsed_time(e)
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        results[name] = round(ms, 2)
-        outs[name] = out
-    if world > 1:
-        same = torch.equal(outs["nccl"], outs["peer"])
+        heap = SymmetricHeap(80 << 20, dev)
+        halos = {"nccl_halo": NCCLHaloCL(), "peer_halo": PeerHaloCL(PeerHalo(heap, tuple(range(world)),
+                                                                             max_halo_elems=4 << 20))}
+        rows = z.shape[3] // world
+        zl = z[:, :, :, rank * rows:(rank + 1) * rows].contiguous()
+        for name, halo in halos.items():
+            fd = FastDecoder(vae, halo)
+            fd.decode(zl[:, :, :2])
+            outs[name], results[name] = _timed(lambda: fd.decode(zl), dev, world)
+        same = torch.equal(outs["nccl_halo"], outs["peer_halo"])
         flag = torch.tensor([1 if same else 0], device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         results["transports_bitwise_equal"] = bool(flag.item())

@@ -66,18 +66,35 @@ def test_mock_study_end_to_end(controller, tmp_path):
 
 
 def test_results_cli(controller, tmp_path):
-    run = tmp_path / "runs" / "r1"
+    """results finalize publishes a v2 summary + report, verify checks it, cleanup removes a
+    whitelisted raw file only after publication, and the v1 format stays writable and readable."""
+    run = tmp_path / "work" / "r1"
     run.mkdir(parents=True)
+    (run / "run.json").write_text(json.dumps({"run_id": "r1", "identity": "abc", "config": {"experiment": "e"},
+                                              "code": {}}))
     (run / "phase-a.json").write_text(json.dumps({"status": "ok", "last": {"summary": {"slo_attainment": 1.0}},
                                                   "gates": {"pass": True}}))
+    (run / "raw.bin").write_bytes(b"\x00" * 8)
     env = dict(os.environ, DITSERVE_PYTHON=sys.executable, DITSERVE_PACKAGE_ROOT=ROOT)
-    fin = subprocess.run([controller, "--json", "results", "finalize", str(run), "--title", "t"], capture_output=True,
-                         text=True, env=env, timeout=300)
+
+    def cli(*args):
+        return subprocess.run([controller, "--json", "results", *args], capture_output=True, text=True, env=env,
+                              timeout=300)
+    dest = tmp_path / "published"
+    fin = cli("finalize", str(run), "--output", str(dest), "--title", "t")
     assert fin.returncode == 0, fin.stderr
-    assert json.loads(fin.stdout)["phases"]["a"]["summary"]["slo_attainment"] == 1.0
-    ver = subprocess.run([controller, "--json", "results", "verify", str(run)], capture_output=True, text=True,
-                         env=env, timeout=300)
+    assert json.loads(fin.stdout)["status"] == "finalized"
+    ver = cli("verify", str(dest))
     assert ver.returncode == 0 and json.loads(ver.stdout)["ok"]
+    dry = cli("cleanup", str(run), "--whitelist", "*.bin", "--dry-run")
+    assert [c["file"] for c in json.loads(dry.stdout)["would_delete"]] == ["raw.bin"]
+    out = cli("cleanup", str(run), "--whitelist", "*.bin")
+    assert json.loads(out.stdout)["reclaimed_bytes"] == 8 and not (run / "raw.bin").exists()
+    old = tmp_path / "old"
+    old.mkdir()
+    (old / "phase-a.json").write_text(json.dumps({"status": "ok"}))
+    assert cli("finalize", str(old), "--v1").returncode == 0
+    assert json.loads(cli("verify", str(old)).stdout)["format"] == "v1"
     bad = subprocess.run([controller, "results", "explode", str(run)], capture_output=True, text=True, env=env)
     assert bad.returncode == 2
 

@@ -42,10 +42,10 @@ def test_results_archive(tmp_path):
     (run / "phase-a.json").write_text(json.dumps({"status": "ok", "last": {"summary": {"slo_attainment": 0.9}},
                                                   "gates": {"pass": True}}))
     (run / "raw.bin").write_bytes(b"\x00" * 10)
-    s = finalize(run, date="20261201")
+    s = finalize(run, date="20261201", format="v1")  # the previous archive format, still writable
     assert s["phases"]["a"]["summary"]["slo_attainment"] == 0.9
     assert (run / "20261201-r1.md").exists()
-    assert verify(run)["ok"] and inspect(run)["files"] == 2
+    assert verify(run)["ok"] and verify(run)["format"] == "v1" and inspect(run)["files"] == 2
     (run / "raw.bin").write_bytes(b"\x01" * 10)
     assert verify(run)["altered"] == ["raw.bin"]
     with pytest.raises(ResultsError):

@@ -8,6 +8,9 @@
 * ``kineto_summary`` — aggregate GPU kernel time by name from a torch.profiler chrome trace.
 * ``nsys_gpu_metrics`` — per-device busy time, top kernels, copies and NVTX ranges from an Nsight
   Systems SQLite export.
+Submodules: ``vbench`` (generation protocol, video export and the pinned official evaluator),
+``datasets`` (VBench / VidProM / DiffusionDB prompt manifests from local files, dev / test roles),
+``collectives`` (all-to-all bandwidth microbench of the communication backend).
 Reference: workers/ditserve/evaluation/{quality.py:39-125, artifacts.py:186-345, datasets.py,
 cuda_profile.py}.
 """

@@ -74,18 +74,9 @@ struct AttnParams {
 // shared memory) and only then rescales O (when needed): the S row and the O chunks are
 // never live together and the 168-register budget of a 384-thread CTA holds without
 // spills.  Shared memory holds Q_A, Q_B and two stages each of K and V.
-//
-// Split-row mode (kHalves = 2): each S row is shared by two softmax warps of the same TMEM
-// lane quarter, one per 64-key half, so every SMSP runs two independent softmax streams of
-// a tile instead of one and the per-row chain (TMEM load, max, exponentials, P store) halves.
-// The halves swap their partial row maxima through shared memory (an mbarrier per tile and
-// lane quarter, bounded waits), keep partial row sums, rescale and store their own half of O,
-// and add the two sums once at the end.  18 warps: 0 producer, 1 MMA, 2-17 softmax.
 constexpr int kAttn2Threads = 384;
 
-__host__ __device__ constexpr int attn_threads(int halves) { return halves == 2 ? 576 : 384; }
-
-template <int D, int kHalves = 1>
+template <int D>
 struct Attn2Cfg {
   static constexpr int kAtoms = D / 64;
   static constexpr int kQBytes = kQT * D * 2;
@@ -93,10 +84,7 @@ struct Attn2Cfg {
   static constexpr int kVBytes = kKT * D * 2;
   static constexpr int KS = 2;
   static constexpr int VS = 2;
-  // split-row exchange: row maxima [2 parities][2 tiles][2 halves][128 rows], row sums [2][2][128]
-  static constexpr int kRedBytes = kHalves == 2 ? (2 * 2 * 2 * kQT + 2 * 2 * kQT) * 4 : 0;
-  static constexpr int kSmemBytes =
-      2 * kQBytes + KS * kKBytes + VS * kVBytes + 1024 /*align*/ + 512 /*barriers*/ + kRedBytes;
+  static constexpr int kSmemBytes = 2 * kQBytes + KS * kKBytes + VS * kVBytes + 1024 /*align*/ + 512 /*barriers*/;
   static constexpr int kTmemCols = 512;
 };
 
@@ -114,11 +102,14 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   return r;
 }
 
-template <int D, int kHalves>
-__global__ void __launch_bounds__(attn_threads(kHalves), 1)
+// kPChunks: the softmax hands P to the MMA warp in this many column chunks (one mbarrier
+// phase per chunk), so the PV MMA of the first keys starts while the exponentials of the
+// last keys are still being computed.
+template <int D, int kPChunks>
+__global__ void __launch_bounds__(kAttn2Threads, 1)
     attention2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ KvMaps kv,
                       AttnParams p) {
-  using Cfg = Attn2Cfg<D, kHalves>;
+  using Cfg = Attn2Cfg<D>;
   constexpr int KS = Cfg::KS;
   constexpr int VS = Cfg::VS;
   const int h = blockIdx.y;
@@ -177,13 +168,10 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
   uint64_t* v_full = k_empty + KS;
   uint64_t* v_empty = v_full + VS;
   uint64_t* s_full = v_empty + VS;  // [2] per tile
-  uint64_t* p_full = s_full + 2;    // [2]
-  uint64_t* pv_done = p_full + 2;   // [2]
-  uint64_t* xbar = pv_done + 2;     // [2 tiles][4 lane quarters] split-row exchange
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 8);
+  uint64_t* p_full = s_full + 2;    // [2 tiles][kPChunks]
+  uint64_t* pv_done = p_full + 2 * kPChunks;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* red_max = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512);  // split-row only
-  float* red_l = red_max + 2 * 2 * 2 * kQT;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -201,10 +189,9 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128 * kHalves);
       mbar_init(&pv_done[i], 1);
     }
-    for (int i = 0; i < 8; ++i) mbar_init(&xbar[i], 64);
+    for (int i = 0; i < 2 * kPChunks; ++i) mbar_init(&p_full[i], 128);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -268,15 +255,20 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
         umma_commit(&s_full[t]);
       };
       auto issue_pv = [&](int t, int j) -> bool {
-        if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, 222 + t)) return false;
-        tc_fence_after();
         const uint32_t d = tmem_base + 256 + t * 128;
         const uint32_t p_tmem = tmem_base + t * kKT;  // bf16 P packed over the first 64 S columns
         const uint32_t v_base = smem_u32(sV + (j % VS) * Cfg::kVBytes);
+        constexpr int kPerChunk = kKT / 16 / kPChunks;  // K=16 MMAs per P chunk
 #pragma unroll
-        for (int kk = 0; kk < kKT / 16; ++kk) {
-          const uint64_t db = umma_desc_sw128(v_base + kk * (16 * 128), kKT * 128, 1024);
-          umma_bf16_ts(d, p_tmem + kk * 8, db, idesc_o, (j | kk) != 0);
+        for (int c = 0; c < kPChunks; ++c) {
+          if (!mbar_wait(&p_full[t * kPChunks + c], j & 1, abort_flag, p.status, 222 + t)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int i = 0; i < kPerChunk; ++i) {
+            const int kk = c * kPerChunk + i;
+            const uint64_t db = umma_desc_sw128(v_base + kk * (16 * 128), kKT * 128, 1024);
+            umma_bf16_ts(d, p_tmem + kk * 8, db, idesc_o, (j | kk) != 0);
+          }
         }
         umma_commit(&pv_done[t]);
         return true;
@@ -308,23 +300,14 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
         }
       }
     }
-  } else if (kHalves == 2 ? warp >= 2 : warp >= 4) {
-    // ---------------- softmax warps ----------------
-    // kHalves 1: warpgroup 1 -> tile A, 2 -> B.  kHalves 2: warps 2-17 in groups of four
-    // consecutive warps (every lane quarter once): group g -> tile g / 2, key half g % 2.
-    constexpr int kCols = kKT / kHalves;   // S columns (keys) per thread
-    constexpr int kOCols = D / kHalves;     // O columns rescaled and stored per thread
-    const int sw = warp - (kHalves == 2 ? 2 : 4);
-    const int t = kHalves == 2 ? (sw >> 3) : (sw >> 2);
-    const int hh = kHalves == 2 ? ((sw >> 2) & 1) : 0;
-    const int col0 = hh * kCols;
+  } else if (wg >= 1) {
+    // ---------------- softmax warpgroups (tile t = wg - 1) ----------------
+    const int t = wg - 1;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_col = tmem_base + lane_addr + t * kKT;
-    const uint32_t o_col = tmem_base + lane_addr + 256 + t * 128 + hh * kOCols;
-    uint64_t* my_xbar = &xbar[t * 4 + quarter];
-    uint32_t xuse = 0;  // completed phases of my_xbar
+    const uint32_t o_col = tmem_base + lane_addr + 256 + t * 128;
     const float sl2 = p.scale_log2;
     const uint64_t sl2x2 = f2_pack(sl2, sl2);
     float m_run = -INFINITY;
@@ -336,41 +319,28 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
         break;
       }
       tc_fence_after();
-      const int valid = ktile_valid(j) - col0;  // this thread's columns >= valid are outside the segment
-      const bool masked = valid < kCols;
-      // one pass over TMEM: the thread's S columns into registers
-      uint32_t s[kCols];
+      const int valid = ktile_valid(j);  // columns >= valid are outside the segment
+      const bool masked = valid < kKT;
+      // one pass over TMEM: the thread's whole 128-column S row into registers
+      uint32_t s[kKT];
 #pragma unroll
-      for (int c = 0; c < kCols / 32; ++c)
-        tmem_ld32(s_col + col0 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+      for (int c = 0; c < kKT / 32; ++c)
+        tmem_ld32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
       float mx = -INFINITY;
       if (masked) {
 #pragma unroll
-        for (int c = 0; c < kCols; ++c)
+        for (int c = 0; c < kKT; ++c)
           if (c < valid) mx = fmaxf(mx, __uint_as_float(s[c]));
       } else {
         float mc[8];  // eight independent chains keep the dependent max sequence short
 #pragma unroll
         for (int i = 0; i < 8; ++i) mc[i] = __uint_as_float(s[i]);
 #pragma unroll
-        for (int c = 8; c < kCols; c += 8)
+        for (int c = 8; c < kKT; c += 8)
 #pragma unroll
           for (int i = 0; i < 8; ++i) mc[i] = fmaxf(mc[i], __uint_as_float(s[c + i]));
         mx = fmaxf(fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3])), fmaxf(fmaxf(mc[4], mc[5]), fmaxf(mc[6], mc[7])));
-      }
-      if constexpr (kHalves == 2) {
-        // swap partial maxima with the other half of the row (double-buffered by tile parity);
-        // both halves have their S in registers after this, so P may overwrite S columns
-        float* slot = red_max + ((j & 1) * 2 + t) * (2 * kQT);
-        slot[hh * kQT + row] = mx;
-        mbar_arrive(my_xbar);
-        if (!mbar_wait(my_xbar, xuse & 1, abort_flag, p.status, 236 + t)) {
-          ok = false;
-          break;
-        }
-        ++xuse;
-        mx = fmaxf(mx, slot[(1 - hh) * kQT + row]);
       }
       const float m_new = fmaxf(m_run, mx);
       const bool need = (m_new - m_run) * sl2 > 8.0f;  // always true on the first tile
@@ -392,6 +362,7 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
       const float neg = -m_run * sl2;
       const uint64_t negx2 = f2_pack(neg, neg);
       float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // per-column-slot partial row sums
+      int signalled = 0;  // P chunks (of 8 columns) already handed to the MMA warp
       // exponentials, row sum, bf16 P into tensor memory; masked tiles
       // (a segment's last) take their own loop so the common tile carries no column tests.
       // (Moving a quarter or half of the exponentials to an FMA-pipe polynomial measured
@@ -405,11 +376,11 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
         pk8[q + 1] = pack_bf16x2(e8[2], e8[3]);
         pk8[q + 2] = pack_bf16x2(e8[4], e8[5]);
         pk8[q + 3] = pack_bf16x2(e8[6], e8[7]);
-        if (ch & 1) tmem_st8(s_col + col0 / 2 + (ch >> 1) * 8, pk8);
+        if (ch & 1) tmem_st8(s_col + (ch >> 1) * 8, pk8);
       };
       if (masked) {
 #pragma unroll
-        for (int ch = 0; ch < kCols / 8; ++ch) {
+        for (int ch = 0; ch < kKT / 8; ++ch) {
           float e8[8];
 #pragma unroll
           for (int e = 0; e < 8; e += 2) {
@@ -427,8 +398,11 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
           p_chunk(ch, e8);
         }
       } else {
+        // with no O rescale pending in this warp (the common case), each finished P chunk is
+        // handed to the MMA warp at once; otherwise all chunks go after the rescale below
+        const bool early = kPChunks > 1 && !(j > 0 && __any_sync(0xffffffffu, need));
 #pragma unroll
-        for (int ch = 0; ch < kCols / 8; ++ch) {
+        for (int ch = 0; ch < kKT / 8; ++ch) {
           float e8[8];
 #pragma unroll
           for (int e = 0; e < 8; e += 2) {
@@ -442,6 +416,12 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
             ls[e + 1] += e8[e + 1];
           }
           p_chunk(ch, e8);
+          if (kPChunks > 1 && early && ((ch + 1) % (kKT / 8 / kPChunks)) == 0) {
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&p_full[t * kPChunks + (ch + 1) / (kKT / 8 / kPChunks) - 1]);
+            signalled = ch + 1;
+          }
         }
       }
       l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
@@ -449,7 +429,7 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
       // add to the peak register use; PV(j) only starts after p_full below
       if (j > 0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-        for (int c = 0; c < kOCols / 32; ++c) {
+        for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32];
           tmem_ld32(o_col + c * 32, o);
           tmem_wait_ld();
@@ -461,20 +441,9 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[t]);
+      for (int c = signalled / (kKT / 8 / kPChunks); c < kPChunks; ++c) mbar_arrive(&p_full[t * kPChunks + c]);
     }
     if (ok) ok = mbar_wait(&pv_done[t], (n_tiles - 1) & 1, abort_flag, p.status, 234 + t);
-    if constexpr (kHalves == 2) {
-      if (ok) {
-        // the row sum is the sum of the two halves' partial sums, added in one fixed order
-        float* ls_slot = red_l + t * (2 * kQT);
-        ls_slot[hh * kQT + row] = l_run;
-        mbar_arrive(my_xbar);
-        ok = mbar_wait(my_xbar, xuse & 1, abort_flag, p.status, 238 + t);
-        ++xuse;
-        if (ok) l_run = ls_slot[row] + ls_slot[kQT + row];
-      }
-    }
     if (ok) {
       tc_fence_after();
       const int qabs = q0 + t * kQT + row;  // absolute row of q / o
@@ -492,9 +461,8 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
       } else {
         orow = p.o + static_cast<int64_t>(qabs) * p.o_stride + h * D;
       }
-      orow += hh * kOCols;
 #pragma unroll 1
-      for (int c = 0; c < kOCols / 32; ++c) {
+      for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         tmem_ld32(o_col + c * 32, o);
         tmem_wait_ld();
@@ -511,7 +479,7 @@ __global__ void __launch_bounds__(attn_threads(kHalves), 1)
           }
         }
       }
-      if (row_ok && hh == 0 && p.lse != nullptr)
+      if (row_ok && p.lse != nullptr)
         p.lse[static_cast<int64_t>(h) * p.lse_stride + qabs] = m_run * p.scale + logf(l_run);
     }
   }
@@ -568,22 +536,16 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
   // grid.x: 256-row query blocks of the longest segment (both ranges in dual-range mode)
   const int max_q = (a.cu_seqlens_q || a.seg_table) ? a.max_seq_q : a.seq_q;
   const int blocks = a.seg_table ? a.max_q_blocks : (max_q + 2 * kQT - 1) / (2 * kQT);
-  // one softmax warp per S row; DS_ATTN_ROWSPLIT=2 selects the split-row variant (two warps
-  // per row), which measured 8 % slower on the Wan 480p shapes (13.54 vs 12.46 ms, batch 2)
-  static const int halves = [] {
-    const char* e = std::getenv("DS_ATTN_ROWSPLIT");
-    return e != nullptr && std::atoi(e) == 2 ? 2 : 1;
+  // P hand-off granularity (DS_ATTN_PCHUNKS = 1, 2 or 4; default 2)
+  static const int pchunks = [] {
+    const char* e = std::getenv("DS_ATTN_PCHUNKS");
+    const int v = e != nullptr ? std::atoi(e) : 2;
+    return v == 1 || v == 4 ? v : 2;
   }();
+  auto kern = pchunks == 1 ? attention2_kernel<D, 1> : pchunks == 4 ? attention2_kernel<D, 4> : attention2_kernel<D, 2>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Cfg<D>::kSmemBytes);
   dim3 grid(blocks, a.heads, a.batch);
-  if (halves == 2) {
-    auto kern = attention2_kernel<D, 2>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Cfg<D, 2>::kSmemBytes);
-    kern<<<grid, attn_threads(2), Attn2Cfg<D, 2>::kSmemBytes, stream>>>(tq, kv, p);
-  } else {
-    auto kern = attention2_kernel<D, 1>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Cfg<D, 1>::kSmemBytes);
-    kern<<<grid, attn_threads(1), Attn2Cfg<D, 1>::kSmemBytes, stream>>>(tq, kv, p);
-  }
+  kern<<<grid, kAttn2Threads, Attn2Cfg<D>::kSmemBytes, stream>>>(tq, kv, p);
 }
 
 }  // namespace

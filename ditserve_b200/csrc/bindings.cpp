@@ -188,9 +188,13 @@ void layernorm_modulate(const at::Tensor& x, at::Tensor& y, const c10::optional<
 
 void rmsnorm_rope(at::Tensor& x, const c10::optional<at::Tensor>& weight, int64_t width, int64_t groups, double eps,
                   const c10::optional<at::Tensor>& cos, const c10::optional<at::Tensor>& sin,
-                  int64_t rows_per_batch, int64_t head_dim) {
+                  int64_t rows_per_batch, int64_t head_dim, const c10::optional<at::Tensor>& weight2,
+                  int64_t seg_offset) {
   check_cuda_bf16_2d(x, "x");
   TORCH_CHECK(x.size(1) == width * groups, "rmsnorm_rope: width*groups must equal the view width");
+  if (weight2.has_value())
+    TORCH_CHECK(seg_offset >= x.size(1) && seg_offset % 8 == 0 && x.stride(0) >= seg_offset + x.size(1),
+                "rmsnorm_rope: the second segment must lie beside the first inside the row stride");
   if (cos.has_value()) {
     TORCH_CHECK(sin.has_value() && cos->scalar_type() == at::kFloat && sin->scalar_type() == at::kFloat &&
                     cos->is_contiguous() && sin->is_contiguous(),
@@ -211,6 +215,8 @@ void rmsnorm_rope(at::Tensor& x, const c10::optional<at::Tensor>& weight, int64_
   a.rope_sin = sin.has_value() ? sin->data_ptr<float>() : nullptr;
   a.rows_per_batch = static_cast<int>(rows_per_batch);
   a.head_dim = static_cast<int>(head_dim);
+  a.weight2 = opt_ptr(weight2);
+  a.seg_offset = seg_offset;
   ds::launch_rmsnorm_rope(a, at::cuda::getCurrentCUDAStream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }

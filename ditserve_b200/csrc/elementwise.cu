@@ -113,12 +113,19 @@ __global__ void __launch_bounds__(256) layernorm_modulate_kernel(LayerNormArgs a
 
 // One warp per row.  kChunks = row width / 256.  kGroupLanes lanes share one
 // normalisation group per chunk (32: whole row, 16: 128-wide heads, 8: 64-wide).
+// With a second segment (weight2 set) consecutive warps take the two segments of one row (q
+// and k of one token, seg_offset elements apart), so one launch normalises both.
 template <int kChunks, int kGroupLanes>
 __global__ void __launch_bounds__(256) rmsnorm_rope_kernel(RmsRopeArgs a) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  const bool two = a.weight2 != nullptr;
+  const int seg = two ? (gw & 1) : 0;
+  const int warp = two ? (gw >> 1) : gw;  // row
   if (warp >= a.rows) return;
-  __nv_bfloat16* x = reinterpret_cast<__nv_bfloat16*>(a.x) + static_cast<int64_t>(warp) * a.x_stride;
+  __nv_bfloat16* x = reinterpret_cast<__nv_bfloat16*>(a.x) + static_cast<int64_t>(warp) * a.x_stride +
+                     static_cast<int64_t>(seg) * a.seg_offset;
+  const void* weight = seg ? a.weight2 : a.weight;
   float v[kChunks][8];
   float part[kChunks];
   float total = 0.f;
@@ -152,8 +159,8 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_kernel(RmsRopeArgs a) {
     const int col = c * 256 + lane * 8;
     const int wcol = kGroupLanes == 32 ? col : (col % a.width);
     float w[8];
-    if (a.weight != nullptr) {
-      load8(reinterpret_cast<const __nv_bfloat16*>(a.weight) + wcol, w);
+    if (weight != nullptr) {
+      load8(reinterpret_cast<const __nv_bfloat16*>(weight) + wcol, w);
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) w[i] = 1.f;
@@ -183,7 +190,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_kernel(RmsRopeArgs a) {
 
 template <int kGroupLanes>
 void launch_rms_lanes(const RmsRopeArgs& a, int chunks, cudaStream_t s) {
-  const int blocks = (a.rows + 7) / 8;
+  const int blocks = (a.rows * (a.weight2 != nullptr ? 2 : 1) + 7) / 8;
   switch (chunks) {
     case 1: rmsnorm_rope_kernel<1, kGroupLanes><<<blocks, 256, 0, s>>>(a); break;
     case 2: rmsnorm_rope_kernel<2, kGroupLanes><<<blocks, 256, 0, s>>>(a); break;

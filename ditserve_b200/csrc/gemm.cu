@@ -563,7 +563,12 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
     const bool forced = a.cta_pair == 1;
     const int m2 = (a.M + 2 * kBM - 1) / (2 * kBM);
     const int sms = a.num_sms > 0 ? a.num_sms : device_sm_count();
-    if (a.N % 256 == 0 && (forced || m2 * (a.N / 256) >= sms / 2)) {
+    // DS_GEMM_PAIR_MAX_BN=128 keeps pair tiles at 256 x 128 (a tuning switch; default 256)
+    static const int pair_max_bn = [] {
+      const char* e = std::getenv("DS_GEMM_PAIR_MAX_BN");
+      return e != nullptr && std::atoi(e) == 128 ? 128 : 256;
+    }();
+    if (pair_max_bn == 256 && a.N % 256 == 0 && (forced || m2 * (a.N / 256) >= sms / 2)) {
       launch_pair<256>(a, stream);
       return;
     }

@@ -125,6 +125,8 @@ struct RmsRopeArgs {
   const float* rope_sin = nullptr;
   int rows_per_batch = 0;
   int head_dim = 128;
+  const void* weight2 = nullptr;  // second segment (e.g. k beside q): its weight, or null for one segment
+  int64_t seg_offset = 0;         // elements from the first segment to the second within a row
 };
 void launch_rmsnorm_rope(const RmsRopeArgs& a, cudaStream_t stream);
 

@@ -348,11 +348,9 @@ class WanTransformer(nn.Module):
             o = pctx.fused_qkv_attention(qkv, a1.norm_q.weight, a1.norm_k.weight, cfg.eps, pk.cos_full, pk.sin_full,
                                          Hh, pk.batch, pk.seq_local)
         else:
-            q, k, v = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
-            ops.rmsnorm_rope_(q, a1.norm_q.weight, eps=cfg.eps, cos=pk.cos, sin=pk.sin,
-                              rows_per_batch=pk.seq_local, head_dim=hd)
-            ops.rmsnorm_rope_(k, a1.norm_k.weight, eps=cfg.eps, cos=pk.cos, sin=pk.sin,
-                              rows_per_batch=pk.seq_local, head_dim=hd)
+            # q and k norm + RoPE in one launch over the fused QKV buffer
+            ops.rmsnorm_rope_qk_(qkv, a1.norm_q.weight, a1.norm_k.weight, eps=cfg.eps, cos=pk.cos, sin=pk.sin,
+                                 rows_per_batch=pk.seq_local, head_dim=hd)
             o = pctx.self_attention_qkv(qkv, Hh, pk.batch, pk.seq_local)
         x = ops.linear(o, a1.to_out[0].weight, a1.to_out[0].bias, residual=x, gate=m[:, 2], rows_per_batch=rpb,
                        out=x if x.is_cuda else None)

@@ -4,13 +4,13 @@ from ._ext import KernelTimeout, KernelTimer, available, check_status, ext, kern
 from .attention import attention, attention_reference, attention_segments, segment_table, segments_reference
 from .conv import conv_bias, conv_cl, conv_cl_reference, conv_weight_2d
 from .gemm import linear, linear_reference
-from .norm import (layernorm_modulate, layernorm_modulate_reference, rms_norm_reference, rmsnorm_rope_,
+from .norm import (layernorm_modulate, layernorm_modulate_reference, rms_norm_reference, rmsnorm_rope_, rmsnorm_rope_qk_,
                    rope_reference)
 from .sched import sched_step, sched_step_reference
 
 __all__ = [
     "KernelTimeout", "KernelTimer", "available", "check_status", "ext", "kernel", "launch_counts", "status_word",
     "attention", "attention_reference", "conv_bias", "conv_cl", "conv_cl_reference", "conv_weight_2d", "attention_segments", "segment_table", "segments_reference", "linear", "linear_reference",
-    "layernorm_modulate", "layernorm_modulate_reference", "rms_norm_reference", "rmsnorm_rope_",
+    "layernorm_modulate", "layernorm_modulate_reference", "rms_norm_reference", "rmsnorm_rope_", "rmsnorm_rope_qk_",
     "rope_reference", "sched_step", "sched_step_reference",
 ]

@@ -120,5 +120,20 @@ def rmsnorm_rope_(x: torch.Tensor, weight: torch.Tensor | None, *, groups: int =
     x2 = x if x.dim() == 2 else x.reshape(-1, x.shape[-1])
     width = x2.shape[1] // groups
     kernel("rmsnorm_rope")(x2, weight, width, groups, float(eps), cos, sin, int(rows_per_batch or x2.shape[0]),
-                       head_dim)
+                           head_dim, None, 0)
     return x
+
+
+def rmsnorm_rope_qk_(qkv: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, *, eps: float = 1e-6,
+                     cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+                     rows_per_batch: int | None = None, head_dim: int = 128) -> torch.Tensor:
+    """In place on the q and k columns of a fused [rows, >= 3D] QKV buffer, in one launch:
+    q = rope(rms_norm(q) * wq), k = rope(rms_norm(k) * wk), norms across all heads (Wan)."""
+    d = wq.numel()
+    q, k = qkv[:, :d], qkv[:, d:2 * d]
+    if not use_kernels(qkv):
+        rmsnorm_rope_(q, wq, eps=eps, cos=cos, sin=sin, rows_per_batch=rows_per_batch, head_dim=head_dim)
+        rmsnorm_rope_(k, wk, eps=eps, cos=cos, sin=sin, rows_per_batch=rows_per_batch, head_dim=head_dim)
+        return qkv
+    kernel("rmsnorm_rope")(q, wq, d, 1, float(eps), cos, sin, int(rows_per_batch or qkv.shape[0]), head_dim, wk, d)
+    return qkv

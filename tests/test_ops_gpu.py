@@ -265,20 +265,21 @@ def test_attention_multi_source_kv_equals_concatenated(sources):
     assert _rel(o.cpu(), ref) < 2e-2
 
 
-@pytest.mark.parametrize("B,Sq,Sk,H", [(2, 300, 300, 2), (1, 129, 1030, 1)])
-def test_attention_split_row_variant(B, Sq, Sk, H):
-    """The split-row softmax (two warps per S row, DS_ATTN_ROWSPLIT=2) in a child process, since
-    the switch is read once per process."""
+@pytest.mark.parametrize("chunks", ["1", "4"])
+def test_attention_p_chunk_variants(chunks):
+    """P handed to the MMA warp in 1 or 4 chunks (DS_ATTN_PCHUNKS; the default is 2) gives the
+    same attention; run in a child process since the switch is read once per process."""
+    import os
     import subprocess
     import sys
     code = (
         "import torch;from ditserve_b200 import ops\n"
-        f"torch.manual_seed(3);d=torch.device('cuda',0);B,Sq,Sk,H={B},{Sq},{Sk},{H}\n"
-        "q=torch.randn(B,Sq,H*128,device=d).bfloat16();k=torch.randn(B,Sk,H*128,device=d).bfloat16()\n"
-        "v=torch.randn(B,Sk,H*128,device=d).bfloat16();o=ops.attention(q,k,v,H);ops.check_status(d)\n"
-        "r=ops.attention_reference(q.cpu(),k.cpu(),v.cpu(),H)\n"
-        "rel=((o.cpu().float()-r.float()).norm()/r.float().norm()).item();print(rel);assert rel<2e-2,rel\n")
-    import os
-    env = dict(os.environ, DS_ATTN_ROWSPLIT="2")
-    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+        "torch.manual_seed(3);d=torch.device('cuda',0)\n"
+        "for B,Sq,Sk,H,D in ((2,300,300,2,128),(1,129,1030,1,64)):\n"
+        "  q=torch.randn(B,Sq,H*D,device=d).bfloat16();k=torch.randn(B,Sk,H*D,device=d).bfloat16()\n"
+        "  v=torch.randn(B,Sk,H*D,device=d).bfloat16();o=ops.attention(q,k,v,H);ops.check_status(d)\n"
+        "  r=ops.attention_reference(q.cpu(),k.cpu(),v.cpu(),H)\n"
+        "  rel=((o.cpu().float()-r.float()).norm()/r.float().norm()).item();assert rel<2e-2,rel\n")
+    r = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, DS_ATTN_PCHUNKS=chunks),
+                       capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr

@@ -215,3 +215,25 @@ def test_inplace_norm_rope_leaves_neighbouring_columns_untouched():
     assert torch.equal(qkv[:, width:], before[:, width:])
     ref = _fp32_norm_rope(before[:, :width], w, 1e-6, ang.cos(), ang.sin(), heads, hd, rows)
     assert _rel(qkv[:, :width], ref) < 1e-2
+
+
+def test_single_launch_qk_norm_equals_two_launches():
+    """q and k normalised + rotated in one launch give the same bits as one launch each, and
+    leave v untouched."""
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(11)
+    rows, heads, hd = 1000, 12, 128
+    width = heads * hd
+    qkv = torch.randn(rows, 3 * width, device=dev).bfloat16()
+    wq = (1 + 0.1 * torch.randn(width, device=dev)).bfloat16()
+    wk = (1 + 0.1 * torch.randn(width, device=dev)).bfloat16()
+    ang = torch.rand(500, hd // 2, device=dev)
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    a, b = qkv.clone(), qkv.clone()
+    ops.rmsnorm_rope_qk_(a, wq, wk, eps=1e-6, cos=cos, sin=sin, rows_per_batch=500, head_dim=hd)
+    ops.rmsnorm_rope_(b[:, :width], wq, eps=1e-6, cos=cos, sin=sin, rows_per_batch=500, head_dim=hd)
+    ops.rmsnorm_rope_(b[:, width:2 * width], wk, eps=1e-6, cos=cos, sin=sin, rows_per_batch=500, head_dim=hd)
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    assert torch.equal(a, b)
+    assert torch.equal(a[:, 2 * width:], qkv[:, 2 * width:])

@@ -237,3 +237,11 @@ def test_single_launch_qk_norm_equals_two_launches():
     ops.check_status(dev)
     assert torch.equal(a, b)
     assert torch.equal(a[:, 2 * width:], qkv[:, 2 * width:])
+
+
+def test_live_exactness_harness_on_the_cuda_kernels():
+    """The exactness tool's live mode: seeded cuts at random block boundaries (continuation
+    packets, step-boundary snapshots) end on the uninterrupted latents bit for bit."""
+    from ditserve_b200.evaluation import exactness
+    out = exactness.live_check(device="cuda", schedules=2, cuts=3, seed=2, spec=dict(SPEC, steps=3))
+    assert out["status"] == "completed", out["runs"]

@@ -498,389 +498,6 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   }
 }
 
-// ---------------------------------------------------------------------------
-// v3: 64-key tiles with double-buffered S in TMEM.
-//
-// In v2 the S of tile j+1 overwrites the TMEM columns that hold P of tile j, so a query
-// tile's next QK^T can only start after its PV; each softmax warpgroup then waits for a PV
-// and a QK^T in series between two tiles.  With 64-key tiles a query tile's S needs 64 TMEM
-// columns, which leaves room for two S buffers per tile next to O:
-//   O_A [0, 128), O_B [128, 256), S_A buffers [256, 320) [320, 384), S_B [384, 448) [448, 512)
-// so S(j+2) is computed into the buffer that P(j) occupied as soon as PV(j) is issued, and
-// S(j+1) is ready before the softmax of tile j ends: the softmax warpgroups run back to back
-// and overlap each other and the tensor core.  MMA issue order per tile step j:
-//   PV_A(j), S_A(j+2), PV_B(j), S_B(j+2)          (after the prologue S_A(0) S_B(0) S_A(1) S_B(1))
-// K runs two tiles ahead of V through 4-stage rings (16 KB stages at head_dim 128).  The
-// softmax waits for PV(j-1) only when it has to rescale O; the barrier cannot run two phases
-// ahead of it because PV(j+1) needs this warpgroup's own P(j+1).
-constexpr int kKT3 = 64;
-
-template <int D>
-struct Attn3Cfg {
-  static constexpr int kAtoms = D / 64;
-  static constexpr int kQBytes = kQT * D * 2;
-  static constexpr int kKBytes = kKT3 * D * 2;
-  static constexpr int kVBytes = kKT3 * D * 2;
-  static constexpr int KS = 4;
-  static constexpr int VS = 4;
-  static constexpr int kSmemBytes = 2 * kQBytes + KS * kKBytes + VS * kVBytes + 1024 + 512;
-  static constexpr int kTmemCols = 512;
-};
-
-template <int D>
-__global__ void __launch_bounds__(kAttn2Threads, 1)
-    attention3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ KvMaps kv,
-                      AttnParams p) {
-  using Cfg = Attn3Cfg<D>;
-  constexpr int KS = Cfg::KS;
-  constexpr int VS = Cfg::VS;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  int qa0, qa1, qb0, qb1, ka0, ka1, kb0, kb1;
-  if (p.seg != nullptr) {
-    const int* sg = p.seg + 8 * b;
-    qa0 = sg[0]; qa1 = sg[1]; qb0 = sg[2]; qb1 = sg[3];
-    ka0 = sg[4]; ka1 = sg[5]; kb0 = sg[6]; kb1 = sg[7];
-  } else if (p.cu_q != nullptr) {
-    qa0 = p.cu_q[b]; qa1 = p.cu_q[b + 1];
-    ka0 = p.cu_k[b]; ka1 = p.cu_k[b + 1];
-    qb0 = qb1 = kb0 = kb1 = 0;
-  } else {
-    qa0 = b * p.seq_q; qa1 = qa0 + p.seq_q;
-    ka0 = b * p.seq_k; ka1 = ka0 + p.seq_k;
-    qb0 = qb1 = kb0 = kb1 = 0;
-  }
-  const int nqa = (qa1 - qa0 + 2 * kQT - 1) / (2 * kQT);
-  const int nqb = (qb1 - qb0 + 2 * kQT - 1) / (2 * kQT);
-  int q0, q_end;
-  if (static_cast<int>(blockIdx.x) < nqa) {
-    q0 = qa0 + blockIdx.x * 2 * kQT;
-    q_end = qa1;
-  } else if (static_cast<int>(blockIdx.x) < nqa + nqb) {
-    q0 = qb0 + (blockIdx.x - nqa) * 2 * kQT;
-    q_end = qb1;
-  } else {
-    return;
-  }
-  const int nka = (ka1 - ka0 + kKT3 - 1) / kKT3;
-  const int per_source = nka + (kb1 - kb0 + kKT3 - 1) / kKT3;
-  const int n_tiles = per_source * p.kv_sources;
-  if (n_tiles <= 0) return;
-  auto ktile_row = [&](int j) {
-    const int jj = j % per_source;
-    return jj < nka ? ka0 + jj * kKT3 : kb0 + (jj - nka) * kKT3;
-  };
-  auto ktile_valid = [&](int j) {
-    const int jj = j % per_source;
-    return jj < nka ? ka1 - (ka0 + jj * kKT3) : kb1 - (kb0 + (jj - nka) * kKT3);
-  };
-  const int hk = h / (p.heads / p.heads_kv);
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + 2 * Cfg::kQBytes;
-  uint8_t* sV = sK + KS * Cfg::kKBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + VS * Cfg::kVBytes);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + KS;
-  uint64_t* v_full = k_empty + KS;
-  uint64_t* v_empty = v_full + VS;
-  uint64_t* s_full = v_empty + VS;  // [2 tiles][2 buffers]
-  uint64_t* p_full = s_full + 4;    // [2 tiles]
-  uint64_t* pv_done = p_full + 2;   // [2 tiles]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int wg = warp >> 2;
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int i = 0; i < KS; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
-    }
-    for (int i = 0; i < VS; ++i) {
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
-    }
-    for (int i = 0; i < 4; ++i) mbar_init(&s_full[i], 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&p_full[i], 128);
-      mbar_init(&pv_done[i], 1);
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) tmem_alloc<Cfg::kTmemCols>(tmem_slot);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer: K two tiles ahead of V ----------------
-      tma_prefetch_desc(&tmQ);
-      for (int src = 0; src < p.kv_sources; ++src) {
-        tma_prefetch_desc(&kv.k[src]);
-        tma_prefetch_desc(&kv.v[src]);
-      }
-      mbar_arrive_expect_tx(q_full, 2 * Cfg::kQBytes);
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_2d(sQ + t * Cfg::kQBytes + a * (kQT * 128), &tmQ, h * D + a * 64, q0 + t * kQT, q_full);
-      auto load_k = [&](int j) -> bool {
-        const int st = j % KS;
-        if (!mbar_wait(&k_empty[st], ((j / KS) & 1) ^ 1, abort_flag, p.status, 410)) return false;
-        mbar_arrive_expect_tx(&k_full[st], Cfg::kKBytes);
-#pragma unroll
-        for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_2d(sK + st * Cfg::kKBytes + a * (kKT3 * 128), &kv.k[j / per_source], hk * D + a * 64,
-                      ktile_row(j), &k_full[st]);
-        return true;
-      };
-      bool ok = load_k(0) && (n_tiles < 2 || load_k(1));
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int st = j % VS;
-        if (!mbar_wait(&v_empty[st], ((j / VS) & 1) ^ 1, abort_flag, p.status, 411)) break;
-        mbar_arrive_expect_tx(&v_full[st], Cfg::kVBytes);
-#pragma unroll
-        for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_2d(sV + st * Cfg::kVBytes + a * (kKT3 * 128), &kv.v[j / per_source], hk * D + a * 64,
-                      ktile_row(j), &v_full[st]);
-        if (j + 2 < n_tiles && !load_k(j + 2)) break;
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc_s = umma_idesc_bf16(kQT, kKT3, false);
-      constexpr uint32_t idesc_o = umma_idesc_bf16(kQT, D, true);
-      auto issue_s = [&](int t, int j) {
-        const int st = j % KS;
-        const uint32_t d = tmem_base + 256 + t * 128 + (j & 1) * kKT3;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t offq = (kk >> 2) * (kQT * 128) + (kk & 3) * 32;
-          const uint32_t offk = (kk >> 2) * (kKT3 * 128) + (kk & 3) * 32;
-          const uint64_t da = umma_desc_sw128(smem_u32(sQ + t * Cfg::kQBytes) + offq, 16, 1024);
-          const uint64_t db = umma_desc_sw128(smem_u32(sK + st * Cfg::kKBytes) + offk, 16, 1024);
-          umma_bf16_ss(d, da, db, idesc_s, kk != 0);
-        }
-        umma_commit(&s_full[t * 2 + (j & 1)]);
-      };
-      auto issue_pv = [&](int t, int j) -> bool {
-        if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, 422 + t)) return false;
-        tc_fence_after();
-        const uint32_t d = tmem_base + t * 128;
-        const uint32_t p_tmem = tmem_base + 256 + t * 128 + (j & 1) * kKT3;  // bf16 P, 32 packed columns
-        const uint32_t v_base = smem_u32(sV + (j % VS) * Cfg::kVBytes);
-#pragma unroll
-        for (int kk = 0; kk < kKT3 / 16; ++kk) {
-          const uint64_t db = umma_desc_sw128(v_base + kk * (16 * 128), kKT3 * 128, 1024);
-          umma_bf16_ts(d, p_tmem + kk * 8, db, idesc_o, (j | kk) != 0);
-        }
-        umma_commit(&pv_done[t]);
-        return true;
-      };
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 420) &&
-                mbar_wait(&k_full[0], 0, abort_flag, p.status, 421);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
-        umma_commit(&k_empty[0]);
-        if (n_tiles > 1) {
-          ok = mbar_wait(&k_full[1], 0, abort_flag, p.status, 421);
-          if (ok) {
-            tc_fence_after();
-            issue_s(0, 1);
-            issue_s(1, 1);
-            umma_commit(&k_empty[1]);
-          }
-        }
-      }
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        if (!mbar_wait(&v_full[j % VS], (j / VS) & 1, abort_flag, p.status, 424)) break;
-        tc_fence_after();
-        if (!issue_pv(0, j)) break;
-        const bool more = j + 2 < n_tiles;
-        if (more) {
-          const int st = (j + 2) % KS;
-          if (!mbar_wait(&k_full[st], ((j + 2) / KS) & 1, abort_flag, p.status, 425)) break;
-          tc_fence_after();
-          issue_s(0, j + 2);
-        }
-        if (!issue_pv(1, j)) break;
-        umma_commit(&v_empty[j % VS]);
-        if (more) {
-          issue_s(1, j + 2);
-          umma_commit(&k_empty[(j + 2) % KS]);
-        }
-      }
-    }
-  } else if (wg >= 1) {
-    // ---------------- softmax warpgroups (tile t = wg - 1) ----------------
-    const int t = wg - 1;
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t o_col = tmem_base + lane_addr + t * 128;
-    const float sl2 = p.scale_log2;
-    const uint64_t sl2x2 = f2_pack(sl2, sl2);
-    float m_run = -INFINITY;
-    float l_run = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait(&s_full[t * 2 + (j & 1)], (j >> 1) & 1, abort_flag, p.status, 430 + t)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t s_col = tmem_base + lane_addr + 256 + t * 128 + (j & 1) * kKT3;
-      const int valid = ktile_valid(j);
-      const bool masked = valid < kKT3;
-      uint32_t s[kKT3];
-#pragma unroll
-      for (int c = 0; c < kKT3 / 32; ++c)
-        tmem_ld32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
-      tmem_wait_ld();
-      float mx = -INFINITY;
-      if (masked) {
-#pragma unroll
-        for (int c = 0; c < kKT3; ++c)
-          if (c < valid) mx = fmaxf(mx, __uint_as_float(s[c]));
-      } else {
-        float mc[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mc[i] = __uint_as_float(s[i]);
-#pragma unroll
-        for (int c = 8; c < kKT3; c += 8)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) mc[i] = fmaxf(mc[i], __uint_as_float(s[c + i]));
-        mx = fmaxf(fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3])), fmaxf(fmaxf(mc[4], mc[5]), fmaxf(mc[6], mc[7])));
-      }
-      const float m_new = fmaxf(m_run, mx);
-      const bool need = (m_new - m_run) * sl2 > 8.0f;  // always true on the first tile
-      float alpha = 1.f;
-      if (need) {
-        alpha = ex2_approx((m_run - m_new) * sl2);
-        m_run = m_new;
-      }
-      const bool rescale = j > 0 && __any_sync(0xffffffffu, need);
-      l_run *= alpha;
-      const float neg = -m_run * sl2;
-      const uint64_t negx2 = f2_pack(neg, neg);
-      float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint32_t pk8[8];
-      // exponentials into bf16 P over the first 32 columns of this tile's S buffer
-#pragma unroll
-      for (int ch = 0; ch < kKT3 / 8; ++ch) {
-        float e8[8];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const int c = ch * 8 + e;
-          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2x2, negx2);
-          float x0, x1;
-          f2_unpack(x2, x0, x1);
-          if (masked) {
-            if (c >= valid) x0 = -INFINITY;
-            if (c + 1 >= valid) x1 = -INFINITY;
-          }
-          e8[e] = ex2_approx(x0);
-          e8[e + 1] = ex2_approx(x1);
-          ls[e] += e8[e];
-          ls[e + 1] += e8[e + 1];
-        }
-        const int q = (ch & 1) * 4;
-        pk8[q + 0] = pack_bf16x2(e8[0], e8[1]);
-        pk8[q + 1] = pack_bf16x2(e8[2], e8[3]);
-        pk8[q + 2] = pack_bf16x2(e8[4], e8[5]);
-        pk8[q + 3] = pack_bf16x2(e8[6], e8[7]);
-        if (ch & 1) tmem_st8(s_col + (ch >> 1) * 8, pk8);
-      }
-      l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
-      if (rescale) {
-        // O is being accumulated by PV(j-1): wait for it, then rescale before PV(j) starts
-        if (!mbar_wait(&pv_done[t], (j - 1) & 1, abort_flag, p.status, 432 + t)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(o_col + c * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(o_col + c * 32, o);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[t]);
-    }
-    if (ok) ok = mbar_wait(&pv_done[t], (n_tiles - 1) & 1, abort_flag, p.status, 434 + t);
-    if (ok) {
-      tc_fence_after();
-      const int qabs = q0 + t * kQT + row;
-      const bool row_ok = qabs < q_end;
-      const float inv_l = 1.0f / l_run;
-      __nv_bfloat16* orow;
-      if (p.o_scatter) {
-        const int qrow = qabs - qa0;
-        const int owner = qrow / p.o_seq_local;
-        const int local = qrow - owner * p.o_seq_local;
-        __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(
-            reinterpret_cast<uint8_t*>(p.o_group.base[owner < p.o_group.size ? owner : 0]) + p.o_off);
-        orow = base + (static_cast<int64_t>(b) * p.o_seq_local + local) * p.o_peer_stride + (p.o_head_offset + h) * D;
-      } else {
-        orow = p.o + static_cast<int64_t>(qabs) * p.o_stride + h * D;
-      }
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(o_col + c * 32, o);
-        tmem_wait_ld();
-        if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(o[q * 8 + 0]) * inv_l, __uint_as_float(o[q * 8 + 1]) * inv_l);
-            w.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv_l, __uint_as_float(o[q * 8 + 3]) * inv_l);
-            w.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv_l, __uint_as_float(o[q * 8 + 5]) * inv_l);
-            w.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv_l, __uint_as_float(o[q * 8 + 7]) * inv_l);
-            dst[q] = w;
-          }
-        }
-      }
-      if (row_ok && p.lse != nullptr)
-        p.lse[static_cast<int64_t>(h) * p.lse_stride + qabs] = m_run * p.scale + logf(l_run);
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (*abort_flag && threadIdx.x == 0) {
-    const unsigned long long t0 = globaltimer_ns();
-    while (globaltimer_ns() - t0 < 1000000ull) {
-    }
-  }
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc<Cfg::kTmemCols>(tmem_base);
-  }
-}
-
 template <int D>
 void launch_d(const AttnArgs& a, cudaStream_t stream) {
   CUtensorMap tq = make_tmap_bf16_2d(a.q, a.total_q, static_cast<uint64_t>(a.heads) * D, a.q_row_stride, kQT);
@@ -919,25 +536,6 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
   // grid.x: 256-row query blocks of the longest segment (both ranges in dual-range mode)
   const int max_q = (a.cu_seqlens_q || a.seg_table) ? a.max_seq_q : a.seq_q;
   const int blocks = a.seg_table ? a.max_q_blocks : (max_q + 2 * kQT - 1) / (2 * kQT);
-  // kernel generation: 2 (128-key tiles) or 3 (64-key tiles, double-buffered S), DS_ATTN_KERNEL
-  static const int gen = [] {
-    const char* e = std::getenv("DS_ATTN_KERNEL");
-    return e != nullptr && std::atoi(e) == 3 ? 3 : 2;
-  }();
-  if (gen == 3) {
-    KvMaps kv3;
-    for (int src = 0; src < a.kv_sources; ++src) {
-      const void* kp = src == 0 ? a.k : a.k_extra[src - 1];
-      const void* vp = src == 0 ? a.v : a.v_extra[src - 1];
-      kv3.k[src] = make_tmap_bf16_2d(kp, a.total_k, static_cast<uint64_t>(a.heads_kv) * D, a.k_row_stride, kKT3);
-      kv3.v[src] = make_tmap_bf16_2d(vp, a.total_k, static_cast<uint64_t>(a.heads_kv) * D, a.v_row_stride, kKT3);
-    }
-    auto kern3 = attention3_kernel<D>;
-    cudaFuncSetAttribute(kern3, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn3Cfg<D>::kSmemBytes);
-    dim3 grid3(blocks, a.heads, a.batch);
-    kern3<<<grid3, kAttn2Threads, Attn3Cfg<D>::kSmemBytes, stream>>>(tq, kv3, p);
-    return;
-  }
   // P hand-off granularity (DS_ATTN_PCHUNKS = 1, 2 or 4; default 2)
   static const int pchunks = [] {
     const char* e = std::getenv("DS_ATTN_PCHUNKS");

@@ -164,6 +164,15 @@ __device__ __forceinline__ void load8f(const __nv_bfloat16* p, float (&f)[8]) {
     f[2 * i + 1] = t.y;
   }
 }
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = unpack_bf16x2(w[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   uint4 u;
   u.x = pack_bf16x2(f[0], f[1]);
@@ -175,8 +184,13 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 
 // One warp per local token row of qkv [B*Sl, 3*H*D].  kChunks = H*D / 256.
 // Destination on rank j: recv[(b*S + rank*Sl + t) * 3*Hl*D + part*Hl*D + (h - j*Hl)*D + d].
+// The warp issues the loads of all three parts (q, k, v) before any arithmetic (widths up to
+// 1536: 3 x kChunks 16-byte loads per lane kept as raw bf16), so a token's whole 3*H*D row is
+// in flight at once; the kernel is bound by HBM latency otherwise (one part in flight).  v is
+// stored as loaded.
 template <int kChunks>
-__global__ void __launch_bounds__(256) qkv_scatter_kernel(QkvScatterArgs a) {
+__global__ void __launch_bounds__(128) qkv_scatter_kernel(QkvScatterArgs a) {
+  constexpr int kPre = kChunks <= 6 ? 3 : 1;  // parts whose loads are issued up front
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= a.rows) return;
@@ -187,34 +201,47 @@ __global__ void __launch_bounds__(256) qkv_scatter_kernel(QkvScatterArgs a) {
   const int64_t dst_row = static_cast<int64_t>(b) * a.seq_local * a.group.size + a.group.rank * a.seq_local + t;
   const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + static_cast<int64_t>(warp) * a.qkv_stride;
   const int half = a.head_dim / 2;
-#pragma unroll 1
+  uint4 raw[kPre][kChunks];
+#pragma unroll
+  for (int p = 0; p < kPre; ++p)
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c)
+      raw[p][c] = *reinterpret_cast<const uint4*>(src + p * width + c * 256 + lane * 8);
+#pragma unroll
   for (int part = 0; part < 3; ++part) {
-    float v[kChunks][8];
-    float ss = 0.f;
+    uint4(&r)[kChunks] = raw[kPre == 3 ? part : 0];
+    if (kPre == 1 && part > 0) {
 #pragma unroll
-    for (int c = 0; c < kChunks; ++c) {
-      load8f(src + part * width + c * 256 + lane * 8, v[c]);
-      // same summation order as rmsnorm_rope_kernel (per-chunk partials), so the fused
-      // and the unfused paths produce bit-identical q/k
-      float cs = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) cs += v[c][i] * v[c][i];
-      ss += cs;
+      for (int c = 0; c < kChunks; ++c)
+        r[c] = *reinterpret_cast<const uint4*>(src + part * width + c * 256 + lane * 8);
     }
     if (part < 2) {
-      // RMS across all heads of the token, weight, bf16 rounding, then RoPE
+      // RMS across all heads of the token, weight, bf16 rounding, then RoPE.  Same
+      // summation order as rmsnorm_rope_kernel (per-chunk partials), so the fused and the
+      // unfused paths produce bit-identical q/k.
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        float v[8];
+        unpack8(r[c], v);
+        float cs = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) cs += v[i] * v[i];
+        ss += cs;
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float r = rsqrtf(ss / static_cast<float>(width) + a.eps);
+      const float rs = rsqrtf(ss / static_cast<float>(width) + a.eps);
       const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(part == 0 ? a.wq : a.wk);
       const int pos = a.pos_base + t + a.group.rank * a.seq_local;  // global position in the sequence
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
         const int col = c * 256 + lane * 8;
-        float wv[8];
+        float v[8], wv[8];
+        unpack8(r[c], v);
         load8f(w + col, wv);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[c][i] = __bfloat162float(__float2bfloat16_rn(v[c][i] * r * wv[i]));
+        for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(__float2bfloat16_rn(v[i] * rs * wv[i]));
         if (a.rope_cos != nullptr) {
           const int pair0 = (col % a.head_dim) / 2;
           const float4 c4 = *reinterpret_cast<const float4*>(a.rope_cos + static_cast<int64_t>(pos) * half + pair0);
@@ -223,11 +250,12 @@ __global__ void __launch_bounds__(256) qkv_scatter_kernel(QkvScatterArgs a) {
           const float sn[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
           for (int p = 0; p < 4; ++p) {
-            const float x0 = v[c][2 * p], x1 = v[c][2 * p + 1];
-            v[c][2 * p] = x0 * cs[p] - x1 * sn[p];
-            v[c][2 * p + 1] = x0 * sn[p] + x1 * cs[p];
+            const float x0 = v[2 * p], x1 = v[2 * p + 1];
+            v[2 * p] = x0 * cs[p] - x1 * sn[p];
+            v[2 * p + 1] = x0 * sn[p] + x1 * cs[p];
           }
         }
+        r[c] = pack8(v);
       }
     }
 #pragma unroll
@@ -236,7 +264,7 @@ __global__ void __launch_bounds__(256) qkv_scatter_kernel(QkvScatterArgs a) {
       const int owner = col / hl_width;
       const int dcol = part * hl_width + (col - owner * hl_width);
       __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(a.group.base[owner]) + a.recv_off);
-      *reinterpret_cast<uint4*>(dst + dst_row * (3 * hl_width) + dcol) = pack8(v[c]);
+      *reinterpret_cast<uint4*>(dst + dst_row * (3 * hl_width) + dcol) = r[c];
     }
   }
 }
@@ -369,13 +397,15 @@ void launch_qkv_scatter(const QkvScatterArgs& a, cudaStream_t s) {
   if (width % 256 != 0 || (width / a.group.size) % 8 != 0 || a.heads % a.group.size != 0)
     throw std::runtime_error("qkv_scatter: heads*head_dim must be a multiple of 256 and split over the group");
   const int chunks = width / 256;
-  const int blocks = (a.rows + 7) / 8;
+  // four warps (tokens) per block: at 100-200 registers a thread, small blocks keep 12-16
+  // warps resident per SM
+  const int blocks = (a.rows + 3) / 4;
   switch (chunks) {
-    case 2: qkv_scatter_kernel<2><<<blocks, 256, 0, s>>>(a); break;
-    case 4: qkv_scatter_kernel<4><<<blocks, 256, 0, s>>>(a); break;
-    case 6: qkv_scatter_kernel<6><<<blocks, 256, 0, s>>>(a); break;
-    case 8: qkv_scatter_kernel<8><<<blocks, 256, 0, s>>>(a); break;
-    case 12: qkv_scatter_kernel<12><<<blocks, 256, 0, s>>>(a); break;
+    case 2: qkv_scatter_kernel<2><<<blocks, 128, 0, s>>>(a); break;
+    case 4: qkv_scatter_kernel<4><<<blocks, 128, 0, s>>>(a); break;
+    case 6: qkv_scatter_kernel<6><<<blocks, 128, 0, s>>>(a); break;
+    case 8: qkv_scatter_kernel<8><<<blocks, 128, 0, s>>>(a); break;
+    case 12: qkv_scatter_kernel<12><<<blocks, 128, 0, s>>>(a); break;
     default: throw std::runtime_error("qkv_scatter: unsupported width");
   }
 }

@@ -39,7 +39,7 @@ def _pct(xs, q):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--video-sms", type=int, default=112)
-    ap.add_argument("--image-sms", type=int, default=36)
+    ap.add_argument("--image-sms", type=int, default=36, help="the image role takes the SMs left after the video split")
     ap.add_argument("--steps", type=int, default=40)
     args = ap.parse_args(argv)
     from ..models.sd35.model import SD35_MEDIUM
@@ -101,8 +101,7 @@ def main(argv=None):
     try:
         t, b = run(pool.stream("video"), pool.stream("image"))
         out["green"] = dict(p50=round(_pct(t, 0.5), 2), p99=round(_pct(t, 0.99), 2), max=round(max(t), 2),
-                            video_blocks=b, video_sms=args.video_sms, image_sms=args.image_sms,
-                            total_sms=pool.total_sms)
+                            video_blocks=b, sm_counts=pool.sm_counts, total_sms=pool.total_sms)
     finally:
         torch.cuda.synchronize()
         pool.close()

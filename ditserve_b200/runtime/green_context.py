@@ -66,12 +66,20 @@ class GreenPool:
         self.roles = list(shares)
         self.streams = {}
         self.contexts = {}
+        self.sm_counts = {}
         remaining = res
-        for role in self.roles:
+        for i, role in enumerate(self.roles):
             count = int(shares[role])
-            err, groups, n, rest = cu.cuDevSmResourceSplitByCount(1, remaining, 0, count)
-            self._check(err, "cuDevSmResourceSplitByCount")
-            err, desc = cu.cuDevResourceGenerateDesc([groups[0]] if isinstance(groups, list) else groups, 1)
+            if i == len(self.roles) - 1 and count >= remaining.sm.smCount:
+                # the last role takes what is left as it is: a split must come in the driver's
+                # SM granularity (8 on this part), which the remainder need not be
+                part, rest = remaining, None
+            else:
+                err, groups, n, rest = cu.cuDevSmResourceSplitByCount(1, remaining, 0, count)
+                self._check(err, f"cuDevSmResourceSplitByCount ({role}: {count} of {remaining.sm.smCount} SMs)")
+                part = groups[0] if isinstance(groups, (list, tuple)) else groups
+            self.sm_counts[role] = int(part.sm.smCount)
+            err, desc = cu.cuDevResourceGenerateDesc([part], 1)
             self._check(err, "cuDevResourceGenerateDesc")
             err, gctx = cu.cuGreenCtxCreate(desc, dev, cu.CUgreenCtxCreate_flags.CU_GREEN_CTX_DEFAULT_STREAM)
             self._check(err, "cuGreenCtxCreate")
@@ -89,7 +97,7 @@ class GreenPool:
         return self.streams[role]
 
     def status(self) -> dict:
-        return dict(total_sms=self.total_sms, roles=self.roles)
+        return dict(total_sms=self.total_sms, roles=self.roles, sm_counts=dict(self.sm_counts))
 
     def close(self):
         for gctx in self.contexts.values():

@@ -52,7 +52,8 @@ def main():
     ap.add_argument("--json", default=None)
     ap.add_argument("--tokens", type=int, default=32760)
     ap.add_argument("--batch", type=int, default=2)
-    ap.add_argument("--only", default=None, help="'fused': only the peer-memory kernels on a one-member group; 'attention': self-attention only")
+    ap.add_argument("--only", default=None, help="'fused': only the peer-memory kernels on a one-member group; 'attention': self-attention only; "
+                         "'memory': the per-token norm kernels and qkv_scatter; 'cross': cross-attention (512 keys) only")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     tflops_peak, hbm_peak, src = peaks()
@@ -79,7 +80,25 @@ def main():
         q, k, v = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
         o = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
         ms = timeit(lambda: ops.attention(q.view(B, S, D), k.view(B, S, D), v.view(B, S, D), H, out=o), iters=5)
+        ops.check_status(dev)  # a kernel whose bounded waits ran out raises here instead of printing a time
         row("self_attention", ms, flops=4.0 * B * H * S * S * 128, impl="ours")
+        if args.json:
+            json.dump(res, open(args.json, "w"), indent=1)
+        return
+    if args.only == "cross":
+        q = torch.randn(M, D, device=dev).bfloat16()
+        kv = torch.randn(B * 512, 2 * D, device=dev).bfloat16()
+        o = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
+        ms = timeit(lambda: ops.attention(q.view(B, S, D), kv[:, :D].view(B, 512, D), kv[:, D:].view(B, 512, D), H,
+                                          out=o), iters=5)
+        ops.check_status(dev)
+        row("cross_attention", ms, flops=4.0 * B * H * S * 512 * 128, impl="ours")
+        if args.json:
+            json.dump(res, open(args.json, "w"), indent=1)
+        return
+    if args.only == "memory":
+        memory_rows(row, timeit, dev, S, B, D, H, flush)
+        fused_rows(row, timeit, dev, S, B, D, H, flush, only=("qkv_scatter",))
         if args.json:
             json.dump(res, open(args.json, "w"), indent=1)
         return
@@ -136,22 +155,32 @@ def main():
     kv = torch.randn(B * 512, 2 * D, device=dev).bfloat16()
     ms = timeit(lambda: ops.attention(q.view(B, S, D), kv[:, :D].view(B, 512, D), kv[:, D:].view(B, 512, D), H), iters=5)
     row("cross_attention", ms, flops=4.0 * B * H * S * 512 * 128, impl="ours")
-    # memory-bound fused kernels
-    mod = torch.randn(B, 6, D, device=dev)
-    y = torch.empty_like(x)
-    ms = timeit(lambda: ops.layernorm_modulate(x, scale=mod[:, 1], shift=mod[:, 0], rows_per_batch=S, out=y), flush=flush)
-    row("layernorm_modulate", ms, bytes_=2 * M * D * 2, impl="ours")
-    w = torch.ones(D, device=dev).bfloat16()
-    ang = torch.rand(S, 64, device=dev)
-    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
-    ms = timeit(lambda: ops.rmsnorm_rope_(q, w, cos=cos, sin=sin, rows_per_batch=S), flush=flush)
-    row("rmsnorm_rope_q", ms, bytes_=2 * M * D * 2, impl="ours")
+    memory_rows(row, timeit, dev, S, B, D, H, flush)
     fused_rows(row, timeit, dev, S, B, D, H, flush)
+    ops.check_status(dev)
     if args.json:
         json.dump(res, open(args.json, "w"), indent=1)
 
 
-def fused_rows(row, timeit, dev, S, B, D, H, flush):
+def memory_rows(row, timeit, dev, S, B, D, H, flush):
+    """The memory-bound per-token kernels of a block: adaLN modulate, q/k RMS norm + RoPE."""
+    M = S * B
+    x = torch.randn(M, D, device=dev).bfloat16()
+    mod = torch.randn(B, 6, D, device=dev)
+    y = torch.empty_like(x)
+    ms = timeit(lambda: ops.layernorm_modulate(x, scale=mod[:, 1], shift=mod[:, 0], rows_per_batch=S, out=y), flush=flush)
+    row("layernorm_modulate", ms, bytes_=2 * M * D * 2, impl="ours")
+    qkv = torch.randn(M, 3 * D, device=dev).bfloat16()
+    w = torch.ones(D, device=dev).bfloat16()
+    ang = torch.rand(S, 64, device=dev)
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    ms = timeit(lambda: ops.rmsnorm_rope_(qkv[:, :D], w, cos=cos, sin=sin, rows_per_batch=S), flush=flush)
+    row("rmsnorm_rope_q", ms, bytes_=2 * M * D * 2, impl="ours")
+    ms = timeit(lambda: ops.rmsnorm_rope_qk_(qkv, w, w, cos=cos, sin=sin, rows_per_batch=S), flush=flush)
+    row("rmsnorm_rope_qk", ms, bytes_=2 * M * 2 * D * 2, impl="ours (q and k in one launch)")
+
+
+def fused_rows(row, timeit, dev, S, B, D, H, flush, only=None):
     """Peer-memory kernels on a one-member group (this GPU's own heap): the stores stay local,
     so these rows measure each kernel's compute and HBM side; NVLink timing comes from the
     multi-GPU selftests."""
@@ -171,6 +200,9 @@ def fused_rows(row, timeit, dev, S, B, D, H, flush):
     ms = timeit(lambda: ext().qkv_scatter(qkv, wq, wk, 1e-6, cos, sin, S, H, hd, 0, base, tmo, recv_off, 0),
                 flush=flush)
     row("qkv_scatter_norm_rope_a2a", ms, bytes_=2 * M * 3 * D * 2, impl="ours (group of 1)")
+    if only is not None and "attention" not in only:
+        del heap
+        return
     recv = heap[recv_off:recv_off + M * 3 * D * 2].view(torch.bfloat16).view(M, 3 * D)
     q, k, v = recv[:, :D], recv[:, D:2 * D], recv[:, 2 * D:]
     fl = 4.0 * B * H * S * S * hd

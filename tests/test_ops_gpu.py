@@ -283,28 +283,3 @@ def test_attention_p_chunk_variants(chunks):
     r = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, DS_ATTN_PCHUNKS=chunks),
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
-
-
-def test_attention_v3_kernel():
-    """The 64-key-tile kernel with double-buffered S (DS_ATTN_KERNEL=3) on dense, masked-tail,
-    cross, packed varlen and LSE cases, in a child process (the switch is read once)."""
-    import os
-    import subprocess
-    import sys
-    code = (
-        "import torch;from ditserve_b200 import ops\n"
-        "torch.manual_seed(3);d=torch.device('cuda',0)\n"
-        "for B,Sq,Sk,H,D in ((2,300,300,2,128),(1,129,1030,1,64),(1,1000,77,2,128),(1,64,512,3,128)):\n"
-        "  q=torch.randn(B,Sq,H*D,device=d).bfloat16();k=torch.randn(B,Sk,H*D,device=d).bfloat16()\n"
-        "  v=torch.randn(B,Sk,H*D,device=d).bfloat16();o,l=ops.attention(q,k,v,H,return_lse=True);ops.check_status(d)\n"
-        "  r,rl=ops.attention_reference(q.cpu(),k.cpu(),v.cpu(),H,return_lse=True)\n"
-        "  rel=((o.cpu().float()-r.float()).norm()/r.float().norm()).item();assert rel<2e-2,rel\n"
-        "  assert (l.cpu()-rl).abs().max().item()<2e-2\n"
-        "cu=torch.tensor([0,100,400,1000],dtype=torch.int32,device=d)\n"
-        "q=torch.randn(1000,256,device=d).bfloat16();k=torch.randn(1000,256,device=d).bfloat16();v=torch.randn(1000,256,device=d).bfloat16()\n"
-        "o=ops.attention(q,k,v,2,cu_seqlens_q=cu,cu_seqlens_k=cu);ops.check_status(d)\n"
-        "r=ops.attention_reference(q.cpu(),k.cpu(),v.cpu(),2,cu_seqlens_q=cu.cpu(),cu_seqlens_k=cu.cpu())\n"
-        "rel=((o.cpu().float()-r.float()).norm()/r.float().norm()).item();assert rel<2e-2,rel\n")
-    r = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, DS_ATTN_KERNEL="3"),
-                       capture_output=True, text=True, timeout=300)
-    assert r.returncode == 0, r.stdout + r.stderr

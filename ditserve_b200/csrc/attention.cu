@@ -59,6 +59,10 @@ struct AttnParams {
   int o_seq_local;
   int o_head_offset;
   int64_t o_peer_stride;
+  // block-sparse key tiles: query block qb (256 rows) attends to the 128-key tiles
+  // blk_index[blk_offsets[qb] .. blk_offsets[qb + 1]) of its segment (null: all tiles)
+  const int* blk_offsets;
+  const int* blk_index;
 };
 
 // ---------------------------------------------------------------------------
@@ -142,16 +146,24 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
     return;
   }
   const int nka = (ka1 - ka0 + kKT - 1) / kKT;
-  const int per_source = nka + (kb1 - kb0 + kKT - 1) / kKT;
+  const int* blk = nullptr;  // block-sparse: this query block's list of key tiles
+  int per_source = nka + (kb1 - kb0 + kKT - 1) / kKT;
+  if (p.blk_offsets != nullptr) {
+    const int o0 = p.blk_offsets[blockIdx.x];
+    blk = p.blk_index + o0;
+    per_source = p.blk_offsets[blockIdx.x + 1] - o0;
+  }
   const int n_tiles = per_source * p.kv_sources;
   if (n_tiles <= 0) return;  // uniform across the CTA
   // tile j reads source j / per_source; within a source the segment's key ranges repeat
   auto ktile_row = [&](int j) {
     const int jj = j % per_source;
+    if (blk != nullptr) return ka0 + blk[jj] * kKT;
     return jj < nka ? ka0 + jj * kKT : kb0 + (jj - nka) * kKT;
   };
   auto ktile_valid = [&](int j) {
     const int jj = j % per_source;
+    if (blk != nullptr) return ka1 - (ka0 + blk[jj] * kKT);
     return jj < nka ? ka1 - (ka0 + jj * kKT) : kb1 - (kb0 + (jj - nka) * kKT);
   };
   const int hk = h / (p.heads / p.heads_kv);
@@ -533,6 +545,10 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
   p.o_seq_local = a.o_seq_local;
   p.o_head_offset = a.o_head_offset;
   p.o_peer_stride = a.o_peer_stride;
+  p.blk_offsets = a.blk_offsets;
+  p.blk_index = a.blk_index;
+  if (a.blk_offsets != nullptr && (a.seg_table != nullptr || a.kv_sources != 1))
+    throw std::runtime_error("attention: block-sparse key tiles need one KV source and no dual-range table");
   // grid.x: 256-row query blocks of the longest segment (both ranges in dual-range mode)
   const int max_q = (a.cu_seqlens_q || a.seg_table) ? a.max_seq_q : a.seq_q;
   const int blocks = a.seg_table ? a.max_q_blocks : (max_q + 2 * kQT - 1) / (2 * kQT);

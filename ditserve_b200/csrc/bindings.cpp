@@ -84,7 +84,8 @@ void attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
                const c10::optional<at::Tensor>& cu_q, const c10::optional<at::Tensor>& cu_k, int64_t max_seq_q,
                int64_t heads, int64_t heads_kv, int64_t head_dim, double scale, const at::Tensor& status,
                const c10::optional<at::Tensor>& seg, int64_t max_q_blocks, std::vector<at::Tensor> k_extra,
-               std::vector<at::Tensor> v_extra) {
+               std::vector<at::Tensor> v_extra, const c10::optional<at::Tensor>& blk_offsets,
+               const c10::optional<at::Tensor>& blk_index) {
   check_cuda_bf16_2d(q, "q");
   check_cuda_bf16_2d(k, "k");
   check_cuda_bf16_2d(v, "v");
@@ -146,6 +147,20 @@ void attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
                 "attention: extra KV sources must match k/v in shape and stride");
     a.k_extra[i] = k_extra[i].data_ptr();
     a.v_extra[i] = v_extra[i].data_ptr();
+  }
+  TORCH_CHECK(blk_offsets.has_value() == blk_index.has_value(), "attention: give both block-sparse tensors or neither");
+  if (blk_offsets.has_value()) {
+    // the contents (every block non-empty, tile ids in range) are validated by the caller,
+    // which builds the table on the host; here only placement and type
+    TORCH_CHECK(blk_offsets->is_cuda() && blk_offsets->scalar_type() == at::kInt && blk_offsets->is_contiguous() &&
+                    blk_index->is_cuda() && blk_index->scalar_type() == at::kInt && blk_index->is_contiguous(),
+                "attention: block-sparse tables must be contiguous int32 on the device");
+    TORCH_CHECK(!seg.has_value() && !cu_q.has_value() && k_extra.empty(),
+                "attention: block-sparse needs uniform batches, one KV source and no seg table");
+    TORCH_CHECK(blk_offsets->numel() == (seq_q + 255) / 256 + 1, "attention: block-sparse offsets must have one "
+                "entry per 256-row query block plus one");
+    a.blk_offsets = blk_offsets->data_ptr<int>();
+    a.blk_index = blk_index->data_ptr<int>();
   }
   ds::launch_attention(a, at::cuda::getCurrentCUDAStream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently

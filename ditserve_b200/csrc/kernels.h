@@ -88,6 +88,11 @@ struct AttnArgs {
   int o_seq_local = 0;
   int o_head_offset = 0;
   int64_t o_peer_stride = 0;
+  // block-sparse attention: int32 CSR over query blocks of 256 rows (grid.x); query block qb
+  // attends only to the 128-key tiles blk_index[blk_offsets[qb] .. blk_offsets[qb + 1]) of its
+  // segment, every block naming at least one tile (one KV source, no dual-range table)
+  const int* blk_offsets = nullptr;
+  const int* blk_index = nullptr;
 };
 void launch_attention(const AttnArgs& a, cudaStream_t stream);
 

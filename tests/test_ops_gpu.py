@@ -283,3 +283,38 @@ def test_attention_p_chunk_variants(chunks):
     r = subprocess.run([sys.executable, "-c", code], env=dict(os.environ, DS_ATTN_PCHUNKS=chunks),
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("B,S,H,D,pattern", [(2, 700, 2, 128, "window"), (1, 1030, 3, 64, "random"),
+                                             (1, 2048, 2, 128, "tiles")])
+def test_block_sparse_attention_matches_masked_fp32(B, S, H, D, pattern):
+    """Only the named 128-key tiles of each 256-row query block are streamed; the result is the
+    fp32 softmax attention restricted to the same token pairs (masked tails included)."""
+    torch.manual_seed(7)
+    dev = torch.device("cuda", 0)
+    q = torch.randn(B, S, H * D, device=dev).bfloat16()
+    k = torch.randn(B, S, H * D, device=dev).bfloat16()
+    v = torch.randn(B, S, H * D, device=dev).bfloat16()
+    if pattern == "window":
+        bm = ops.sliding_window_block_mask(S, S, 200)
+    elif pattern == "tiles":
+        bm = ops.tile_window_block_mask((2, 32, 32), (1, 4, 4))
+    else:
+        g = torch.Generator().manual_seed(3)
+        bm = torch.rand(-(-S // 256), -(-S // 128), generator=g) < 0.4
+        bm[:, -1] = True  # the ragged last tile is always present
+    o, lse = ops.attention(q, k, v, H, block_mask=bm, return_lse=True)
+    ops.check_status(dev)
+    r, rl = ops.attention_reference(q.cpu(), k.cpu(), v.cpu(), H, return_lse=True, mask=ops.token_mask(bm, S, S))
+    rel = ((o.cpu().float() - r.float()).norm() / r.float().norm()).item()
+    assert rel < 2e-2, rel
+    assert (lse.cpu().view(H, B, S).transpose(0, 1) - rl).abs().max().item() < 2e-2
+
+
+def test_block_sparse_all_tiles_equals_dense_bitwise():
+    torch.manual_seed(8)
+    dev = torch.device("cuda", 0)
+    B, S, H, D = 2, 900, 2, 128
+    q, k, v = (torch.randn(B, S, H * D, device=dev).bfloat16() for _ in range(3))
+    full = torch.ones(-(-S // 256), -(-S // 128), dtype=torch.bool)
+    assert torch.equal(ops.attention(q, k, v, H, block_mask=full), ops.attention(q, k, v, H))

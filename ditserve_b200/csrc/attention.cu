@@ -63,6 +63,19 @@ struct AttnParams {
   // blk_index[blk_offsets[qb] .. blk_offsets[qb + 1]) of its segment (null: all tiles)
   const int* blk_offsets;
   const int* blk_index;
+  unsigned long long* trace;  // timeline of one CTA (kTrace instantiation only), else null
+};
+
+// Timeline instrumentation (kTrace): one CTA in the middle of the grid records SM clock
+// stamps of its MMA warp and of row 0 of each softmax warpgroup for the first kTraceTiles
+// key tiles: trace[j * kTraceEvents + e].  Off in every production instantiation.
+constexpr int kTraceTiles = 32;
+constexpr int kTraceEvents = 16;
+enum TraceEvent {
+  kTrVFull = 0, kTrPvA = 1, kTrSA = 2, kTrPvB = 3, kTrSB = 4,   // MMA warp
+  kTrSoftBase = 5,                                               // + 5 * tile below
+  kTrSFull = 0, kTrLoaded = 1, kTrMax = 2, kTrExp = 3, kTrArrive = 4,
+  kTrEnd = 15,
 };
 
 // ---------------------------------------------------------------------------
@@ -109,7 +122,7 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 // kPChunks: the softmax hands P to the MMA warp in this many column chunks (one mbarrier
 // phase per chunk), so the PV MMA of the first keys starts while the exponentials of the
 // last keys are still being computed.
-template <int D, int kPChunks>
+template <int D, int kPChunks, bool kTrace = false>
 __global__ void __launch_bounds__(kAttn2Threads, 1)
     attention2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ KvMaps kv,
                       AttnParams p) {
@@ -212,6 +225,11 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const bool tracing = kTrace && p.trace != nullptr && blockIdx.x == gridDim.x / 2 && blockIdx.y == 0 &&
+                       blockIdx.z == 0;
+  auto rec = [&](int j, int e) {
+    if (kTrace && tracing && j < kTraceTiles) p.trace[j * kTraceEvents + e] = clock64();
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -295,20 +313,25 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       }
       for (int j = 0; ok && j < n_tiles; ++j) {
         if (!mbar_wait(&v_full[j % VS], (j / VS) & 1, abort_flag, p.status, 224)) break;
+        rec(j, kTrVFull);
         tc_fence_after();
         if (!issue_pv(0, j)) break;
+        rec(j, kTrPvA);
         const bool more = j + 1 < n_tiles;
         if (more) {
           const int st = (j + 1) % KS;
           if (!mbar_wait(&k_full[st], ((j + 1) / KS) & 1, abort_flag, p.status, 225)) break;
           tc_fence_after();
           issue_s(0, j + 1);
+          rec(j, kTrSA);
         }
         if (!issue_pv(1, j)) break;
+        rec(j, kTrPvB);
         umma_commit(&v_empty[j % VS]);
         if (more) {
           issue_s(1, j + 1);
           umma_commit(&k_empty[(j + 1) % KS]);
+          rec(j, kTrSB);
         }
       }
     }
@@ -325,11 +348,16 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = true;
+    const bool trace_row = row == 0;
+    auto srec = [&](int j, int e) {
+      if (kTrace && trace_row) rec(j, kTrSoftBase + 5 * t + e);
+    };
     for (int j = 0; j < n_tiles; ++j) {
       if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.status, 230 + t)) {
         ok = false;
         break;
       }
+      srec(j, kTrSFull);
       tc_fence_after();
       const int valid = ktile_valid(j);  // columns >= valid are outside the segment
       const bool masked = valid < kKT;
@@ -339,6 +367,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       for (int c = 0; c < kKT / 32; ++c)
         tmem_ld32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
+      srec(j, kTrLoaded);
       float mx = -INFINITY;
       if (masked) {
 #pragma unroll
@@ -355,6 +384,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         mx = fmaxf(fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3])), fmaxf(fmaxf(mc[4], mc[5]), fmaxf(mc[6], mc[7])));
       }
       const float m_new = fmaxf(m_run, mx);
+      srec(j, kTrMax);
       const bool need = (m_new - m_run) * sl2 > 8.0f;  // always true on the first tile
       float alpha = 1.f;
       if (need) {
@@ -437,6 +467,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         }
       }
       l_run += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+      srec(j, kTrExp);
       // O rescale after the exponentials: the S row is dead by now, so the O chunks do not
       // add to the peak register use; PV(j) only starts after p_full below
       if (j > 0 && __any_sync(0xffffffffu, need)) {
@@ -454,6 +485,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       tmem_wait_st();
       tc_fence_before();
       for (int c = signalled / (kKT / 8 / kPChunks); c < kPChunks; ++c) mbar_arrive(&p_full[t * kPChunks + c]);
+      srec(j, kTrArrive);
     }
     if (ok) ok = mbar_wait(&pv_done[t], (n_tiles - 1) & 1, abort_flag, p.status, 234 + t);
     if (ok) {
@@ -498,6 +530,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (kTrace && tracing && threadIdx.x == 0) p.trace[kTrEnd] = clock64();
   if (*abort_flag && threadIdx.x == 0) {
     const unsigned long long t0 = globaltimer_ns();
     while (globaltimer_ns() - t0 < 1000000ull) {
@@ -558,7 +591,11 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
     const int v = e != nullptr ? std::atoi(e) : 2;
     return v == 1 || v == 4 ? v : 2;
   }();
-  auto kern = pchunks == 1 ? attention2_kernel<D, 1> : pchunks == 4 ? attention2_kernel<D, 4> : attention2_kernel<D, 2>;
+  p.trace = a.trace;
+  auto kern = a.trace != nullptr ? attention2_kernel<D, 2, true>
+              : pchunks == 1     ? attention2_kernel<D, 1>
+              : pchunks == 4     ? attention2_kernel<D, 4>
+                                 : attention2_kernel<D, 2>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Cfg<D>::kSmemBytes);
   dim3 grid(blocks, a.heads, a.batch);
   kern<<<grid, kAttn2Threads, Attn2Cfg<D>::kSmemBytes, stream>>>(tq, kv, p);

@@ -427,6 +427,42 @@ void qkv_scatter(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& 
   C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
 
+// Dense uniform-batch attention with the timeline of one CTA recorded into `trace`
+// (int64 [32 * 16], SM clock stamps); profiling only.
+void attention_trace(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, int64_t batch,
+                     int64_t seq, int64_t heads, int64_t head_dim, double scale, const at::Tensor& status,
+                     at::Tensor& trace) {
+  check_cuda_bf16_2d(q, "q");
+  check_cuda_bf16_2d(k, "k");
+  check_cuda_bf16_2d(v, "v");
+  check_cuda_bf16_2d(o, "o");
+  TORCH_CHECK(q.size(0) == batch * seq && k.size(0) == batch * seq && v.size(0) == batch * seq &&
+                  q.size(1) == heads * head_dim && o.sizes() == q.sizes(),
+              "attention_trace: shapes");
+  TORCH_CHECK(trace.is_cuda() && trace.scalar_type() == at::kLong && trace.is_contiguous() && trace.numel() >= 32 * 16,
+              "attention_trace: trace must be int64 [>= 512] on the device");
+  const c10::cuda::CUDAGuard guard(q.device());
+  ds::AttnArgs a;
+  a.q = q.data_ptr();
+  a.q_row_stride = q.stride(0);
+  a.k = k.data_ptr();
+  a.k_row_stride = k.stride(0);
+  a.v = v.data_ptr();
+  a.v_row_stride = v.stride(0);
+  a.o = o.data_ptr();
+  a.o_row_stride = o.stride(0);
+  a.total_q = a.total_k = static_cast<int>(q.size(0));
+  a.batch = static_cast<int>(batch);
+  a.seq_q = a.seq_k = static_cast<int>(seq);
+  a.heads = a.heads_kv = static_cast<int>(heads);
+  a.head_dim = static_cast<int>(head_dim);
+  a.softmax_scale = static_cast<float>(scale);
+  a.status = status_ptr(status);
+  a.trace = reinterpret_cast<unsigned long long*>(trace.data_ptr<int64_t>());
+  ds::launch_attention(a, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void attention_scatter(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t batch, int64_t seq,
                        int64_t heads, int64_t head_dim, double scale, int64_t rank, const std::vector<int64_t>& bases,
                        int64_t timeout_ns, int64_t o_off, int64_t seq_local, int64_t head_offset,
@@ -611,6 +647,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("group_barrier", &group_barrier, "bounded flag barrier over peer memory");
   m.def("cfg_step_peer", &cfg_step_peer, "CFG exchange over NVLink fused with guidance + latent update");
   m.def("qkv_scatter", &qkv_scatter, "RMS qk-norm + RoPE + Ulysses all-to-all scatter");
+  m.def("attention_trace", &attention_trace, "attention with a one-CTA clock timeline (profiling)");
   m.def("attention_scatter", &attention_scatter, "attention with the head->sequence all-to-all in its epilogue");
   m.def("allgather_rows", &allgather_rows, "sequence all-gather by peer stores");
   m.def("strided_put", &strided_put, "strided slice -> contiguous buffer of a group member (halo exchange)");

@@ -186,7 +186,7 @@ class FusedCFG:
         epoch = self.heap.next_epoch(self.group.channel)
         st = status_word(sample.device)
 
-        def kernel(cond, uncond, g, x, sigma, corr, pred, x0_out=None, last_out=None):
+        def step_kernel(cond, uncond, g, x, sigma, corr, pred, x0_out=None, last_out=None):
             c = corr or {}
             kernel("cfg_step_peer")(
                 slot, slot_off, self.cfg_rank, float(g), x, float(sigma), corr is not None, c.get("last"),
@@ -196,7 +196,7 @@ class FusedCFG:
                 x0_out, last_out, r, bases, tmo, self.group.channel, epoch, st, delta_out)
             return x
 
-        return scheduler.step(sample, mine.reshape(-1), None, guidance, kernel=kernel)
+        return scheduler.step(sample, mine.reshape(-1), None, guidance, kernel=step_kernel)
 
 
 def upgrade(layout, rank, device, pctx, cfg_plan, sp_groups, cfg_groups, seq_local=None, cfg=None,

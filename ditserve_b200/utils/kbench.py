@@ -53,7 +53,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=32760)
     ap.add_argument("--batch", type=int, default=2)
     ap.add_argument("--only", default=None, help="'fused': only the peer-memory kernels on a one-member group; 'attention': self-attention only; "
-                         "'memory': the per-token norm kernels and qkv_scatter; 'cross': cross-attention (512 keys) only")
+                         "'memory': the per-token norm kernels and qkv_scatter; 'cross': cross-attention (512 keys) only; 'trace': SM-clock timeline of one self-attention CTA")
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     tflops_peak, hbm_peak, src = peaks()
@@ -84,6 +84,9 @@ def main():
         row("self_attention", ms, flops=4.0 * B * H * S * S * 128, impl="ours")
         if args.json:
             json.dump(res, open(args.json, "w"), indent=1)
+        return
+    if args.only == "trace":
+        attention_timeline(dev, S, B, D, H)
         return
     if args.only == "cross":
         q = torch.randn(M, D, device=dev).bfloat16()
@@ -160,6 +163,35 @@ def main():
     ops.check_status(dev)
     if args.json:
         json.dump(res, open(args.json, "w"), indent=1)
+
+
+def attention_timeline(dev, S, B, D, H):
+    """SM-clock timeline of one CTA of the self-attention kernel (middle of the grid): per key
+    tile, when the MMA warp got V and each P, issued the next S, and when row 0 of each softmax
+    warpgroup saw S, had it loaded, had the max, finished the exponentials and handed P over."""
+    from ..ops._ext import ext, status_word
+    M = S * B
+    qkv = torch.randn(M, 3 * D, device=dev).bfloat16()
+    q, k, v = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
+    o = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
+    tr = torch.zeros(32 * 16, dtype=torch.int64, device=dev)
+    for _ in range(3):  # warm clocks and caches; the last launch's stamps are kept
+        tr.zero_()
+        ext().attention_trace(q, k, v, o, B, S, H, D // H, 1.0 / math.sqrt(D // H), status_word(dev), tr)
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    t = tr.view(32, 16).cpu()
+    t0 = int(t[0, 0])
+    names = ["vfull", "pvA_issued", "sA_next_issued", "pvB_issued", "sB_next_issued",
+             "A_sfull", "A_loaded", "A_max", "A_exp", "A_arrive", "B_sfull", "B_loaded", "B_max", "B_exp", "B_arrive"]
+    for j in range(32):
+        print(json.dumps({"tile": j, **{n: int(t[j, e]) - t0 if int(t[j, e]) else None for e, n in enumerate(names)}}))
+    per = (int(t[24, 0]) - int(t[8, 0])) / 16
+    a_soft = sum(int(t[j, 8]) - int(t[j, 5]) for j in range(8, 24)) / 16
+    b_soft = sum(int(t[j, 13]) - int(t[j, 10]) for j in range(8, 24)) / 16
+    a_ld = sum(int(t[j, 6]) - int(t[j, 5]) for j in range(8, 24)) / 16
+    print(json.dumps({"cycles_per_tile": per, "A_sfull_to_exp_done": a_soft, "B_sfull_to_exp_done": b_soft,
+                      "A_tmem_load": a_ld, "cta_cycles": int(t[0, 15]) - t0 if int(t[0, 15]) else None}))
 
 
 def memory_rows(row, timeit, dev, S, B, D, H, flush):

@@ -92,3 +92,4 @@ def test_elastic_paths_multi_gpu():
     assert r.returncode == 0, r.stderr[-3000:]
     res = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
     assert res["flags_agree"] and res["broadcast_bitwise"] and res["broadcast_ce_bitwise"], res
+

@@ -93,16 +93,25 @@ enum TraceEvent {
 // spills.  Shared memory holds Q_A, Q_B and two stages each of K and V.
 constexpr int kAttn2Threads = 384;
 
-template <int D>
+// kTiles = 2 is the kernel described above.  kTiles = 1 is its short-KV form (cross-attention
+// over a few hundred text keys): one 128-row Q tile and one softmax warpgroup per CTA (192
+// threads: producer warp, MMA warp, softmax warps 2..5), 256 TMEM columns (S, O) and single K
+// and V stages (97 KB of shared memory), so two CTAs share an SM.  With only a handful of key
+// tiles per CTA, most of a CTA's life is its prologue (Q load, first QK^T) and epilogue (O
+// read-out and store); a second resident CTA runs its main loop through them.
+template <int D, int kTiles = 2>
 struct Attn2Cfg {
   static constexpr int kAtoms = D / 64;
   static constexpr int kQBytes = kQT * D * 2;
   static constexpr int kKBytes = kKT * D * 2;
   static constexpr int kVBytes = kKT * D * 2;
-  static constexpr int KS = 2;
-  static constexpr int VS = 2;
-  static constexpr int kSmemBytes = 2 * kQBytes + KS * kKBytes + VS * kVBytes + 1024 /*align*/ + 512 /*barriers*/;
-  static constexpr int kTmemCols = 512;
+  static constexpr int KS = kTiles == 2 ? 2 : 1;
+  static constexpr int VS = kTiles == 2 ? 2 : 1;
+  static constexpr int kSmemBytes =
+      kTiles * kQBytes + KS * kKBytes + VS * kVBytes + 1024 /*align*/ + 512 /*barriers*/;
+  static constexpr int kTmemCols = kTiles == 2 ? 512 : 256;
+  static constexpr int kThreads = kTiles == 2 ? 384 : 192;
+  static constexpr int kOBase = kTiles * 128;  // first TMEM column of O (S tiles come first)
 };
 
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
@@ -122,13 +131,14 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 // kPChunks: the softmax hands P to the MMA warp in this many column chunks (one mbarrier
 // phase per chunk), so the PV MMA of the first keys starts while the exponentials of the
 // last keys are still being computed.
-template <int D, int kPChunks, bool kTrace = false>
-__global__ void __launch_bounds__(kAttn2Threads, 1)
+template <int D, int kPChunks, bool kTrace = false, int kTiles = 2>
+__global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1 : 2)
     attention2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ KvMaps kv,
                       AttnParams p) {
-  using Cfg = Attn2Cfg<D>;
+  using Cfg = Attn2Cfg<D, kTiles>;
   constexpr int KS = Cfg::KS;
   constexpr int VS = Cfg::VS;
+  constexpr int kQBlock = kTiles * kQT;  // query rows per CTA
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   // segment = query rows [qa0,qa1) u [qb0,qb1) attending to keys [ka0,ka1) u [kb0,kb1)
@@ -146,14 +156,14 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
     ka0 = b * p.seq_k; ka1 = ka0 + p.seq_k;
     qb0 = qb1 = kb0 = kb1 = 0;
   }
-  const int nqa = (qa1 - qa0 + 2 * kQT - 1) / (2 * kQT);
-  const int nqb = (qb1 - qb0 + 2 * kQT - 1) / (2 * kQT);
+  const int nqa = (qa1 - qa0 + kQBlock - 1) / kQBlock;
+  const int nqb = (qb1 - qb0 + kQBlock - 1) / kQBlock;
   int q0, q_end;
   if (static_cast<int>(blockIdx.x) < nqa) {
-    q0 = qa0 + blockIdx.x * 2 * kQT;
+    q0 = qa0 + blockIdx.x * kQBlock;
     q_end = qa1;
   } else if (static_cast<int>(blockIdx.x) < nqa + nqb) {
-    q0 = qb0 + (blockIdx.x - nqa) * 2 * kQT;
+    q0 = qb0 + (blockIdx.x - nqa) * kQBlock;
     q_end = qb1;
   } else {
     return;
@@ -184,7 +194,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                   // [2][kQBytes]
-  uint8_t* sK = sQ + 2 * Cfg::kQBytes;                  // [KS][kKBytes]
+  uint8_t* sK = sQ + kTiles * Cfg::kQBytes;             // [KS][kKBytes]
   uint8_t* sV = sK + KS * Cfg::kKBytes;                 // [VS][kVBytes]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + VS * Cfg::kVBytes);
   uint64_t* q_full = bars;
@@ -193,9 +203,9 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   uint64_t* v_full = k_empty + KS;
   uint64_t* v_empty = v_full + VS;
   uint64_t* s_full = v_empty + VS;  // [2] per tile
-  uint64_t* p_full = s_full + 2;    // [2 tiles][kPChunks]
-  uint64_t* pv_done = p_full + 2 * kPChunks;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+  uint64_t* p_full = s_full + kTiles;    // [kTiles][kPChunks]
+  uint64_t* pv_done = p_full + kTiles * kPChunks;  // [kTiles]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + kTiles);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -212,11 +222,11 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kTiles; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&pv_done[i], 1);
     }
-    for (int i = 0; i < 2 * kPChunks; ++i) mbar_init(&p_full[i], 128);
+    for (int i = 0; i < kTiles * kPChunks; ++i) mbar_init(&p_full[i], 128);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -239,9 +249,9 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         tma_prefetch_desc(&kv.k[src]);
         tma_prefetch_desc(&kv.v[src]);
       }
-      mbar_arrive_expect_tx(q_full, 2 * Cfg::kQBytes);
+      mbar_arrive_expect_tx(q_full, kTiles * Cfg::kQBytes);
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
+      for (int t = 0; t < kTiles; ++t)
 #pragma unroll
         for (int a = 0; a < Cfg::kAtoms; ++a)
           tma_load_2d(sQ + t * Cfg::kQBytes + a * (kQT * 128), &tmQ, h * D + a * 64, q0 + t * kQT, q_full);
@@ -285,7 +295,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         umma_commit(&s_full[t]);
       };
       auto issue_pv = [&](int t, int j) -> bool {
-        const uint32_t d = tmem_base + 256 + t * 128;
+        const uint32_t d = tmem_base + Cfg::kOBase + t * 128;
         const uint32_t p_tmem = tmem_base + t * kKT;  // bf16 P packed over the first 64 S columns
         const uint32_t v_base = smem_u32(sV + (j % VS) * Cfg::kVBytes);
         constexpr int kPerChunk = kKT / 16 / kPChunks;  // K=16 MMAs per P chunk
@@ -308,10 +318,24 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       if (ok) {
         tc_fence_after();
         issue_s(0, 0);
-        issue_s(1, 0);
+        if (kTiles == 2) issue_s(1, 0);
         umma_commit(&k_empty[0]);
       }
-      for (int j = 0; ok && j < n_tiles; ++j) {
+      for (int j = 0; ok && kTiles == 1 && j < n_tiles; ++j) {
+        // one Q tile: PV(j), then S(j+1) into the columns P(j) occupied
+        if (!mbar_wait(&v_full[j % VS], (j / VS) & 1, abort_flag, p.status, 224)) break;
+        tc_fence_after();
+        if (!issue_pv(0, j)) break;
+        umma_commit(&v_empty[j % VS]);
+        if (j + 1 < n_tiles) {
+          const int st = (j + 1) % KS;
+          if (!mbar_wait(&k_full[st], ((j + 1) / KS) & 1, abort_flag, p.status, 225)) break;
+          tc_fence_after();
+          issue_s(0, j + 1);
+          umma_commit(&k_empty[st]);
+        }
+      }
+      for (int j = 0; ok && kTiles == 2 && j < n_tiles; ++j) {
         if (!mbar_wait(&v_full[j % VS], (j / VS) & 1, abort_flag, p.status, 224)) break;
         rec(j, kTrVFull);
         tc_fence_after();
@@ -335,14 +359,14 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
         }
       }
     }
-  } else if (wg >= 1) {
-    // ---------------- softmax warpgroups (tile t = wg - 1) ----------------
-    const int t = wg - 1;
+  } else if (kTiles == 2 ? wg >= 1 : warp >= 2) {
+    // ---------------- softmax warpgroups (tile t = wg - 1; warps 2..5 when kTiles = 1) ----------------
+    const int t = kTiles == 2 ? wg - 1 : 0;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_col = tmem_base + lane_addr + t * kKT;
-    const uint32_t o_col = tmem_base + lane_addr + 256 + t * 128;
+    const uint32_t o_col = tmem_base + lane_addr + Cfg::kOBase + t * 128;
     const float sl2 = p.scale_log2;
     const uint64_t sl2x2 = f2_pack(sl2, sl2);
     float m_run = -INFINITY;
@@ -592,6 +616,22 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
     return v == 1 || v == 4 ? v : 2;
   }();
   p.trace = a.trace;
+  // short key ranges (cross-attention): one Q tile per CTA, two CTAs per SM.  Uniform batches
+  // only (the 256-row block numbering of the dual-range and block-sparse tables stays as is);
+  // DS_ATTN_SHORT_KV sets the largest key count that takes this form (default 1024, 0: never)
+  static const int short_kv = [] {
+    const char* e = std::getenv("DS_ATTN_SHORT_KV");
+    return e != nullptr ? std::atoi(e) : 1024;
+  }();
+  const bool uniform = a.cu_seqlens_q == nullptr && a.seg_table == nullptr && a.blk_offsets == nullptr;
+  if (uniform && a.trace == nullptr && static_cast<int64_t>(a.seq_k) * a.kv_sources <= short_kv) {
+    using C1 = Attn2Cfg<D, 1>;
+    auto kern1 = attention2_kernel<D, 2, false, 1>;
+    cudaFuncSetAttribute(kern1, cudaFuncAttributeMaxDynamicSharedMemorySize, C1::kSmemBytes);
+    dim3 grid1((a.seq_q + kQT - 1) / kQT, a.heads, a.batch);
+    kern1<<<grid1, C1::kThreads, C1::kSmemBytes, stream>>>(tq, kv, p);
+    return;
+  }
   auto kern = a.trace != nullptr ? attention2_kernel<D, 2, true>
               : pchunks == 1     ? attention2_kernel<D, 1>
               : pchunks == 4     ? attention2_kernel<D, 4>

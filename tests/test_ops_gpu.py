@@ -318,3 +318,31 @@ def test_block_sparse_all_tiles_equals_dense_bitwise():
     q, k, v = (torch.randn(B, S, H * D, device=dev).bfloat16() for _ in range(3))
     full = torch.ones(-(-S // 256), -(-S // 128), dtype=torch.bool)
     assert torch.equal(ops.attention(q, k, v, H, block_mask=full), ops.attention(q, k, v, H))
+
+
+@pytest.mark.parametrize("B,Sq,Sk,H,D", [(2, 1000, 512, 3, 128), (1, 777, 77, 2, 64)])
+def test_short_kv_form_equals_two_tile_form_bitwise(tmp_path, B, Sq, Sk, H, D):
+    """Key ranges up to DS_ATTN_SHORT_KV (default 1024) run one Q tile per CTA, two CTAs per SM;
+    the per-row arithmetic is the two-tile kernel's, so the outputs agree bit for bit."""
+    import os
+    import subprocess
+    import sys
+    torch.manual_seed(9)
+    d = _dev()
+    q = torch.randn(B, Sq, H * D).bfloat16()
+    k = torch.randn(B, Sk, H * D).bfloat16()
+    v = torch.randn(B, Sk, H * D).bfloat16()
+    torch.save((q, k, v), tmp_path / "in.pt")
+    o, lse = ops.attention(q.to(d), k.to(d), v.to(d), H, return_lse=True)
+    ops.check_status(d)
+    code = ("import torch,sys;from ditserve_b200 import ops\n"
+            f"q,k,v=torch.load(sys.argv[1]);d=torch.device('cuda',0)\n"
+            f"o,l=ops.attention(q.to(d),k.to(d),v.to(d),{H},return_lse=True);ops.check_status(d)\n"
+            "torch.save((o.cpu(),l.cpu()),sys.argv[2])\n")
+    r = subprocess.run([sys.executable, "-c", code, str(tmp_path / "in.pt"), str(tmp_path / "out.pt")],
+                       env=dict(os.environ, DS_ATTN_SHORT_KV="0"), capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    o2, l2 = torch.load(tmp_path / "out.pt")
+    assert torch.equal(o.cpu(), o2) and torch.equal(lse.cpu(), l2)
+    ro = ops.attention_reference(q, k, v, H)
+    assert _rel(o.cpu(), ro) < 2e-2

@@ -70,12 +70,14 @@ struct AttnParams {
 // stamps of its MMA warp and of row 0 of each softmax warpgroup for the first kTraceTiles
 // key tiles: trace[j * kTraceEvents + e].  Off in every production instantiation.
 constexpr int kTraceTiles = 32;
-constexpr int kTraceEvents = 16;
+constexpr int kTraceEvents = 24;
 enum TraceEvent {
   kTrVFull = 0, kTrPvA = 1, kTrSA = 2, kTrPvB = 3, kTrSB = 4,   // MMA warp
   kTrSoftBase = 5,                                               // + 5 * tile below
   kTrSFull = 0, kTrLoaded = 1, kTrMax = 2, kTrExp = 3, kTrArrive = 4,
-  kTrEnd = 15,
+  kTrArriveQuarter = 15,  // + quarter - 1: final P arrive of tile A rows 32, 64, 96
+  kTrPWaitA = 18,         // + chunk: the MMA warp's wait for P chunk of tile A returned
+  kTrEnd = 23,
 };
 
 // ---------------------------------------------------------------------------
@@ -127,6 +129,7 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
   return r;
 }
+
 
 // kPChunks: the softmax hands P to the MMA warp in this many column chunks (one mbarrier
 // phase per chunk), so the PV MMA of the first keys starts while the exponentials of the
@@ -302,6 +305,7 @@ __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1
 #pragma unroll
         for (int c = 0; c < kPChunks; ++c) {
           if (!mbar_wait(&p_full[t * kPChunks + c], j & 1, abort_flag, p.status, 222 + t)) return false;
+          if (t == 0 && c < 2) rec(j, kTrPWaitA + c);
           tc_fence_after();
 #pragma unroll
           for (int i = 0; i < kPerChunk; ++i) {
@@ -375,6 +379,7 @@ __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1
     const bool trace_row = row == 0;
     auto srec = [&](int j, int e) {
       if (kTrace && trace_row) rec(j, kTrSoftBase + 5 * t + e);
+      if (kTrace && e == kTrArrive && t == 0 && lane == 0 && quarter > 0) rec(j, kTrArriveQuarter + quarter - 1);
     };
     for (int j = 0; j < n_tiles; ++j) {
       if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.status, 230 + t)) {
@@ -467,6 +472,7 @@ __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1
         // with no O rescale pending in this warp (the common case), each finished P chunk is
         // handed to the MMA warp at once; otherwise all chunks go after the rescale below
         const bool early = kPChunks > 1 && !(j > 0 && __any_sync(0xffffffffu, need));
+        constexpr int kChunkCh = kKT / 8 / kPChunks;  // 8-column steps per P chunk
 #pragma unroll
         for (int ch = 0; ch < kKT / 8; ++ch) {
           float e8[8];
@@ -482,10 +488,10 @@ __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1
             ls[e + 1] += e8[e + 1];
           }
           p_chunk(ch, e8);
-          if (kPChunks > 1 && early && ((ch + 1) % (kKT / 8 / kPChunks)) == 0) {
+          if (kPChunks > 1 && early && ((ch + 1) % kChunkCh) == 0) {
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&p_full[t * kPChunks + (ch + 1) / (kKT / 8 / kPChunks) - 1]);
+            mbar_arrive(&p_full[t * kPChunks + (ch + 1) / kChunkCh - 1]);
             signalled = ch + 1;
           }
         }

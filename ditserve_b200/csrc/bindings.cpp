@@ -428,7 +428,7 @@ void qkv_scatter(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& 
 }
 
 // Dense uniform-batch attention with the timeline of one CTA recorded into `trace`
-// (int64 [32 * 16], SM clock stamps); profiling only.
+// (int64 [32 * 24], SM clock stamps); profiling only.
 void attention_trace(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, int64_t batch,
                      int64_t seq, int64_t heads, int64_t head_dim, double scale, const at::Tensor& status,
                      at::Tensor& trace) {
@@ -439,8 +439,8 @@ void attention_trace(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
   TORCH_CHECK(q.size(0) == batch * seq && k.size(0) == batch * seq && v.size(0) == batch * seq &&
                   q.size(1) == heads * head_dim && o.sizes() == q.sizes(),
               "attention_trace: shapes");
-  TORCH_CHECK(trace.is_cuda() && trace.scalar_type() == at::kLong && trace.is_contiguous() && trace.numel() >= 32 * 16,
-              "attention_trace: trace must be int64 [>= 512] on the device");
+  TORCH_CHECK(trace.is_cuda() && trace.scalar_type() == at::kLong && trace.is_contiguous() && trace.numel() >= 32 * 24,
+              "attention_trace: trace must be int64 [>= 768] on the device");
   const c10::cuda::CUDAGuard guard(q.device());
   ds::AttnArgs a;
   a.q = q.data_ptr();

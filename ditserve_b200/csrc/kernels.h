@@ -93,7 +93,7 @@ struct AttnArgs {
   // segment, every block naming at least one tile (one KV source, no dual-range table)
   const int* blk_offsets = nullptr;
   const int* blk_index = nullptr;
-  // optional timeline of one CTA (SM clock stamps, [32 tiles][16 events]); profiling only
+  // optional timeline of one CTA (SM clock stamps, [32 tiles][24 events]); profiling only
   unsigned long long* trace = nullptr;
 };
 void launch_attention(const AttnArgs& a, cudaStream_t stream);

@@ -174,16 +174,17 @@ def attention_timeline(dev, S, B, D, H):
     qkv = torch.randn(M, 3 * D, device=dev).bfloat16()
     q, k, v = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
     o = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
-    tr = torch.zeros(32 * 16, dtype=torch.int64, device=dev)
+    tr = torch.zeros(32 * 24, dtype=torch.int64, device=dev)
     for _ in range(3):  # warm clocks and caches; the last launch's stamps are kept
         tr.zero_()
         ext().attention_trace(q, k, v, o, B, S, H, D // H, 1.0 / math.sqrt(D // H), status_word(dev), tr)
     torch.cuda.synchronize()
     ops.check_status(dev)
-    t = tr.view(32, 16).cpu()
+    t = tr.view(32, 24).cpu()
     t0 = int(t[0, 0])
     names = ["vfull", "pvA_issued", "sA_next_issued", "pvB_issued", "sB_next_issued",
-             "A_sfull", "A_loaded", "A_max", "A_exp", "A_arrive", "B_sfull", "B_loaded", "B_max", "B_exp", "B_arrive"]
+             "A_sfull", "A_loaded", "A_max", "A_exp", "A_arrive", "B_sfull", "B_loaded", "B_max", "B_exp", "B_arrive",
+             "A_arrive_w1", "A_arrive_w2", "A_arrive_w3", "mma_pA0_seen", "mma_pA1_seen"]
     for j in range(32):
         print(json.dumps({"tile": j, **{n: int(t[j, e]) - t0 if int(t[j, e]) else None for e, n in enumerate(names)}}))
     per = (int(t[24, 0]) - int(t[8, 0])) / 16
@@ -191,7 +192,7 @@ def attention_timeline(dev, S, B, D, H):
     b_soft = sum(int(t[j, 13]) - int(t[j, 10]) for j in range(8, 24)) / 16
     a_ld = sum(int(t[j, 6]) - int(t[j, 5]) for j in range(8, 24)) / 16
     print(json.dumps({"cycles_per_tile": per, "A_sfull_to_exp_done": a_soft, "B_sfull_to_exp_done": b_soft,
-                      "A_tmem_load": a_ld, "cta_cycles": int(t[0, 15]) - t0 if int(t[0, 15]) else None}))
+                      "A_tmem_load": a_ld, "cta_cycles": int(t[0, 23]) - t0 if int(t[0, 23]) else None}))
 
 
 def memory_rows(row, timeit, dev, S, B, D, H, flush):

@@ -111,7 +111,7 @@ def main():
             json.dump(res, open(args.json, "w"), indent=1)
         return
     x = torch.randn(M, D, device=dev).bfloat16()
-    for name, N, K, kw in [("qkv_proj", 3 * D, D, {}), ("out_proj_gated", D, D, {"gate": True}),
+    for name, N, K, kw in [("qkv_proj", 3 * D, D, {}), ("out_proj_plain", D, D, {}), ("out_proj_gated", D, D, {"gate": True}),
                            ("ffn_up_gelu", F, D, {"act": "gelu"}), ("ffn_down_gated", D, F, {"gate": True})]:
         a = torch.randn(M, K, device=dev).bfloat16()
         w = (torch.randn(N, K, device=dev) / math.sqrt(K)).bfloat16()

@@ -62,21 +62,38 @@ struct EpiParams {
   int* status;
 };
 
-// Drains accumulator columns [c_begin*32, c_end*32) of one TMEM lane (row m of the output)
-// through the fused epilogue into C.  `taddr` addresses the lane's first accumulator column.
-template <int BN, int EPI>
-__device__ __forceinline__ void epilogue_rows(const EpiParams& p, uint32_t taddr, int m, bool row_ok, int n0,
-                                              const float* gate_row, int c_begin, int c_end) {
-#pragma unroll 1
-  for (int c = c_begin; c < c_end; ++c) {
-    const int n = n0 + c * 32;
-    // the residual row segment is requested before the TMEM load so both latencies overlap
-    uint4 rv[4];
-    if ((EPI == kEpiGatedRes || EPI == kEpiRes) && row_ok) {
-      const uint4* rp = reinterpret_cast<const uint4*>(p.R + static_cast<int64_t>(m) * p.ldr + n);
+// The residual segment of one output row that an epilogue thread drains: kCount chunks of 32
+// bf16 starting at column n0 + c_begin * 32.  It is requested before the thread waits for the
+// accumulator, so the loads travel while the tile's main loop runs (a short-K GEMM such as the
+// gated out-projection otherwise waits for one residual round trip per chunk).
+template <int kCount>
+struct ResidualRow {
+  uint4 v[kCount][4];
+};
+
+template <int kCount, int EPI>
+__device__ __forceinline__ void prefetch_residual(const EpiParams& p, int m, bool row_ok, int n0, int c_begin,
+                                                  ResidualRow<kCount>& rr) {
+  if ((EPI == kEpiGatedRes || EPI == kEpiRes) && row_ok) {
+    const uint4* rp = reinterpret_cast<const uint4*>(p.R + static_cast<int64_t>(m) * p.ldr + n0 + c_begin * 32);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) rv[q] = rp[q];
-    }
+    for (int i = 0; i < kCount; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) rr.v[i][q] = rp[i * 4 + q];
+  }
+}
+
+// Drains accumulator columns [c_begin*32, (c_begin + kCount)*32) of one TMEM lane (row m of the
+// output) through the fused epilogue into C.  `taddr` addresses the lane's first accumulator column.
+template <int BN, int EPI, int kCount>
+__device__ __forceinline__ void epilogue_rows(const EpiParams& p, uint32_t taddr, int m, bool row_ok, int n0,
+                                              const float* gate_row, int c_begin, const ResidualRow<kCount>& rr) {
+  // gate rows are fp32 [B, N]; 16-byte vector loads when the row allows them
+  const bool gate_vec = gate_row != nullptr && (reinterpret_cast<uintptr_t>(gate_row) & 15) == 0;
+#pragma unroll
+  for (int i = 0; i < kCount; ++i) {
+    const int c = c_begin + i;
+    const int n = n0 + c * 32;
     uint32_t r[32];
     tmem_ld32(taddr + c * 32, r);
     tmem_wait_ld();
@@ -103,16 +120,32 @@ __device__ __forceinline__ void epilogue_rows(const EpiParams& p, uint32_t taddr
         for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
       }
       if (EPI == kEpiGatedRes || EPI == kEpiRes) {
+        float g[32];
+        if (EPI == kEpiGatedRes) {
+          if (gate_vec) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 t4 = __ldg(reinterpret_cast<const float4*>(gate_row + n) + q);
+              g[q * 4 + 0] = t4.x;
+              g[q * 4 + 1] = t4.y;
+              g[q * 4 + 2] = t4.z;
+              g[q * 4 + 3] = t4.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) g[j] = gate_row[n + j];
+          }
+        }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const uint32_t rw[4] = {rv[q].x, rv[q].y, rv[q].z, rv[q].w};
+          const uint32_t rw[4] = {rr.v[i][q].x, rr.v[i][q].y, rr.v[i][q].z, rr.v[i][q].w};
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
             float2 f = unpack_bf16x2(rw[t]);
             const int j = q * 8 + t * 2;
             if (EPI == kEpiGatedRes) {
-              v[j] = f.x + gate_row[n + j] * v[j];
-              v[j + 1] = f.y + gate_row[n + j + 1] * v[j + 1];
+              v[j] = f.x + g[j] * v[j];
+              v[j + 1] = f.y + g[j + 1] * v[j + 1];
             } else {
               v[j] = f.x + v[j];
               v[j + 1] = f.y + v[j + 1];
@@ -241,24 +274,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = quarter * 32 + lane;
     const int col_half = (warp - 2) / 4;
     constexpr int kChunks = BN / 32;
-    const int c_begin = col_half * (kChunks / 2), c_end = c_begin + kChunks / 2;
+    const int c_begin = col_half * (kChunks / 2);
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       const int m0 = (tile / num_n) * kBM;
       const int n0 = (tile % num_n) * BN;
-      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, 30)) break;
-      tc_fence_after();
       const int m = m0 + row_in_tile;
       const bool row_ok = m < p.M;
+      ResidualRow<kChunks / 2> rr;
+      prefetch_residual<kChunks / 2, EPI>(p, m, row_ok, n0, c_begin, rr);
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, 30)) break;
+      tc_fence_after();
       const float* gate_row = nullptr;
       if (EPI == kEpiGatedRes && row_ok) {
         const int bidx = p.row_batch != nullptr ? __ldg(p.row_batch + m) : m / p.rows_per_batch;
         gate_row = p.gate + static_cast<int64_t>(bidx) * p.gate_stride;
       }
-      epilogue_rows<BN, EPI>(p, tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN, m, row_ok, n0,
-                             gate_row, c_begin, c_end);
+      epilogue_rows<BN, EPI, kChunks / 2>(p, tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN, m,
+                                          row_ok, n0, gate_row, c_begin, rr);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
     }
@@ -404,24 +439,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = quarter * 32 + lane;
     const int col_half = (warp - 2) / 4;
     constexpr int kChunks = BN / 32;
-    const int c_begin = col_half * (kChunks / 2), c_end = c_begin + kChunks / 2;
+    const int c_begin = col_half * (kChunks / 2);
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += pairs, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       const int m0 = (tile / num_n) * (2 * kBM) + static_cast<int>(rank) * kBM;
       const int n0 = (tile % num_n) * BN;
-      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, 43)) break;
-      tc_fence_after();
       const int m = m0 + row_in_tile;
       const bool row_ok = m < p.M;
+      ResidualRow<kChunks / 2> rr;
+      prefetch_residual<kChunks / 2, EPI>(p, m, row_ok, n0, c_begin, rr);
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, 43)) break;
+      tc_fence_after();
       const float* gate_row = nullptr;
       if (EPI == kEpiGatedRes && row_ok) {
         const int bidx = p.row_batch != nullptr ? __ldg(p.row_batch + m) : m / p.rows_per_batch;
         gate_row = p.gate + static_cast<int64_t>(bidx) * p.gate_stride;
       }
-      epilogue_rows<BN, EPI>(p, tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN, m, row_ok, n0,
-                             gate_row, c_begin, c_end);
+      epilogue_rows<BN, EPI, kChunks / 2>(p, tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN, m,
+                                          row_ok, n0, gate_row, c_begin, rr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));

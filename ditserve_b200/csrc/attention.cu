@@ -134,7 +134,10 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 // kPChunks: the softmax hands P to the MMA warp in this many column chunks (one mbarrier
 // phase per chunk), so the PV MMA of the first keys starts while the exponentials of the
 // last keys are still being computed.
-template <int D, int kPChunks, bool kTrace = false, int kTiles = 2>
+// kDiag (timeline builds only, DS_ATTN_DIAG; the output is then not attention): removes one
+// ingredient of the softmax loop to see what the exponential phase is waiting on.
+//   1: no P stores to tensor memory; 2: no bf16 packing; 4: no row sums; 8: a multiply instead of ex2
+template <int D, int kPChunks, bool kTrace = false, int kTiles = 2, int kDiag = 0>
 __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1 : 2)
     attention2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ KvMaps kv,
                       AttnParams p) {
@@ -443,11 +446,22 @@ __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1
       uint32_t pk8[8];
       auto p_chunk = [&](int ch, float (&e8)[8]) {
         const int q = (ch & 1) * 4;
-        pk8[q + 0] = pack_bf16x2(e8[0], e8[1]);
-        pk8[q + 1] = pack_bf16x2(e8[2], e8[3]);
-        pk8[q + 2] = pack_bf16x2(e8[4], e8[5]);
-        pk8[q + 3] = pack_bf16x2(e8[6], e8[7]);
-        if (ch & 1) tmem_st8(s_col + (ch >> 1) * 8, pk8);
+        if (kDiag & 2) {
+          pk8[q + 0] = __float_as_uint(e8[0]) ^ __float_as_uint(e8[1]);
+          pk8[q + 1] = __float_as_uint(e8[2]) ^ __float_as_uint(e8[3]);
+          pk8[q + 2] = __float_as_uint(e8[4]) ^ __float_as_uint(e8[5]);
+          pk8[q + 3] = __float_as_uint(e8[6]) ^ __float_as_uint(e8[7]);
+        } else {
+          pk8[q + 0] = pack_bf16x2(e8[0], e8[1]);
+          pk8[q + 1] = pack_bf16x2(e8[2], e8[3]);
+          pk8[q + 2] = pack_bf16x2(e8[4], e8[5]);
+          pk8[q + 3] = pack_bf16x2(e8[6], e8[7]);
+        }
+        if (kDiag & 1) {
+          if (ch == kKT / 8 - 1) tmem_st8(s_col, pk8);  // keep one store so the values stay live
+        } else if (ch & 1) {
+          tmem_st8(s_col + (ch >> 1) * 8, pk8);
+        }
       };
       if (masked) {
 #pragma unroll
@@ -482,11 +496,19 @@ __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1
             const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2x2, negx2);
             float x0, x1;
             f2_unpack(x2, x0, x1);
-            e8[e] = ex2_approx(x0);
-            e8[e + 1] = ex2_approx(x1);
-            ls[e] += e8[e];
-            ls[e + 1] += e8[e + 1];
+            if (kDiag & 8) {
+              e8[e] = x0 * 0.5f;
+              e8[e + 1] = x1 * 0.5f;
+            } else {
+              e8[e] = ex2_approx(x0);
+              e8[e + 1] = ex2_approx(x1);
+            }
+            if (!(kDiag & 4)) {
+              ls[e] += e8[e];
+              ls[e + 1] += e8[e + 1];
+            }
           }
+          if (kDiag & 4) ls[0] += e8[7];
           p_chunk(ch, e8);
           if (kPChunks > 1 && early && ((ch + 1) % kChunkCh) == 0) {
             tmem_wait_st();
@@ -642,6 +664,20 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
               : pchunks == 1     ? attention2_kernel<D, 1>
               : pchunks == 4     ? attention2_kernel<D, 4>
                                  : attention2_kernel<D, 2>;
+  if (a.trace != nullptr && D == 128) {
+    static const int diag = [] {
+      const char* e = std::getenv("DS_ATTN_DIAG");
+      return e != nullptr ? std::atoi(e) : 0;
+    }();
+    switch (diag) {
+      case 1: kern = attention2_kernel<D, 2, true, 2, 1>; break;
+      case 2: kern = attention2_kernel<D, 2, true, 2, 2>; break;
+      case 4: kern = attention2_kernel<D, 2, true, 2, 4>; break;
+      case 8: kern = attention2_kernel<D, 2, true, 2, 8>; break;
+      case 15: kern = attention2_kernel<D, 2, true, 2, 15>; break;
+      default: break;
+    }
+  }
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Cfg<D>::kSmemBytes);
   dim3 grid(blocks, a.heads, a.batch);
   kern<<<grid, kAttn2Threads, Attn2Cfg<D>::kSmemBytes, stream>>>(tq, kv, p);

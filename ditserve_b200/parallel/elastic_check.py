@@ -7,13 +7,17 @@
 * regroup transfer (SM stores and copy engines): a Wan-request-like snapshot (fp32 latents + solver history, ``--mb``
   MB in total) broadcast from rank 0 by ``PeerStateBroadcast`` and by
   ``broadcast_state_nccl``; both must be bit-identical to the source; device time of each
-  (max over ranks).  Rank 0 prints one JSON line.
+  (max over ranks);
+* regroup latency with group formation: wall clock from "form a new group of ranks 0 and 1" to
+  the first completed state transfer in it, for a peer-memory group and for a new NCCL group.
+Rank 0 prints one JSON line.
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
+import time
 from datetime import timedelta
 
 import torch
@@ -48,7 +52,7 @@ def main():
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     members = tuple(range(world))
     cap = int(args.mb * (1 << 20)) + (8 << 20)
-    heap = SymmetricHeap(cap + (4 << 20), dev)
+    heap = SymmetricHeap(2 * cap + (8 << 20), dev)  # two broadcasters (the second for the new group)
     fp, fn = GroupFlagPeer(heap, members), GroupFlagNCCL(None, dev)
     g = torch.Generator().manual_seed(11)
     agree = True
@@ -89,11 +93,36 @@ def main():
     bc_peer_ms = _timed(lambda: bc(src, 0), 5, dev)
     bc_nccl_ms = _timed(lambda: broadcast_state_nccl(src, 0, device=dev), 5, dev)
     nbytes = 4 * (4 * n + n + 3)
+    # regroup latency including group formation (host wall clock to the first completed transfer,
+    # max over ranks): a new peer-memory group is a host-side view of the existing heap, a new
+    # NCCL group creates a communicator on its first collective
+    sub = members[:2]
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    if rank in sub:
+        bc2 = PeerStateBroadcast(heap, sub, int(args.mb * (1 << 20)) + (2 << 20), channel=8)
+        bc2(src, 0)
+        torch.cuda.synchronize()
+    new_peer_ms = (time.perf_counter() - t0) * 1e3
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    pg = dist.new_group(list(sub))
+    if rank in sub:
+        broadcast_state_nccl(src, 0, device=dev, group=pg)
+        torch.cuda.synchronize()
+    new_nccl_ms = (time.perf_counter() - t0) * 1e3
+    tt = torch.tensor([new_peer_ms, new_nccl_ms], device=dev, dtype=torch.float64)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    new_peer_ms, new_nccl_ms = (float(v) for v in tt.tolist())
     out = dict(world=world, flags_agree=bool(agree), flag_peer_us=round(flag_peer_us, 1),
                flag_nccl_us=round(flag_nccl_us, 1), state_mb=round(nbytes / 2 ** 20, 1), broadcast_bitwise=bool(ok),
                broadcast_peer_ms=round(bc_peer_ms, 3), broadcast_nccl_ms=round(bc_nccl_ms, 3),
                broadcast_ce_bitwise=bool(ok_ce), broadcast_ce_ms=round(bc_ce_ms, 3),
-               broadcast_peer_gbs=round(nbytes * (world - 1) / bc_peer_ms / 1e6, 1))
+               broadcast_peer_gbs=round(nbytes * (world - 1) / bc_peer_ms / 1e6, 1),
+               new_group_first_transfer_peer_ms=round(new_peer_ms, 2),
+               new_group_first_transfer_nccl_ms=round(new_nccl_ms, 2))
     if rank == 0:
         print(json.dumps(out), flush=True)
     del ref

@@ -64,6 +64,13 @@ struct AttnParams {
   const int* blk_offsets;
   const int* blk_index;
   unsigned long long* trace;  // timeline of one CTA (kTrace instantiation only), else null
+  // work list (null: one CTA per (query block, head, batch) from the grid): CTA i runs
+  // work[i] = {query block | (partial slot + 1) << 16, head, batch, first key tile | end << 16};
+  // a CTA with a partial slot covers a key range of its unit and leaves unnormalised O and
+  // (max, sum) per row in part_o / part_ml for attention_merge
+  const int4* work;
+  float* part_o;    // [slots][kQBlock rows][D]
+  float2* part_ml;  // [slots][kQBlock rows]
 };
 
 // Timeline instrumentation (kTrace): one CTA in the middle of the grid records SM clock
@@ -145,8 +152,16 @@ __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1
   constexpr int KS = Cfg::KS;
   constexpr int VS = Cfg::VS;
   constexpr int kQBlock = kTiles * kQT;  // query rows per CTA
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
+  int qblk = blockIdx.x, h = blockIdx.y, b = blockIdx.z, slot = -1, kv_first = 0, kv_end = -1;
+  if (p.work != nullptr) {
+    const int4 wd = p.work[blockIdx.x];
+    qblk = wd.x & 0xffff;
+    slot = (wd.x >> 16) - 1;
+    h = wd.y;
+    b = wd.z;
+    kv_first = wd.w & 0xffff;
+    kv_end = wd.w >> 16;
+  }
   // segment = query rows [qa0,qa1) u [qb0,qb1) attending to keys [ka0,ka1) u [kb0,kb1)
   int qa0, qa1, qb0, qb1, ka0, ka1, kb0, kb1;
   if (p.seg != nullptr) {
@@ -165,11 +180,11 @@ __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1
   const int nqa = (qa1 - qa0 + kQBlock - 1) / kQBlock;
   const int nqb = (qb1 - qb0 + kQBlock - 1) / kQBlock;
   int q0, q_end;
-  if (static_cast<int>(blockIdx.x) < nqa) {
-    q0 = qa0 + blockIdx.x * kQBlock;
+  if (qblk < nqa) {
+    q0 = qa0 + qblk * kQBlock;
     q_end = qa1;
-  } else if (static_cast<int>(blockIdx.x) < nqa + nqb) {
-    q0 = qb0 + (blockIdx.x - nqa) * kQBlock;
+  } else if (qblk < nqa + nqb) {
+    q0 = qb0 + (qblk - nqa) * kQBlock;
     q_end = qb1;
   } else {
     return;
@@ -178,20 +193,25 @@ __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1
   const int* blk = nullptr;  // block-sparse: this query block's list of key tiles
   int per_source = nka + (kb1 - kb0 + kKT - 1) / kKT;
   if (p.blk_offsets != nullptr) {
-    const int o0 = p.blk_offsets[blockIdx.x];
+    const int o0 = p.blk_offsets[qblk];
     blk = p.blk_index + o0;
-    per_source = p.blk_offsets[blockIdx.x + 1] - o0;
+    per_source = p.blk_offsets[qblk + 1] - o0;
+  }
+  int kv_base = 0;  // work-list CTAs start at their first key tile (one source, one range)
+  if (p.work != nullptr) {
+    kv_base = kv_first;
+    per_source = kv_end - kv_first;
   }
   const int n_tiles = per_source * p.kv_sources;
   if (n_tiles <= 0) return;  // uniform across the CTA
   // tile j reads source j / per_source; within a source the segment's key ranges repeat
   auto ktile_row = [&](int j) {
-    const int jj = j % per_source;
+    const int jj = j % per_source + kv_base;
     if (blk != nullptr) return ka0 + blk[jj] * kKT;
     return jj < nka ? ka0 + jj * kKT : kb0 + (jj - nka) * kKT;
   };
   auto ktile_valid = [&](int j) {
-    const int jj = j % per_source;
+    const int jj = j % per_source + kv_base;
     if (blk != nullptr) return ka1 - (ka0 + blk[jj] * kKT);
     return jj < nka ? ka1 - (ka0 + jj * kKT) : kb1 - (kb0 + (jj - nka) * kKT);
   };
@@ -241,7 +261,7 @@ __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const bool tracing = kTrace && p.trace != nullptr && blockIdx.x == gridDim.x / 2 && blockIdx.y == 0 &&
+  const bool tracing = kTrace && p.trace != nullptr && qblk == static_cast<int>(gridDim.x / 2) && blockIdx.y == 0 &&
                        blockIdx.z == 0;
   auto rec = [&](int j, int e) {
     if (kTrace && tracing && j < kTraceTiles) p.trace[j * kTraceEvents + e] = clock64();
@@ -540,6 +560,24 @@ __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1
       srec(j, kTrArrive);
     }
     if (ok) ok = mbar_wait(&pv_done[t], (n_tiles - 1) & 1, abort_flag, p.status, 234 + t);
+    if (ok && slot >= 0) {
+      // partial unit: unnormalised O and (max, sum) of this key range, merged by attention_merge
+      tc_fence_after();
+      const int64_t prow = static_cast<int64_t>(slot) * kQBlock + t * kQT + row;
+      float4* dst = reinterpret_cast<float4*>(p.part_o + prow * D);
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_col + c * 32, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          dst[c * 8 + q] = make_float4(__uint_as_float(o[q * 4]), __uint_as_float(o[q * 4 + 1]),
+                                       __uint_as_float(o[q * 4 + 2]), __uint_as_float(o[q * 4 + 3]));
+      }
+      p.part_ml[prow] = make_float2(m_run, l_run);
+      ok = false;  // the bf16 epilogue below is the merge kernel's job
+    }
     if (ok) {
       tc_fence_after();
       const int qabs = q0 + t * kQT + row;  // absolute row of q / o
@@ -595,6 +633,79 @@ __global__ void __launch_bounds__(Attn2Cfg<D, kTiles>::kThreads, kTiles == 2 ? 1
   }
 }
 
+// Combines the key-range partials of split units: one warp per (unit, query row).  With
+// part i = (m_i, l_i, O_i) over its key range, M = max m_i, w_i = 2^((m_i - M) * scale_log2):
+// O = sum w_i O_i / sum w_i l_i and LSE = M * scale + ln(sum w_i l_i).  The row is written
+// where the attention epilogue would have written it (locally or into its owner's buffer).
+struct MergeParams {
+  const int4* units;  // {query block, head, batch, first slot | parts << 16}
+  int num_units;
+  const float* part_o;
+  const float2* part_ml;
+  int seq_q;
+  float scale_log2, scale;
+  __nv_bfloat16* o;
+  int64_t o_stride;
+  float* lse;
+  int64_t lse_stride;
+  int o_scatter;
+  PeerGroup o_group;
+  int64_t o_off;
+  int o_seq_local;
+  int o_head_offset;
+  int64_t o_peer_stride;
+};
+
+template <int D, int kQBlock>
+__global__ void __launch_bounds__(256) attention_merge_kernel(MergeParams p) {
+  constexpr int kPer = D / 32;  // columns per lane
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int unit = gw / kQBlock;
+  const int r = gw - unit * kQBlock;
+  if (unit >= p.num_units) return;
+  const int4 u = p.units[unit];
+  const int q = u.x * kQBlock + r;
+  if (q >= p.seq_q) return;
+  const int h = u.y, b = u.z, slot0 = u.w & 0xffff, parts = u.w >> 16;
+  float mmax = -INFINITY;
+  for (int i = 0; i < parts; ++i) mmax = fmaxf(mmax, p.part_ml[static_cast<int64_t>(slot0 + i) * kQBlock + r].x);
+  float acc[kPer];
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) acc[e] = 0.f;
+  float lsum = 0.f;
+  for (int i = 0; i < parts; ++i) {
+    const int64_t prow = static_cast<int64_t>(slot0 + i) * kQBlock + r;
+    const float2 ml = p.part_ml[prow];
+    const float w = ex2_approx((ml.x - mmax) * p.scale_log2);
+    lsum += w * ml.y;
+    const float* src = p.part_o + prow * D + lane * kPer;
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) acc[e] += w * src[e];
+  }
+  const float inv = 1.0f / lsum;
+  __nv_bfloat16* orow;
+  if (p.o_scatter) {
+    const int owner = q / p.o_seq_local;
+    const int local = q - owner * p.o_seq_local;
+    __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(
+        reinterpret_cast<uint8_t*>(p.o_group.base[owner < p.o_group.size ? owner : 0]) + p.o_off);
+    orow = base + (static_cast<int64_t>(b) * p.o_seq_local + local) * p.o_peer_stride + (p.o_head_offset + h) * D;
+  } else {
+    orow = p.o + (static_cast<int64_t>(b) * p.seq_q + q) * p.o_stride + h * D;
+  }
+  if (kPer == 4) {
+    uint2 v;
+    v.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+    v.y = pack_bf16x2(acc[2 % kPer] * inv, acc[3 % kPer] * inv);
+    *reinterpret_cast<uint2*>(orow + lane * kPer) = v;
+  } else {
+    *reinterpret_cast<uint32_t*>(orow + lane * kPer) = pack_bf16x2(acc[0] * inv, acc[1 % kPer] * inv);
+  }
+  if (lane == 0 && p.lse != nullptr)
+    p.lse[static_cast<int64_t>(h) * p.lse_stride + static_cast<int64_t>(b) * p.seq_q + q] = mmax * p.scale + logf(lsum);
+}
+
 template <int D>
 void launch_d(const AttnArgs& a, cudaStream_t stream) {
   CUtensorMap tq = make_tmap_bf16_2d(a.q, a.total_q, static_cast<uint64_t>(a.heads) * D, a.q_row_stride, kQT);
@@ -632,6 +743,12 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
   p.o_peer_stride = a.o_peer_stride;
   p.blk_offsets = a.blk_offsets;
   p.blk_index = a.blk_index;
+  p.work = a.work;
+  p.part_o = a.part_o;
+  p.part_ml = reinterpret_cast<float2*>(a.part_ml);
+  if (a.work != nullptr && (a.seg_table != nullptr || a.cu_seqlens_q != nullptr || a.blk_offsets != nullptr ||
+                            a.kv_sources != 1 || a.trace != nullptr))
+    throw std::runtime_error("attention: a work list needs uniform batches, one KV source, no sparse table");
   if (a.blk_offsets != nullptr && (a.seg_table != nullptr || a.kv_sources != 1))
     throw std::runtime_error("attention: block-sparse key tiles need one KV source and no dual-range table");
   // grid.x: 256-row query blocks of the longest segment (both ranges in dual-range mode)
@@ -652,7 +769,7 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
     return e != nullptr ? std::atoi(e) : 1024;
   }();
   const bool uniform = a.cu_seqlens_q == nullptr && a.seg_table == nullptr && a.blk_offsets == nullptr;
-  if (uniform && a.trace == nullptr && static_cast<int64_t>(a.seq_k) * a.kv_sources <= short_kv) {
+  if (uniform && a.trace == nullptr && a.work == nullptr && static_cast<int64_t>(a.seq_k) * a.kv_sources <= short_kv) {
     using C1 = Attn2Cfg<D, 1>;
     auto kern1 = attention2_kernel<D, 2, false, 1>;
     cudaFuncSetAttribute(kern1, cudaFuncAttributeMaxDynamicSharedMemorySize, C1::kSmemBytes);
@@ -679,6 +796,34 @@ void launch_d(const AttnArgs& a, cudaStream_t stream) {
     }
   }
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Cfg<D>::kSmemBytes);
+  if (a.work != nullptr) {
+    // work list: whole units first, then the key-range parts of the tail units; the merge
+    // kernel runs after them on the same stream
+    kern<<<a.num_work, kAttn2Threads, Attn2Cfg<D>::kSmemBytes, stream>>>(tq, kv, p);
+    if (a.num_merge_units > 0) {
+      MergeParams mp;
+      mp.units = a.merge_units;
+      mp.num_units = a.num_merge_units;
+      mp.part_o = a.part_o;
+      mp.part_ml = reinterpret_cast<const float2*>(a.part_ml);
+      mp.seq_q = a.seq_q;
+      mp.scale_log2 = p.scale_log2;
+      mp.scale = p.scale;
+      mp.o = p.o;
+      mp.o_stride = p.o_stride;
+      mp.lse = p.lse;
+      mp.lse_stride = p.lse_stride;
+      mp.o_scatter = p.o_scatter;
+      mp.o_group = p.o_group;
+      mp.o_off = p.o_off;
+      mp.o_seq_local = p.o_seq_local;
+      mp.o_head_offset = p.o_head_offset;
+      mp.o_peer_stride = p.o_peer_stride;
+      const int warps = a.num_merge_units * 2 * kQT;
+      attention_merge_kernel<D, 2 * kQT><<<(warps + 7) / 8, 256, 0, stream>>>(mp);
+    }
+    return;
+  }
   dim3 grid(blocks, a.heads, a.batch);
   kern<<<grid, kAttn2Threads, Attn2Cfg<D>::kSmemBytes, stream>>>(tq, kv, p);
 }

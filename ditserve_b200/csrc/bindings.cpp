@@ -8,6 +8,10 @@
 #include <c10/cuda/CUDAException.h>
 
 #include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <tuple>
 
 #include "kernels.h"
 
@@ -22,6 +26,99 @@ void check_cuda_bf16_2d(const at::Tensor& t, const char* name) {
 }
 
 const void* opt_ptr(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr() : nullptr; }
+
+// Tail split of the attention grid.  With U (query block, head, batch) units of 256 rows over
+// S SMs (one CTA each), the last round holds U mod S units and leaves the rest of the GPU
+// idle.  Those tail units are cut into k key ranges (k chosen to fill the last round best),
+// their parts run after the whole units and attention_merge combines them.  The work list and
+// the merge table depend only on the shape, so they are built once per (device, shape).
+struct SplitPlan {
+  at::Tensor work;    // int32 [num_work, 4] on the device
+  at::Tensor merge;   // int32 [num_merge, 4] on the device
+  int num_work = 0, num_merge = 0, slots = 0;
+};
+
+const SplitPlan* split_plan(int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads, const at::Device& dev) {
+  static const bool enabled = [] {
+    const char* e = std::getenv("DS_ATTN_SPLIT");
+    return e == nullptr || std::atoi(e) != 0;
+  }();
+  if (!enabled) return nullptr;
+  static std::mutex mu;
+  static std::map<std::tuple<int, int64_t, int64_t, int64_t, int64_t>, std::unique_ptr<SplitPlan>> cache;
+  const auto key = std::make_tuple(static_cast<int>(dev.index()), batch, seq_q, seq_k, heads);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second.get();
+  std::unique_ptr<SplitPlan> plan;
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev.index());
+  const int64_t nq = (seq_q + 255) / 256, tiles = (seq_k + 127) / 128, units = nq * heads * batch;
+  const int64_t full = sms > 0 ? units / sms : 0, tail = sms > 0 ? units - full * sms : 0;
+  // time in unit lengths: full + 1 without a split, full + ceil(tail * k / sms) / k with one
+  int best_k = 1;
+  double best_t = static_cast<double>(full + 1);
+  for (int k = 2; k <= 8 && tail > 0 && tiles / k >= 8; ++k) {
+    const double t = full + static_cast<double>((tail * k + sms - 1) / sms) / k;
+    if (t < best_t * 0.97) {
+      best_t = t;
+      best_k = k;
+    }
+  }
+  if (best_k > 1 && units < (1 << 16) && tiles < (1 << 16)) {
+    plan = std::make_unique<SplitPlan>();
+    std::vector<int32_t> work, merge;
+    const int64_t whole = units - tail;
+    auto unit_of = [&](int64_t u, int32_t& qb, int32_t& h, int32_t& b) {
+      qb = static_cast<int32_t>(u % nq);
+      h = static_cast<int32_t>((u / nq) % heads);
+      b = static_cast<int32_t>(u / (nq * heads));
+    };
+    for (int64_t u = 0; u < whole; ++u) {
+      int32_t qb, h, b;
+      unit_of(u, qb, h, b);
+      work.insert(work.end(), {qb, h, b, static_cast<int32_t>(0 | (tiles << 16))});
+    }
+    int32_t slot = 0;
+    for (int64_t u = whole; u < units; ++u) {
+      int32_t qb, h, b;
+      unit_of(u, qb, h, b);
+      merge.insert(merge.end(), {qb, h, b, static_cast<int32_t>(slot | (best_k << 16))});
+      for (int i = 0; i < best_k; ++i) {
+        const int32_t t0 = static_cast<int32_t>(tiles * i / best_k), t1 = static_cast<int32_t>(tiles * (i + 1) / best_k);
+        work.insert(work.end(), {static_cast<int32_t>(qb | ((slot + 1) << 16)), h, b, static_cast<int32_t>(t0 | (t1 << 16))});
+        ++slot;
+      }
+    }
+    auto opts = at::TensorOptions().dtype(at::kInt);
+    plan->num_work = static_cast<int>(work.size() / 4);
+    plan->num_merge = static_cast<int>(merge.size() / 4);
+    plan->slots = slot;
+    plan->work = at::from_blob(work.data(), {plan->num_work, 4}, opts).clone().to(dev);
+    plan->merge = at::from_blob(merge.data(), {plan->num_merge, 4}, opts).clone().to(dev);
+  }
+  const SplitPlan* out = plan.get();
+  cache.emplace(key, std::move(plan));
+  return out;
+}
+
+// Fills the work-list fields of `a` for a uniform one-source call when a split pays; the
+// partial buffers come from the caching allocator and live until the launch is enqueued
+// (stream-ordered reuse keeps them valid for the kernels that use them).
+void apply_split(ds::AttnArgs& a, const at::Device& dev, std::vector<at::Tensor>& keep) {
+  if (a.kv_sources != 1 || a.head_dim != 128) return;
+  const SplitPlan* plan = split_plan(a.batch, a.seq_q, a.seq_k, a.heads, dev);
+  if (plan == nullptr) return;
+  auto f = at::TensorOptions().dtype(at::kFloat).device(dev);
+  keep.push_back(at::empty({static_cast<int64_t>(plan->slots) * 256 * a.head_dim}, f));
+  keep.push_back(at::empty({static_cast<int64_t>(plan->slots) * 256 * 2}, f));
+  a.part_o = keep[keep.size() - 2].data_ptr<float>();
+  a.part_ml = keep.back().data_ptr<float>();
+  a.work = reinterpret_cast<const int4*>(plan->work.data_ptr<int32_t>());
+  a.num_work = plan->num_work;
+  a.merge_units = reinterpret_cast<const int4*>(plan->merge.data_ptr<int32_t>());
+  a.num_merge_units = plan->num_merge;
+}
 
 int* status_ptr(const at::Tensor& status) {
   TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt && status.numel() >= 2,
@@ -162,6 +259,9 @@ void attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
     a.blk_offsets = blk_offsets->data_ptr<int>();
     a.blk_index = blk_index->data_ptr<int>();
   }
+  std::vector<at::Tensor> keep;
+  if (!seg.has_value() && !cu_q.has_value() && !blk_offsets.has_value() && k_extra.empty() && seq_k > 1024)
+    apply_split(a, q.device(), keep);
   ds::launch_attention(a, at::cuda::getCurrentCUDAStream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }
@@ -501,6 +601,8 @@ void attention_scatter(const at::Tensor& q, const at::Tensor& k, const at::Tenso
     a.k_extra[i] = reinterpret_cast<const void*>(k_extra_ptrs[i]);
     a.v_extra[i] = reinterpret_cast<const void*>(v_extra_ptrs[i]);
   }
+  std::vector<at::Tensor> keep;
+  if (k_extra_ptrs.empty() && seq > 1024) apply_split(a, q.device(), keep);
   ds::launch_attention(a, at::cuda::getCurrentCUDAStream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();  // a failed launch raises here, never passes silently
 }

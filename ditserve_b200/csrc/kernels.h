@@ -95,6 +95,17 @@ struct AttnArgs {
   const int* blk_index = nullptr;
   // optional timeline of one CTA (SM clock stamps, [32 tiles][24 events]); profiling only
   unsigned long long* trace = nullptr;
+  // optional work list (uniform batches, one KV source): CTA i runs work[i] =
+  // {query block | (partial slot + 1) << 16, head, batch, first key tile | end tile << 16};
+  // partial slots leave fp32 O [slots][256][head_dim] in part_o and (max, sum) [slots][256]
+  // in part_ml, and merge_units[u] = {query block, head, batch, first slot | parts << 16}
+  // name the units whose parts attention_merge combines into the output
+  const int4* work = nullptr;
+  int num_work = 0;
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+  const int4* merge_units = nullptr;
+  int num_merge_units = 0;
 };
 void launch_attention(const AttnArgs& a, cudaStream_t stream);
 

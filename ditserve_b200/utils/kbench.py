@@ -52,6 +52,7 @@ def main():
     ap.add_argument("--json", default=None)
     ap.add_argument("--tokens", type=int, default=32760)
     ap.add_argument("--batch", type=int, default=2)
+    ap.add_argument("--heads", type=int, default=12, help="attention heads of --only attention (the per-GPU heads of a form)")
     ap.add_argument("--only", default=None, help="'fused': only the peer-memory kernels on a one-member group; 'attention': self-attention only; "
                          "'memory': the per-token norm kernels and qkv_scatter; 'cross': cross-attention (512 keys) only; 'trace': SM-clock timeline of one self-attention CTA")
     args = ap.parse_args()
@@ -76,12 +77,14 @@ def main():
 
     torch.manual_seed(0)
     if args.only == "attention":
+        H = args.heads
+        D = H * 128
         qkv = torch.randn(M, 3 * D, device=dev).bfloat16()
         q, k, v = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
         o = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
         ms = timeit(lambda: ops.attention(q.view(B, S, D), k.view(B, S, D), v.view(B, S, D), H, out=o), iters=5)
         ops.check_status(dev)  # a kernel whose bounded waits ran out raises here instead of printing a time
-        row("self_attention", ms, flops=4.0 * B * H * S * S * 128, impl="ours")
+        row("self_attention", ms, flops=4.0 * B * H * S * S * 128, impl="ours", shape=[B, S, H, 128])
         if args.json:
             json.dump(res, open(args.json, "w"), indent=1)
         return

@@ -346,3 +346,36 @@ def test_short_kv_form_equals_two_tile_form_bitwise(tmp_path, B, Sq, Sk, H, D):
     assert torch.equal(o.cpu(), o2) and torch.equal(lse.cpu(), l2)
     ro = ops.attention_reference(q, k, v, H)
     assert _rel(o.cpu(), ro) < 2e-2
+
+
+@pytest.mark.parametrize("B,S,H", [(1, 4096, 3), (2, 2100, 4), (1, 33000, 1)])
+def test_tail_split_matches_unsplit_and_fp32(tmp_path, B, S, H):
+    """Units of the last partial round run as key-range parts merged by attention_merge
+    (DS_ATTN_SPLIT, on by default); against the unsplit grid (a child process with the split
+    off) only the merge's rounding differs, and both match the fp32 statement."""
+    import os
+    import subprocess
+    import sys
+    D = 128
+    torch.manual_seed(12)
+    d = _dev()
+    q = torch.randn(B, S, H * D).bfloat16()
+    k = torch.randn(B, S, H * D).bfloat16()
+    v = torch.randn(B, S, H * D).bfloat16()
+    torch.save((q, k, v), tmp_path / "in.pt")
+    o, lse = ops.attention(q.to(d), k.to(d), v.to(d), H, return_lse=True)
+    ops.check_status(d)
+    code = ("import torch,sys;from ditserve_b200 import ops\n"
+            "q,k,v=torch.load(sys.argv[1]);d=torch.device('cuda',0)\n"
+            f"o,l=ops.attention(q.to(d),k.to(d),v.to(d),{H},return_lse=True);ops.check_status(d)\n"
+            "torch.save((o.cpu(),l.cpu()),sys.argv[2])\n")
+    r = subprocess.run([sys.executable, "-c", code, str(tmp_path / "in.pt"), str(tmp_path / "out.pt")],
+                       env=dict(os.environ, DS_ATTN_SPLIT="0"), capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    o2, l2 = torch.load(tmp_path / "out.pt")
+    assert _rel(o.cpu(), o2) < 5e-3, _rel(o.cpu(), o2)
+    assert (lse.cpu() - l2).abs().max().item() < 1e-3
+    if S <= 4096:
+        ro, rl = ops.attention_reference(q, k, v, H, return_lse=True)
+        assert _rel(o.cpu(), ro) < 2e-2
+        torch.testing.assert_close(lse.cpu().reshape(H, B, S).transpose(0, 1), rl, rtol=1e-3, atol=2e-2)

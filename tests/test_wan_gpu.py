@@ -109,8 +109,10 @@ def _fp32_attention(q, k, v, batch, seq, heads, hd):
     return (p @ vh).transpose(1, 2).reshape(batch * seq, heads * hd)
 
 
-@pytest.mark.parametrize("heads,hd,seq", [(12, 128, 333), (8, 64, 400)])
+@pytest.mark.parametrize("heads,hd,seq", [(12, 128, 333), (8, 64, 400), (4, 128, 2100)])
 def test_fused_ulysses_kernels_as_a_one_member_group(heads, hd, seq):
+    # (4, 128, 2100): 72 query-block units on 148 SMs, so the attention grid runs key-range
+    # parts and the merge kernel stores the rows through the peer-store path
     dev = torch.device("cuda", 0)
     ext = ops.ext()
     batch, eps = 2, 1e-6

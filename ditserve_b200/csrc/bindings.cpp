@@ -38,6 +38,23 @@ struct SplitPlan {
   int num_work = 0, num_merge = 0, slots = 0;
 };
 
+// Number of key ranges for the tail units (1: no split): the k in 2..8 (each range at least 8
+// key tiles) that minimises full + ceil(tail * k / sms) / k, kept only when it saves 3 %.
+int tail_split_parts(int64_t units, int64_t tiles, int64_t sms) {
+  if (sms <= 0) return 1;
+  const int64_t full = units / sms, tail = units - full * sms;
+  int best_k = 1;
+  double best_t = static_cast<double>(full + 1);
+  for (int k = 2; k <= 8 && tail > 0 && tiles / k >= 8; ++k) {
+    const double t = full + static_cast<double>((tail * k + sms - 1) / sms) / k;
+    if (t < best_t * 0.97) {
+      best_t = t;
+      best_k = k;
+    }
+  }
+  return best_k;
+}
+
 const SplitPlan* split_plan(int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads, const at::Device& dev) {
   static const bool enabled = [] {
     const char* e = std::getenv("DS_ATTN_SPLIT");
@@ -54,17 +71,8 @@ const SplitPlan* split_plan(int64_t batch, int64_t seq_q, int64_t seq_k, int64_t
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev.index());
   const int64_t nq = (seq_q + 255) / 256, tiles = (seq_k + 127) / 128, units = nq * heads * batch;
-  const int64_t full = sms > 0 ? units / sms : 0, tail = sms > 0 ? units - full * sms : 0;
-  // time in unit lengths: full + 1 without a split, full + ceil(tail * k / sms) / k with one
-  int best_k = 1;
-  double best_t = static_cast<double>(full + 1);
-  for (int k = 2; k <= 8 && tail > 0 && tiles / k >= 8; ++k) {
-    const double t = full + static_cast<double>((tail * k + sms - 1) / sms) / k;
-    if (t < best_t * 0.97) {
-      best_t = t;
-      best_k = k;
-    }
-  }
+  const int64_t tail = sms > 0 ? units % sms : 0;
+  const int best_k = tail_split_parts(units, tiles, sms);
   if (best_k > 1 && units < (1 << 16) && tiles < (1 << 16)) {
     plan = std::make_unique<SplitPlan>();
     std::vector<int32_t> work, merge;
@@ -749,6 +757,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("group_barrier", &group_barrier, "bounded flag barrier over peer memory");
   m.def("cfg_step_peer", &cfg_step_peer, "CFG exchange over NVLink fused with guidance + latent update");
   m.def("qkv_scatter", &qkv_scatter, "RMS qk-norm + RoPE + Ulysses all-to-all scatter");
+  m.def("attention_tail_split_parts", [](int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads, int64_t sms) {
+    return tail_split_parts(((seq_q + 255) / 256) * heads * batch, (seq_k + 127) / 128, sms);
+  }, "key ranges the attention grid gives its tail units (1: no split) for a shape on `sms` SMs");
   m.def("attention_trace", &attention_trace, "attention with a one-CTA clock timeline (profiling)");
   m.def("attention_scatter", &attention_scatter, "attention with the head->sequence all-to-all in its epilogue");
   m.def("allgather_rows", &allgather_rows, "sequence all-gather by peer stores");

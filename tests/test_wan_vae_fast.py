@@ -84,3 +84,14 @@ def test_conv_kernel_decode_matches_fp32_cpu(variant):
     assert out.shape == ref.shape
     rel = ((out.float().cpu() - ref).norm() / ref.norm()).item()
     assert rel < 5e-2, rel
+
+
+def test_decode_halo_transport_choice():
+    from ditserve_b200.models.wan.backend import decode_halo_transport
+    assert decode_halo_transport("auto", 2, "cuda") == "peer"
+    assert decode_halo_transport("auto", 4, "cuda") == "nccl"
+    assert decode_halo_transport("peer", 8, "cuda") == "peer"
+    assert decode_halo_transport("auto", 2, "cpu") == "nccl"
+    import pytest
+    with pytest.raises(ValueError):
+        decode_halo_transport("nvls", 2, "cuda")
